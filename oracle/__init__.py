@@ -1,0 +1,22 @@
+"""CPU oracle for the mzoo attention hot path -- TEST INFRASTRUCTURE ONLY.
+
+This package restates, in numpy (float32 / float64 on the host), the arithmetic of
+pmonad/mzoo's pure-PyTorch reference for the path the CUDA library replaces:
+
+- ``oracle.quant``     fp8 / fp4 fake-quant rules (``src/mzoo/archs/owlet1/quant.py``)
+                       plus the OCP-MXFP4 and FP8-per-tile-absmax rules;
+- ``oracle.attention`` window / sparse shared-latent attention, forward and backward
+                       (``src/mzoo/layers/attn/golden_ref.py``);
+- ``oracle.indexer``   lightning-indexer scores and top-k
+                       (``golden_ref.py:213-243``, ``indexer/fwd.py``, ``indexer/bwd.py``);
+- ``oracle.mla``       576/512 latent sparse prefill and paged decode over FP8 rows.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
+import it, and only as the checker.  The product path (``mzoo_b200``) never imports
+anything from here and has no CPU fallback.
+
+Pinning: ``tests/golden/`` holds input/output vectors produced by importing the
+reference itself (``tests/golden/make_golden.py``); ``tests/test_oracle.py`` checks
+this oracle against them bit-for-bit (quant, top-k sets) or to fp32 rounding
+(attention, scores).
+"""

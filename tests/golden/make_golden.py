@@ -1,0 +1,132 @@
+"""Generate the golden input/output vectors under ``tests/golden/`` by running the
+reference (pmonad/mzoo) itself on the CPU.
+
+Run in a container where the reference sources are importable, e.g.::
+
+    MZOO_REF_SRC=<path to mzoo>/src python tests/golden/make_golden.py
+
+It imports the reference's pure-PyTorch functions
+(``mzoo.archs.owlet1.quant``, ``mzoo.layers.attn.golden_ref``) and writes small ``.npz``
+fixtures.  Nothing at test time imports the reference: the fixtures are the pin.
+bf16 tensors are stored as uint16 bit patterns.
+"""
+
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _ref():
+    src = os.environ.get("MZOO_REF_SRC")
+    if src:
+        sys.path.insert(0, src)
+    from mzoo.archs.owlet1 import quant  # noqa: E402
+    from mzoo.layers.attn import golden_ref  # noqa: E402
+    return quant, golden_ref
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.bfloat16:
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+    return t.contiguous().numpy()
+
+
+def quant_inputs(seed: int) -> dict:
+    """Random blocks plus hand-picked edge cases: ties of the e2m1 grid, exact
+    thresholds, zeros, negative zero, tiny (subnormal) and large magnitudes."""
+    g = torch.Generator().manual_seed(seed)
+    cases = {}
+    cases["randn"] = torch.randn(8, 4, 128, generator=g)
+    cases["wide"] = torch.randn(4, 256, generator=g) * torch.logspace(-30, 30, 256).view(1, 256)
+    # e2m1 ties: an amax of 6 makes the ue8m0 scale exactly 1, so q == x
+    ties = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0,
+                         -0.25, -0.75, -1.25, -1.75, -2.5, -3.5, -5.0, -6.0,
+                         0.0, -0.0, 0.2499, 0.2501, 0.7499, 0.7501, 1.2501, 1.7499,
+                         2.4999, 2.5001, 3.4999, 3.5001, 4.9999, 5.0001, 1e-30, -1e-30])
+    cases["ties"] = ties.view(1, 32)
+    cases["zeros"] = torch.zeros(2, 64)
+    cases["tiny"] = torch.randn(2, 64, generator=g) * 1e-38
+    cases["huge"] = torch.randn(2, 64, generator=g) * 1e30
+    # fp8: values straddling e4m3 rounding points after a pow2 scale of 1 (amax 448)
+    fp8 = torch.tensor([448.0, 240.0, 232.0, 248.0, 17.0, 19.0, 0.001953125, 0.0029296875,
+                        0.0009765625, 0.015625, 0.0146484375, -0.013671875, 1.0625, 1.1875, -3.25, 0.0])
+    cases["fp8pts"] = fp8.repeat(2).view(1, 32)
+    cases["ragged"] = torch.randn(3, 40, generator=g)  # 40 % 32 != 0 -> returned unchanged
+    return cases
+
+
+def make_quant(quant) -> None:
+    out = {}
+    for name, x in quant_inputs(0).items():
+        for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+            xx = x.to(dt)
+            out[f"{name}.{tag}.x"] = bits(xx)
+            out[f"{name}.{tag}.fp4_32"] = bits(quant._fake_quant_fp4_block(xx, 32))
+            out[f"{name}.{tag}.fp4_16e4m3"] = bits(quant._fake_quant_fp4_block(xx, 16, e4m3_scales=True))
+            out[f"{name}.{tag}.fp8_32"] = bits(quant._fake_quant_fp8_block(xx, 32))
+            out[f"{name}.{tag}.fp8_16"] = bits(quant._fake_quant_fp8_block(xx, 16))
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **out)
+
+
+def make_attention(golden_ref) -> None:
+    out = {}
+    g = torch.Generator().manual_seed(1)
+    # window level, fp32, with and without sinks (golden_ref.py:103-147)
+    b, s, h, d = 1, 96, 4, 32
+    q = torch.randn(b, s, h, d, generator=g)
+    kv = torch.randn(b, s, 1, d, generator=g)
+    sinks = torch.randn(h, generator=g)
+    for w in (1, 16, 40, 200):
+        o, lse = golden_ref.golden(q, kv, level="window", window=w)
+        out[f"window{w}.o"], out[f"window{w}.lse"] = o.numpy(), lse.numpy()
+    o, lse = golden_ref.golden(q, kv, level="window", window=16, sinks=sinks)
+    out["window16sink.o"], out["window16sink.lse"] = o.numpy(), lse.numpy()
+    out["q"], out["kv"], out["sinks"] = q.numpy(), kv.numpy(), sinks.numpy()
+    # sparse level: main_kv + indices with -1 padding and a duplicate (golden dedups)
+    gcount, topk, ratio = 20, 8, 4
+    main = torch.randn(b, gcount, 1, d, generator=g)
+    vis = (torch.arange(s) + 1) // ratio
+    idx = torch.full((b, s, topk), -1, dtype=torch.int64)
+    for t in range(s):
+        n = int(min(vis[t].item(), gcount))
+        perm = torch.randperm(n, generator=g)[:topk] if n else torch.zeros(0, dtype=torch.int64)
+        idx[0, t, :len(perm)] = perm
+    o, lse = golden_ref.golden(q, kv, level="sparse", window=16, main_kv=main,
+                               compress_ratio=ratio, indices=idx)
+    out["main"], out["idx"] = main.numpy(), idx.numpy()
+    out["sparse.o"], out["sparse.lse"] = o.numpy(), lse.numpy()
+    # gradients of the window level through autograd (dq, dkv, dsinks)
+    qg, kvg, sg = q.clone().requires_grad_(), kv.clone().requires_grad_(), sinks.clone().requires_grad_()
+    o, _ = golden_ref.golden(qg, kvg, level="window", window=16, sinks=sg)
+    do = torch.randn(o.shape, generator=g)
+    o.backward(do)
+    out["bwd.do"], out["bwd.dq"], out["bwd.dkv"], out["bwd.dsinks"] = (
+        do.numpy(), qg.grad.numpy(), kvg.grad.numpy(), sg.grad.numpy())
+    np.savez_compressed(os.path.join(HERE, "attention.npz"), **out)
+
+
+def make_indexer(golden_ref) -> None:
+    out = {}
+    g = torch.Generator().manual_seed(2)
+    b, s, hi, di, t, ratio = 2, 64, 8, 32, 20, 2
+    q = torch.randn(b, s, hi, di, generator=g)
+    k = torch.randn(b, t, di, generator=g)
+    w = torch.randn(b, s, hi, generator=g) * hi**-0.5
+    sc = golden_ref.indexer_scores(q, k, w, ratio)
+    out["q"], out["k"], out["w"], out["scores"] = q.numpy(), k.numpy(), w.numpy(), sc.numpy()
+    for topk in (4, 16, 25):
+        out[f"topk{topk}"] = golden_ref.topk_indices(sc, topk).numpy()
+    np.savez_compressed(os.path.join(HERE, "indexer.npz"), **out)
+
+
+if __name__ == "__main__":
+    torch.set_num_threads(1)
+    quant, golden_ref = _ref()
+    make_quant(quant)
+    make_attention(golden_ref)
+    make_indexer(golden_ref)
+    print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
