@@ -43,6 +43,7 @@ extern "C" {
 #define MZB_F32 0
 #define MZB_BF16 1
 #define MZB_F16 2
+#define MZB_E4M3 3 /* float8_e4m3fn codes (uint8) */
 
 MZB_API const char* mzb_last_error(void);
 MZB_API int mzb_version(void);
@@ -66,6 +67,35 @@ MZB_API int mzb_fq_fp4(const void* x, void* y, int64_t rows, int64_t n, int dtyp
                void* stream);
 MZB_API int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtype, int block_size, int rule,
                void* stream);
+
+/* ------------------------------------------------------------------ lightning indexer
+ * mzb_indexer_scores -- replaces `indexer.fwd.fwd` / kernel `index_score`
+ *   (src/mzoo/layers/attn/indexer/fwd.py:48-132; golden_ref.py:213 `indexer_scores`).
+ *   scores[b,s,t] = scale * sk[b,t] * sum_h w[b,s,h]*sq[b,s,h] * relu(q[b,s,h,:].k[b,t,:])
+ *   for t < (q_offset + s + 1) / ratio, else -inf (q_offset = 0 is the reference's
+ *   prefill positions 0..S-1; the model uses absolute positions,
+ *   archs/dsv4/modeling_deepseek_v41.py:555).  q [B,S,Hi,Di], k [B,T,Di] are bf16
+ *   (dtype MZB_BF16; sq, sk may be NULL) or e4m3 codes (MZB_E4M3; sq [B,S,Hi], sk [B,T]
+ *   fp32 required); w [B,S,Hi] fp32; scores [B,S,T] fp32.  Hi % 16 == 0 (the host pads
+ *   smaller head counts with zero weights); Di in {32,64,96,128,256} (bf16) or
+ *   {64,128} (e4m3).  write_tail = 0 skips the -inf fill of keys past the block's causal
+ *   frontier (the top-k path never reads them).  `err` (device int, may be NULL)
+ *   receives a non-zero code if a bounded device wait gives up.
+ * mzb_indexer_topk -- replaces `indexer.attn.attn` (indexer/attn.py:67-81: torch.topk on
+ *   the score matrix, -inf -> -1) and `golden_ref.topk_indices` (golden_ref.py:230).
+ *   Reads `scores` from mzb_indexer_scores (same arguments) and writes out [B,S,topk]
+ *   int32: the top-k keys of the exact fp64 canonical score (ties to the lower index),
+ *   ascending, -1 padded when fewer than topk keys are visible.  kbmax_ws is a float
+ *   workspace of B*16 entries.  eps bounds the relative error of the fp32 scores (see
+ *   indexer.cu); *err = MZB_ERR_BOUND if the bound leaves too many candidates.
+ */
+MZB_API int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,
+                               float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di, int dtype,
+                               int ratio, int64_t q_offset, float scale, int write_tail, int* err, void* stream);
+MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, const float* w, const float* sq,
+                             const float* sk, float* kbmax_ws, int32_t* out, int64_t B, int64_t S, int64_t T,
+                             int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale, int topk,
+                             float eps, int* err, void* stream);
 
 #ifdef __cplusplus
 }

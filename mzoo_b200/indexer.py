@@ -1,0 +1,126 @@
+"""Lightning indexer with mzoo's call signatures, on sm_100a kernels.
+
+Drop-in for ``src/mzoo/layers/attn/indexer``:
+
+- ``fwd(q, k, w, *, compress_ratio)`` -> fp32 [B,S,T] scores  (``indexer/fwd.py:112``)
+- ``attn(q, k, w, *, compress_ratio, topk)`` -> int32 [B,S,topk] (``indexer/attn.py:67``)
+
+Additive keyword arguments (defaults reproduce the reference):
+
+- ``q_offset`` -- absolute position of query 0 (the model's ``position_ids``,
+  ``archs/dsv4/modeling_deepseek_v41.py:555``); the reference kernel assumes 0.
+- ``scales=(sq, sk)`` -- FP8 mode: ``q``/``k`` are ``torch.float8_e4m3fn`` codes with
+  fp32 scales per (token, head) ``[B,S,Hi]`` and per key ``[B,T]``.
+- ``softmax_scale`` -- the overall factor (default ``Di**-0.5`` in bf16 mode, 1 in fp8).
+
+``attn`` returns, per query, the indices of the ``topk`` largest scores -- exact with
+respect to the fp64 canonical score (see ``csrc/indexer.cu``), ties to the lower index --
+in ascending order, ``-1`` padded where fewer keys are visible.  (The reference returns
+``torch.topk(sorted=False)`` order; its tests compare sets.)
+"""
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, require_cuda, stream_ptr
+
+KB_PARTS = 16
+# relative bound on the fp32 tensor-core score error: |approx - exact| <= EPS * A_s * B_t
+EPS = 2.0**-12
+
+
+def _prep(q, k, w, scales, softmax_scale):
+    require_cuda(q, k, w)
+    fp8 = q.dtype == torch.float8_e4m3fn
+    if fp8:
+        assert k.dtype == torch.float8_e4m3fn, f"fp8 q needs fp8 k, got {k.dtype}"
+        assert scales is not None, "fp8 inputs need scales=(sq [B,S,Hi], sk [B,T])"
+        sq, sk = (s.float().contiguous() for s in scales)
+    else:
+        assert q.dtype == k.dtype == torch.bfloat16, f"q/k must be bf16, got {q.dtype}/{k.dtype}"
+        assert scales is None, "scales are for fp8 inputs only"
+        sq = sk = None
+    B, S, Hi, Di = q.shape
+    assert k.dim() == 3 and k.shape[0] == B and k.shape[2] == Di, f"k must be [B, T, {Di}], got {tuple(k.shape)}"
+    assert w.shape == (B, S, Hi), f"w must be [B, S, Hi]={(B, S, Hi)}, got {tuple(w.shape)}"
+    if sq is not None:
+        assert sq.shape == (B, S, Hi) and sk.shape == (B, k.shape[1]), "scales must be [B,S,Hi] and [B,T]"
+    w = w.float().contiguous()
+    q, k = q.contiguous(), k.contiguous()
+    if Hi % 16:  # the kernel tiles heads by 16: zero-weight heads contribute exactly 0
+        pad = 16 - Hi % 16
+        q = torch.cat([q, q.new_zeros(B, S, pad, Di)], dim=2)
+        w = torch.cat([w, w.new_zeros(B, S, pad)], dim=2).contiguous()
+        if sq is not None:
+            sq = torch.cat([sq, sq.new_ones(B, S, pad)], dim=2).contiguous()
+    scale = softmax_scale if softmax_scale is not None else (1.0 if fp8 else Di**-0.5)
+    dt = 3 if fp8 else 1
+    return q, k, w, sq, sk, float(scale), dt
+
+
+def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, err):
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
+    call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(out), B, S, T, Hi, Di, dt,
+         ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
+    return out
+
+
+def _check_err(err: torch.Tensor, what: str) -> None:
+    code = int(err.item())
+    if code == _lib.MZB_ERR_BOUND:
+        raise _lib.MzbError(f"{what}: error bound left too many top-k candidates (raise EPS coverage)")
+    if code:
+        raise _lib.MzbError(f"{what}: device wait gave up (code {code})")
+
+
+def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, q_offset: int = 0,
+        scales=None, softmax_scale: float | None = None, check: bool = True) -> torch.Tensor:
+    """Lightning-indexer score matrix (``indexer/fwd.py:112``): q bf16 [B,S,Hi,Di], k bf16
+    [B,T,Di], w fp32 [B,S,Hi] (already scaled by Hi**-0.5) -> fp32 [B,S,T], ``-inf`` where
+    ``t >= (q_offset + s + 1) // compress_ratio``."""
+    assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
+    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale)
+    B, S = q.shape[:2]
+    if k.shape[1] == 0:
+        return q.new_empty((B, S, 0), dtype=torch.float32)
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    out = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, err)
+    if check:
+        _check_err(err, "indexer.fwd")
+    return out
+
+
+def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, topk: int, q_offset: int = 0,
+         scales=None, softmax_scale: float | None = None, check: bool = True) -> torch.Tensor:
+    """``indexer/attn.py:67``: -> ``Indices`` int32 [B,S,topk] (``-1`` = empty slot)."""
+    assert topk >= 0, f"topk must be >= 0, got {topk}"
+    assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
+    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale)
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    out = torch.full((B, S, topk), -1, dtype=torch.int32, device=q.device)
+    if topk == 0 or T == 0:
+        return out
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, err)
+    kb = torch.empty(B * KB_PARTS, dtype=torch.float32, device=q.device)
+    call("mzb_indexer_topk", ptr(sc), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(kb), ptr(out), B, S, T, Hi,
+         Di, dt, compress_ratio, q_offset, scale, topk, EPS, ptr(err), stream_ptr(q.device))
+    if check:
+        _check_err(err, "indexer.attn")
+    return out
+
+
+def quantize_fp8(x: torch.Tensor, dim_tile: int | None = None):
+    """Absmax e4m3 quantisation of indexer inputs: per row of the last
+    dim (or per ``dim_tile`` elements), ``scale = amax / 448`` -> (codes, fp32 scales)."""
+    xf = x.float()
+    n = xf.shape[-1]
+    tile = dim_tile or n
+    blocks = xf.view(*xf.shape[:-1], n // tile, tile)
+    amax = blocks.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    codes = (blocks / scale.unsqueeze(-1)).clamp(-448, 448).to(torch.float8_e4m3fn).view(x.shape)
+    return codes, (scale.squeeze(-1) if dim_tile is None else scale)

@@ -1,0 +1,189 @@
+"""Lightning indexer: oracle pinned to the reference's golden vectors (CPU); the sm_100a
+score kernel against the oracle within the reference's acceptance criterion and with an
+exactly equal -inf mask; top-k index sets bit-exact against the canonical oracle (GPU).
+
+Reference tests mirrored: ``indexer/fwd_test.py:52-83`` (Hi x Di matrix, ratios,
+non-aligned / empty T), ``indexer/attn_test.py:28-46`` (per-row set equality, topk > T
+padding).
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import indexer as I
+from oracle import quant as Q
+
+
+def _golden():
+    return np.load(os.path.join(GOLDEN, "indexer.npz"))
+
+
+# ----------------------------------------------------------------------------- CPU: oracle pin
+
+def test_oracle_scores_match_reference_golden():
+    d = _golden()
+    got = I.scores_ref(d["q"], d["k"], d["w"], 2)
+    ref = d["scores"]
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), fin)
+    np.testing.assert_allclose(got[fin], ref[fin], rtol=0, atol=1e-5)
+
+
+@pytest.mark.parametrize("topk", [4, 16, 25])
+def test_oracle_topk_matches_reference_golden(topk):
+    d = _golden()
+    ref = np.sort(np.where(d[f"topk{topk}"] < 0, 1 << 30, d[f"topk{topk}"]), -1)
+    ref = np.where(ref == 1 << 30, -1, ref)
+    assert np.array_equal(I.topk_ref(d["scores"], topk), ref)
+
+
+def test_canonical_topk_equals_reference_sets():
+    """The canonical fp64 definition selects the same sets as the reference's fp32 path
+    on its golden inputs (no near-ties there)."""
+    d = _golden()
+    q, k, w = d["q"], d["k"], d["w"]
+    c = I.canonical_scores(q, k, w, None, None, 2, 0, scale=float(np.float32(q.shape[-1] ** -0.5)), fp8=False)
+    for topk in (4, 16, 25):
+        ref = I.topk_ref(d["scores"], topk)
+        assert np.array_equal(I.canonical_topk(c, topk, 2), ref.astype(np.int32))
+
+
+def test_canonical_fp8_dot_is_order_independent():
+    """e4m3 products are multiples of 2^-18 below 2^17.6: any fp64 summation order is exact."""
+    rng = np.random.default_rng(0)
+    codes, _ = Q.quantize_fp8_rows(rng.standard_normal((64, 128)).astype(np.float32), 128)
+    kc, _ = Q.quantize_fp8_rows(rng.standard_normal((32, 128)).astype(np.float32), 128)
+    a = codes.astype(np.float64) @ kc.astype(np.float64).T
+    b = np.zeros_like(a)
+    for i in range(127, -1, -1):
+        b = b + codes[:, None, i].astype(np.float64) * kc[None, :, i].astype(np.float64)
+    assert np.array_equal(a, b)
+
+
+# ----------------------------------------------------------------------------- GPU
+
+def _bf16_inputs(torch, dev, B, S, Hi, Di, T, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(B, S, Hi, Di, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, T, Di, generator=g).to(torch.bfloat16)
+    w = torch.randn(B, S, Hi, generator=g) * Hi**-0.5
+    return q.to(dev), k.to(dev), w.to(dev)
+
+
+def _check_scores(torch, dev, B, S, Hi, Di, T, ratio, q_offset=0):
+    from mzoo_b200 import indexer
+    q, k, w = _bf16_inputs(torch, dev, B, S, Hi, Di, T)
+    got = indexer.fwd(q, k, w, compress_ratio=ratio, q_offset=q_offset).cpu().numpy()
+    qf, kf, wf = (x.float().cpu().numpy() for x in (q, k, w))
+    ref = I.scores_ref(qf, kf, wf, ratio, q_offset)
+    assert got.shape == (B, S, T) and got.dtype == np.float32
+    masked = ~np.isfinite(ref)
+    assert np.array_equal(~np.isfinite(got), masked), "group-causal -inf mask differs"
+    fin = ~masked
+    if fin.any():
+        # reference criterion (dense_attn/ref.py:65): err <= 2 x torch-bf16 err + 1e-5; the
+        # kernel's inputs are bf16 and it accumulates in fp32, so its error is fp32 noise
+        err = np.abs(got[fin] - ref[fin]).max()
+        scale = np.abs(ref[fin]).max()
+        assert err <= 1e-5 * max(1.0, scale), f"max err {err}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads", [4, 32, 64])
+@pytest.mark.parametrize("dim", [64, 96, 128, 256])
+def test_scores_match_reference(cuda, dim, heads):
+    import torch
+    _check_scores(torch, cuda, 2, 256, heads, dim, 128, 2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ratio", [1, 2, 4])
+def test_compress_ratios(cuda, ratio):
+    import torch
+    _check_scores(torch, cuda, 1, 256, 32, 128, 256 // ratio, ratio)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("T", [128, 400, 7])
+def test_kv_lengths(cuda, T):
+    import torch
+    _check_scores(torch, cuda, 1, 256, 32, 128, T, 2)
+
+
+@pytest.mark.gpu
+def test_ragged_seq_and_offset(cuda):
+    """S not a multiple of the token block, absolute positions (q_offset)."""
+    import torch
+    _check_scores(torch, cuda, 2, 258, 32, 128, 300, 4, q_offset=1000)
+
+
+@pytest.mark.gpu
+def test_empty_kv(cuda):
+    import torch
+    from mzoo_b200 import indexer
+    q, k, w = _bf16_inputs(torch, cuda, 1, 256, 32, 128, 0)
+    assert indexer.fwd(q, k, w, compress_ratio=2).shape == (1, 256, 0)
+    assert (indexer.attn(q, k, w, compress_ratio=2, topk=8) == -1).all()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("topk,T", [(64, 128), (135, 128), (16, 400)])
+def test_topk_bf16_exact(cuda, topk, T):
+    import torch
+    from mzoo_b200 import indexer
+    B, S, Hi, Di, ratio = 2, 256, 32, 128, 1
+    q, k, w = _bf16_inputs(torch, cuda, B, S, Hi, Di, T, seed=3)
+    got = indexer.attn(q, k, w, compress_ratio=ratio, topk=topk).cpu().numpy()
+    qf, kf, wf = (x.float().cpu().numpy() for x in (q, k, w))
+    canon = I.canonical_scores(qf, kf, wf, None, None, ratio, 0, scale=float(np.float32(Di**-0.5)), fp8=False)
+    assert np.array_equal(got, I.canonical_topk(canon, topk, ratio))
+    # and the same sets as the reference's fp32 scores + topk
+    ref = I.topk_ref(I.scores_ref(qf, kf, wf, ratio), topk)
+    assert np.array_equal(got, ref.astype(np.int32))
+
+
+def _fp8_case(torch, dev, B, S, Hi, Di, T, seed):
+    from mzoo_b200 import indexer
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = torch.randn(B, S, Hi, Di, generator=g)
+    k = torch.randn(B, T, Di, generator=g)
+    w = torch.randn(B, S, Hi, generator=g) / 8
+    q8, sq = indexer.quantize_fp8(q.to(dev))
+    k8, sk = indexer.quantize_fp8(k.to(dev))
+    return q8, sq, k8, sk, w.to(dev)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("q_offset", [0, 1536])
+def test_topk_fp8_exact(cuda, q_offset):
+    """BASELINE config 2 at reduced size: fp8 q/k with absmax scales, ratio 4, top-k 64."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, Hi, Di, T, ratio, topk = 2, 512, 64, 128, 512, 4, 64
+    q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 7)
+    got = indexer.attn(q8, k8, w, compress_ratio=ratio, topk=topk, q_offset=q_offset, scales=(sq, sk))
+    qv = q8.float().cpu().numpy()
+    kv = k8.float().cpu().numpy()
+    canon = I.canonical_scores(qv, kv, w.cpu().numpy(), sq.cpu().numpy(), sk.cpu().numpy(), ratio, q_offset)
+    assert np.array_equal(got.cpu().numpy(), I.canonical_topk(canon, topk, ratio, q_offset))
+
+
+@pytest.mark.gpu
+def test_fp8_score_error_within_bound(cuda):
+    """The fp32 tensor-core scores stay well inside the bound the top-k relies on:
+    |approx - exact| <= EPS * A_s * max_t B_t, with a 16x margin."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, Hi, Di, T, ratio = 1, 512, 64, 128, 1024, 1
+    q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 11)
+    approx = indexer.fwd(q8, k8, w, compress_ratio=ratio, q_offset=T, scales=(sq, sk)).cpu().numpy()
+    qv, kv, wn, sqn, skn = (x.float().cpu().numpy() for x in (q8, k8, w, sq, sk))
+    canon = I.canonical_scores(qv, kv, wn, sqn, skn, ratio, T)
+    A, Bt = I.bound_factors(qv, kv, wn, sqn, skn)
+    bound = A[..., None] * Bt.max(-1)[:, None, None]
+    ratio_err = (np.abs(approx.astype(np.float64) - canon) / bound).max()
+    print(f"max |approx-exact| / (A_s max B_t) = {ratio_err:.3e} (EPS = {indexer.EPS:.3e})")
+    assert ratio_err <= indexer.EPS / 16
