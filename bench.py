@@ -1,0 +1,321 @@
+#!/usr/bin/env python
+"""Benchmark of the mzoo attention hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl mzb|reference]
+
+Configs (BASELINE.json ``configs``; synthetic seeded inputs with the stated shapes and
+distributions -- there is no dataset):
+
+- ``indexer`` (default, configs[1]): lightning indexer + top-512 over FP8 q/k, B=2,
+  4096 queries at absolute positions 12288..16383 x 4096 compressed keys (ratio 4),
+  Hi=64, Di=128.  Metric: indexer Mq/s (queries per second, whole job).
+
+A "step" is one pass of the hot path over one batch.  ``value`` times the device path with
+inputs resident in HBM (L2 flushed with a 256 MB write before every timed step);
+``e2e`` times the public API call with pinned host inputs, host->device copies, the
+kernels and the device->host copy of the result inside the timed region.  Multi-GPU:
+one process per GPU (torchrun), each rank runs its own independent instance (weak
+scaling, no data-path collective); timing is the max over ranks of CUDA-event time.
+
+``--impl reference`` times the reference's CPU path (the numpy restatement in
+``oracle/``; the reference itself is Python and cannot travel to the GPU host) on a
+bounded sample of the same workload, with all host threads, and prints the same metric.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        d["_source"] = "measured"
+        return d
+    d = dict(FALLBACK_PEAKS)
+    d["_source"] = "fallback"
+    return d
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        load = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ----------------------------------------------------------------------------- timing helpers
+
+class Timer:
+    """Per-step CUDA-event timing on the current stream with an L2 flush before each step."""
+
+    def __init__(self, torch, device):
+        self.torch = torch
+        self.flush_buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    def flush(self):
+        self.flush_buf.zero_()
+
+    def run(self, fn, steps: int, flush: bool = True) -> list:
+        torch = self.torch
+        times = []
+        for _ in range(steps):
+            if flush:
+                self.flush()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        return [s.elapsed_time(e) for s, e in times]
+
+
+def max_over_ranks(torch, dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- indexer (C2)
+
+C2 = dict(B=2, S=4096, T=4096, Hi=64, Di=128, ratio=4, topk=512, q_offset=12288)
+
+
+def c2_pairs(cfg=C2) -> int:
+    """Visible (query, key) pairs per batch element: sum_s min(T, (q_offset + s + 1) // ratio)."""
+    return sum(min(cfg["T"], (cfg["q_offset"] + s + 1) // cfg["ratio"]) for s in range(cfg["S"]))
+
+
+def c2_inputs(torch, seed: int):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    B, S, T, Hi, Di = (C2[k] for k in ("B", "S", "T", "Hi", "Di"))
+    q = torch.randn(B, S, Hi, Di, generator=g)
+    k = torch.randn(B, T, Di, generator=g)
+    w = torch.randn(B, S, Hi, generator=g) / 8
+    return q, k, w
+
+
+def bench_indexer(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import indexer, _lib
+
+    q, k, w = c2_inputs(torch, seed=rank)
+    q8, sq = indexer.quantize_fp8(q.to(device))
+    k8, sk = indexer.quantize_fp8(k.to(device))
+    w = w.to(device)
+    B, S, T, Hi, Di = (C2[x] for x in ("B", "S", "T", "Hi", "Di"))
+    kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk), check=False)
+    step = lambda: indexer.attn(q8, k8, w, **kw)  # noqa: E731
+    timer = Timer(torch, device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    t_steps = timer.run(step, args.steps)
+    # the dominant kernel alone (score GEMM), for the roofline
+    qp, kp, wp, sqp, skp, scale, dt = indexer._prep(q8, k8, w, (sq, sk), None)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C2["ratio"], C2["q_offset"], scale, dt,
+                                                False, err), args.steps)
+    # end to end through the public API from pinned host memory
+    hq8 = q8.view(torch.uint8).cpu().pin_memory()
+    hk8 = k8.view(torch.uint8).cpu().pin_memory()
+    hsq, hsk, hw = (x.cpu().pin_memory() for x in (sq, sk, w))
+    dq8, dk8 = torch.empty_like(hq8, device=device), torch.empty_like(hk8, device=device)
+    dsq, dsk, dw = (torch.empty_like(x, device=device) for x in (hsq, hsk, hw))
+    hout = torch.empty(B, S, C2["topk"], dtype=torch.int32).pin_memory()
+
+    def e2e():
+        for d, h in ((dq8, hq8), (dk8, hk8), (dsq, hsq), (dsk, hsk), (dw, hw)):
+            d.copy_(h, non_blocking=True)
+        idx = indexer.attn(dq8.view(torch.float8_e4m3fn), dk8.view(torch.float8_e4m3fn), dw,
+                           compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"],
+                           scales=(dsq, dsk), check=False)
+        hout.copy_(idx, non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    clocks = sampler.stop()
+    torch.cuda.synchronize()
+    code = int(err.item())
+    assert code == 0, f"device error word {code}"
+    h2d = sum(x.numel() * x.element_size() for x in (hq8, hk8, hsq, hsk, hw))
+    d2h = hout.numel() * hout.element_size()
+
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_score = sum(t_score) / len(t_score)
+    queries = B * S * world
+    flops = 2.0 * B * c2_pairs() * Hi * Di
+    pk = peaks()
+    fp8_peak = 2.0 * pk["bf16_tflops"]
+    achieved = flops / (ms_score * 1e-3) / 1e12
+    out = {
+        "metric": "indexer Mq/s", "value": queries / (ms * 1e-3) / 1e6, "unit": "Mq/s",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 (fp32 accumulate)", "data": "synthetic (seeded N(0,1), absmax fp8)",
+        "config": {"workload": "C2 lightning indexer + top-k", "B": B, "queries": S, "keys": T, "Hi": Hi, "Di": Di,
+                   "compress_ratio": C2["ratio"], "topk": C2["topk"], "q_offset": C2["q_offset"],
+                   "parallelism": f"independent instance per GPU x{world}", "l2": "flushed (256 MB write) per step"},
+        "e2e": {"value": queries / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128>", "achieved": achieved,
+                     "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
+                     "peak_note": f"dense FP8 = 2 x {pk['_source']} bf16 burst {pk['bf16_tflops']} TFLOP/s",
+                     "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_score, "traffic": None},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_indexer(torch, q, k, w, sample=args.cpu_sample)
+    return out
+
+
+def cpu_indexer(torch, q, k, w, sample: int) -> dict:
+    """Oracle port on the host: canonical fp64 scores + exact top-k for `sample` queries
+    (the last ones of batch 0, every key visible to most of them)."""
+    import numpy as np
+    from oracle import indexer as I
+    from oracle import quant as Q
+    qn = q[0:1, -sample:].numpy()
+    kn = k[0:1].numpy()
+    wn = w[0:1, -sample:].cpu().numpy()
+    qv, sq = Q.quantize_fp8_rows(qn, C2["Di"])
+    kv, sk = Q.quantize_fp8_rows(kn, C2["Di"])
+    off = C2["q_offset"] + C2["S"] - sample
+    t0 = time.perf_counter()
+    sc = I.canonical_scores(qv, kv, wn, sq[..., 0], sk[..., 0], C2["ratio"], off)
+    I.canonical_topk(sc, C2["topk"], C2["ratio"], off)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt / 1e6, "unit": "Mq/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{sample} queries of batch 0 (positions {off}..{off + sample - 1}), numpy fp64 canonical "
+                      f"scores + top-{C2['topk']}, {dt:.2f} s"}
+
+
+def reference_indexer(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    q, k, w = c2_inputs(torch, seed=0)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_indexer(torch, q, k, w, sample=min(args.cpu_sample, 256))
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    r["value"] = v
+    return {"metric": "indexer Mq/s", "value": v, "unit": "Mq/s", "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": C2["B"] * C2["S"] / (v * 1e6) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (oracle port)",
+            "data": "synthetic (seeded N(0,1), absmax fp8)",
+            "config": {"workload": "C2 lightning indexer + top-k", "B": C2["B"], "queries": C2["S"], "keys": C2["T"],
+                       "Hi": C2["Hi"], "Di": C2["Di"], "compress_ratio": C2["ratio"], "topk": C2["topk"],
+                       "q_offset": C2["q_offset"]},
+            "cpu_baseline": r,
+            "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+BENCHES = {"indexer": (bench_indexer, reference_indexer)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="indexer", choices=sorted(BENCHES))
+    ap.add_argument("--impl", default="mzb", choices=["mzb", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = BENCHES[args.config][1](args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    res = BENCHES[args.config][0](args, torch, dist, rank, world, device)
+    res.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup})
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

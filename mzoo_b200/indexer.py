@@ -26,7 +26,7 @@ from ._lib import call, ptr, require_cuda, stream_ptr
 
 KB_PARTS = 16
 # relative bound on the fp32 tensor-core score error: |approx - exact| <= EPS * A_s * B_t
-EPS = 2.0**-12
+EPS = 2.0**-21
 
 
 def _prep(q, k, w, scales, softmax_scale):
