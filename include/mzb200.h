@@ -97,6 +97,27 @@ MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, 
                              int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale, int topk,
                              float eps, int* err, void* stream);
 
+/* ------------------------------------------------------------------ sparse latent attention
+ * mzb_sparse_mla_fwd -- the 576/512 FP8-latent form of `csa2_attn.fwd` / kernel `flashattn`
+ *   (src/mzoo/layers/attn/csa2_attn/fwd.py:70-286; golden_ref.py:149-168 level "sparse"),
+ *   prefill and paged decode.  Per query token tk (sequence b = tk / tok_per_seq, absolute
+ *   position q_pos[tk]): one softmax over the raw-latent window [q_pos-window+1, q_pos] and
+ *   the compressed entries indices[tk, 0..topk) (-1 or >= the sequence's compressed length
+ *   = empty; duplicates count twice), logits = softmax_scale * q . k (576 channels),
+ *   o = P V with V = the first 512 channels.
+ *   q bf16 [n_tok, 128, 576]; KV rows of 672 B ([0,512) e4m3, [512,544) 8 fp32 scales per
+ *   64 channels, [544,672) 64 bf16 rope) in kv_raw / kv_cmp: dense [B, raw_len] /
+ *   [B, cmp_len] rows when the page table is NULL, else 64-row pages addressed through
+ *   raw_page_table [B, raw_ptw] / cmp_page_table [B, cmp_ptw].  cmp_lens [B] (or NULL =
+ *   cmp_len) bounds valid compressed indices.  Outputs o bf16 [n_tok, 128, 512] and
+ *   lse fp32 [n_tok, 128] (natural log).  slots_ws: int32 workspace [n_tok].
+ */
+MZB_API int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void* kv_cmp, const int32_t* indices,
+                               const int32_t* q_pos, const int32_t* raw_page_table, const int32_t* cmp_page_table,
+                               const int32_t* cmp_lens, int32_t* slots_ws, void* o, float* lse, int64_t n_tok,
+                               int tok_per_seq, int topk, int window, int64_t raw_len, int64_t cmp_len, int raw_ptw,
+                               int cmp_ptw, float softmax_scale, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
