@@ -274,7 +274,159 @@ def reference_indexer(args, rank, world) -> dict:
             "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-BENCHES = {"indexer": (bench_indexer, reference_indexer)}
+# ----------------------------------------------------------------------------- sparse MLA prefill (C3)
+
+C3 = dict(B=1, S=16384, H=128, G=4096, ratio=4, topk=2048, window=128)
+
+
+def sorted_causal_indices(torch, S, G, topk, ratio, gen, device, q_offset=0, chunk=2048):
+    """Per query t: seeded random distinct compressed indices from [0, (t+q_offset+1)//ratio),
+    the first topk of a random permutation, sorted ascending, -1 padded."""
+    out = torch.empty(S, topk, dtype=torch.int32, device=device)
+    cols = torch.arange(G, device=device)
+    for s0 in range(0, S, chunk):
+        s1 = min(S, s0 + chunk)
+        r = torch.rand(s1 - s0, G, generator=gen, device=device)
+        vis = (torch.arange(s0, s1, device=device) + q_offset + 1) // ratio
+        r.masked_fill_(cols[None, :] >= vis[:, None], 2.0)
+        vals, ind = r.topk(topk, dim=1, largest=False)
+        ind = torch.where(vals < 2.0, ind, torch.full_like(ind, 1 << 30)).sort(dim=1).values
+        out[s0:s1] = torch.where(ind == (1 << 30), torch.full_like(ind, -1), ind).to(torch.int32)
+    return out
+
+
+def c3_inputs(torch, device, seed: int):
+    from mzoo_b200 import sparse_mla
+    S, G = C3["S"], C3["G"]
+    g = torch.Generator(device=device).manual_seed(seed)
+    q = torch.randn(1, S, C3["H"], 576, generator=g, device=device, dtype=torch.bfloat16)
+    raw = sparse_mla.pack_kv(torch.randn(1, S, 576, generator=g, device=device))
+    cmp = sparse_mla.pack_kv(torch.randn(1, G, 576, generator=g, device=device))
+    g1 = torch.Generator(device=device).manual_seed(seed + 1)
+    idx = sorted_causal_indices(torch, S, G, C3["topk"], C3["ratio"], g1, device).view(1, S, C3["topk"])
+    return q, raw, cmp, idx
+
+
+def c3_pairs(torch, idx) -> int:
+    S = idx.shape[1]
+    win = sum(min(C3["window"], t + 1) for t in range(S))
+    return int((idx >= 0).sum().item()) + win
+
+
+def bench_prefill(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import sparse_mla
+    q, raw, cmp, idx = c3_inputs(torch, device, seed=2 * rank)
+    pairs = c3_pairs(torch, idx)
+    flops = sparse_mla.pair_flops(pairs)
+    step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], check=False)  # noqa: E731
+    timer = Timer(torch, device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    t_steps = timer.run(step, args.steps)
+    clocks = sampler.stop()
+    # end to end from pinned host buffers
+    hq, hraw, hcmp, hidx = (x.cpu().pin_memory() for x in (q, raw, cmp, idx))
+    dq, draw, dcmp, didx = (torch.empty_like(x, device=device) for x in (hq, hraw, hcmp, hidx))
+    ho = torch.empty(1, C3["S"], C3["H"], 512, dtype=torch.bfloat16).pin_memory()
+    hl = torch.empty(1, C3["H"], C3["S"], dtype=torch.float32).pin_memory()
+
+    def e2e():
+        for d, h in ((dq, hq), (draw, hraw), (dcmp, hcmp), (didx, hidx)):
+            d.copy_(h, non_blocking=True)
+        o, lse = sparse_mla.prefill(dq, draw, dcmp, didx, window=C3["window"], check=False)
+        ho.copy_(o, non_blocking=True)
+        hl.copy_(lse, non_blocking=True)
+
+    e2e()
+    t_e2e = timer.run(e2e, max(2, args.steps // 4), flush=False)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hraw, hcmp, hidx))
+    d2h = ho.numel() * ho.element_size() + hl.numel() * hl.element_size()
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    pk = peaks()
+    tflops = flops * world / (ms * 1e-3) / 1e12
+    achieved = flops / (ms * 1e-3) / 1e12
+    out = {
+        "metric": "sparse-MLA prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp8 KV dequant, fp32 acc)",
+        "data": "synthetic (seeded N(0,1); FP8 no-rope rows with per-64 absmax scales)",
+        "config": {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": C3["S"], "heads": C3["H"],
+                   "d_qk": 576, "d_v": 512, "topk": C3["topk"], "window": C3["window"], "compressed": C3["G"],
+                   "selected_pairs": pairs, "parallelism": f"independent instance per GPU x{world}",
+                   "l2": "inputs (2.4 GB q) larger than L2; 256 MB flush per step"},
+        "e2e": {"value": flops * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "kernel": "mzb::mla::mla_fwd_kernel", "achieved": achieved,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
+                     "peak_note": f"{pk['_source']} bf16 burst", "algorithmic_flops_per_launch": flops,
+                     "ms_per_launch": ms, "traffic": None},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        toks = _prefill_sample(C3["S"], max(8, args.cpu_sample // 16))
+        out["cpu_baseline"] = cpu_prefill(q[0, toks].float().cpu().numpy(), toks, raw[0].cpu().numpy(),
+                                          cmp[0].cpu().numpy(), idx[0, toks].cpu().numpy())
+    return out
+
+
+def cpu_prefill(q_rows, toks, raw_rows, cmp_rows, idx_rows) -> dict:
+    """Oracle port: sparse attention for the sampled query tokens (all 128 heads), reported
+    as TFLOP/s of the sample's selected pairs (extrapolation to the full config is by
+    selected-pair count)."""
+    from oracle import mla as M
+    t0 = time.perf_counter()
+    pairs = 0
+    for i, t in enumerate(toks):
+        keys = M.unpack_rows(M.token_keys(raw_rows, cmp_rows, idx_rows[i], int(t), C3["window"]))
+        pairs += keys.shape[0]
+        M.attend_rows(q_rows[i], keys, 576**-0.5)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * 128 * 1088 * pairs
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{len(toks)} evenly spaced query tokens x 128 heads ({pairs} selected pairs), numpy fp64, "
+                      f"{dt:.2f} s, extrapolated by selected-pair count"}
+
+
+def _prefill_sample(S, n_tok):
+    import numpy as np
+    return [int(t) for t in np.linspace(S // n_tok, S - 1, n_tok)]
+
+
+def reference_prefill(args, rank, world) -> dict:
+    import torch
+    from oracle import mla as M
+    if rank != 0:
+        return None
+    S = C3["S"]
+    n_tok = max(8, args.cpu_sample // 64)
+    toks = _prefill_sample(S, n_tok)
+    g = torch.Generator().manual_seed(0)
+    q_rows = torch.randn(n_tok, 128, 576, generator=g).to(torch.bfloat16).float().numpy()
+    raw = M.pack_rows(torch.randn(S, 576, generator=g).numpy())
+    cmp = M.pack_rows(torch.randn(C3["G"], 576, generator=g).numpy())
+    idx = sorted_causal_indices(torch, S, C3["G"], C3["topk"], C3["ratio"], torch.Generator().manual_seed(1),
+                                torch.device("cpu"))[toks].numpy()
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_prefill(q_rows, toks, raw, cmp, idx)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    r["value"] = v
+    return {"metric": "sparse-MLA prefill TFLOP/s", "value": v, "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
+            "config": {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": S, "heads": 128, "topk": C3["topk"],
+                       "window": C3["window"]},
+            "cpu_baseline": r, "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill)}
 
 
 def main():

@@ -78,7 +78,8 @@ MZB_API int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtyp
  *   (dtype MZB_BF16; sq, sk may be NULL) or e4m3 codes (MZB_E4M3; sq [B,S,Hi], sk [B,T]
  *   fp32 required); w [B,S,Hi] fp32; scores [B,S,T] fp32.  Hi % 16 == 0 (the host pads
  *   smaller head counts with zero weights); Di in {32,64,96,128,256} (bf16) or
- *   {64,128} (e4m3).  write_tail = 0 skips the -inf fill of keys past the block's causal
+ *   {64,128} (e4m3).  q_pos [B*S] int32 (may be NULL) gives each query's absolute position
+ *   (decode: one query per sequence at seq_len-1) and overrides q_offset + s.  write_tail = 0 skips the -inf fill of keys past the block's causal
  *   frontier (the top-k path never reads them).  `err` (device int, may be NULL)
  *   receives a non-zero code if a bounded device wait gives up.
  * mzb_indexer_topk -- replaces `indexer.attn.attn` (indexer/attn.py:67-81: torch.topk on
@@ -90,12 +91,13 @@ MZB_API int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtyp
  *   indexer.cu); *err = MZB_ERR_BOUND if the bound leaves too many candidates.
  */
 MZB_API int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,
-                               float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di, int dtype,
-                               int ratio, int64_t q_offset, float scale, int write_tail, int* err, void* stream);
+                               const int32_t* q_pos, float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di,
+                               int dtype, int ratio, int64_t q_offset, float scale, int write_tail, int* err,
+                               void* stream);
 MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, const float* w, const float* sq,
-                             const float* sk, float* kbmax_ws, int32_t* out, int64_t B, int64_t S, int64_t T,
-                             int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale, int topk,
-                             float eps, int* err, void* stream);
+                             const float* sk, const int32_t* q_pos, float* kbmax_ws, int32_t* out, int64_t B,
+                             int64_t S, int64_t T, int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale,
+                             int topk, float eps, int* err, void* stream);
 
 /* ------------------------------------------------------------------ sparse latent attention
  * mzb_sparse_mla_fwd -- the 576/512 FP8-latent form of `csa2_attn.fwd` / kernel `flashattn`

@@ -35,10 +35,10 @@ SIGNATURES = {
     "mzb_version": [],
     "mzb_fq_fp4": [_P, _P, _I64, _I64, _I32, _I32, _I32, _P],
     "mzb_fq_fp8": [_P, _P, _I64, _I64, _I32, _I32, _I32, _P],
-    "mzb_indexer_scores": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64, _F32, _I32,
-                           _P, _P],
-    "mzb_indexer_topk": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64, _F32,
-                         _I32, _F32, _P, _P],
+    "mzb_indexer_scores": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64, _F32,
+                           _I32, _P, _P],
+    "mzb_indexer_topk": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64,
+                         _F32, _I32, _F32, _P, _P],
     "mzb_sparse_mla_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64, _I32,
                            _I32, _F32, _P, _P],
 }

@@ -65,6 +65,7 @@ struct ScoreArgs {
   const float* w;
   const float* sq;
   const float* sk;
+  const int32_t* q_pos;  // [B*S] absolute positions, or null (q_offset + s)
   float* scores;
   int B, S, T, Hi, Tq, N;
   int ratio;
@@ -77,6 +78,13 @@ struct ScoreArgs {
 __device__ __forceinline__ int visible_keys(long long q_offset, long long s, int ratio, int T) {
   long long v = (q_offset + s + 1) / ratio;
   return v < 0 ? 0 : (v > T ? T : int(v));
+}
+
+// Visible keys of query (b, s): position q_pos[b*S+s] when given, else q_offset + s.
+__device__ __forceinline__ int visible_of(const int32_t* q_pos, long long q_offset, int b, int S, int s, int ratio,
+                                          int T) {
+  if (q_pos) return visible_keys(0, (long long)q_pos[(long long)b * S + s], ratio, T);
+  return visible_keys(q_offset, s, ratio, T);
 }
 
 template <bool FP8, int DI>
@@ -125,9 +133,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   const int n_tb = (a.S + a.Tq - 1) / a.Tq;
   const int items = a.B * n_tb;
-  auto item_tiles = [&](int tb) {
-    const int s_last = min((tb + 1) * a.Tq, a.S) - 1;
-    const int vis = visible_keys(a.q_offset, s_last, a.ratio, a.T);
+  auto item_tiles = [&](int tb, int b) {
+    int vis = 0;
+    for (int s = tb * a.Tq; s < min((tb + 1) * a.Tq, a.S); ++s)
+      vis = max(vis, visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T));
     return (vis + BM - 1) / BM;
   };
 
@@ -147,7 +156,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                           tb * a.Tq * a.Hi, b);
         q_issued |= 1u << qb;
         q_par[qb] = qpar;
-        const int n_kt = item_tiles(tb);
+        const int n_kt = item_tiles(tb, b);
         for (int kt = 0; kt < n_kt; ++kt) {
           if (!tc::mbar_wait(&k_empty[ks_i], ks_ph ^ 1, a.err, 102)) { *abort_flag = 1; break; }
           tc::mbar_expect_tx(&k_full[ks_i], C::K_BYTES);
@@ -174,11 +183,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t idesc = tc::make_idesc(BM, a.N, kFmt, kFmt);
       int ks_i = 0, ks_ph = 0, acc = 0, acc_ph = 0, qi = 0;
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const int tb = n_tb - 1 - it / a.B;
+        const int tb = n_tb - 1 - it / a.B, b = it % a.B;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_full[qb], qpar, a.err, 103)) { *abort_flag = 1; break; }
         const uint32_t q_base = smem_u32(qs + qb * C::Q_BYTES);
-        const int n_kt = item_tiles(tb);
+        const int n_kt = item_tiles(tb, b);
         for (int kt = 0; kt < n_kt; ++kt) {
           if (!tc::mbar_wait(&acc_empty[acc], acc_ph ^ 1, a.err, 104)) { *abort_flag = 1; break; }
           if (!tc::mbar_wait(&k_full[ks_i], ks_ph, a.err, 105)) { *abort_flag = 1; break; }
@@ -223,7 +232,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         cw[i] = c;
       }
       tc::bar_sync(1, NEPI);
-      const int n_kt = item_tiles(tb);
+      const int n_kt = item_tiles(tb, b);
       for (int kt = 0; kt < n_kt; ++kt) {
         if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { *abort_flag = 1; break; }
         tc::fence_after_sync();
@@ -256,7 +265,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           const int s = s0 + t;
           if (s < a.S && j < a.T) {
-            const int vis = visible_keys(a.q_offset, s, a.ratio, a.T);
+            const int vis = visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T);
             a.scores[(size_t(b) * a.S + s) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
           }
         }
@@ -296,6 +305,7 @@ struct TopkArgs {
   const float* sq;
   const float* sk;
   const float* kbmax;  // [B, KB_PARTS]
+  const int32_t* q_pos;
   int32_t* out;
   int B, S, T, Hi, Di, topk, ratio;
   long long q_offset;
@@ -356,7 +366,7 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
   const int b = row / a.S, s = row % a.S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int32_t* out = a.out + size_t(row) * a.topk;
-  const int V = visible_keys(a.q_offset, s, a.ratio, a.T);
+  const int V = visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T);
   if (V <= a.topk) {
     for (int i = tid; i < a.topk; i += TK_THREADS) out[i] = i < V ? i : -1;
     return;
@@ -587,14 +597,15 @@ static int indexer_common_checks(const void* q, const void* k, int64_t B, int64_
 }
 
 extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,
-                                  float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di, int dtype,
-                                  int ratio, int64_t q_offset, float scale, int write_tail, int* err, void* stream) {
+                                  const int32_t* q_pos, float* scores, int64_t B, int64_t S, int64_t T, int Hi,
+                                  int Di, int dtype, int ratio, int64_t q_offset, float scale, int write_tail,
+                                  int* err, void* stream) {
   int e = indexer_common_checks(q, k, B, S, T, Hi, Di, dtype, ratio);
   if (e) return e;
   MZB_REQUIRE(dtype == MZB_BF16 || (sq && sk), MZB_ERR_SHAPE, "indexer: fp8 inputs need sq and sk scales");
   if (T == 0) return MZB_OK;
   idx::ScoreArgs a{};
-  a.w = w; a.sq = sq; a.sk = sk; a.scores = scores;
+  a.w = w; a.sq = sq; a.sk = sk; a.q_pos = q_pos; a.scores = scores;
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi;
   const int nmax = (Di * (dtype == MZB_E4M3 ? 1 : 2) <= 256) ? 256 : 128;
   a.Tq = nmax / Hi;
@@ -621,7 +632,8 @@ extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, 
 }
 
 extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* k, const float* w, const float* sq,
-                                const float* sk, float* kbmax_ws, int32_t* out, int64_t B, int64_t S, int64_t T,
+                                const float* sk, const int32_t* q_pos, float* kbmax_ws, int32_t* out, int64_t B,
+                                int64_t S, int64_t T,
                                 int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale, int topk,
                                 float eps, int* err, void* stream) {
   int e = indexer_common_checks(q, k, B, S, T, Hi, Di, dtype, ratio);
@@ -635,7 +647,7 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
               (long long)T, smem);
   idx::TopkArgs a{};
   a.scores = scores; a.q = static_cast<const uint8_t*>(q); a.k = static_cast<const uint8_t*>(k);
-  a.w = w; a.sq = sq; a.sk = sk; a.kbmax = kbmax_ws; a.out = out;
+  a.w = w; a.sq = sq; a.sk = sk; a.q_pos = q_pos; a.kbmax = kbmax_ws; a.out = out;
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi; a.Di = Di; a.topk = topk; a.ratio = ratio;
   a.q_offset = q_offset; a.scale = scale; a.eps = eps; a.fp8 = dtype == MZB_E4M3; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -12,6 +12,8 @@ Additive keyword arguments (defaults reproduce the reference):
 - ``scales=(sq, sk)`` -- FP8 mode: ``q``/``k`` are ``torch.float8_e4m3fn`` codes with
   fp32 scales per (token, head) ``[B,S,Hi]`` and per key ``[B,T]``.
 - ``softmax_scale`` -- the overall factor (default ``Di**-0.5`` in bf16 mode, 1 in fp8).
+- ``q_pos`` -- int32 [B, S] absolute position per query (decode: ``seq_len - 1``);
+  overrides ``q_offset``.
 
 ``attn`` returns, per query, the indices of the ``topk`` largest scores -- exact with
 respect to the fp64 canonical score (see ``csrc/indexer.cu``), ties to the lower index --
@@ -58,13 +60,21 @@ def _prep(q, k, w, scales, softmax_scale):
     return q, k, w, sq, sk, float(scale), dt
 
 
-def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, err):
+def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, err, q_pos=None):
     B, S, Hi, Di = q.shape
     T = k.shape[1]
     out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
-    call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(out), B, S, T, Hi, Di, dt,
+    call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(out), B, S, T, Hi, Di, dt,
          ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
     return out
+
+
+def _positions(q_pos, B, S, device):
+    if q_pos is None:
+        return None
+    q_pos = q_pos.to(device=device, dtype=torch.int32).contiguous()
+    assert q_pos.shape == (B, S), f"q_pos must be [B, S]={(B, S)}, got {tuple(q_pos.shape)}"
+    return q_pos
 
 
 def _check_err(err: torch.Tensor, what: str) -> None:
@@ -76,7 +86,8 @@ def _check_err(err: torch.Tensor, what: str) -> None:
 
 
 def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, q_offset: int = 0,
-        scales=None, softmax_scale: float | None = None, check: bool = True) -> torch.Tensor:
+        scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
+        check: bool = True) -> torch.Tensor:
     """Lightning-indexer score matrix (``indexer/fwd.py:112``): q bf16 [B,S,Hi,Di], k bf16
     [B,T,Di], w fp32 [B,S,Hi] (already scaled by Hi**-0.5) -> fp32 [B,S,T], ``-inf`` where
     ``t >= (q_offset + s + 1) // compress_ratio``."""
@@ -86,14 +97,15 @@ def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: in
     if k.shape[1] == 0:
         return q.new_empty((B, S, 0), dtype=torch.float32)
     err = torch.zeros(1, dtype=torch.int32, device=q.device)
-    out = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, err)
+    out = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, err, _positions(q_pos, B, S, q.device))
     if check:
         _check_err(err, "indexer.fwd")
     return out
 
 
 def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, topk: int, q_offset: int = 0,
-         scales=None, softmax_scale: float | None = None, check: bool = True) -> torch.Tensor:
+         scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
+         check: bool = True) -> torch.Tensor:
     """``indexer/attn.py:67``: -> ``Indices`` int32 [B,S,topk] (``-1`` = empty slot)."""
     assert topk >= 0, f"topk must be >= 0, got {topk}"
     assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
@@ -104,10 +116,11 @@ def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: i
     if topk == 0 or T == 0:
         return out
     err = torch.zeros(1, dtype=torch.int32, device=q.device)
-    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, err)
+    qp = _positions(q_pos, B, S, q.device)
+    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, err, qp)
     kb = torch.empty(B * KB_PARTS, dtype=torch.float32, device=q.device)
-    call("mzb_indexer_topk", ptr(sc), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(kb), ptr(out), B, S, T, Hi,
-         Di, dt, compress_ratio, q_offset, scale, topk, EPS, ptr(err), stream_ptr(q.device))
+    call("mzb_indexer_topk", ptr(sc), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(qp), ptr(kb), ptr(out), B, S,
+         T, Hi, Di, dt, compress_ratio, q_offset, scale, topk, EPS, ptr(err), stream_ptr(q.device))
     if check:
         _check_err(err, "indexer.attn")
     return out
