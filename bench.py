@@ -438,7 +438,13 @@ def main():
     ap.add_argument("--impl", default="mzb", choices=["mzb", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true",
+                    help="shrunken workload (profiling captures only; not a bench number)")
     args = ap.parse_args()
+    if args.small:  # a few hundred MB on the device: safe for multi-pass ncu captures
+        C2.update(S=1024, q_offset=4096 - 1024)
+        C3.update(S=2048)
+        args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
