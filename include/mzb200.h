@@ -120,6 +120,22 @@ MZB_API int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void* kv
                                int tok_per_seq, int topk, int window, int64_t raw_len, int64_t cmp_len, int raw_ptw,
                                int cmp_ptw, float softmax_scale, int* err, void* stream);
 
+/* mzb_sparse_mla_fwd_noalloc -- no counterpart in the reference.  Same arguments and
+ *   result as mzb_sparse_mla_fwd minus `slots_ws`: for callers that cannot allocate device
+ *   memory at launch time (a serving engine whose free HBM all belongs to its KV-cache
+ *   pool, or a host whose own memory manager must not be bypassed).  The workspace comes
+ *   from a fixed 65536-entry (256 KB) array inside the library, present on every GPU that
+ *   loads it until the process exits; n_tok above 65536 is rejected with MZB_ERR_SHAPE.
+ *   Calls share that array: two calls that overlap on the GPU race.  The first call on a
+ *   device resolves the array's address; make it before any stream capture.
+ */
+MZB_API int mzb_sparse_mla_fwd_noalloc(const void* q, const void* kv_raw, const void* kv_cmp, const int32_t* indices,
+                                       const int32_t* q_pos, const int32_t* raw_page_table,
+                                       const int32_t* cmp_page_table, const int32_t* cmp_lens, void* o, float* lse,
+                                       int64_t n_tok, int tok_per_seq, int topk, int window, int64_t raw_len,
+                                       int64_t cmp_len, int raw_ptw, int cmp_ptw, float softmax_scale, int* err,
+                                       void* stream);
+
 #ifdef __cplusplus
 }
 #endif

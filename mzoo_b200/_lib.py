@@ -41,6 +41,8 @@ SIGNATURES = {
                          _F32, _I32, _F32, _P, _P],
     "mzb_sparse_mla_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64, _I32,
                            _I32, _F32, _P, _P],
+    "mzb_sparse_mla_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64,
+                                   _I32, _I32, _F32, _P, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

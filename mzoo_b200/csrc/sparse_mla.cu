@@ -532,3 +532,71 @@ extern "C" int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void*
   mla::mla_fwd_kernel<<<unsigned(2 * pairs), mla::NTHREADS, mla::SMEM_DYN, st>>>(tq, a);
   return launch_status("sparse_mla_fwd");
 }
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of mzb_sparse_mla_fwd.
+//
+// Some callers cannot allocate device memory when they launch attention: a serving engine
+// that has already handed every free byte of HBM to its paged KV-cache pool, or a C/C++
+// host with its own memory manager, where a cudaMalloc would implicitly synchronise the
+// device and stall every other stream.  mzb_sparse_mla_fwd itself allocates nothing, but
+// it asks the caller for an int32 workspace of n_tok entries (the per-token key-list
+// lengths).  This entry point takes that workspace from a fixed array in the library's own
+// device memory instead, so the caller passes only inputs and outputs.
+//
+// The array holds MZB_NOALLOC_MAX_TOKENS entries (256 KB) and exists on every GPU that
+// loads the library, for the life of the process.  Larger calls are rejected.  The array
+// is shared by every call on a device and keeps the last call's contents; each call
+// rewrites every entry it reads, so nothing needs clearing, but two calls whose kernels
+// overlap on the GPU (different streams, no ordering between them) race on it.  The first
+// call on each device looks up the array's device address (cudaGetSymbolAddress, with that
+// device current) and caches it; make that first call before any stream capture.
+// ------------------------------------------------------------------------------------------
+#include <mutex>
+
+#define MZB_NOALLOC_MAX_TOKENS 65536
+
+static __device__ __align__(256) int32_t g_noalloc_slots[MZB_NOALLOC_MAX_TOKENS];
+
+namespace {
+constexpr int kMaxDevices = 64;
+int32_t* g_noalloc_addr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(int32_t** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    mzb::set_error("sparse_mla_fwd_noalloc: no usable current device");
+    return MZB_ERR_LAUNCH;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_slots);
+    if (e != cudaSuccess || p == nullptr) {
+      mzb::set_error("sparse_mla_fwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return MZB_ERR_LAUNCH;
+    }
+    g_noalloc_addr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_noalloc_addr[dev];
+  return MZB_OK;
+}
+}  // namespace
+
+extern "C" int mzb_sparse_mla_fwd_noalloc(const void* q, const void* kv_raw, const void* kv_cmp,
+                                          const int32_t* indices, const int32_t* q_pos,
+                                          const int32_t* raw_page_table, const int32_t* cmp_page_table,
+                                          const int32_t* cmp_lens, void* o, float* lse, int64_t n_tok,
+                                          int tok_per_seq, int topk, int window, int64_t raw_len, int64_t cmp_len,
+                                          int raw_ptw, int cmp_ptw, float softmax_scale, int* err, void* stream) {
+  MZB_REQUIRE(n_tok >= 0 && n_tok <= MZB_NOALLOC_MAX_TOKENS, MZB_ERR_SHAPE,
+              "sparse_mla_fwd_noalloc: n_tok=%lld exceeds the fixed scratch of %d tokens (use mzb_sparse_mla_fwd "
+              "with a caller workspace)",
+              (long long)n_tok, MZB_NOALLOC_MAX_TOKENS);
+  int32_t* slots = nullptr;
+  if (int r = noalloc_scratch(&slots)) return r;
+  return mzb_sparse_mla_fwd(q, kv_raw, kv_cmp, indices, q_pos, raw_page_table, cmp_page_table, cmp_lens, slots, o,
+                            lse, n_tok, tok_per_seq, topk, window, raw_len, cmp_len, raw_ptw, cmp_ptw, softmax_scale,
+                            err, stream);
+}
