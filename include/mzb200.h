@@ -99,6 +99,21 @@ MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, 
                              int64_t S, int64_t T, int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale,
                              int topk, float eps, int* err, void* stream);
 
+/* ------------------------------------------------------------------ shared-latent MQA (D <= 256)
+ * mzb_attn_fwd -- replaces `swa_attn.fwd` / kernel `flashattn` (src/mzoo/layers/attn/
+ *   swa_attn/fwd.py:55-208) and `csa2_attn.fwd` (csa2_attn/fwd.py:70-286).
+ *   q bf16 [B, S*H, D] (BSHD packed rows), kv bf16 [B, S, D] (K == V latent), v bf16
+ *   [B, S, D] or NULL (= kv; a distinct v only without gathered entries), main_kv bf16
+ *   [B, G, D] + indices int32 [B, S, topk] or NULL (window-only), sinks fp32 [H] or NULL.
+ *   Row (t, h) attends keys t-window < k <= t plus main_kv[indices[t, :]] (out-of-range =
+ *   empty, duplicates count twice); one softmax (+ sink column in the denominator).
+ *   o bf16 [B, S*H, D]; lse fp32 [B, S*H] (natural log, packed token-major).
+ *   H must divide 128; D in {64, 128, 256}.
+ */
+MZB_API int mzb_attn_fwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
+                         const float* sinks, void* o, float* lse, int64_t B, int64_t S, int H, int D, int window,
+                         int64_t G, int topk, float softmax_scale, int* err, void* stream);
+
 /* ------------------------------------------------------------------ sparse latent attention
  * mzb_sparse_mla_fwd -- the 576/512 FP8-latent form of `csa2_attn.fwd` / kernel `flashattn`
  *   (src/mzoo/layers/attn/csa2_attn/fwd.py:70-286; golden_ref.py:149-168 level "sparse"),

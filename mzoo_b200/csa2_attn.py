@@ -1,0 +1,37 @@
+"""Window + top-k gathered shared-latent MQA with mzoo's ``csa2_attn`` call signatures, on
+the sm_100a kernel of ``csrc/attn_fwd.cu``.
+
+Drop-in for ``src/mzoo/layers/attn/csa2_attn``: ``fwd(q, kv, main_kv, indices, *, window,
+compress_ratio, causal=True, sinks=None) -> (o, lse)`` (``csa2_attn/fwd.py:238``).  As in
+the reference, ``compress_ratio`` is documentation only (group-causality lives in
+``indices``), an index outside ``[0, G)`` is an empty slot, duplicates count twice, and
+``G == 0`` / ``topk == 0`` reduce to ``swa_attn``.
+"""
+
+import torch
+
+from ._attn_common import check_mqa, run_fwd
+
+
+def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch.Tensor, *, window: int,
+        compress_ratio: int, causal: bool = True, sinks: torch.Tensor | None = None,
+        softmax_scale: float | None = None):
+    """q bf16 [B,S,H,D], kv bf16 [B,S,1,D], main_kv bf16 [B,G,1,D], indices int32/int64
+    [B,S,topk] -> (o bf16 [B,S,H,D], lse fp32 [B,H,S])."""
+    assert causal, "csa2_attn is causal-only: a non-causal sliding window is not a model shape"
+    assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
+    assert isinstance(compress_ratio, int) and compress_ratio >= 1, \
+        f"compress_ratio must be a positive int, got {compress_ratio!r}"
+    B, S, H, D = check_mqa(q, kv, "csa2_attn")
+    G = main_kv.shape[1]
+    assert main_kv.shape == (B, G, 1, D), f"main_kv must be [B, G, 1, D], got {tuple(main_kv.shape)}"
+    assert indices.dtype in (torch.int32, torch.int64), f"indices must be int32/int64, got {indices.dtype}"
+    assert indices.dim() == 3 and indices.shape[:2] == (B, S), \
+        f"indices must be [B, S, topk]=[{B}, {S}, *], got {tuple(indices.shape)}"
+    if sinks is not None:
+        assert sinks.shape == (H,), f"sinks must be [H]={H}, got {tuple(sinks.shape)}"
+        sinks = sinks.detach().float().contiguous()
+    scale = softmax_scale if softmax_scale is not None else D**-0.5
+    main = main_kv.contiguous() if G else None
+    idx = indices.to(torch.int32).contiguous() if (G and indices.shape[2]) else None
+    return run_fwd(q.contiguous(), kv.contiguous(), None, main, idx, sinks, min(window, S), scale)

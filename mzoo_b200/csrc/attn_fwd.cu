@@ -1,0 +1,470 @@
+// Shared-latent MQA attention forward with packed (token, head) rows: the sliding-window
+// kernel (`swa_attn`) and the window + gathered top-k kernel (`csa2_attn`), bf16 in, fp32
+// accumulate, bf16 out, natural-log lse.
+//
+// Reference: src/mzoo/layers/attn/swa_attn/fwd.py:55-208 and csa2_attn/fwd.py:70-286:
+//   rows = q.view(B, S*H, D) (T_q = 128 / H tokens x H heads per tile), keys of the window
+//   t-W < k <= t (self included), then per token its gathered main_kv[indices[t, :]] rows
+//   (index outside [0, G) = empty; duplicates count twice; only that token's rows see them),
+//   one online softmax over both, optional per-head sink (denominator only), scale D^-1/2.
+//   K == V (the shared latent) by default; a distinct V (where K and V
+//   are quantised differently) is accepted for the window-only kernel.
+//
+// tcgen05 kernel, one CTA per 128-row query tile, persistent over tiles:
+//   warp 0      TMA: Q tile, window K (and V) tiles into a ring of stages
+//   warp 1      TMEM allocation + the MMA-issuing thread
+//   warps 4-7   softmax, lazy O correction, epilogue (thread = row = TMEM lane)
+//   warps 8-11  gathered-tile producers (ld.global of main_kv rows -> swizzled smem)
+// S = Q K^T (M=128 rows, N=NK keys) and O += P V (N=D) accumulate in TMEM; P goes through
+// shared memory as bf16.  MMA order QK_0, QK_1, PV_0, QK_2, PV_1, ... as in sparse_mla.cu.
+#include "tc.cuh"
+
+namespace mzb {
+namespace attn {
+
+constexpr int NTHREADS = 384;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+
+template <int D, bool SEP_V>
+struct Cfg {
+  static constexpr int NK = D == 256 ? 64 : 128;  // keys per tile
+  static constexpr int DB = D / 64;               // 64-channel column blocks
+  static constexpr int Q_BYTES = 128 * D * 2;
+  static constexpr int K_BYTES = NK * D * 2;
+  static constexpr int STAGE_BYTES = K_BYTES * (SEP_V ? 2 : 1);
+  static constexpr int P_BYTES = 128 * NK * 2;
+  static constexpr int STAGES = SEP_V ? 2 : 3;
+  static constexpr int TILE_BYTES = Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES;
+  static constexpr int MISC = 512 + 2 * 128 * 4;
+  static constexpr int SMEM = TILE_BYTES + MISC;
+  static constexpr int S_COL0 = D;  // O in columns [0, D), S buffers after it
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(D + 2 * NK <= 512, "TMEM budget");
+};
+
+struct Args {
+  const __nv_bfloat16* main_kv;  // [B, G, D] gathered source (csa2) or null
+  const int32_t* idx;            // [B, S, topk] or null
+  const float* sinks;            // [H] or null
+  __nv_bfloat16* o;              // [B, S*H, D]
+  float* lse;                    // [B, S*H]
+  int B, S, H, window, G, topk;
+  float scale_log2;
+  int* err;
+};
+
+enum Bar { Q_FULL = 0, Q_EMPTY, O_DONE, O_EMPTY, S_FULL, S_FULL1, S_EMPTY, S_EMPTY1, P_FULL, P_FULL1, KV_FULL_W,
+           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, NBAR = KV_EMPTY + 4 };
+
+__device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Per item (query tile): window tile range and the number of gathered tiles.
+struct Item {
+  int b, qt, t0, t1, kt0, n_win, n_gat, tq_valid;
+};
+
+template <int NK>
+__device__ __forceinline__ Item make_item(const Args& a, int it, int n_qt) {
+  Item m;
+  m.b = it % a.B;
+  m.qt = n_qt - 1 - it / a.B;  // heavy (late) tiles first
+  const int tq = 128 / a.H;
+  m.t0 = m.qt * tq;
+  m.t1 = min(a.S, m.t0 + tq) - 1;
+  m.tq_valid = m.t1 - m.t0 + 1;
+  const int lo = max(0, m.t0 - a.window + 1);
+  m.kt0 = lo / NK;
+  m.n_win = m.t1 / NK - m.kt0 + 1;
+  const int gt = (a.main_kv && a.topk > 0 && a.G > 0) ? (a.topk + NK - 1) / NK : 0;
+  m.n_gat = gt * m.tq_valid;
+  return m;
+}
+
+template <int D, bool SEP_V>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, Args a) {
+  using C = Cfg<D, SEP_V>;
+  constexpr int NK = C::NK;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* qs = smem;
+  uint8_t* kvs = qs + C::Q_BYTES;
+  uint8_t* ps = kvs + C::STAGES * C::STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 8 * NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::TILE_BYTES + 8 * NBAR + 4);
+  uint32_t* colmask = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 256);  // unused slot
+  (void)colmask;
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(a.err, MZB_ERR_ALIGN);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NBAR; ++i) {
+      uint32_t c = 1;
+      if (i == O_EMPTY || i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1) c = 4;
+      if (i >= KV_FULL_G && i < KV_EMPTY) c = 4;
+      tc::mbar_init(&bars[i], c);
+    }
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tq);
+    tc::prefetch_tmap(&tk);
+    if (SEP_V) tc::prefetch_tmap(&tv);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  const int tqn = 128 / a.H;
+  const int n_qt = (a.S + tqn - 1) / tqn;
+  const int items = a.B * n_qt;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int g = 0, ii = 0;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const Item m = make_item<NK>(a, it, n_qt);
+        if (!tc::mbar_wait(&bars[Q_EMPTY], (ii & 1) ^ 1, a.err, 301)) { *abort_flag = 1; break; }
+        tc::mbar_expect_tx(&bars[Q_FULL], C::Q_BYTES);
+        for (int cb = 0; cb < C::DB; ++cb) tc::tma_load_3d(qs + cb * 128 * 128, &tq, &bars[Q_FULL], cb * 64, m.qt * 128, m.b);
+        bool ok = true;
+        for (int j = 0; j < m.n_win + m.n_gat; ++j, ++g) {
+          const int st = g % C::STAGES, ph = (g / C::STAGES) & 1;
+          if (j >= m.n_win) continue;  // gathered tiles: warps 8-11
+          if (!tc::mbar_wait(&bars[KV_EMPTY + st], ph ^ 1, a.err, 302)) { ok = false; break; }
+          uint8_t* kt = kvs + st * C::STAGE_BYTES;
+          tc::mbar_expect_tx(&bars[KV_FULL_W + st], C::STAGE_BYTES);
+          for (int cb = 0; cb < C::DB; ++cb) {
+            tc::tma_load_3d(kt + cb * NK * 128, &tk, &bars[KV_FULL_W + st], cb * 64, (m.kt0 + j) * NK, m.b);
+            if (SEP_V)
+              tc::tma_load_3d(kt + C::K_BYTES + cb * NK * 128, &tv, &bars[KV_FULL_W + st], cb * 64, (m.kt0 + j) * NK,
+                              m.b);
+          }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = tc::make_idesc(128, NK, 1, 1);
+      const uint32_t idesc_pv = tc::make_idesc(128, D, 1, 1, false, true);
+      const uint32_t q_base = smem_u32(qs), kv_base = smem_u32(kvs), p_base = smem_u32(ps);
+      int g = 0, ii = 0;
+      int uses_w[4] = {0, 0, 0, 0}, uses_g[4] = {0, 0, 0, 0};
+      auto pv = [&](int gg, bool first, int item) -> bool {
+        const int st = gg % C::STAGES, pb = gg & 1;
+        if (first && !tc::mbar_wait(&bars[O_EMPTY], (item & 1) ^ 1, a.err, 311)) return false;
+        if (!tc::mbar_wait(&bars[P_FULL + pb], (gg >> 1) & 1, a.err, 312)) return false;
+        tc::fence_after_sync();
+        const uint32_t vb = kv_base + st * C::STAGE_BYTES + (SEP_V ? C::K_BYTES : 0);
+#pragma unroll
+        for (int jj = 0; jj < NK / 16; ++jj) {
+          const int cb = jj >> 2, off = (jj & 3) * 32;
+          const uint64_t ad = tc::make_sdesc<128>(p_base + pb * C::P_BYTES + cb * 128 * 128 + off, 16, 1024);
+          const uint64_t bd = tc::make_sdesc<128>(vb + jj * 16 * 128, NK * 128, 1024);
+          tc::mma_ss<0>(tmem, ad, bd, idesc_pv, (first && jj == 0) ? 0u : 1u);
+        }
+        tc::mma_commit(&bars[KV_EMPTY + st]);
+        tc::mma_commit(&bars[O_DONE]);
+        return true;
+      };
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const Item m = make_item<NK>(a, it, n_qt);
+        const int n = m.n_win + m.n_gat;
+        if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 310)) { *abort_flag = 1; break; }
+        bool ok = true;
+        for (int j = 0; j < n; ++j, ++g) {
+          const int st = g % C::STAGES, sb = g & 1;
+          const bool win = j < m.n_win;
+          const int par = win ? (uses_w[st]++ & 1) : (uses_g[st]++ & 1);
+          if (!tc::mbar_wait(&bars[(win ? KV_FULL_W : KV_FULL_G) + st], par, a.err, 313) ||
+              !tc::mbar_wait(&bars[S_EMPTY + sb], ((g >> 1) & 1) ^ 1, a.err, 314)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t kb = kv_base + st * C::STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int cb = kk >> 2, off = (kk & 3) * 32;
+            const uint64_t ad = tc::make_sdesc<128>(q_base + cb * 128 * 128 + off, 16, 1024);
+            const uint64_t bd = tc::make_sdesc<128>(kb + cb * NK * 128 + off, 16, 1024);
+            tc::mma_ss<0>(tmem + C::S_COL0 + sb * NK, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          tc::mma_commit(&bars[S_FULL + sb]);
+          if (j == n - 1) tc::mma_commit(&bars[Q_EMPTY]);
+          if (j >= 1 && !pv(g - 1, j == 1, ii)) { ok = false; break; }
+        }
+        if (!ok || !pv(g - 1, n == 1, ii)) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------------------------------------------------------- softmax / epilogue
+    const int sw = warp - 4, r = sw * 32 + lane;
+    const float sl = a.scale_log2;
+    int g = 0, ii = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+      const Item m = make_item<NK>(a, it, n_qt);
+      const int n = m.n_win + m.n_gat;
+      const int tr = r / a.H;          // token of this row within the tile
+      const int t = m.t0 + tr;         // absolute token
+      const int h = r % a.H;
+      const bool row_ok = t < a.S;
+      const int gtiles = m.n_gat / max(1, m.tq_valid);
+      float mrow = -1e30f, lsum = 0.0f;
+      bool ok = true;
+      for (int j = 0; j < n; ++j, ++g) {
+        const int sb = g & 1;
+        // column validity of this tile for this row
+        const bool win = j < m.n_win;
+        int k0 = 0, wlo = 0, whi = -1, gtok = -1;
+        uint32_t gm[NK / 32];
+        if (win) {
+          k0 = (m.kt0 + j) * NK;
+          wlo = max(0, t - a.window + 1) - k0;  // valid columns [wlo, whi]
+          whi = t - k0;
+        } else {
+          const int gj = j - m.n_win;
+          gtok = gj / gtiles;
+          const int e0 = (gj % gtiles) * NK;
+          const int32_t* irow = a.idx + ((long long)m.b * a.S + (m.t0 + gtok)) * a.topk;
+#pragma unroll
+          for (int w = 0; w < NK / 32; ++w) {
+            const int e = e0 + w * 32 + lane;
+            bool v = false;
+            if (e < a.topk) {
+              const int gi = irow[e];
+              v = gi >= 0 && gi < a.G;
+            }
+            gm[w] = __ballot_sync(0xffffffffu, v);
+          }
+        }
+        if (!tc::mbar_wait(&bars[S_FULL + sb], (g >> 1) & 1, a.err, 320)) { ok = false; break; }
+        tc::fence_after_sync();
+        const uint32_t sbase = tc::taddr(tmem, sw * 32, C::S_COL0 + sb * NK);
+        auto valid = [&](int c) -> bool {
+          if (!row_ok) return false;
+          if (win) return c >= wlo && c <= whi;
+          return tr == gtok && ((gm[c >> 5] >> (c & 31)) & 1u);
+        };
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c0 = 0; c0 < NK; c0 += 32) {
+          uint32_t sr[32];
+          tc::tmem_ld32(sbase + c0, sr);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (valid(c0 + i)) mt = fmaxf(mt, __uint_as_float(sr[i]));
+        }
+        const bool need = mt * sl > mrow * sl + 8.0f;
+        const float m_new = need ? mt : mrow;
+        const float alpha = exp2f((mrow - m_new) * sl);
+        const float ms = m_new * sl;
+        float psum = 0.0f;
+        uint8_t* prow = ps + sb * C::P_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+        for (int c0 = 0; c0 < NK; c0 += 32) {
+          uint32_t sr[32];
+          tc::tmem_ld32(sbase + c0, sr);
+          tc::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = valid(c0 + 2 * i) ? exp2f(fmaf(__uint_as_float(sr[2 * i]), sl, -ms)) : 0.0f;
+            const float p1 = valid(c0 + 2 * i + 1) ? exp2f(fmaf(__uint_as_float(sr[2 * i + 1]), sl, -ms)) : 0.0f;
+            psum += p0 + p1;
+            pk[i] = pack_bf16(p0, p1);
+          }
+          // row r of column block c0/64: 4 chunks of 16 B (keys c0..c0+31 -> chunks (c0%64)/8 ..)
+          uint8_t* blk = prow + (c0 >> 6) * 128 * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int ch = ((c0 & 63) >> 3) + q;
+            st_shared16(blk + ((ch ^ (r & 7)) * 16), make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]));
+          }
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[S_EMPTY + sb]);
+        lsum = lsum * alpha + psum;
+        if (j > 0 && __any_sync(0xffffffffu, need)) {
+          if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 321)) { ok = false; break; }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t ov[32];
+            tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tc::tmem_st32(tc::taddr(tmem, sw * 32, c0), ov);
+          }
+          tc::tmem_wait_st();
+        }
+        mrow = m_new;
+        tc::fence_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[P_FULL + sb]);
+      }
+      if (!ok) { *abort_flag = 1; break; }
+      if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 322)) { *abort_flag = 1; break; }
+      tc::fence_after_sync();
+      if (a.sinks) lsum += exp2f(a.sinks[h] * LOG2E - mrow * sl);
+      const float inv = 1.0f / lsum;
+      const long long grow = (long long)m.qt * 128 + r;  // packed row within the batch
+      if (row_ok) {
+        __nv_bfloat16* orow = a.o + ((long long)m.b * a.S * a.H + grow) * D;
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t ov[32];
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
+          tc::tmem_wait_ld();
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16(__uint_as_float(ov[8 * q]) * inv, __uint_as_float(ov[8 * q + 1]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv));
+        }
+        a.lse[(long long)m.b * a.S * a.H + grow] = (mrow * sl + log2f(lsum)) * LN2;
+      } else {
+        // keep the warp-collective TMEM loads uniform: rows past S read and discard
+#pragma unroll
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t ov[32];
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
+          tc::tmem_wait_ld();
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[O_EMPTY]);
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------------- gathered-tile producers
+    const int t = threadIdx.x - 256;  // 0..127
+    constexpr int TPR = 128 / NK;     // threads per row
+    constexpr int CPT = D / 8 / TPR;  // 16-byte chunks per thread
+    const int row = t / TPR, sub = t % TPR;
+    int g = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+      const Item m = make_item<NK>(a, it, n_qt);
+      const int n = m.n_win + m.n_gat;
+      const int gtiles = m.n_gat / max(1, m.tq_valid);
+      bool ok = true;
+      for (int j = 0; j < n; ++j, ++g) {
+        if (j < m.n_win) continue;
+        const int st = g % C::STAGES, ph = (g / C::STAGES) & 1;
+        const int gj = j - m.n_win, gtok = gj / gtiles, e = (gj % gtiles) * NK + row;
+        int gi = -1;
+        if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
+        const bool v = gi >= 0 && gi < a.G;
+        const uint4* src = reinterpret_cast<const uint4*>(a.main_kv + ((long long)m.b * a.G + (v ? gi : 0)) * D);
+        uint4 raw[CPT];
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) raw[q] = v ? __ldg(src + sub * CPT + q) : make_uint4(0, 0, 0, 0);
+        if (!tc::mbar_wait(&bars[KV_EMPTY + st], ph ^ 1, a.err, 330)) { ok = false; break; }
+        uint8_t* kt = kvs + st * C::STAGE_BYTES;
+#pragma unroll
+        for (int q = 0; q < CPT; ++q) {
+          const int ch = sub * CPT + q;  // chunk within the row (8 bf16 each)
+          const int cb = ch >> 3, c16 = ch & 7;
+          st_shared16(kt + cb * NK * 128 + row * 128 + ((c16 ^ (row & 7)) * 16), raw[q]);
+        }
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[KV_FULL_G + st]);
+      }
+      if (!ok) { *abort_flag = 1; break; }
+    }
+  }
+
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_free(tmem, 512);
+  }
+}
+
+template <int D, bool SEP_V>
+int launch(const void* q, const void* k, const void* v, const Args& a, cudaStream_t st) {
+  using C = Cfg<D, SEP_V>;
+  CUtensorMap tq, tk, tv;
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.S) * a.H, uint64_t(a.B)};
+    const uint64_t str[2] = {uint64_t(D) * 2, uint64_t(a.S) * a.H * D * 2};
+    const uint32_t box[3] = {64, 128, 1};
+    if (int r = encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+  }
+  const uint64_t dims[3] = {uint64_t(D), uint64_t(a.S), uint64_t(a.B)};
+  const uint64_t str[2] = {uint64_t(D) * 2, uint64_t(a.S) * D * 2};
+  const uint32_t box[3] = {64, uint32_t(C::NK), 1};
+  if (int r = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, k, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    return r;
+  if (int r = encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, SEP_V ? v : k, dims, str, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return r;
+  auto kern = attn_fwd_kernel<D, SEP_V>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    return launch_status("attn_fwd(smem attr)");
+  const int n_qt = (a.S + 128 / a.H - 1) / (128 / a.H);
+  const int items = a.B * n_qt;
+  const int grid = items < num_sms() ? items : num_sms();
+  kern<<<grid, NTHREADS, C::SMEM, st>>>(tq, tk, tv, a);
+  return launch_status("attn_fwd");
+}
+
+}  // namespace attn
+}  // namespace mzb
+
+using namespace mzb;
+
+extern "C" int mzb_attn_fwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
+                            const float* sinks, void* o, float* lse, int64_t B, int64_t S, int H, int D, int window,
+                            int64_t G, int topk, float softmax_scale, int* err, void* stream) {
+  MZB_REQUIRE(B >= 1 && S >= 1 && window >= 1 && topk >= 0 && G >= 0, MZB_ERR_SHAPE,
+              "attn_fwd: bad sizes B=%lld S=%lld window=%d topk=%d G=%lld", (long long)B, (long long)S, window, topk,
+              (long long)G);
+  MZB_REQUIRE(H >= 1 && H <= 128 && 128 % H == 0, MZB_ERR_UNSUPPORTED,
+              "attn_fwd: heads must divide 128 (packed 128-row tiles), got %d", H);
+  MZB_REQUIRE(D == 64 || D == 128 || D == 256, MZB_ERR_UNSUPPORTED, "attn_fwd: unsupported head dim %d", D);
+  MZB_REQUIRE(v == nullptr || v == kv || main_kv == nullptr || topk == 0, MZB_ERR_UNSUPPORTED,
+              "attn_fwd: a separate V is supported for the window-only kernel");
+  MZB_REQUIRE(err != nullptr, MZB_ERR_SHAPE, "attn_fwd: needs an error word");
+  MZB_REQUIRE(S * H * D < (int64_t(1) << 40), MZB_ERR_SHAPE, "attn_fwd: too large");
+  attn::Args a{};
+  a.main_kv = static_cast<const __nv_bfloat16*>(main_kv);
+  a.idx = indices;
+  a.sinks = sinks;
+  a.o = static_cast<__nv_bfloat16*>(o);
+  a.lse = lse;
+  a.B = int(B); a.S = int(S); a.H = H; a.window = window; a.G = int(G); a.topk = topk;
+  if (!main_kv || topk == 0 || G == 0) { a.main_kv = nullptr; a.topk = 0; }
+  a.scale_log2 = softmax_scale * attn::LOG2E;
+  a.err = err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool sep = v != nullptr && v != kv;
+  switch (D) {
+    case 64: return sep ? attn::launch<64, true>(q, kv, v, a, st) : attn::launch<64, false>(q, kv, v, a, st);
+    case 128: return sep ? attn::launch<128, true>(q, kv, v, a, st) : attn::launch<128, false>(q, kv, v, a, st);
+    default: return sep ? attn::launch<256, true>(q, kv, v, a, st) : attn::launch<256, false>(q, kv, v, a, st);
+  }
+}

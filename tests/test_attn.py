@@ -1,0 +1,160 @@
+"""swa_attn / csa2_attn (K == V shared-latent MQA, D <= 256): oracle pinned to the
+reference's golden vectors (CPU); the sm_100a forward against the oracle (GPU).
+
+Reference tests mirrored: ``swa_attn/fwd_test.py:53-130`` (window not tile-aligned,
+window >= S, sinks), ``csa2_attn/fwd_test.py:82-195`` (topk > visible, non-power-of-2 G,
+-1 padding, feature-off equals swa bit-for-bit).  Tolerance: the north-star max-abs
+2e-2 + rel 1e-2 against the fp64 oracle on the same bf16 inputs.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+from oracle import attention as A
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def _golden():
+    return np.load(os.path.join(GOLDEN, "attention.npz"))
+
+
+# ----------------------------------------------------------------------------- CPU: oracle pin
+
+@pytest.mark.parametrize("w", [1, 16, 40, 200])
+def test_oracle_window_matches_reference(w):
+    d = _golden()
+    o, lse = A.attend(d["q"], d["kv"], window=w)
+    np.testing.assert_allclose(o, d[f"window{w}.o"], atol=2e-6)
+    np.testing.assert_allclose(lse, d[f"window{w}.lse"], atol=2e-6)
+
+
+def test_oracle_sink_and_sparse_match_reference():
+    d = _golden()
+    o, lse = A.attend(d["q"], d["kv"], window=16, sinks=d["sinks"])
+    np.testing.assert_allclose(o, d["window16sink.o"], atol=2e-6)
+    np.testing.assert_allclose(lse, d["window16sink.lse"], atol=2e-6)
+    o, lse = A.attend(d["q"], d["kv"], window=16, main_kv=d["main"], indices=d["idx"])
+    np.testing.assert_allclose(o, d["sparse.o"], atol=2e-6)
+    np.testing.assert_allclose(lse, d["sparse.lse"], atol=2e-6)
+
+
+def test_oracle_gradients_match_reference_autograd():
+    d = _golden()
+    g = A.attend_bwd(d["q"], d["kv"], d["bwd.do"], window=16, sinks=d["sinks"])
+    np.testing.assert_allclose(g["dq"], d["bwd.dq"], atol=5e-6)
+    np.testing.assert_allclose(g["dkv"], d["bwd.dkv"].reshape(g["dkv"].shape), atol=5e-6)
+    np.testing.assert_allclose(g["dsinks"], d["bwd.dsinks"], atol=5e-6)
+
+
+# ----------------------------------------------------------------------------- GPU
+
+def _inputs(torch, dev, B, S, H, D, G=0, topk=0, ratio=4, seed=0, dup=False, holes=False, sinks=False, sep_v=False):
+    rng = np.random.default_rng(seed)
+    f = lambda *s: torch.from_numpy(rng.standard_normal(s).astype(np.float32)).to(torch.bfloat16)  # noqa: E731
+    q, kv = f(B, S, H, D), f(B, S, 1, D)
+    v = f(B, S, 1, D) if sep_v else None
+    main = f(B, G, 1, D) if G else None
+    idx = None
+    if topk:
+        idx = np.full((B, S, topk), -1, np.int32)
+        for b in range(B):
+            for s in range(S):
+                vis = min(G, (s + 1) // ratio)
+                sel = np.sort(rng.permutation(vis)[:topk]) if vis else []
+                idx[b, s, :len(sel)] = sel
+                if dup and len(sel) >= 2:
+                    idx[b, s, 1] = idx[b, s, 0]
+                if holes and len(sel) >= 3:
+                    idx[b, s, 2] = -1
+        idx = torch.from_numpy(idx)
+    sk = torch.from_numpy(rng.standard_normal(H).astype(np.float32)) if sinks else None
+    mv = lambda t: None if t is None else t.to(dev)  # noqa: E731
+    return mv(q), mv(kv), mv(v), mv(main), mv(idx), mv(sk)
+
+
+def _np(t):
+    return None if t is None else t.float().cpu().numpy()
+
+
+def _check(o, lse, ref_o, ref_lse, what):
+    o, lse = _np(o), _np(lse)
+    eo = np.abs(o - ref_o).max()
+    el = np.abs(lse - ref_lse).max()
+    print(f"{what}: max|o-ref|={eo:.3e} max|lse-ref|={el:.3e}")
+    assert np.all(np.abs(o - ref_o) <= ATOL + RTOL * np.abs(ref_o)), f"{what}: o err {eo}"
+    assert np.all(np.abs(lse - ref_lse) <= ATOL + RTOL * np.abs(ref_lse)), f"{what}: lse err {el}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("H", [4, 16, 64])
+def test_swa_fwd(cuda, D, H):
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, _, _, _, _ = _inputs(torch, cuda, 2, 160, H, D, seed=D + H)
+    o, lse = swa_attn.fwd(q, kv, window=100)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=100)
+    _check(o, lse, ref_o, ref_lse, f"swa D{D} H{H}")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("window", [1, 128, 513, 4096])
+def test_swa_windows_and_sinks(cuda, window):
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, _, _, _, sk = _inputs(torch, cuda, 1, 600, 32, 128, seed=window, sinks=True)
+    o, lse = swa_attn.fwd(q, kv, window=window, sinks=sk)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=window, sinks=_np(sk))
+    _check(o, lse, ref_o, ref_lse, f"swa window {window}")
+
+
+@pytest.mark.gpu
+def test_swa_separate_v(cuda):
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, v, _, _, _ = _inputs(torch, cuda, 2, 300, 64, 128, seed=4, sep_v=True)
+    o, lse = swa_attn.fwd(q, kv, window=160, v=v)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=160, v=_np(v)[:, :, 0])
+    _check(o, lse, ref_o, ref_lse, "swa K!=V")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (64, 256, 70, 64), (4, 128, 50, 135)])
+def test_csa2_fwd(cuda, H, D, G, topk):
+    import torch
+    from mzoo_b200 import csa2_attn
+    q, kv, _, main, idx, sk = _inputs(torch, cuda, 2, 200, H, D, G=G, topk=topk, seed=G + topk, holes=True,
+                                      sinks=True)
+    o, lse = csa2_attn.fwd(q, kv, main, idx, window=100, compress_ratio=4, sinks=sk)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=100, main_kv=_np(main)[:, :, 0],
+                              indices=idx.cpu().numpy(), sinks=_np(sk))
+    _check(o, lse, ref_o, ref_lse, f"csa2 H{H} D{D} G{G} topk{topk}")
+
+
+@pytest.mark.gpu
+def test_csa2_duplicates_count_twice(cuda):
+    import torch
+    from mzoo_b200 import csa2_attn
+    q, kv, _, main, idx, _ = _inputs(torch, cuda, 1, 128, 64, 128, G=40, topk=32, seed=8, dup=True)
+    o, lse = csa2_attn.fwd(q, kv, main, idx, window=64, compress_ratio=4)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=64, main_kv=_np(main)[:, :, 0],
+                              indices=idx.cpu().numpy())
+    _check(o, lse, ref_o, ref_lse, "csa2 duplicates")
+
+
+@pytest.mark.gpu
+def test_csa2_feature_off_equals_swa_bitwise(cuda):
+    """csa2_attn/fwd_test.py:145-168: all -1 indices, or G == 0, is swa_attn bit for bit."""
+    import torch
+    from mzoo_b200 import csa2_attn, swa_attn
+    q, kv, _, main, idx, sk = _inputs(torch, cuda, 2, 256, 64, 128, G=64, topk=64, seed=2, sinks=True)
+    ref = swa_attn.fwd(q, kv, window=128, sinks=sk)
+    got = csa2_attn.fwd(q, kv, main, torch.full_like(idx, -1), window=128, compress_ratio=4, sinks=sk)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
+    empty = main[:, :0]
+    got = csa2_attn.fwd(q, kv, empty, idx, window=128, compress_ratio=4, sinks=sk)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
