@@ -114,6 +114,20 @@ MZB_API int mzb_attn_fwd(const void* q, const void* kv, const void* v, const voi
                          const float* sinks, void* o, float* lse, int64_t B, int64_t S, int H, int D, int window,
                          int64_t G, int topk, float softmax_scale, int* err, void* stream);
 
+/* mzb_attn_bwd -- replaces `swa_attn.bwd` (swa_attn/bwd.py:79-119: preprocess, bwd_kv,
+ *   bwd_dq) and `csa2_attn.bwd` (csa2_attn/bwd.py:67-130, bwd_dq.py:60-187).  Inputs as
+ *   mzb_attn_fwd plus o, lse (packed [B, S*H]) and dout bf16 [B, S*H, D].  Outputs: dq bf16
+ *   [B, S*H, D]; dk bf16 [B, S, D] (= dK + dV when v is NULL, i.e. K == V); dv bf16 [B, S, D]
+ *   (separate v only); dmain_f32 fp32 [B, G, D] accumulated with atomics (caller zeroes it;
+ *   not bit-reproducible, as in the reference).  delta_ws, lse2_ws: fp32 workspaces of
+ *   B * ceil(S*H/128)*128 entries.  D in {64, 128}.  dsinks is a host-side reduction of lse
+ *   and delta (as in the reference).
+ */
+MZB_API int mzb_attn_bwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
+                         const void* o, const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                         float* dmain_f32, float* delta_ws, float* lse2_ws, int64_t B, int64_t S, int H, int D,
+                         int window, int64_t G, int topk, float softmax_scale, int* err, void* stream);
+
 /* ------------------------------------------------------------------ sparse latent attention
  * mzb_sparse_mla_fwd -- the 576/512 FP8-latent form of `csa2_attn.fwd` / kernel `flashattn`
  *   (src/mzoo/layers/attn/csa2_attn/fwd.py:70-286; golden_ref.py:149-168 level "sparse"),

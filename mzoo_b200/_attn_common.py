@@ -34,3 +34,33 @@ def run_fwd(q, kv, v, main_kv, idx, sinks, window, scale, check=True):
     if check and int(err.item()):
         raise _lib.MzbError(f"attn_fwd: device error code {int(err.item())}")
     return o, lse.view(B, S, H).permute(0, 2, 1).contiguous()
+
+
+def run_bwd(q, kv, v, main_kv, idx, o, lse, do, sinks, window, scale, check=True):
+    """-> (dq [B,S,H,D], dkv [B,S,1,D] (dK+dV when v is None, else dK), dv or None,
+    dmain [B,G,1,D] or None, dsinks [H] or None)."""
+    require_cuda(q, kv, v, main_kv, idx, o, lse, do)
+    B, S, H, D = q.shape
+    dev = q.device
+    rpad = -(-S * H // 128) * 128
+    lse_packed = lse.permute(0, 2, 1).reshape(B, S * H).contiguous()  # [B,H,S] -> token-major rows
+    dq = torch.empty_like(q)
+    dk = torch.empty(B, S, 1, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty_like(dk) if v is not None else None
+    G = main_kv.shape[1] if main_kv is not None else 0
+    topk = idx.shape[2] if idx is not None else 0
+    dmain = torch.zeros(B, max(G, 1), D, dtype=torch.float32, device=dev) if G else None
+    delta = torch.empty(B, rpad, dtype=torch.float32, device=dev)
+    lse2 = torch.empty(B, rpad, dtype=torch.float32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    call("mzb_attn_bwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(o), ptr(lse_packed), ptr(do), ptr(dq),
+         ptr(dk), ptr(dv), ptr(dmain), ptr(delta), ptr(lse2), B, S, H, D, window, G, topk, float(scale), ptr(err),
+         stream_ptr(dev))
+    if check and int(err.item()):
+        raise _lib.MzbError(f"attn_bwd: device error code {int(err.item())}")
+    dsinks = None
+    if sinks is not None:  # swa_attn/bwd.py, csa2_attn/bwd.py:123-127: a torch reduce over lse / delta
+        d = delta[:, :S * H].view(B, S, H).permute(0, 2, 1)
+        dsinks = -(torch.exp(sinks.detach().float().view(1, H, 1) - lse) * d).sum(dim=(0, 2))
+    dmain_out = dmain.to(torch.bfloat16).view(B, G, 1, D) if G else None
+    return dq, dk, dv, dmain_out, dsinks

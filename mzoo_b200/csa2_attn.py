@@ -10,7 +10,7 @@ the reference, ``compress_ratio`` is documentation only (group-causality lives i
 
 import torch
 
-from ._attn_common import check_mqa, run_fwd
+from ._attn_common import check_mqa, run_bwd, run_fwd
 
 
 def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch.Tensor, *, window: int,
@@ -35,3 +35,53 @@ def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch
     main = main_kv.contiguous() if G else None
     idx = indices.to(torch.int32).contiguous() if (G and indices.shape[2]) else None
     return run_fwd(q.contiguous(), kv.contiguous(), None, main, idx, sinks, min(window, S), scale)
+
+
+def bwd(q, kv, main_kv, indices, o, lse, do, *, window: int, compress_ratio: int, causal: bool = True, sinks=None,
+        cfg=None, splits=None, scatter: str = "atomic", softmax_scale: float | None = None):
+    """``csa2_attn/bwd.py:67``: -> (dq [B,S,H,D], dkv [B,S,1,D], dmain_kv [B,G,1,D],
+    dsinks [H] or None).  ``dmain_kv`` is accumulated with fp32 atomics (not bitwise
+    reproducible run to run, like the reference).  ``cfg`` / ``splits`` are accepted and
+    ignored; ``scatter`` must be "atomic" (the reference's other values are its bench
+    ablations)."""
+    assert causal, "csa2_attn is causal-only"
+    assert scatter == "atomic", "only the atomic scatter is a real gradient"
+    assert q.shape == o.shape == do.shape, "shape mismatch"
+    assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
+    B, S, H, D = check_mqa(q, kv, "csa2_attn")
+    assert D in (64, 128), f"csa2_attn backward supports head dim 64 / 128 here, got {D}"
+    G = main_kv.shape[1]
+    scale = softmax_scale if softmax_scale is not None else D**-0.5
+    main = main_kv.contiguous() if G else None
+    idx = indices.to(torch.int32).contiguous() if (G and indices.shape[2]) else None
+    dq, dkv, _, dmain, dsinks = run_bwd(q.contiguous(), kv.contiguous(), None, main, idx, o.contiguous(),
+                                        lse.contiguous(), do.contiguous(), sinks, min(window, S), scale)
+    if dmain is None:
+        dmain = torch.zeros_like(main_kv)
+    return dq, dkv, dmain, dsinks
+
+
+class _Attn(torch.autograd.Function):
+    """``csa2_attn/attn.py:20``: saves (q, kv, main_kv, indices, o, lse[, sinks])."""
+
+    @staticmethod
+    def forward(ctx, q, kv, main_kv, indices, window, compress_ratio, causal, sinks):
+        o, lse = fwd(q, kv, main_kv, indices, window=window, compress_ratio=compress_ratio, causal=causal,
+                     sinks=sinks)
+        saved = (q, kv, main_kv, indices, o, lse)
+        ctx.save_for_backward(*(saved if sinks is None else saved + (sinks,)))
+        ctx.window, ctx.ratio, ctx.causal = window, compress_ratio, causal
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, kv, main_kv, indices, o, lse, *rest = ctx.saved_tensors
+        dq, dkv, dmain, dsinks = bwd(q, kv, main_kv, indices, o, lse, do, window=ctx.window,
+                                     compress_ratio=ctx.ratio, causal=ctx.causal, sinks=rest[0] if rest else None)
+        return dq, dkv, dmain, None, None, None, None, dsinks
+
+
+def attn(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch.Tensor, *, window: int,
+         compress_ratio: int, causal: bool = True, sinks: torch.Tensor | None = None) -> torch.Tensor:
+    """``csa2_attn/attn.py:40``: differentiable window + gathered attention -> o."""
+    return _Attn.apply(q, kv, main_kv, indices, window, compress_ratio, causal, sinks)

@@ -1,0 +1,713 @@
+// Shared-latent MQA attention backward (swa_attn / csa2_attn), tcgen05 kernels.
+//
+// Reference: src/mzoo/layers/attn/swa_attn/bwd.py:79-119 (preprocess, bwd_kv, bwd_dq) and
+// csa2_attn/bwd.py:67-130 + bwd_dq.py:60-187 (dQ plus the fp32-atomic scatter of dmain_kv).
+// With P the softmax (sink column included through lse), delta = rowsum(dO * O):
+//   dS = P * (dO V^T - delta),  dQ = scale dS K,  dK = scale dS^T Q,  dV = P^T dO,
+//   K == V: dKV = dK + dV;  gathered rows: dmain[idx] += dK_g + dV_g (fp32 atomics, so not
+//   bit-reproducible run to run, as in the reference).
+//
+// Kernels (one CTA per tile, persistent):
+//   preprocess  delta and lse*log2(e) per packed row, into 128-row-padded buffers
+//   dkv         key owner: 128 window keys; loops over the query tiles that see them;
+//               S^T = K Q^T and dP^T = V dO^T in TMEM; the compute warps (thread = key)
+//               turn them into P^T, dS^T and store them back into TMEM as bf16, which the
+//               TS MMAs dV += P^T dO, dK += dS^T Q read as their A operand.
+//   dq          query owner: 128 rows; loops over window tiles then gathered tiles;
+//               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K); gathered tiles also
+//               keep dS and P in shared memory for dM = dS^T Q + P^T dO, scattered into
+//               dmain by the compute warps with fp32 atomics.
+#include "tc.cuh"
+
+namespace mzb {
+namespace attnb {
+
+constexpr float LOG2E = 1.4426950408889634f;
+
+__device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+struct Args {
+  const __nv_bfloat16* o;
+  const __nv_bfloat16* dout;
+  const float* lse;      // [B, S*H] natural log
+  float* delta;          // [B, Rpad] workspace
+  float* lse2;           // [B, Rpad] workspace (lse * log2 e)
+  const __nv_bfloat16* main_kv;
+  const int32_t* idx;
+  __nv_bfloat16* dq;     // [B, S*H, D]
+  __nv_bfloat16* dk;     // [B, S, D]  (dK + dV when K == V)
+  __nv_bfloat16* dv;     // [B, S, D] or null
+  float* dmain;          // [B, G, D] fp32 accumulator (zeroed by the caller) or null
+  int B, S, H, D, window, G, topk, Rpad;
+  float scale, scale_log2;
+  int* err;
+};
+
+// ------------------------------------------------------------------ preprocess
+__global__ void preprocess_kernel(Args a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const long long R = (long long)a.S * a.H;
+  if (warp >= (long long)a.B * a.Rpad) return;
+  const int b = warp / a.Rpad, r = warp % a.Rpad;
+  float d = 0.0f, l2 = 0.0f;
+  if (r < R) {
+    const __nv_bfloat16* op = a.o + ((long long)b * R + r) * a.D;
+    const __nv_bfloat16* gp = a.dout + ((long long)b * R + r) * a.D;
+    for (int i = lane; i < a.D; i += 32) d = fmaf(__bfloat162float(op[i]), __bfloat162float(gp[i]), d);
+    for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    l2 = a.lse[(long long)b * R + r] * LOG2E;
+  }
+  if (lane == 0) {
+    a.delta[(long long)b * a.Rpad + r] = d;
+    a.lse2[(long long)b * a.Rpad + r] = l2;
+  }
+}
+
+// ------------------------------------------------------------------ dkv (key owner)
+template <int D, bool SEP_V>
+struct KvCfg {
+  static constexpr int DB = D / 64;
+  static constexpr int T_BYTES = 128 * D * 2;  // one 128-row tile of Q, dO, K or V
+  static constexpr int STAGE = 2 * T_BYTES + 1024;  // Q, dO, lse2[128], delta[128]
+  static constexpr int TILE_BYTES = (SEP_V ? 2 : 1) * T_BYTES + 2 * STAGE;
+  static constexpr int SMEM = TILE_BYTES + 256;
+  static constexpr int C_DK = 0, C_DV = D, C_S = 2 * D, C_DP = 2 * D + 128;
+  static_assert(C_DP + 128 <= 512, "TMEM");
+  static_assert(SMEM <= 232448, "smem");
+};
+
+enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FULL, PT_FULL, O_DONE, ACC_EMPTY,
+             KV_NBAR };
+
+struct KvItem {
+  int b, kt, k0, qt0, nq;
+};
+
+__device__ __forceinline__ KvItem kv_item(const Args& a, int it, int n_kt) {
+  KvItem m;
+  m.b = it % a.B;
+  m.kt = it / a.B;
+  m.k0 = m.kt * 128;
+  const int k1 = min(a.S - 1, m.k0 + 127);
+  const int tmax = min(a.S - 1, k1 + a.window - 1);
+  const long long r_lo = (long long)m.k0 * a.H, r_hi = (long long)(tmax + 1) * a.H - 1;
+  m.qt0 = int(r_lo / 128);
+  m.nq = int(r_hi / 128) - m.qt0 + 1;
+  (void)n_kt;
+  return m;
+}
+
+template <int D, bool SEP_V>
+__global__ void __launch_bounds__(256, 1)
+    dkv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+               const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Args a) {
+  using C = KvCfg<D, SEP_V>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* ks = smem;
+  uint8_t* vs = SEP_V ? smem + C::T_BYTES : smem;
+  uint8_t* st0 = smem + (SEP_V ? 2 : 1) * C::T_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 8 * KV_NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::TILE_BYTES + 8 * KV_NBAR + 4);
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(a.err, MZB_ERR_ALIGN);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < KV_NBAR; ++i) tc::mbar_init(&bars[i], (i == PT_FULL || i == ACC_EMPTY) ? 4 : 1);
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int n_kt = (a.S + 127) / 128;
+  const int items = a.B * n_kt;
+  auto stage = [&](int s) { return st0 + s * C::STAGE; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0, ii = 0;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const KvItem m = kv_item(a, it, n_kt);
+        if (!tc::mbar_wait(&bars[KV_EMPTY], (ii & 1) ^ 1, a.err, 401)) { *abort_flag = 1; break; }
+        tc::mbar_expect_tx(&bars[KV_FULL], (SEP_V ? 2 : 1) * C::T_BYTES);
+        for (int cb = 0; cb < C::DB; ++cb) {
+          tc::tma_load_3d(ks + cb * 128 * 128, &tk, &bars[KV_FULL], cb * 64, m.k0, m.b);
+          if (SEP_V) tc::tma_load_3d(vs + cb * 128 * 128, &tv, &bars[KV_FULL], cb * 64, m.k0, m.b);
+        }
+        bool ok = true;
+        for (int i = 0; i < m.nq; ++i, ++g) {
+          const int s = g & 1, ph = (g >> 1) & 1;
+          if (!tc::mbar_wait(&bars[QD_EMPTY + s], ph ^ 1, a.err, 402)) { ok = false; break; }
+          uint8_t* sp = stage(s);
+          const int qt = m.qt0 + i;
+          tc::mbar_expect_tx(&bars[QD_FULL + s], 2 * C::T_BYTES + 1024);
+          for (int cb = 0; cb < C::DB; ++cb) {
+            tc::tma_load_3d(sp + cb * 128 * 128, &tq, &bars[QD_FULL + s], cb * 64, qt * 128, m.b);
+            tc::tma_load_3d(sp + C::T_BYTES + cb * 128 * 128, &tdo, &bars[QD_FULL + s], cb * 64, qt * 128, m.b);
+          }
+          tc::bulk_load(sp + 2 * C::T_BYTES, a.lse2 + (long long)m.b * a.Rpad + qt * 128, 512, &bars[QD_FULL + s]);
+          tc::bulk_load(sp + 2 * C::T_BYTES + 512, a.delta + (long long)m.b * a.Rpad + qt * 128, 512,
+                        &bars[QD_FULL + s]);
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::make_idesc(128, 128, 1, 1);
+      const uint32_t idesc_acc = tc::make_idesc(128, D, 1, 1, false, true);
+      const uint32_t k_base = smem_u32(ks), v_base = smem_u32(vs);
+      int g = 0, ii = 0;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const KvItem m = kv_item(a, it, n_kt);
+        if (!tc::mbar_wait(&bars[KV_FULL], ii & 1, a.err, 410)) { *abort_flag = 1; break; }
+        bool ok = true;
+        for (int i = 0; i < m.nq; ++i, ++g) {
+          const int s = g & 1, ph = (g >> 1) & 1;
+          if (!tc::mbar_wait(&bars[QD_FULL + s], ph, a.err, 411)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int cb = kk >> 2, off = (kk & 3) * 32;
+            tc::mma_ss<0>(tmem + C::C_S, tc::make_sdesc<128>(k_base + cb * 16384 + off, 16, 1024),
+                          tc::make_sdesc<128>(q_base + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int cb = kk >> 2, off = (kk & 3) * 32;
+            tc::mma_ss<0>(tmem + C::C_DP, tc::make_sdesc<128>(v_base + cb * 16384 + off, 16, 1024),
+                          tc::make_sdesc<128>(do_base + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+          }
+          tc::mma_commit(&bars[S_FULL]);
+          if (i == 0 && !tc::mbar_wait(&bars[ACC_EMPTY], (ii & 1) ^ 1, a.err, 412)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[PT_FULL], g & 1, a.err, 413)) { ok = false; break; }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {  // 128 query rows, 16 per step
+            const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
+            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + kk * 8,
+                       tc::make_sdesc<128>(do_base + kk * 2048, 16384, 1024), idesc_acc, acc);
+            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8,
+                       tc::make_sdesc<128>(q_base + kk * 2048, 16384, 1024), idesc_acc, acc);
+          }
+          tc::mma_commit(&bars[QD_EMPTY + s]);
+          if (i == m.nq - 1) {
+            tc::mma_commit(&bars[O_DONE]);
+            tc::mma_commit(&bars[KV_EMPTY]);
+          }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp >= 4) {
+    const int sw = warp - 4, row = sw * 32 + lane;  // TMEM lane = key within the tile
+    const float sl = a.scale_log2;
+    int g = 0, ii = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+      const KvItem m = kv_item(a, it, n_kt);
+      const int j = m.k0 + row;
+      bool ok = true;
+      for (int i = 0; i < m.nq; ++i, ++g) {
+        const int s = g & 1;
+        if (!tc::mbar_wait(&bars[S_FULL], g & 1, a.err, 420)) { ok = false; break; }
+        tc::fence_after_sync();
+        const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
+        const float* dl = l2 + 128;
+        const long long r0 = (long long)(m.qt0 + i) * 128;
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t sv[32], dv[32];
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
+          tc::tmem_wait_ld();
+          uint32_t pp[16], dd[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            float p2[2], d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int c = c0 + 2 * q + e;
+              const long long r = r0 + c;
+              const int t = int(r / a.H);
+              const bool valid = j < a.S && t < a.S && j <= t && j > t - a.window;
+              const float p = valid ? exp2f(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2[c])) : 0.0f;
+              p2[e] = p;
+              d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl[c]);
+            }
+            pp[q] = pack_bf16(p2[0], p2[1]);
+            dd[q] = pack_bf16(d2[0], d2[1]);
+          }
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), pp);
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_DP + c0 / 2), dd);
+        }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[PT_FULL]);
+      }
+      if (!ok) { *abort_flag = 1; break; }
+      if (!tc::mbar_wait(&bars[O_DONE], ii & 1, a.err, 421)) { *abort_flag = 1; break; }
+      tc::fence_after_sync();
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t kv[32], vv[32];
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DK + c0), kv);
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DV + c0), vv);
+        tc::tmem_wait_ld();
+        if (j < a.S) {
+          uint4* dst = reinterpret_cast<uint4*>(a.dk + ((long long)m.b * a.S + j) * D + c0);
+          uint4* dstv = SEP_V ? reinterpret_cast<uint4*>(a.dv + ((long long)m.b * a.S + j) * D + c0) : nullptr;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4], wv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int x = 8 * q + 2 * e;
+              float k0 = __uint_as_float(kv[x]) * a.scale, k1 = __uint_as_float(kv[x + 1]) * a.scale;
+              const float v0 = __uint_as_float(vv[x]), v1 = __uint_as_float(vv[x + 1]);
+              if (!SEP_V) { k0 += v0; k1 += v1; }
+              w[e] = pack_bf16(k0, k1);
+              wv[e] = pack_bf16(v0, v1);
+            }
+            dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
+            if (SEP_V) dstv[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[ACC_EMPTY]);
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_free(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ dq (query owner)
+template <int D, bool SEP_V>
+struct QCfg {
+  static constexpr int DB = D / 64;
+  static constexpr int T_BYTES = 128 * D * 2;
+  static constexpr int KV_STAGE = (SEP_V ? 2 : 1) * T_BYTES;
+  static constexpr int STAGES = 2;
+  static constexpr int P_BYTES = 128 * 128 * 2;  // dS / P tile [rows][128 keys] bf16 (gathered tiles)
+  static constexpr int NP = SEP_V ? 0 : 2;       // dS and P copies (csa2 only)
+  static constexpr int TILE_BYTES = 2 * T_BYTES + STAGES * KV_STAGE + NP * P_BYTES;
+  static constexpr int SMEM = TILE_BYTES + 512;
+  static constexpr int C_DQ = 0, C_S = D, C_DP = D + 128, C_DM = D + 256;
+  static_assert(C_DP + 128 <= 512 && (SEP_V || C_DM + D <= 512), "TMEM");
+  static_assert(SMEM <= 232448, "smem");
+};
+
+enum QBar { Q_FULL = 0, Q_EMPTY, S_FULL_Q, DS_FULL, DM_FULL, DM_EMPTY, QO_DONE, QACC_EMPTY, KVW_FULL,
+            KVG_FULL = KVW_FULL + 2, KVQ_EMPTY = KVG_FULL + 2, Q_NBAR = KVQ_EMPTY + 2 };
+
+struct QItem {
+  int b, qt, t0, t1, kt0, n_win, n_gat, gtiles, tq_valid;
+};
+
+__device__ __forceinline__ QItem q_item(const Args& a, int it, int n_qt) {
+  QItem m;
+  m.b = it % a.B;
+  m.qt = n_qt - 1 - it / a.B;
+  const int tq = 128 / a.H;
+  m.t0 = m.qt * tq;
+  m.t1 = min(a.S, m.t0 + tq) - 1;
+  m.tq_valid = m.t1 - m.t0 + 1;
+  const int lo = max(0, m.t0 - a.window + 1);
+  m.kt0 = lo / 128;
+  m.n_win = m.t1 / 128 - m.kt0 + 1;
+  m.gtiles = (a.main_kv && a.topk > 0 && a.G > 0) ? (a.topk + 127) / 128 : 0;
+  m.n_gat = m.gtiles * m.tq_valid;
+  return m;
+}
+
+template <int D, bool SEP_V>
+__global__ void __launch_bounds__(384, 1)
+    dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+              const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Args a) {
+  using C = QCfg<D, SEP_V>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* qs = smem;
+  uint8_t* dos = smem + C::T_BYTES;
+  uint8_t* kvs = smem + 2 * C::T_BYTES;
+  uint8_t* dss = kvs + C::STAGES * C::KV_STAGE;  // csa2: dS tile then P tile
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 8 * Q_NBAR);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::TILE_BYTES + 8 * Q_NBAR + 4);
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicExch(a.err, MZB_ERR_ALIGN);
+    return;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < Q_NBAR; ++i) {
+      uint32_t c = 1;
+      if (i == DS_FULL || i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1) c = 4;
+      tc::mbar_init(&bars[i], c);
+    }
+    *abort_flag = 0;
+    tc::fence_barrier_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, 512);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int tqn = 128 / a.H;
+  const int n_qt = (a.S + tqn - 1) / tqn;
+  const int items = a.B * n_qt;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0, ii = 0;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const QItem m = q_item(a, it, n_qt);
+        if (!tc::mbar_wait(&bars[Q_EMPTY], (ii & 1) ^ 1, a.err, 501)) { *abort_flag = 1; break; }
+        tc::mbar_expect_tx(&bars[Q_FULL], 2 * C::T_BYTES);
+        for (int cb = 0; cb < C::DB; ++cb) {
+          tc::tma_load_3d(qs + cb * 16384, &tq, &bars[Q_FULL], cb * 64, m.qt * 128, m.b);
+          tc::tma_load_3d(dos + cb * 16384, &tdo, &bars[Q_FULL], cb * 64, m.qt * 128, m.b);
+        }
+        bool ok = true;
+        for (int j = 0; j < m.n_win + m.n_gat; ++j, ++g) {
+          const int st = g & 1, ph = (g >> 1) & 1;
+          if (j >= m.n_win) continue;
+          if (!tc::mbar_wait(&bars[KVQ_EMPTY + st], ph ^ 1, a.err, 502)) { ok = false; break; }
+          uint8_t* kt = kvs + st * C::KV_STAGE;
+          tc::mbar_expect_tx(&bars[KVW_FULL + st], C::KV_STAGE);
+          for (int cb = 0; cb < C::DB; ++cb) {
+            tc::tma_load_3d(kt + cb * 16384, &tk, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * 128, m.b);
+            if (SEP_V)
+              tc::tma_load_3d(kt + C::T_BYTES + cb * 16384, &tv, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * 128,
+                              m.b);
+          }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc_s = tc::make_idesc(128, 128, 1, 1);
+      const uint32_t idesc_dq = tc::make_idesc(128, D, 1, 1, false, true);
+      const uint32_t idesc_dm = tc::make_idesc(128, D, 1, 1, true, true);
+      const uint32_t q_base = smem_u32(qs), do_base = smem_u32(dos), kv_base = smem_u32(kvs);
+      const uint32_t ds_base = smem_u32(dss), p_base = ds_base + C::P_BYTES;
+      int g = 0, ii = 0, gm = 0;
+      int uses_w[2] = {0, 0}, uses_g[2] = {0, 0};
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+        const QItem m = q_item(a, it, n_qt);
+        const int n = m.n_win + m.n_gat;
+        if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 510)) { *abort_flag = 1; break; }
+        bool ok = true;
+        for (int j = 0; j < n; ++j, ++g) {
+          const int st = g & 1;
+          const bool win = j < m.n_win;
+          const int par = win ? (uses_w[st]++ & 1) : (uses_g[st]++ & 1);
+          if (!tc::mbar_wait(&bars[(win ? KVW_FULL : KVG_FULL) + st], par, a.err, 511)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint32_t kb = kv_base + st * C::KV_STAGE, vb = kb + (SEP_V ? C::T_BYTES : 0);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int cb = kk >> 2, off = (kk & 3) * 32;
+            tc::mma_ss<0>(tmem + C::C_S, tc::make_sdesc<128>(q_base + cb * 16384 + off, 16, 1024),
+                          tc::make_sdesc<128>(kb + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int cb = kk >> 2, off = (kk & 3) * 32;
+            tc::mma_ss<0>(tmem + C::C_DP, tc::make_sdesc<128>(do_base + cb * 16384 + off, 16, 1024),
+                          tc::make_sdesc<128>(vb + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+          }
+          tc::mma_commit(&bars[S_FULL_Q]);
+          if (j == 0 && !tc::mbar_wait(&bars[QACC_EMPTY], (ii & 1) ^ 1, a.err, 512)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[DS_FULL], g & 1, a.err, 513)) { ok = false; break; }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per step: dQ += dS K
+            tc::mma_ts(tmem + C::C_DQ, tmem + C::C_S + kk * 8, tc::make_sdesc<128>(kb + kk * 2048, 16384, 1024),
+                       idesc_dq, (j == 0 && kk == 0) ? 0u : 1u);
+          if (!win) {
+            if (!tc::mbar_wait(&bars[DM_EMPTY], (gm & 1) ^ 1, a.err, 514)) { ok = false; break; }
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {  // 128 query rows: dM = dS^T Q + P^T dO
+              tc::mma_ss<0>(tmem + C::C_DM, tc::make_sdesc<128>(ds_base + kk * 2048, 16384, 1024),
+                            tc::make_sdesc<128>(q_base + kk * 2048, 16384, 1024), idesc_dm, kk > 0);
+              tc::mma_ss<0>(tmem + C::C_DM, tc::make_sdesc<128>(p_base + kk * 2048, 16384, 1024),
+                            tc::make_sdesc<128>(do_base + kk * 2048, 16384, 1024), idesc_dm, 1u);
+            }
+            tc::mma_commit(&bars[DM_FULL]);
+            ++gm;
+          }
+          tc::mma_commit(&bars[KVQ_EMPTY + st]);
+          if (j == n - 1) {
+            tc::mma_commit(&bars[Q_EMPTY]);
+            tc::mma_commit(&bars[QO_DONE]);
+          }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    const int sw = warp - 4, r = sw * 32 + lane;
+    const float sl = a.scale_log2;
+    int g = 0, ii = 0, gm = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+      const QItem m = q_item(a, it, n_qt);
+      const int n = m.n_win + m.n_gat;
+      const int tr = r / a.H, t = m.t0 + tr;
+      const bool row_ok = t < a.S;
+      const long long grow = (long long)m.qt * 128 + r;
+      const float l2 = a.lse2[(long long)m.b * a.Rpad + grow];
+      const float dl = a.delta[(long long)m.b * a.Rpad + grow];
+      bool ok = true;
+      for (int j = 0; j < n; ++j, ++g) {
+        const bool win = j < m.n_win;
+        int k0 = 0, wlo = 0, whi = -1, gtok = -1, e0 = 0;
+        uint32_t gmask[4] = {0, 0, 0, 0};
+        if (win) {
+          k0 = (m.kt0 + j) * 128;
+          wlo = max(0, t - a.window + 1) - k0;
+          whi = t - k0;
+        } else {
+          const int gj = j - m.n_win;
+          gtok = gj / m.gtiles;
+          e0 = (gj % m.gtiles) * 128;
+          const int32_t* irow = a.idx + ((long long)m.b * a.S + (m.t0 + gtok)) * a.topk;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int e = e0 + w * 32 + lane;
+            bool v = false;
+            if (e < a.topk) {
+              const int gi = irow[e];
+              v = gi >= 0 && gi < a.G;
+            }
+            gmask[w] = __ballot_sync(0xffffffffu, v);
+          }
+        }
+        if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
+        tc::fence_after_sync();
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 32) {
+          uint32_t sv[32], dv[32];
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
+          tc::tmem_wait_ld();
+          uint32_t dd[16], ds[16], pp[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            float d2[2], p2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int c = c0 + 2 * q + e;
+              const bool valid = row_ok && (win ? (c >= wlo && c <= whi) : (tr == gtok && ((gmask[c >> 5] >> (c & 31)) & 1u)));
+              const float p = valid ? exp2f(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2)) : 0.0f;
+              p2[e] = p;
+              d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl);
+            }
+            dd[q] = pack_bf16(d2[0], d2[1]);
+            ds[q] = pack_bf16(d2[0] * a.scale, d2[1] * a.scale);  // dK carries the softmax scale
+            pp[q] = pack_bf16(p2[0], p2[1]);
+          }
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), dd);
+          if (!win) {  // keep scale*dS and P in smem for the gathered-row gradient
+            uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
+            uint8_t* pr = dsr + C::P_BYTES;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int ch = ((c0 & 63) >> 3) + q;
+              st_shared16(dsr + ((ch ^ (r & 7)) * 16), make_uint4(ds[4 * q], ds[4 * q + 1], ds[4 * q + 2], ds[4 * q + 3]));
+              st_shared16(pr + ((ch ^ (r & 7)) * 16), make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]));
+            }
+          }
+        }
+        tc::tmem_wait_st();
+        if (!win) tc::fence_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[DS_FULL]);
+        if (!win) {
+          // dM rows (thread = key slot of the tile) -> fp32 atomics into dmain
+          if (!tc::mbar_wait(&bars[DM_FULL], gm & 1, a.err, 521)) { ok = false; break; }
+          tc::fence_after_sync();
+          const int e = e0 + r;
+          int gi = -1;
+          if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
+          const bool v = gi >= 0 && gi < a.G;
+          float* dst = a.dmain + ((long long)m.b * a.G + (v ? gi : 0)) * D;
+#pragma unroll 1
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t mv[32];
+            tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DM + c0), mv);
+            tc::tmem_wait_ld();
+            if (v) {
+#pragma unroll
+              for (int q = 0; q < 32; ++q) atomicAdd(dst + c0 + q, __uint_as_float(mv[q]));
+            }
+          }
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bars[DM_EMPTY]);
+          ++gm;
+        }
+      }
+      if (!ok) { *abort_flag = 1; break; }
+      if (!tc::mbar_wait(&bars[QO_DONE], ii & 1, a.err, 522)) { *abort_flag = 1; break; }
+      tc::fence_after_sync();
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t qv[32];
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DQ + c0), qv);
+        tc::tmem_wait_ld();
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(a.dq + ((long long)m.b * a.S * a.H + grow) * D + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16(__uint_as_float(qv[8 * q]) * a.scale, __uint_as_float(qv[8 * q + 1]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 2]) * a.scale, __uint_as_float(qv[8 * q + 3]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 4]) * a.scale, __uint_as_float(qv[8 * q + 5]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 6]) * a.scale, __uint_as_float(qv[8 * q + 7]) * a.scale));
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[QACC_EMPTY]);
+    }
+  } else if (warp >= 8) {
+    // gathered-row producers (csa2): main_kv rows -> the K stage (K == V)
+    const int t = threadIdx.x - 256, row = t;  // 128 rows, one per thread
+    int g = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+      const QItem m = q_item(a, it, n_qt);
+      const int n = m.n_win + m.n_gat;
+      bool ok = true;
+      for (int j = 0; j < n; ++j, ++g) {
+        if (j < m.n_win) continue;
+        const int st = g & 1, ph = (g >> 1) & 1;
+        const int gj = j - m.n_win, gtok = gj / m.gtiles, e = (gj % m.gtiles) * 128 + row;
+        int gi = -1;
+        if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
+        const bool v = gi >= 0 && gi < a.G;
+        const uint4* src = reinterpret_cast<const uint4*>(a.main_kv + ((long long)m.b * a.G + (v ? gi : 0)) * D);
+        uint4 raw[D / 8];
+#pragma unroll
+        for (int q = 0; q < D / 8; ++q) raw[q] = v ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
+        if (!tc::mbar_wait(&bars[KVQ_EMPTY + st], ph ^ 1, a.err, 530)) { ok = false; break; }
+        uint8_t* kt = kvs + st * C::KV_STAGE;
+#pragma unroll
+        for (int q = 0; q < D / 8; ++q)
+          st_shared16(kt + (q >> 3) * 16384 + row * 128 + (((q & 7) ^ (row & 7)) * 16), raw[q]);
+        tc::fence_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[KVG_FULL + st]);
+      }
+      if (!ok) { *abort_flag = 1; break; }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_free(tmem, 512);
+  }
+}
+
+template <int D, bool SEP_V>
+int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStream_t st) {
+  CUtensorMap tq, tdo, tk, tv;
+  const uint32_t box[3] = {64, 128, 1};
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.S) * a.H, uint64_t(a.B)};
+    const uint64_t str[2] = {uint64_t(D) * 2, uint64_t(a.S) * a.H * D * 2};
+    if (int r = encode_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+    if (int r = encode_tmap(&tdo, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.dout, dims, str, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+  }
+  {
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.S), uint64_t(a.B)};
+    const uint64_t str[2] = {uint64_t(D) * 2, uint64_t(a.S) * D * 2};
+    if (int r = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, kv, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+    if (int r = encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, SEP_V ? v : kv, dims, str, box,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+  }
+  const long long rows = (long long)a.B * a.Rpad;
+  preprocess_kernel<<<unsigned((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  if (int r = launch_status("attn_bwd_preprocess")) return r;
+
+  auto kkv = dkv_kernel<D, SEP_V>;
+  if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, KvCfg<D, SEP_V>::SMEM) != cudaSuccess)
+    return launch_status("attn_bwd_dkv(smem attr)");
+  const int kv_items = a.B * ((a.S + 127) / 128);
+  kkv<<<kv_items < num_sms() ? kv_items : num_sms(), 256, KvCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
+  if (int r = launch_status("attn_bwd_dkv")) return r;
+
+  auto kq = dq_kernel<D, SEP_V>;
+  if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<D, SEP_V>::SMEM) != cudaSuccess)
+    return launch_status("attn_bwd_dq(smem attr)");
+  const int tqn = 128 / a.H;
+  const int q_items = a.B * ((a.S + tqn - 1) / tqn);
+  kq<<<q_items < num_sms() ? q_items : num_sms(), 384, QCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
+  return launch_status("attn_bwd_dq");
+}
+
+}  // namespace attnb
+}  // namespace mzb
+
+using namespace mzb;
+
+extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
+                            const void* o, const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                            float* dmain_f32, float* delta_ws, float* lse2_ws, int64_t B, int64_t S, int H, int D,
+                            int window, int64_t G, int topk, float softmax_scale, int* err, void* stream) {
+  MZB_REQUIRE(B >= 1 && S >= 1 && window >= 1 && topk >= 0 && G >= 0, MZB_ERR_SHAPE, "attn_bwd: bad sizes");
+  MZB_REQUIRE(H >= 1 && H <= 128 && 128 % H == 0, MZB_ERR_UNSUPPORTED, "attn_bwd: heads must divide 128, got %d",
+              H);
+  MZB_REQUIRE(D == 64 || D == 128, MZB_ERR_UNSUPPORTED, "attn_bwd: head dim %d not built (64, 128)", D);
+  const bool sep = v != nullptr && v != kv;
+  const bool gathered = main_kv != nullptr && topk > 0 && G > 0;
+  MZB_REQUIRE(!(sep && gathered), MZB_ERR_UNSUPPORTED, "attn_bwd: a separate V only for the window-only kernel");
+  MZB_REQUIRE(!gathered || dmain_f32 != nullptr, MZB_ERR_SHAPE, "attn_bwd: gathered rows need a dmain accumulator");
+  MZB_REQUIRE(err && delta_ws && lse2_ws, MZB_ERR_SHAPE, "attn_bwd: needs err and workspaces");
+  attnb::Args a{};
+  a.o = static_cast<const __nv_bfloat16*>(o);
+  a.dout = static_cast<const __nv_bfloat16*>(dout);
+  a.lse = lse;
+  a.delta = delta_ws;
+  a.lse2 = lse2_ws;
+  a.main_kv = gathered ? static_cast<const __nv_bfloat16*>(main_kv) : nullptr;
+  a.idx = gathered ? indices : nullptr;
+  a.dq = static_cast<__nv_bfloat16*>(dq);
+  a.dk = static_cast<__nv_bfloat16*>(dk);
+  a.dv = sep ? static_cast<__nv_bfloat16*>(dv) : nullptr;
+  a.dmain = gathered ? dmain_f32 : nullptr;
+  a.B = int(B); a.S = int(S); a.H = H; a.D = D; a.window = window; a.G = gathered ? int(G) : 0;
+  a.topk = gathered ? topk : 0;
+  a.Rpad = int(((S * H + 127) / 128) * 128);
+  a.scale = softmax_scale;
+  a.scale_log2 = softmax_scale * attnb::LOG2E;
+  a.err = err;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 64) return sep ? attnb::launch<64, true>(q, kv, v, a, st) : attnb::launch<64, false>(q, kv, v, a, st);
+  return sep ? attnb::launch<128, true>(q, kv, v, a, st) : attnb::launch<128, false>(q, kv, v, a, st);
+}

@@ -158,3 +158,80 @@ def test_csa2_feature_off_equals_swa_bitwise(cuda):
     empty = main[:, :0]
     got = csa2_attn.fwd(q, kv, empty, idx, window=128, compress_ratio=4, sinks=sk)
     assert torch.equal(got[0], ref[0]) and torch.equal(got[1], ref[1])
+
+
+# ----------------------------------------------------------------------------- GPU: backward
+
+def _check_grad(got, ref, what):
+    got = _np(got)
+    err = np.abs(got - ref)
+    tol = ATOL + RTOL * np.abs(ref)
+    print(f"{what}: max|d-ref|={err.max():.3e} (ref max {np.abs(ref).max():.2e})")
+    assert np.all(err <= tol), f"{what}: worst excess {(err - tol).max():.3e}"
+
+
+def _do(torch, dev, shape, seed):
+    rng = np.random.default_rng(seed)
+    return torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(torch.bfloat16).to(dev)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,D,window", [(64, 128, 100), (16, 64, 37), (4, 128, 300)])
+def test_swa_bwd(cuda, H, D, window):
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, _, _, _, sk = _inputs(torch, cuda, 2, 200, H, D, seed=H + D, sinks=True)
+    o, lse = swa_attn.fwd(q, kv, window=window, sinks=sk)
+    do = _do(torch, cuda, q.shape, 7)
+    dq, dkv, dsinks = swa_attn.bwd(q, kv, o, lse, do, window=window, sinks=sk)
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=window, sinks=_np(sk))
+    _check_grad(dq, ref["dq"], f"swa dq H{H} D{D}")
+    _check_grad(dkv[:, :, 0], ref["dkv"], f"swa dkv H{H} D{D}")
+    _check_grad(dsinks, ref["dsinks"], f"swa dsinks H{H} D{D}")
+
+
+@pytest.mark.gpu
+def test_swa_bwd_separate_v(cuda):
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, v, _, _, _ = _inputs(torch, cuda, 2, 256, 64, 128, seed=11, sep_v=True)
+    o, lse = swa_attn.fwd(q, kv, window=200, v=v)
+    do = _do(torch, cuda, q.shape, 8)
+    dq, dk, _, dv = swa_attn.bwd(q, kv, o, lse, do, window=200, v=v)
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=200, v=_np(v)[:, :, 0])
+    _check_grad(dq, ref["dq"], "swa K!=V dq")
+    _check_grad(dk[:, :, 0], ref["dk"], "swa K!=V dk")
+    _check_grad(dv[:, :, 0], ref["dv"], "swa K!=V dv")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48)])
+def test_csa2_bwd(cuda, H, D, G, topk):
+    import torch
+    from mzoo_b200 import csa2_attn
+    q, kv, _, main, idx, sk = _inputs(torch, cuda, 2, 160, H, D, G=G, topk=topk, seed=G, dup=True, holes=True,
+                                      sinks=True)
+    o, lse = csa2_attn.fwd(q, kv, main, idx, window=64, compress_ratio=4, sinks=sk)
+    do = _do(torch, cuda, q.shape, 9)
+    dq, dkv, dmain, dsinks = csa2_attn.bwd(q, kv, main, idx, o, lse, do, window=64, compress_ratio=4, sinks=sk)
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=64, main_kv=_np(main)[:, :, 0],
+                       indices=idx.cpu().numpy(), sinks=_np(sk))
+    _check_grad(dq, ref["dq"], f"csa2 dq H{H}")
+    _check_grad(dkv[:, :, 0], ref["dkv"], f"csa2 dkv H{H}")
+    _check_grad(dmain[:, :, 0], ref["dmain"], f"csa2 dmain H{H}")
+    _check_grad(dsinks, ref["dsinks"], f"csa2 dsinks H{H}")
+
+
+@pytest.mark.gpu
+def test_swa_attn_autograd(cuda):
+    """swa_attn/attn_test.py: gradients through the autograd wrapper."""
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, _, _, _, _ = _inputs(torch, cuda, 1, 130, 32, 128, seed=12)
+    q.requires_grad_()
+    kv.requires_grad_()
+    do = _do(torch, cuda, q.shape, 10)
+    swa_attn.attn(q, kv, window=50).backward(do)
+    ref = A.attend_bwd(_np(q.detach()), _np(kv.detach())[:, :, 0], _np(do), window=50)
+    _check_grad(q.grad, ref["dq"], "autograd dq")
+    _check_grad(kv.grad[:, :, 0], ref["dkv"], "autograd dkv")
