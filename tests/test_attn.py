@@ -162,12 +162,47 @@ def test_csa2_feature_off_equals_swa_bitwise(cuda):
 
 # ----------------------------------------------------------------------------- GPU: backward
 
-def _check_grad(got, ref, what):
+def _check_grad(got, ref, what, torch_bf16=None):
+    """Gradients: max-abs error within 2e-2 + 1e-2 * max|ref| (taken
+    relative to the tensor's scale: a bf16 backward rounds P and dS to 8 bits, so keys fed by
+    near-one probabilities carry errors near 1e-2 of the tensor maximum), and -- the reference's
+    own acceptance criterion, ``dense_attn/ref.py:65`` -- at most 2x torch-bf16's error."""
     got = _np(got)
-    err = np.abs(got - ref)
-    tol = ATOL + RTOL * np.abs(ref)
-    print(f"{what}: max|d-ref|={err.max():.3e} (ref max {np.abs(ref).max():.2e})")
-    assert np.all(err <= tol), f"{what}: worst excess {(err - tol).max():.3e}"
+    err = np.abs(got - ref).max()
+    scale = np.abs(ref).max()
+    msg = f"{what}: max|d-ref|={err:.3e} (ref max {scale:.2e})"
+    if torch_bf16 is not None:
+        terr = np.abs(_np(torch_bf16) - ref).max()
+        msg += f" torch-bf16 err {terr:.3e} ratio {err / max(terr, 1e-30):.2f}"
+        assert err <= 2.0 * terr + 1e-5, msg
+    print(msg)
+    assert err <= ATOL + RTOL * scale, msg
+
+
+def _torch_bf16_grads(torch, q, kv, do, window, sinks=None, v=None):
+    """golden(dtype=bf16)-style reference: bf16 matmuls, fp32 softmax, bf16 probabilities,
+    autograd for dq / dk / dv (golden_ref.py:83-100 with mm_dtype = bf16)."""
+    B, S, H, D = q.shape
+    qq = q.detach().clone().requires_grad_()
+    kk = kv.detach().clone().requires_grad_()
+    vv = (v if v is not None else kv).detach().clone().requires_grad_()
+    qt = qq.transpose(1, 2)
+    kt = kk.transpose(1, 2)
+    vt = vv.transpose(1, 2)
+    logits = torch.matmul(qt, kt.transpose(-1, -2)).float() * D**-0.5
+    i = torch.arange(S, device=q.device)
+    vis = (i[None, :] <= i[:, None]) & (i[None, :] > i[:, None] - window)
+    logits = logits.masked_fill(~vis, float("-inf"))
+    if sinks is not None:
+        logits = torch.cat([logits, sinks.float().view(1, H, 1, 1).expand(B, H, S, 1)], -1)
+    probs = torch.softmax(logits, -1)
+    if sinks is not None:
+        probs = probs[..., :-1]
+    o = torch.matmul(probs.to(torch.bfloat16), vt).transpose(1, 2)
+    o.backward(do)
+    if v is None:  # K == V: the latent's gradient is dK + dV
+        return qq.grad, (kk.grad.float() + vv.grad.float()), None
+    return qq.grad, kk.grad, vv.grad
 
 
 def _do(torch, dev, shape, seed):
@@ -185,8 +220,9 @@ def test_swa_bwd(cuda, H, D, window):
     do = _do(torch, cuda, q.shape, 7)
     dq, dkv, dsinks = swa_attn.bwd(q, kv, o, lse, do, window=window, sinks=sk)
     ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=window, sinks=_np(sk))
-    _check_grad(dq, ref["dq"], f"swa dq H{H} D{D}")
-    _check_grad(dkv[:, :, 0], ref["dkv"], f"swa dkv H{H} D{D}")
+    tq, tk, _ = _torch_bf16_grads(torch, q, kv, do, window, sinks=sk)
+    _check_grad(dq, ref["dq"], f"swa dq H{H} D{D}", tq)
+    _check_grad(dkv[:, :, 0], ref["dkv"], f"swa dkv H{H} D{D}", tk[:, :, 0])
     _check_grad(dsinks, ref["dsinks"], f"swa dsinks H{H} D{D}")
 
 
@@ -199,9 +235,10 @@ def test_swa_bwd_separate_v(cuda):
     do = _do(torch, cuda, q.shape, 8)
     dq, dk, _, dv = swa_attn.bwd(q, kv, o, lse, do, window=200, v=v)
     ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=200, v=_np(v)[:, :, 0])
-    _check_grad(dq, ref["dq"], "swa K!=V dq")
-    _check_grad(dk[:, :, 0], ref["dk"], "swa K!=V dk")
-    _check_grad(dv[:, :, 0], ref["dv"], "swa K!=V dv")
+    tq, tk, tv = _torch_bf16_grads(torch, q, kv, do, 200, v=v)
+    _check_grad(dq, ref["dq"], "swa K!=V dq", tq)
+    _check_grad(dk[:, :, 0], ref["dk"], "swa K!=V dk", tk[:, :, 0])
+    _check_grad(dv[:, :, 0], ref["dv"], "swa K!=V dv", tv[:, :, 0])
 
 
 @pytest.mark.gpu
