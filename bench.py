@@ -426,7 +426,167 @@ def reference_prefill(args, rank, world) -> dict:
                        "window": C3["window"]},
             "cpu_baseline": r, "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
-BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill)}
+# ----------------------------------------------------------------------------- SWA train + fake quant (C5)
+
+C5 = dict(B=4, S=8192, H=64, D=128, window=512)
+
+
+def c5_band(cfg=C5) -> int:
+    """Visible (query, key) pairs per (batch, head): sum_t min(t + 1, window)."""
+    return sum(min(t + 1, cfg["window"]) for t in range(cfg["S"]))
+
+
+def c5_flops(cfg=C5) -> tuple:
+    fwd = 4.0 * cfg["B"] * cfg["H"] * cfg["D"] * c5_band(cfg)
+    return fwd, 2.5 * fwd
+
+
+def c5_step(q, k, v, do):
+    """One training step of the path: fake quant (Q, K: OCP MXFP4 block 32; V: FP8 per-128
+    absmax), window attention forward, backward; straight-through gradients."""
+    from mzoo_b200 import quant, swa_attn
+    qf = quant.fake_quant_fp4_block(q, 32, rule="ocp")
+    kf = quant.fake_quant_fp4_block(k, 32, rule="ocp")
+    vf = quant.fake_quant_fp8_block(v, 128, rule="absmax")
+    o, lse = swa_attn.fwd(qf, kf, window=C5["window"], v=vf)
+    dq, dk, _, dv = swa_attn.bwd(qf, kf, o, lse, do, window=C5["window"], v=vf)
+    return dq, dk, dv  # STE: gradients w.r.t. the pre-quant inputs
+
+
+def bench_train(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import quant, swa_attn
+    B, S, H, D, W = (C5[x] for x in ("B", "S", "H", "D", "window"))
+    g = torch.Generator(device=device).manual_seed(10 + rank)
+    q = torch.randn(B, S, H, D, generator=g, device=device, dtype=torch.bfloat16)
+    k = torch.randn(B, S, 1, D, generator=g, device=device, dtype=torch.bfloat16)
+    v = torch.randn(B, S, 1, D, generator=g, device=device, dtype=torch.bfloat16)
+    do = torch.randn(B, S, H, D, generator=g, device=device, dtype=torch.bfloat16)
+    fwd_flops, bwd_flops = c5_flops()
+    timer = Timer(torch, device)
+    step = lambda: c5_step(q, k, v, do)  # noqa: E731
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    t_steps = timer.run(step, args.steps)
+    clocks = sampler.stop()
+    # per-kernel legs for the roofline
+    qf = quant.fake_quant_fp4_block(q, 32, rule="ocp")
+    kf = quant.fake_quant_fp4_block(k, 32, rule="ocp")
+    vf = quant.fake_quant_fp8_block(v, 128, rule="absmax")
+    o, lse = swa_attn.fwd(qf, kf, window=W, v=vf)
+    t_fwd = timer.run(lambda: swa_attn.fwd(qf, kf, window=W, v=vf), args.steps)
+    t_bwd = timer.run(lambda: swa_attn.bwd(qf, kf, o, lse, do, window=W, v=vf), args.steps)
+    t_fq = timer.run(lambda: quant.fake_quant_fp4_block(q, 32, rule="ocp"), args.steps)
+    # end to end from pinned host memory
+    hq, hk, hv, hdo = (x.cpu().pin_memory() for x in (q, k, v, do))
+    dq_, dk_, dv_, ddo = (torch.empty_like(x, device=device) for x in (hq, hk, hv, hdo))
+    hdq, hdk, hdv = (torch.empty_like(x).pin_memory() for x in (hq, hk, hv))
+
+    def e2e():
+        for d, h in ((dq_, hq), (dk_, hk), (dv_, hv), (ddo, hdo)):
+            d.copy_(h, non_blocking=True)
+        gq, gk, gv = c5_step(dq_, dk_, dv_, ddo)
+        hdq.copy_(gq, non_blocking=True)
+        hdk.copy_(gk, non_blocking=True)
+        hdv.copy_(gv, non_blocking=True)
+
+    e2e()
+    t_e2e = timer.run(e2e, max(2, args.steps // 2), flush=False)
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv, hdo))
+    d2h = sum(x.numel() * x.element_size() for x in (hdq, hdk, hdv))
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_fwd, ms_bwd, ms_fq = (sum(t) / len(t) for t in (t_fwd, t_bwd, t_fq))
+    pk = peaks()
+    total = fwd_flops + bwd_flops
+    ach_bwd = bwd_flops / (ms_bwd * 1e-3) / 1e12
+    fq_bytes = 2 * q.numel() * 2
+    out = {
+        "metric": "SWA train fwd+bwd TFLOP/s (fake-quant Q/K MXFP4, V FP8)", "value": total * world / (ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 (fp32 acc)", "data": "synthetic (seeded N(0,1) bf16 inputs and dO)",
+        "config": {"workload": "C5 SWA train + fake quant", "B": B, "S": S, "heads": H, "head_dim": D, "window": W,
+                   "fq": "Q,K OCP MXFP4 block 32; V FP8 absmax per 128; STE", "parallelism": f"x{world} independent",
+                   "l2": "256 MB flush per step"},
+        "e2e": {"value": total * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "tensor", "kernel": "mzb::attnb::dkv_kernel + dq_kernel (backward)",
+                     "achieved": ach_bwd, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": ach_bwd / pk["bf16_tflops"], "peak_note": f"{pk['_source']} bf16 burst",
+                     "algorithmic_flops_per_launch": bwd_flops, "ms_per_launch": ms_bwd, "traffic": None},
+        "legs": {"fwd_ms": ms_fwd, "fwd_tflops": fwd_flops / (ms_fwd * 1e-3) / 1e12, "bwd_ms": ms_bwd,
+                 "fq_q_ms": ms_fq, "fq_q_gbs": fq_bytes / (ms_fq * 1e-3) / 1e9},
+        "gpu_launches": 7 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 16))
+    return out
+
+
+def cpu_train(q, k, v, do, n_tok: int) -> dict:
+    """Oracle port: fake quant + window attention fwd/bwd (fp64 numpy) for n_tok query tokens
+    of batch 0 (all 64 heads, full 512-key window each), as TFLOP/s of their band pairs."""
+    import numpy as np
+    from oracle import quant as Q
+    S, W, D = C5["S"], C5["window"], C5["D"]
+    toks = [int(t) for t in np.linspace(W, S - 1, n_tok)]
+    qs = q[0].float().cpu().numpy()
+    ks = k[0, :, 0].float().cpu().numpy()
+    vs = v[0, :, 0].float().cpu().numpy()
+    dos = do[0].float().cpu().numpy().astype(np.float64)
+    t0 = time.perf_counter()
+    pairs = 0
+    for t in toks:
+        lo = t - W + 1
+        qq = Q.fake_quant_fp4(qs[t], 32, "ocp").astype(np.float64)
+        kk = Q.fake_quant_fp4(ks[lo:t + 1], 32, "ocp").astype(np.float64)
+        vv = Q.fake_quant_fp8(vs[lo:t + 1], 128, "absmax").astype(np.float64)
+        z = qq @ kk.T * D**-0.5
+        p = np.exp(z - z.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        o = p @ vv
+        dp = dos[t] @ vv.T
+        ds = p * (dp - (dos[t] * o).sum(1, keepdims=True))
+        _ = (ds @ kk * D**-0.5, ds.T @ qq * D**-0.5, p.T @ dos[t])
+        pairs += 64 * W
+    dt = time.perf_counter() - t0
+    flops = 4.0 * D * pairs * 3.5
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_tok} query tokens x 64 heads x {W}-key window, numpy fp64 fake quant + fwd + bwd, "
+                      f"{dt:.2f} s, extrapolated by band pairs"}
+
+
+def reference_train(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    g = torch.Generator().manual_seed(10)
+    S = C5["S"]
+    q = torch.randn(1, S, 64, 128, generator=g).to(torch.bfloat16)
+    k = torch.randn(1, S, 1, 128, generator=g).to(torch.bfloat16)
+    v = torch.randn(1, S, 1, 128, generator=g).to(torch.bfloat16)
+    do = torch.randn(1, S, 64, 128, generator=g).to(torch.bfloat16)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 32))
+        if i >= args.warmup:
+            vals.append(r["value"])
+    val = statistics.mean(vals)
+    r["value"] = val
+    return {"metric": "SWA train fwd+bwd TFLOP/s (fake-quant Q/K MXFP4, V FP8)", "value": val, "unit": "TFLOP/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (oracle port)",
+            "data": "synthetic", "config": {"workload": "C5 SWA train + fake quant", **C5},
+            "cpu_baseline": r, "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
+           "train": (bench_train, reference_train)}
 
 
 def main():
@@ -444,6 +604,7 @@ def main():
     if args.small:  # a few hundred MB on the device: safe for multi-pass ncu captures
         C2.update(S=1024, q_offset=4096 - 1024)
         C3.update(S=2048)
+        C5.update(B=1, S=2048)
         args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 
