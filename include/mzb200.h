@@ -120,13 +120,18 @@ MZB_API int mzb_attn_fwd(const void* q, const void* kv, const void* v, const voi
  *   [B, S*H, D]; dk bf16 [B, S, D] (= dK + dV when v is NULL, i.e. K == V); dv bf16 [B, S, D]
  *   (separate v only); dmain_f32 fp32 [B, G, D] accumulated with atomics (caller zeroes it;
  *   not bit-reproducible, as in the reference).  delta_ws, lse2_ws: fp32 workspaces of
- *   B * ceil(S*H/128)*128 entries.  D in {64, 128}.  dsinks is a host-side reduction of lse
+ *   B * ceil(S*H/128)*128 entries; dkv_part_ws: splits * B * S * 2 * D fp32 (the split
+ *   partials of dK/dV, summed in a fixed order: dq / dk / dv are deterministic).  D in {64, 128}.  dsinks is a host-side reduction of lse
  *   and delta (as in the reference).
  */
 MZB_API int mzb_attn_bwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
                          const void* o, const float* lse, const void* dout, void* dq, void* dk, void* dv,
-                         float* dmain_f32, float* delta_ws, float* lse2_ws, int64_t B, int64_t S, int H, int D,
-                         int window, int64_t G, int topk, float softmax_scale, int* err, void* stream);
+                         float* dmain_f32, float* delta_ws, float* lse2_ws, float* dkv_part_ws, int splits,
+                         int64_t B, int64_t S, int H, int D, int window, int64_t G, int topk, float softmax_scale,
+                         int* err, void* stream);
+/* Query-loop split count mzb_attn_bwd expects for these sizes (the key-owner kernel's
+ * partial sums; dkv_part_ws holds splits * B * S * 2 * D floats).  Host-only, no launch. */
+MZB_API int mzb_attn_bwd_splits(int64_t B, int64_t S, int H, int window);
 
 /* ------------------------------------------------------------------ sparse latent attention
  * mzb_sparse_mla_fwd -- the 576/512 FP8-latent form of `csa2_attn.fwd` / kernel `flashattn`

@@ -53,9 +53,11 @@ def run_bwd(q, kv, v, main_kv, idx, o, lse, do, sinks, window, scale, check=True
     delta = torch.empty(B, rpad, dtype=torch.float32, device=dev)
     lse2 = torch.empty(B, rpad, dtype=torch.float32, device=dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
+    splits = _lib.lib().mzb_attn_bwd_splits(B, S, H, window)
+    part = torch.empty(splits * B * S * 2 * D, dtype=torch.float32, device=dev)
     call("mzb_attn_bwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(o), ptr(lse_packed), ptr(do), ptr(dq),
-         ptr(dk), ptr(dv), ptr(dmain), ptr(delta), ptr(lse2), B, S, H, D, window, G, topk, float(scale), ptr(err),
-         stream_ptr(dev))
+         ptr(dk), ptr(dv), ptr(dmain), ptr(delta), ptr(lse2), ptr(part), splits, B, S, H, D, window, G, topk,
+         float(scale), ptr(err), stream_ptr(dev))
     if check and int(err.item()):
         raise _lib.MzbError(f"attn_bwd: device error code {int(err.item())}")
     dsinks = None

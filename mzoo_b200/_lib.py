@@ -40,8 +40,9 @@ SIGNATURES = {
     "mzb_indexer_topk": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64,
                          _F32, _I32, _F32, _P, _P],
     "mzb_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I64, _I32, _F32, _P, _P],
-    "mzb_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I64,
-                     _I32, _F32, _P, _P],
+    "mzb_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I32, _I32,
+                     _I32, _I64, _I32, _F32, _P, _P],
+    "mzb_attn_bwd_splits": [_I64, _I64, _I32, _I32],
     "mzb_sparse_mla_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64, _I32,
                            _I32, _F32, _P, _P],
     "mzb_sparse_mla_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64,

@@ -45,7 +45,8 @@ struct Args {
   __nv_bfloat16* dk;     // [B, S, D]  (dK + dV when K == V)
   __nv_bfloat16* dv;     // [B, S, D] or null
   float* dmain;          // [B, G, D] fp32 accumulator (zeroed by the caller) or null
-  int B, S, H, D, window, G, topk, Rpad;
+  float* dkv_part;       // [splits, B, S, 2, D] fp32 partial dK (scaled) | dV per query-loop split
+  int B, S, H, D, window, G, topk, Rpad, hshift, splits;
   float scale, scale_log2;
   int* err;
 };
@@ -87,20 +88,27 @@ enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FU
              KV_NBAR };
 
 struct KvItem {
-  int b, kt, k0, qt0, nq;
+  int b, kt, k0, sp, qt0, nq;  // query tiles [qt0, qt0 + nq) of this split (nq may be 0)
 };
 
-__device__ __forceinline__ KvItem kv_item(const Args& a, int it, int n_kt) {
+// Item = (key tile, batch, split of the query loop): the reference's split query loop
+// (swa_attn/bwd.py:66 pick_splits) so every SM has work; partials are summed by
+// dkv_finalize_kernel in a fixed order (deterministic).
+__device__ __forceinline__ KvItem kv_item(const Args& a, int it) {
   KvItem m;
-  m.b = it % a.B;
-  m.kt = it / a.B;
+  m.sp = it % a.splits;
+  const int rest = it / a.splits;
+  m.b = rest % a.B;
+  m.kt = rest / a.B;
   m.k0 = m.kt * 128;
   const int k1 = min(a.S - 1, m.k0 + 127);
   const int tmax = min(a.S - 1, k1 + a.window - 1);
-  const long long r_lo = (long long)m.k0 * a.H, r_hi = (long long)(tmax + 1) * a.H - 1;
-  m.qt0 = int(r_lo / 128);
-  m.nq = int(r_hi / 128) - m.qt0 + 1;
-  (void)n_kt;
+  const int q_lo = (m.k0 << a.hshift) / 128, q_hi = (((tmax + 1) << a.hshift) - 1) / 128;
+  const int total = q_hi - q_lo + 1;
+  const int per = (total + a.splits - 1) / a.splits;
+  const int s0 = min(total, m.sp * per), s1 = min(total, s0 + per);
+  m.qt0 = q_lo + s0;
+  m.nq = s1 - s0;
   return m;
 }
 
@@ -132,15 +140,17 @@ __global__ void __launch_bounds__(256, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
   const int n_kt = (a.S + 127) / 128;
-  const int items = a.B * n_kt;
+  const int items = a.B * n_kt * a.splits;
   auto stage = [&](int s) { return st0 + s * C::STAGE; };
 
   if (warp == 0) {
     if (lane == 0) {
       int g = 0, ii = 0;
-      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-        const KvItem m = kv_item(a, it, n_kt);
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const KvItem m = kv_item(a, it);
+        if (m.nq == 0) continue;
         if (!tc::mbar_wait(&bars[KV_EMPTY], (ii & 1) ^ 1, a.err, 401)) { *abort_flag = 1; break; }
+        ++ii;
         tc::mbar_expect_tx(&bars[KV_FULL], (SEP_V ? 2 : 1) * C::T_BYTES);
         for (int cb = 0; cb < C::DB; ++cb) {
           tc::tma_load_3d(ks + cb * 128 * 128, &tk, &bars[KV_FULL], cb * 64, m.k0, m.b);
@@ -169,9 +179,11 @@ __global__ void __launch_bounds__(256, 1)
       const uint32_t idesc_s = tc::make_idesc(128, 128, 1, 1);
       const uint32_t idesc_acc = tc::make_idesc(128, D, 1, 1, false, true);
       const uint32_t k_base = smem_u32(ks), v_base = smem_u32(vs);
-      int g = 0, ii = 0;
-      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-        const KvItem m = kv_item(a, it, n_kt);
+      int g = 0, ii = -1;
+      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+        const KvItem m = kv_item(a, it);
+        if (m.nq == 0) continue;
+        ++ii;
         if (!tc::mbar_wait(&bars[KV_FULL], ii & 1, a.err, 410)) { *abort_flag = 1; break; }
         bool ok = true;
         for (int i = 0; i < m.nq; ++i, ++g) {
@@ -215,10 +227,18 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp >= 4) {
     const int sw = warp - 4, row = sw * 32 + lane;  // TMEM lane = key within the tile
     const float sl = a.scale_log2;
-    int g = 0, ii = 0;
-    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-      const KvItem m = kv_item(a, it, n_kt);
+    const int tpt = 128 >> a.hshift;  // tokens per query tile
+    int g = 0, ii = -1;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
+      const KvItem m = kv_item(a, it);
       const int j = m.k0 + row;
+      float* part = a.dkv_part + (((long long)m.sp * a.B + m.b) * a.S + j) * 2 * D;
+      if (m.nq == 0) {  // this split has no query tiles: contribute zeros
+        if (j < a.S)
+          for (int c = 0; c < 2 * D; c += 4) *reinterpret_cast<float4*>(part + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+        continue;
+      }
+      ++ii;
       bool ok = true;
       for (int i = 0; i < m.nq; ++i, ++g) {
         const int s = g & 1;
@@ -226,7 +246,9 @@ __global__ void __launch_bounds__(256, 1)
         tc::fence_after_sync();
         const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
         const float* dl = l2 + 128;
-        const long long r0 = (long long)(m.qt0 + i) * 128;
+        const int tb = ((m.qt0 + i) * 128) >> a.hshift;  // token of column 0
+        // key j sees every row of this tile: j <= tb and j > tb + tpt - 1 - window, tiles in range
+        const bool full = j < a.S && tb + tpt - 1 < a.S && j <= tb && j > tb + tpt - 1 - a.window;
 #pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
           uint32_t sv[32], dv[32];
@@ -240,10 +262,11 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int c = c0 + 2 * q + e;
-              const long long r = r0 + c;
-              const int t = int(r / a.H);
-              const bool valid = j < a.S && t < a.S && j <= t && j > t - a.window;
-              const float p = valid ? exp2f(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2[c])) : 0.0f;
+              float p = fast_exp2(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2[c]));
+              if (!full) {
+                const int t = tb + (c >> a.hshift);
+                p = (j < a.S && t < a.S && j <= t && j > t - a.window) ? p : 0.0f;
+              }
               p2[e] = p;
               d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl[c]);
             }
@@ -268,22 +291,14 @@ __global__ void __launch_bounds__(256, 1)
         tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DV + c0), vv);
         tc::tmem_wait_ld();
         if (j < a.S) {
-          uint4* dst = reinterpret_cast<uint4*>(a.dk + ((long long)m.b * a.S + j) * D + c0);
-          uint4* dstv = SEP_V ? reinterpret_cast<uint4*>(a.dv + ((long long)m.b * a.S + j) * D + c0) : nullptr;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t w[4], wv[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int x = 8 * q + 2 * e;
-              float k0 = __uint_as_float(kv[x]) * a.scale, k1 = __uint_as_float(kv[x + 1]) * a.scale;
-              const float v0 = __uint_as_float(vv[x]), v1 = __uint_as_float(vv[x + 1]);
-              if (!SEP_V) { k0 += v0; k1 += v1; }
-              w[e] = pack_bf16(k0, k1);
-              wv[e] = pack_bf16(v0, v1);
-            }
-            dst[q] = make_uint4(w[0], w[1], w[2], w[3]);
-            if (SEP_V) dstv[q] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+          for (int q = 0; q < 32; q += 4) {
+            *reinterpret_cast<float4*>(part + c0 + q) =
+                make_float4(__uint_as_float(kv[q]) * a.scale, __uint_as_float(kv[q + 1]) * a.scale,
+                            __uint_as_float(kv[q + 2]) * a.scale, __uint_as_float(kv[q + 3]) * a.scale);
+            *reinterpret_cast<float4*>(part + D + c0 + q) =
+                make_float4(__uint_as_float(vv[q]), __uint_as_float(vv[q + 1]), __uint_as_float(vv[q + 2]),
+                            __uint_as_float(vv[q + 3]));
           }
         }
       }
@@ -297,6 +312,27 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_free(tmem, 512);
+  }
+}
+
+// Sum the per-split partials in split order: dk = sum dK (+ sum dV when K == V), dv = sum dV.
+__global__ void dkv_finalize_kernel(Args a, int sep_v) {
+  const long long n = (long long)a.B * a.S * a.D;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / a.D;
+    const int d = int(i % a.D);
+    float k = 0.0f, v = 0.0f;
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float* p = a.dkv_part + ((long long)sp * a.B * a.S + row) * 2 * a.D;
+      k += p[d];
+      v += p[a.D + d];
+    }
+    if (sep_v) {
+      a.dk[i] = __float2bfloat16_rn(k);
+      a.dv[i] = __float2bfloat16_rn(v);
+    } else {
+      a.dk[i] = __float2bfloat16_rn(k + v);
+    }
   }
 }
 
@@ -502,6 +538,7 @@ __global__ void __launch_bounds__(384, 1)
             gmask[w] = __ballot_sync(0xffffffffu, v);
           }
         }
+        const bool full = row_ok && win && wlo <= 0 && whi >= 127;
         if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
@@ -517,8 +554,9 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const int c = c0 + 2 * q + e;
-              const bool valid = row_ok && (win ? (c >= wlo && c <= whi) : (tr == gtok && ((gmask[c >> 5] >> (c & 31)) & 1u)));
-              const float p = valid ? exp2f(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2)) : 0.0f;
+              const bool valid = full || (row_ok && (win ? (c >= wlo && c <= whi)
+                                                          : (tr == gtok && ((gmask[c >> 5] >> (c & 31)) & 1u))));
+              const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2)) : 0.0f;
               p2[e] = p;
               d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl);
             }
@@ -658,9 +696,16 @@ int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStre
   auto kkv = dkv_kernel<D, SEP_V>;
   if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, KvCfg<D, SEP_V>::SMEM) != cudaSuccess)
     return launch_status("attn_bwd_dkv(smem attr)");
-  const int kv_items = a.B * ((a.S + 127) / 128);
+  const int kv_items = a.B * ((a.S + 127) / 128) * a.splits;
   kkv<<<kv_items < num_sms() ? kv_items : num_sms(), 256, KvCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
   if (int r = launch_status("attn_bwd_dkv")) return r;
+  {
+    const long long n = (long long)a.B * a.S * a.D;
+    long long blocks = (n + 255) / 256;
+    if (blocks > 8LL * num_sms()) blocks = 8LL * num_sms();
+    dkv_finalize_kernel<<<unsigned(blocks), 256, 0, st>>>(a, SEP_V ? 1 : 0);
+    if (int r = launch_status("attn_bwd_dkv_finalize")) return r;
+  }
 
   auto kq = dq_kernel<D, SEP_V>;
   if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<D, SEP_V>::SMEM) != cudaSuccess)
@@ -676,10 +721,22 @@ int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStre
 
 using namespace mzb;
 
+extern "C" int mzb_attn_bwd_splits(int64_t B, int64_t S, int H, int window) {
+  // query-loop splits of the key-owner kernel: ~4 items per SM (the reference targets 768
+  // CTAs, swa_attn/bwd.py:57-76), at most 16, never more than the query tiles of a key tile
+  const int n_kt = int((S + 127) / 128);
+  const long long q_tiles = ((long long)(127 + window) * H + 127) / 128 + 1;
+  int sp = int((4LL * num_sms() + B * n_kt - 1) / (B * n_kt));
+  if (sp > 16) sp = 16;
+  if (sp > q_tiles) sp = int(q_tiles);
+  return sp < 1 ? 1 : sp;
+}
+
 extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const void* main_kv, const int32_t* indices,
                             const void* o, const float* lse, const void* dout, void* dq, void* dk, void* dv,
-                            float* dmain_f32, float* delta_ws, float* lse2_ws, int64_t B, int64_t S, int H, int D,
-                            int window, int64_t G, int topk, float softmax_scale, int* err, void* stream) {
+                            float* dmain_f32, float* delta_ws, float* lse2_ws, float* dkv_part_ws, int splits,
+                            int64_t B, int64_t S, int H, int D, int window, int64_t G, int topk, float softmax_scale,
+                            int* err, void* stream) {
   MZB_REQUIRE(B >= 1 && S >= 1 && window >= 1 && topk >= 0 && G >= 0, MZB_ERR_SHAPE, "attn_bwd: bad sizes");
   MZB_REQUIRE(H >= 1 && H <= 128 && 128 % H == 0, MZB_ERR_UNSUPPORTED, "attn_bwd: heads must divide 128, got %d",
               H);
@@ -688,7 +745,8 @@ extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const 
   const bool gathered = main_kv != nullptr && topk > 0 && G > 0;
   MZB_REQUIRE(!(sep && gathered), MZB_ERR_UNSUPPORTED, "attn_bwd: a separate V only for the window-only kernel");
   MZB_REQUIRE(!gathered || dmain_f32 != nullptr, MZB_ERR_SHAPE, "attn_bwd: gathered rows need a dmain accumulator");
-  MZB_REQUIRE(err && delta_ws && lse2_ws, MZB_ERR_SHAPE, "attn_bwd: needs err and workspaces");
+  MZB_REQUIRE(err && delta_ws && lse2_ws && dkv_part_ws, MZB_ERR_SHAPE, "attn_bwd: needs err and workspaces");
+  MZB_REQUIRE(splits >= 1 && splits <= 64, MZB_ERR_SHAPE, "attn_bwd: splits must be in [1, 64], got %d", splits);
   attnb::Args a{};
   a.o = static_cast<const __nv_bfloat16*>(o);
   a.dout = static_cast<const __nv_bfloat16*>(dout);
@@ -704,6 +762,9 @@ extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const 
   a.B = int(B); a.S = int(S); a.H = H; a.D = D; a.window = window; a.G = gathered ? int(G) : 0;
   a.topk = gathered ? topk : 0;
   a.Rpad = int(((S * H + 127) / 128) * 128);
+  a.dkv_part = dkv_part_ws;
+  a.splits = splits;
+  a.hshift = __builtin_ctz(unsigned(H));
   a.scale = softmax_scale;
   a.scale_log2 = softmax_scale * attnb::LOG2E;
   a.err = err;

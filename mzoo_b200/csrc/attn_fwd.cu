@@ -260,21 +260,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (win) return c >= wlo && c <= whi;
           return tr == gtok && ((gm[c >> 5] >> (c & 31)) & 1u);
         };
-        float mt = -INFINITY;
+        // a window tile this row sees completely needs no per-column mask
+        const bool full = row_ok && win && wlo <= 0 && whi >= NK - 1;
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c0 = 0; c0 < NK; c0 += 32) {
           uint32_t sr[32];
           tc::tmem_ld32(sbase + c0, sr);
           tc::tmem_wait_ld();
+          if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (valid(c0 + i)) mt = fmaxf(mt, __uint_as_float(sr[i]));
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sr[i]));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (valid(c0 + i)) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sr[i]));
+          }
         }
+        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         const bool need = mt * sl > mrow * sl + 8.0f;
         const float m_new = need ? mt : mrow;
-        const float alpha = exp2f((mrow - m_new) * sl);
+        const float alpha = fast_exp2((mrow - m_new) * sl);
         const float ms = m_new * sl;
-        float psum = 0.0f;
+        float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         uint8_t* prow = ps + sb * C::P_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
         for (int c0 = 0; c0 < NK; c0 += 32) {
@@ -284,9 +292,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = valid(c0 + 2 * i) ? exp2f(fmaf(__uint_as_float(sr[2 * i]), sl, -ms)) : 0.0f;
-            const float p1 = valid(c0 + 2 * i + 1) ? exp2f(fmaf(__uint_as_float(sr[2 * i + 1]), sl, -ms)) : 0.0f;
-            psum += p0 + p1;
+            float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), sl, -ms));
+            float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), sl, -ms));
+            if (!full) {
+              p0 = valid(c0 + 2 * i) ? p0 : 0.0f;
+              p1 = valid(c0 + 2 * i + 1) ? p1 : 0.0f;
+            }
+            ps4[i & 3] += p0 + p1;
             pk[i] = pack_bf16(p0, p1);
           }
           // row r of column block c0/64: 4 chunks of 16 B (keys c0..c0+31 -> chunks (c0%64)/8 ..)
@@ -297,6 +309,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             st_shared16(blk + ((ch ^ (r & 7)) * 16), make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]));
           }
         }
+        const float psum = (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[S_EMPTY + sb]);

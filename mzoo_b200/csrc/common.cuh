@@ -109,6 +109,13 @@ __device__ __forceinline__ float e2m1_value(float q) {
 
 // ---------------------------------------------------------------- PTX helpers
 
+// 2^x on the SFU (ex2.approx, relative error ~2^-22; -inf -> +0).  Softmax numerators only.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -280,6 +280,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int j = 0; j < n; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
+        // key validity (global index loads) before waiting on the MMA
+        const uint32_t vmask = __ballot_sync(0xffffffffu, slot_valid(a, s, tk, j * NT + kh * NTH + lane));
         if (!tc::mbar_wait(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
         tc::fence_after_sync();
         uint32_t sr[32];
@@ -288,14 +290,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive_cluster(leader_bar(S_EMPTY + st));
-        const uint32_t vmask = __ballot_sync(0xffffffffu, slot_valid(a, s, tk, j * NT + kh * NTH + lane));
         float sv[32];
-        float mt = -INFINITY;
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           sv[i] = (vmask >> i & 1u) ? __uint_as_float(sr[i]) : -INFINITY;
-          mt = fmaxf(mt, sv[i]);
+          mx4[i & 3] = fmaxf(mx4[i & 3], sv[i]);
         }
+        float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
         // exchange with the thread holding the other key half of this head (mbarrier, bounded)
         red_m[st][l] = mt;
         __syncwarp();
@@ -304,17 +306,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         mt = fmaxf(mt, red_m[st][l ^ 64]);
         const bool need = mt * sl > m * sl + 8.0f;
         const float m_new = need ? mt : m;
-        const float alpha = exp2f((m - m_new) * sl);
+        const float alpha = fast_exp2((m - m_new) * sl);
         const float ms = m_new * sl;
         uint32_t pk[16];
-        float psum = 0.0f;
+        float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = exp2f(fmaf(sv[2 * i], sl, -ms));
-          const float p1 = exp2f(fmaf(sv[2 * i + 1], sl, -ms));
-          psum += p0 + p1;
+          const float p0 = fast_exp2(fmaf(sv[2 * i], sl, -ms));
+          const float p1 = fast_exp2(fmaf(sv[2 * i + 1], sl, -ms));
+          ps4[i & 3] += p0 + p1;
           pk[i] = pack_bf16(p0, p1);
         }
+        const float psum = (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
         lsum = lsum * alpha + psum;
         uint8_t* prow = ps + st * P_BYTES + hrow * 128;
 #pragma unroll
