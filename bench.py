@@ -585,8 +585,188 @@ def reference_train(args, rank, world) -> dict:
             "cpu_baseline": r, "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ----------------------------------------------------------------------------- paged decode + indexer (C4)
+
+C4 = dict(B=128, L_lo=8192, L_hi=131072, ratio=4, topk=2048, window=128, Hi=64, Di=128, page=64)
+
+
+def c4_lens(torch, n=None):
+    g = torch.Generator().manual_seed(1)
+    return torch.randint(C4["L_lo"], C4["L_hi"] + 1, (C4["B"] if n is None else n,), generator=g)
+
+
+def shard_sequences(lens, world: int) -> list:
+    """Greedy longest-first assignment of sequences to ranks by context length (balances the
+    indexer's per-sequence key stream); returns the sorted sequence ids of each rank."""
+    order = sorted(range(len(lens)), key=lambda b: -int(lens[b]))
+    load = [0] * world
+    owned = [[] for _ in range(world)]
+    for b in order:
+        r = min(range(world), key=lambda i: load[i])
+        owned[r].append(b)
+        load[r] += int(lens[b])
+    return [sorted(o) for o in owned]
+
+
+def _random_rows(torch, n_rows: int, device, gen, chunk: int = 1 << 20):
+    """n_rows KV rows of 672 B with valid e4m3 codes (no NaN), scales in [1/448, 4/448] and
+    N(0,1) bf16 rope channels."""
+    rows = torch.empty(n_rows, 672, dtype=torch.uint8, device=device)
+    for r0 in range(0, n_rows, chunk):
+        r1 = min(n_rows, r0 + chunk)
+        n = r1 - r0
+        codes = torch.randint(0, 255, (n, 512), generator=gen, device=device, dtype=torch.int32)
+        codes = torch.where((codes & 0x7F) == 0x7F, codes - 1, codes).to(torch.uint8)
+        rows[r0:r1, :512] = codes
+        sc = (torch.rand(n, 8, generator=gen, device=device) * 3 + 1) / 448.0
+        rows[r0:r1, 512:544] = sc.view(torch.uint8).view(n, 32)
+        rope = torch.randn(n, 64, generator=gen, device=device).to(torch.bfloat16)
+        rows[r0:r1, 544:] = rope.view(torch.uint8).view(n, 128)
+    return rows
+
+
+def c4_inputs(torch, device, seqs, lens):
+    """Device inputs for the sequences `seqs` (global ids): paged raw / compressed latent
+    caches with random page tables, dense per-sequence FP8 index keys, queries."""
+    B = len(seqs)
+    L = torch.tensor([int(lens[b]) for b in seqs], dtype=torch.int32)
+    pages = (L + 63) // 64
+    cl = L // C4["ratio"]
+    cpages = (cl + 63) // 64
+    g = torch.Generator(device=device).manual_seed(100 + seqs[0])
+    gc = torch.Generator().manual_seed(200 + seqs[0])
+    n_raw, n_cmp = int(pages.sum()), int(cpages.sum())
+    pt = torch.full((B, int(pages.max())), 0, dtype=torch.int32)
+    perm = torch.randperm(n_raw, generator=gc).to(torch.int32)
+    o = 0
+    for i in range(B):
+        pt[i, :pages[i]] = perm[o:o + pages[i]]
+        o += int(pages[i])
+    cpt = torch.full((B, int(cpages.max())), 0, dtype=torch.int32)
+    cperm = torch.randperm(n_cmp, generator=gc).to(torch.int32)
+    o = 0
+    for i in range(B):
+        cpt[i, :cpages[i]] = cperm[o:o + cpages[i]]
+        o += int(cpages[i])
+    raw = _random_rows(torch, n_raw * 64, device, g).view(n_raw, 64, 672)
+    cmp = _random_rows(torch, n_cmp * 64, device, g).view(n_cmp, 64, 672)
+    T = int(cl.max())
+    kcodes = torch.randint(0, 255, (B, T, C4["Di"]), generator=g, device=device, dtype=torch.int32)
+    k8 = torch.where((kcodes & 0x7F) == 0x7F, kcodes - 1, kcodes).to(torch.uint8).view(torch.float8_e4m3fn)
+    sk = (torch.rand(B, T, generator=g, device=device) * 3 + 1) / 448.0
+    qcodes = torch.randint(0, 255, (B, 1, C4["Hi"], C4["Di"]), generator=g, device=device, dtype=torch.int32)
+    q8 = torch.where((qcodes & 0x7F) == 0x7F, qcodes - 1, qcodes).to(torch.uint8).view(torch.float8_e4m3fn)
+    sq = (torch.rand(B, 1, C4["Hi"], generator=g, device=device) * 3 + 1) / 448.0
+    w = torch.randn(B, 1, C4["Hi"], generator=g, device=device) / 8
+    q = torch.randn(B, 128, 576, generator=g, device=device, dtype=torch.bfloat16)
+    dev = lambda t: t.to(device)  # noqa: E731
+    return dict(q=q, raw=raw, pt=dev(pt), lens=dev(L), cmp=cmp, cpt=dev(cpt), cmp_lens=dev(cl.to(torch.int32)),
+                q8=q8, sq=sq, k8=k8, sk=sk, w=w, pos=dev((L - 1).view(B, 1)))
+
+
+def c4_step(x):
+    from mzoo_b200 import indexer, sparse_mla
+    idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"], scales=(x["sq"], x["sk"]),
+                       q_pos=x["pos"], check=False)
+    return sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"], idx[:, 0],
+                             window=C4["window"], check=False)
+
+
+def c4_bytes(lens_sub) -> float:
+    """Algorithmic HBM bytes of one decode step for these sequences."""
+    tot = 0.0
+    for L in lens_sub:
+        L = int(L)
+        tot += (L // C4["ratio"]) * (C4["Di"] + 4)                 # index keys + scales
+        tot += min(L, C4["window"]) * 672 + min(C4["topk"], L // C4["ratio"]) * 672  # selected latent rows
+        tot += 128 * 576 * 2 + 128 * 512 * 2 + 128 * 4             # q, o, lse
+        tot += C4["Hi"] * (C4["Di"] + 8) + C4["topk"] * 4          # indexer q / scales / w, indices
+    return tot
+
+
+def bench_decode(args, torch, dist, rank, world, device) -> dict:
+    lens = c4_lens(torch)
+    mine = shard_sequences(lens.tolist(), world)[rank]
+    x = c4_inputs(torch, device, mine, lens)
+    nbytes = c4_bytes([lens[b] for b in mine])
+    total_bytes = c4_bytes(lens.tolist())
+    n_mine = len(mine)
+    shard = -(-C4["B"] // world)
+    gather_buf = torch.empty(world * shard, 128, 512, dtype=torch.bfloat16, device=device) if dist else None
+
+    def step():
+        o, lse = c4_step(x)
+        if dist:  # the one collective: gather every rank's outputs (padded shards)
+            part = torch.zeros(shard, 128, 512, dtype=torch.bfloat16, device=device)
+            part[:n_mine] = o
+            dist.all_gather_into_tensor(gather_buf, part)
+        return o
+
+    timer = Timer(torch, device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    t_steps = timer.run(step, args.steps)
+    clocks = sampler.stop()
+    # dominant kernel legs
+    from mzoo_b200 import indexer
+    qp, kp, wp, sqp, skp, scale, dt = indexer._prep(x["q8"], x["k8"], x["w"], (x["sq"], x["sk"]), None)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    qpos = x["pos"].to(torch.int32).contiguous()
+    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C4["ratio"], 0, scale, dt, False, err, qpos),
+                        args.steps)
+    # e2e: queries / indexer queries / weights from pinned host memory, o back to the host
+    hq, hq8, hw = x["q"].cpu().pin_memory(), x["q8"].view(torch.uint8).cpu().pin_memory(), x["w"].cpu().pin_memory()
+    ho = torch.empty(n_mine, 128, 512, dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        x["q"].copy_(hq, non_blocking=True)
+        x["q8"].view(torch.uint8).copy_(hq8, non_blocking=True)
+        x["w"].copy_(hw, non_blocking=True)
+        o = step()
+        ho.copy_(o, non_blocking=True)
+
+    e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_score = sum(t_score) / len(t_score)
+    pk = peaks()
+    score_bytes = sum((int(lens[b]) // 4) * (C4["Di"] + 4) + C4["Hi"] * (C4["Di"] + 8) for b in mine)
+    ach = score_bytes / (ms_score * 1e-3) / 1e9
+    out = {
+        "metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)", "value": total_bytes / (ms * 1e-3) / 1e9,
+        "unit": "GB/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3 KV / bf16 q (fp32 acc)", "data": "synthetic (seeded lengths, random page tables, random FP8 rows)",
+        "config": {"workload": "C4 paged decode + indexer", "sequences": C4["B"], "context": "U[8192,131072] seed 1",
+                   "mean_context": float(lens.float().mean()), "heads": 128, "topk": C4["topk"],
+                   "window": C4["window"], "page": 64, "algorithmic_bytes_per_step": total_bytes,
+                   "parallelism": f"sequences sharded over {world} GPU(s) (greedy by length) + o all-gather",
+                   "l2": "caches (~8 GB) larger than L2; 256 MB flush per step"},
+        "e2e": {"value": total_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": hq.numel() * 2 + hq8.numel() + hw.numel() * 4,
+                "d2h_bytes_per_step": ho.numel() * 2},
+        "roofline": {"bound": "hbm", "kernel": "mzb::idx::score_kernel<fp8,128> (decode indexer)", "achieved": ach,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                     "peak_note": f"{pk['_source']} HBM copy", "algorithmic_bytes_per_launch": score_bytes,
+                     "ms_per_launch": ms_score, "traffic": None},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+    }
+    return out
+
+
+def reference_decode(args, rank, world) -> dict:
+    return {"impl": "reference", "metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)",
+            "unavailable": "the reference has no decode path (csa2_attn_design.md: 'no decode, no paged cache')"}
+
+
 BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
-           "train": (bench_train, reference_train)}
+           "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode)}
 
 
 def main():
@@ -605,6 +785,7 @@ def main():
         C2.update(S=1024, q_offset=4096 - 1024)
         C3.update(S=2048)
         C5.update(B=1, S=2048)
+        C4.update(B=8)
         args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 
