@@ -757,12 +757,64 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
         "gpu_launches": 6 * args.steps,
         "clocks": clocks,
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_decode(max(1, args.cpu_sample // 256))
     return out
 
 
+def cpu_decode(n_seq: int) -> dict:
+    """Oracle port of one decode step for n_seq sequences (the first of the seeded lengths):
+    canonical fp64 indexer scores over L/4 FP8 keys -> exact top-2048 -> sparse attention
+    over window + selected latent rows (numpy fp64), as GB/s of their algorithmic bytes."""
+    import numpy as np
+    import torch
+    from oracle import indexer as I
+    from oracle import mla as M
+    lens = c4_lens(torch)[:n_seq].tolist()
+    rng = np.random.default_rng(5)
+    t_total = 0.0
+    for L in lens:
+        T = L // C4["ratio"]
+        codes = rng.integers(0, 255, (T, C4["Di"]), dtype=np.uint8)
+        codes[(codes & 0x7F) == 0x7F] -= 1
+        kv = M.e4m3_values(codes)[None]
+        qc = rng.integers(0, 255, (1, 1, C4["Hi"], C4["Di"]), dtype=np.uint8)
+        qc[(qc & 0x7F) == 0x7F] -= 1
+        qv = M.e4m3_values(qc)
+        sk = ((rng.random((1, T)) * 3 + 1) / 448).astype(np.float32)
+        sq = ((rng.random((1, 1, C4["Hi"])) * 3 + 1) / 448).astype(np.float32)
+        w = (rng.standard_normal((1, 1, C4["Hi"])) / 8).astype(np.float32)
+        raw_rows = M.pack_rows(rng.standard_normal((C4["window"], 576)).astype(np.float32))
+        cmp_rows = M.pack_rows(rng.standard_normal((min(T, C4["topk"]), 576)).astype(np.float32))
+        q = rng.standard_normal((128, 576)).astype(np.float32)
+        t0 = time.perf_counter()
+        sc = I.canonical_scores(qv, kv, w, sq, sk, C4["ratio"], L - 1)
+        sel = I.canonical_topk(sc, C4["topk"], C4["ratio"], L - 1)[0, 0]
+        keys = M.unpack_rows(np.concatenate([raw_rows, cmp_rows[:int((sel >= 0).sum())]], 0))
+        M.attend_rows(q, keys, 576**-0.5)
+        t_total += time.perf_counter() - t0
+    nbytes = c4_bytes(lens)
+    return {"value": nbytes / t_total / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_seq} sequences (L = {lens}), numpy fp64 canonical indexer + exact top-2048 + sparse "
+                      f"attention, {t_total:.2f} s"}
+
+
 def reference_decode(args, rank, world) -> dict:
-    return {"impl": "reference", "metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)",
-            "unavailable": "the reference has no decode path (csa2_attn_design.md: 'no decode, no paged cache')"}
+    if rank != 0:
+        return None
+    n = max(1, args.cpu_sample // 512)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_decode(n)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    r["value"] = v
+    return {"metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)", "value": v, "unit": "GB/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64 (oracle port)",
+            "data": "synthetic", "config": {"workload": "C4 paged decode + indexer", "sequences": C4["B"]},
+            "cpu_baseline": r, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
