@@ -94,6 +94,17 @@ MZB_API int mzb_indexer_scores(const void* q, const void* k, const float* w, con
                                const int32_t* q_pos, float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di,
                                int dtype, int ratio, int64_t q_offset, float scale, int write_tail, int* err,
                                void* stream);
+/* mzb_indexer_bwd -- replaces `indexer.bwd.bwd` / kernel `index_score_bwd`
+ *   (src/mzoo/layers/attn/indexer/bwd.py:38-133): with r = q.k recomputed and d = dl on the
+ *   group-causal visible keys (masked entries ignored whatever they hold), scale given:
+ *   dw = sum_t relu(r)*scale*d (fp32), dr = d*w*scale*[r > 0], dq = sum_t dr k (bf16),
+ *   dk = sum_{s,h} dr q (bf16; deterministic here, fp32 atomics in the reference).
+ *   q bf16 [B,S,Hi,Di], k bf16 [B,T,Di], w / dl fp32 [B,S,Hi] / [B,S,T]; Hi divides 256 and is a
+ *   multiple of 16 (the host pads with zero weights); Di in {64, 128}; T >= 1.
+ */
+MZB_API int mzb_indexer_bwd(const void* q, const void* k, const float* w, const float* dl, void* dq, void* dk,
+                            float* dw, int64_t B, int64_t S, int64_t T, int Hi, int Di, int ratio, int64_t q_offset,
+                            float scale, int* err, void* stream);
 MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, const float* w, const float* sq,
                              const float* sk, const int32_t* q_pos, float* kbmax_ws, int32_t* out, int64_t B,
                              int64_t S, int64_t T, int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale,

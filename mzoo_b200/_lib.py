@@ -39,6 +39,7 @@ SIGNATURES = {
                            _I32, _P, _P],
     "mzb_indexer_topk": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64,
                          _F32, _I32, _F32, _P, _P],
+    "mzb_indexer_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I64, _F32, _P, _P],
     "mzb_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I64, _I32, _F32, _P, _P],
     "mzb_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I32, _I32,
                      _I32, _I64, _I32, _F32, _P, _P],

@@ -126,6 +126,66 @@ def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: i
     return out
 
 
+def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, compress_ratio: int,
+        q_offset: int = 0, softmax_scale: float | None = None, check: bool = True):
+    """``indexer/bwd.py:104``: q bf16 [B,S,Hi,Di], k bf16 [B,T,Di], w fp32 [B,S,Hi], dl fp32
+    [B,S,T] -> (dq bf16 [B,S,Hi,Di], dk bf16 [B,T,Di], dw fp32 [B,S,Hi]).  Entries of ``dl`` at
+    group-causally masked positions are ignored, whatever they hold."""
+    require_cuda(q, k, w, dl)
+    assert q.dtype == k.dtype == torch.bfloat16, f"q/k must be bf16, got {q.dtype}/{k.dtype}"
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    assert k.shape == (B, T, Di) and w.shape == (B, S, Hi), "shape mismatch"
+    assert dl.shape == (B, S, T) and dl.dtype == torch.float32, \
+        f"dl must be [B,S,T] fp32, got {tuple(dl.shape)} {dl.dtype}"
+    assert T > 0, "bwd of an empty key axis is all zeros -- handle at the caller"
+    assert Di in (64, 128), f"indexer backward supports index head dim 64 / 128 here, got {Di}"
+    hp = 16
+    while hp < Hi:
+        hp *= 2
+    qp, wp = q.contiguous(), w.float().contiguous()
+    if hp != Hi:  # pad heads to a power of two >= 16 with zero weights (their gradients are discarded)
+        qp = torch.cat([qp, qp.new_zeros(B, S, hp - Hi, Di)], dim=2).contiguous()
+        wp = torch.cat([wp, wp.new_zeros(B, S, hp - Hi)], dim=2).contiguous()
+    dq = torch.empty(B, S, hp, Di, dtype=torch.bfloat16, device=q.device)
+    dk = torch.empty(B, T, Di, dtype=torch.bfloat16, device=q.device)
+    dw = torch.empty(B, S, hp, dtype=torch.float32, device=q.device)
+    err = torch.zeros(1, dtype=torch.int32, device=q.device)
+    scale = softmax_scale if softmax_scale is not None else Di**-0.5
+    call("mzb_indexer_bwd", ptr(qp), ptr(k.contiguous()), ptr(wp), ptr(dl.contiguous()), ptr(dq), ptr(dk), ptr(dw),
+         B, S, T, hp, Di, compress_ratio, q_offset, float(scale), ptr(err), stream_ptr(q.device))
+    if check:
+        _check_err(err, "indexer.bwd")
+    return dq[:, :, :Hi], dk, dw[:, :, :Hi]
+
+
+class _ScoresAutograd(torch.autograd.Function):
+    """``indexer/attn.py:37-50``: fwd + bwd glued; saves only q, k, w."""
+
+    @staticmethod
+    def forward(ctx, q, k, w, compress_ratio):
+        ctx.save_for_backward(q, k, w)
+        ctx.compress_ratio = compress_ratio
+        return fwd(q, k, w, compress_ratio=compress_ratio)
+
+    @staticmethod
+    def backward(ctx, dl):
+        q, k, w = ctx.saved_tensors
+        dq, dk, dw = bwd(q, k, w, dl.contiguous().float(), compress_ratio=ctx.compress_ratio)
+        return dq, dk, dw, None
+
+
+def scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int,
+           fake_quant_fp4: bool = False) -> torch.Tensor:
+    """``indexer/attn.py:53``: differentiable ``fwd``.  ``fake_quant_fp4=True`` round-trips q/k
+    through the fp4 block-32 quantiser with a straight-through gradient first
+    (``indexer/attn.py:29-34``)."""
+    if fake_quant_fp4:
+        from .quant import fake_quant_fp4_ste
+        q, k = fake_quant_fp4_ste(q, 32), fake_quant_fp4_ste(k, 32)
+    return _ScoresAutograd.apply(q, k, w, compress_ratio)
+
+
 def quantize_fp8(x: torch.Tensor, dim_tile: int | None = None):
     """Absmax e4m3 quantisation of indexer inputs: per row of the last
     dim (or per ``dim_tile`` elements), ``scale = amax / 448`` -> (codes, fp32 scales)."""

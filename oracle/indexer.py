@@ -119,3 +119,24 @@ def bound_factors(q: np.ndarray, k: np.ndarray, w, sq, sk, scale: float = 1.0):
     skd = np.asarray(sk, np.float64) if sk is not None else 1.0
     Bt = abs(scale) * np.abs(skd) * np.sqrt((k * k).sum(-1))
     return A, Bt
+
+
+def scores_bwd_ref(q, k, w, dl, ratio: int, q_offset: int = 0, scale: float | None = None):
+    """Gradients of ``indexer_scores`` (``indexer/bwd.py:4-22`` closed form) in float64:
+    with r = q.k, d = dl * scale on visible keys (0 elsewhere, whatever dl holds there):
+    dw = sum_t relu(r) d, dr = d w [r > 0], dq = sum_t dr k, dk = sum_{s,h} dr q."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    w = np.asarray(w, np.float64)
+    dl = np.asarray(dl, np.float64)
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    scale = Di**-0.5 if scale is None else scale
+    vis = np.arange(T)[None, :] < visible(np.arange(S), ratio, q_offset, T)[:, None]
+    d = np.where(vis[None], dl, 0.0) * scale
+    r = np.einsum("bshd,btd->bsht", q, k)
+    dw = (np.maximum(r, 0) * d[:, :, None, :]).sum(-1)
+    dr = d[:, :, None, :] * w[..., None] * (r > 0)
+    dq = np.einsum("bsht,btd->bshd", dr, k)
+    dk = np.einsum("bsht,bshd->btd", dr, q)
+    return dq, dk, dw

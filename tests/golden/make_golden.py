@@ -120,6 +120,13 @@ def make_indexer(golden_ref) -> None:
     out["q"], out["k"], out["w"], out["scores"] = q.numpy(), k.numpy(), w.numpy(), sc.numpy()
     for topk in (4, 16, 25):
         out[f"topk{topk}"] = golden_ref.topk_indices(sc, topk).numpy()
+    # gradients through the reference's differentiable scores (autograd of indexer_scores)
+    qg, kg, wg = (x.clone().requires_grad_() for x in (q, k, w))
+    sg = golden_ref.indexer_scores(qg, kg, wg, ratio)
+    dl = torch.randn(sg.shape, generator=g)
+    sg.backward(dl)
+    out["bwd.dl"], out["bwd.dq"], out["bwd.dk"], out["bwd.dw"] = (dl.numpy(), qg.grad.numpy(), kg.grad.numpy(),
+                                                                  wg.grad.numpy())
     np.savez_compressed(os.path.join(HERE, "indexer.npz"), **out)
 
 

@@ -187,3 +187,80 @@ def test_fp8_score_error_within_bound(cuda):
     ratio_err = (np.abs(approx.astype(np.float64) - canon) / bound).max()
     print(f"max |approx-exact| / (A_s max B_t) = {ratio_err:.3e} (EPS = {indexer.EPS:.3e})")
     assert ratio_err <= indexer.EPS / 16
+
+
+# ----------------------------------------------------------------------------- backward
+
+def test_oracle_bwd_matches_reference_autograd():
+    d = _golden()
+    dq, dk, dw = I.scores_bwd_ref(d["q"], d["k"], d["w"], d["bwd.dl"], 2)
+    np.testing.assert_allclose(dq, d["bwd.dq"], atol=2e-6)
+    np.testing.assert_allclose(dk, d["bwd.dk"], atol=2e-6)
+    np.testing.assert_allclose(dw, d["bwd.dw"], atol=5e-6)
+
+
+def _grad_close(got, ref, what, rel=1e-2, atol=2e-2):
+    got = got.float().cpu().numpy()
+    err = np.abs(got - ref).max()
+    scale = np.abs(ref).max()
+    print(f"{what}: max err {err:.3e} (ref max {scale:.2e})")
+    assert err <= atol + rel * scale, what
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("heads,dim,ratio", [(4, 64, 2), (32, 128, 4), (64, 128, 1), (16, 128, 2)])
+def test_bwd_matches_oracle(cuda, heads, dim, ratio):
+    """indexer/bwd_test.py:29-62: dq / dk / dw against autograd through the fp32 scores."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, T = 2, 256, 160
+    q, k, w = _bf16_inputs(torch, cuda, B, S, heads, dim, T, seed=heads + dim)
+    g = torch.Generator(device="cpu").manual_seed(5)
+    dl = torch.randn(B, S, T, generator=g).to(cuda)
+    dq, dk, dw = indexer.bwd(q, k, w, dl, compress_ratio=ratio)
+    rq, rk, rw = I.scores_bwd_ref(q.float().cpu().numpy(), k.float().cpu().numpy(), w.cpu().numpy(),
+                                  dl.cpu().numpy(), ratio)
+    _grad_close(dq, rq, "dq")
+    _grad_close(dk, rk, "dk")
+    _grad_close(dw, rw, "dw", rel=1e-4, atol=1e-4)
+
+
+@pytest.mark.gpu
+def test_bwd_ignores_masked_junk(cuda):
+    """indexer/bwd_test.py:86-108: NaN / huge values at masked positions change nothing."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, T, ratio = 1, 256, 128, 2
+    q, k, w = _bf16_inputs(torch, cuda, B, S, 32, 128, T, seed=1)
+    dl = torch.randn(B, S, T, device=cuda)
+    s_idx = torch.arange(S, device=cuda)[:, None]
+    t_idx = torch.arange(T, device=cuda)[None, :]
+    masked = t_idx >= (s_idx + 1) // ratio
+    clean = indexer.bwd(q, k, w, dl.masked_fill(masked, 0.0), compress_ratio=ratio)
+    junk = indexer.bwd(q, k, w, dl.masked_fill(masked, float("nan")), compress_ratio=ratio)
+    for a_, b_ in zip(clean, junk):
+        assert torch.equal(a_, b_)
+
+
+@pytest.mark.gpu
+def test_scores_autograd_and_fp4_ste(cuda):
+    """indexer/attn.py:53 + bwd_test.py:147-190: feature-off forward equals fwd bit for bit;
+    the fp4 STE forward equals fwd on quantised inputs and its gradient is the plain one."""
+    import torch
+    from mzoo_b200 import indexer, quant
+    q, k, w = _bf16_inputs(torch, cuda, 1, 256, 32, 128, 128, seed=2)
+    qg, kg, wg = (x.clone().requires_grad_() for x in (q, k, w))
+    out = indexer.scores(qg, kg, wg, compress_ratio=2)
+    assert torch.equal(out, indexer.fwd(q, k, w, compress_ratio=2))
+    dl = torch.randn_like(out).masked_fill(torch.isinf(out), 0.0)
+    out.backward(dl)
+    dq, dk, dw = indexer.bwd(q, k, w, dl, compress_ratio=2)
+    assert torch.equal(qg.grad, dq) and torch.equal(kg.grad, dk) and torch.equal(wg.grad, dw)
+    qg2, kg2 = q.clone().requires_grad_(), k.clone().requires_grad_()
+    out2 = indexer.scores(qg2, kg2, w, compress_ratio=2, fake_quant_fp4=True)
+    ref2 = indexer.fwd(quant._fake_quant_fp4_block(q, 32), quant._fake_quant_fp4_block(k, 32), w, compress_ratio=2)
+    assert torch.equal(out2, ref2)
+    out2.backward(dl)
+    dq2, dk2, _ = indexer.bwd(quant._fake_quant_fp4_block(q, 32), quant._fake_quant_fp4_block(k, 32), w, dl,
+                              compress_ratio=2)
+    assert torch.equal(qg2.grad, dq2) and torch.equal(kg2.grad, dk2)
