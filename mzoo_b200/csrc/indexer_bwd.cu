@@ -30,7 +30,7 @@ struct Cfg {
   static constexpr int Q_BYTES = NMAX * DI * 2;
   static constexpr int K_BYTES = BM * DI * 2;
   static constexpr int DR_BYTES = BM * NMAX * 2;  // dr tile [key][(token, head)] bf16
-  static constexpr int SMEM_A = Q_BYTES + 2 * K_BYTES + DR_BYTES + NMAX * 4 * 2 + 512;  // + w, dw
+  static constexpr int SMEM_A = Q_BYTES + 2 * K_BYTES + DR_BYTES + NMAX * 4 * 5 + 512;  // + w, 4 dw partials
   static constexpr int SMEM_B = 2 * Q_BYTES + K_BYTES + 2 * NMAX * 4 + 512;
   static_assert(SMEM_A <= 232448 && SMEM_B <= 232448, "smem");
 };
@@ -74,8 +74,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t* ks = qs + C::Q_BYTES;
   uint8_t* drs = ks + 2 * C::K_BYTES;
   float* wsm = reinterpret_cast<float*>(drs + C::DR_BYTES);
-  float* dwsm = wsm + C::NMAX;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(dwsm + C::NMAX);
+  float* dwsm = wsm + C::NMAX;  // [4 lane quarters][NMAX] partial sums: each column is owned by one
+                                // warpgroup, each (quarter, column) by one warp -> no atomics
+  uint64_t* bars = reinterpret_cast<uint64_t*>(dwsm + 4 * C::NMAX);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + A_NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   if (smem_u32(smem) & 1023) {
@@ -185,7 +186,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = et; i < C::NMAX; i += 256) {
         const int s = s0 + i / a.Hi;
         wsm[i] = (i < a.N && s < a.S) ? a.w[((long long)b * a.S + s) * a.Hi + i % a.Hi] : 0.0f;
-        dwsm[i] = 0.0f;
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) dwsm[qq * C::NMAX + i] = 0.0f;
       }
       tc::bar_sync(1, 256);
       bool ok = true;
@@ -229,7 +231,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             // lane l now holds column (l & 15)'s partial over the 16 lanes sharing bit 4
             const float other = __shfl_xor_sync(0xffffffffu, dwv[0], 16);
-            if (lane < 16) atomicAdd(&dwsm[c0 + lane], dwv[0] + other);
+            if (lane < 16) dwsm[quarter * C::NMAX + c0 + lane] += dwv[0] + other;
           }
         }
         tc::fence_async_smem();
@@ -269,10 +271,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
       tc::fence_before_sync();
-      tc::bar_sync(1, 256);  // every dw atomic of this block landed
+      tc::bar_sync(1, 256);  // every dw partial of this block landed
       for (int i = et; i < a.N; i += 256) {
         const int s = s0 + i / a.Hi;
-        if (s < a.S) a.dw[((long long)b * a.S + s) * a.Hi + i % a.Hi] = dwsm[i];
+        const float v = ((dwsm[i] + dwsm[C::NMAX + i]) + dwsm[2 * C::NMAX + i]) + dwsm[3 * C::NMAX + i];
+        if (s < a.S) a.dw[((long long)b * a.S + s) * a.Hi + i % a.Hi] = v;
       }
       __syncwarp();
       if (lane == 0 && n > 0) tc::mbar_arrive(&bars[A_DQ_EMPTY]);
