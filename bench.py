@@ -595,19 +595,6 @@ def c4_lens(torch, n=None):
     return torch.randint(C4["L_lo"], C4["L_hi"] + 1, (C4["B"] if n is None else n,), generator=g)
 
 
-def shard_sequences(lens, world: int) -> list:
-    """Greedy longest-first assignment of sequences to ranks by context length (balances the
-    indexer's per-sequence key stream); returns the sorted sequence ids of each rank."""
-    order = sorted(range(len(lens)), key=lambda b: -int(lens[b]))
-    load = [0] * world
-    owned = [[] for _ in range(world)]
-    for b in order:
-        r = min(range(world), key=lambda i: load[i])
-        owned[r].append(b)
-        load[r] += int(lens[b])
-    return [sorted(o) for o in owned]
-
-
 def _random_rows(torch, n_rows: int, device, gen, chunk: int = 1 << 20):
     """n_rows KV rows of 672 B with valid e4m3 codes (no NaN), scales in [1/448, 4/448] and
     N(0,1) bf16 rope channels."""
@@ -686,6 +673,7 @@ def c4_bytes(lens_sub) -> float:
 
 def bench_decode(args, torch, dist, rank, world, device) -> dict:
     lens = c4_lens(torch)
+    from mzoo_b200.sharding import shard_sequences
     mine = shard_sequences(lens.tolist(), world)[rank]
     x = c4_inputs(torch, device, mine, lens)
     nbytes = c4_bytes([lens[b] for b in mine])
