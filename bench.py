@@ -72,19 +72,41 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
-    def stop(self) -> dict:
+    def _rows(self) -> list:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        return rows
+
+    def ready(self, timeout: float = 5.0) -> None:
+        """Block until nvidia-smi has written its first sample (it takes ~0.1-1 s to start),
+        and remember how many rows precede the timed region."""
+        t0 = time.time()
+        while self.proc is not None and not self._rows() and time.time() - t0 < timeout:
+            time.sleep(0.02)
+        self.n0 = len(self._rows()) if self.proc is not None else 0
+
+    def stop(self, busy=None, min_samples: int = 2, timeout: float = 3.0) -> dict:
+        """Stop sampling.  A timed region of a few milliseconds is shorter than the 200 ms
+        sampling period, so ``busy`` (one more step of the same workload) keeps the GPU
+        under that load until ``min_samples`` rows were taken after the region started."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        t0 = time.time()
+        n0 = getattr(self, "n0", 0)
+        while busy is not None and len(self._rows()) < n0 + min_samples and time.time() - t0 < timeout:
+            busy()
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        rows = self._rows()[n0:]
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
@@ -162,13 +184,14 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk), check=False)
     step = lambda: indexer.attn(q8, k8, w, **kw)  # noqa: E731
     timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    sampler.ready()
     if dist:
         dist.barrier()
-    sampler = ClockSampler(device.index)
-    sampler.start()
     t_steps = timer.run(step, args.steps)
     # the dominant kernel alone (score GEMM), for the roofline
     qp, kp, wp, sqp, skp, scale, dt = indexer._prep(q8, k8, w, (sq, sk), None)
@@ -194,7 +217,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     for _ in range(2):
         e2e()
     t_e2e = timer.run(e2e, args.steps, flush=False)
-    clocks = sampler.stop()
+    clocks = sampler.stop(busy=step)
     torch.cuda.synchronize()
     code = int(err.item())
     assert code == 0, f"device error word {code}"
@@ -320,15 +343,16 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     flops = sparse_mla.pair_flops(pairs)
     step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], check=False)  # noqa: E731
     timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    sampler.ready()
     if dist:
         dist.barrier()
-    sampler = ClockSampler(device.index)
-    sampler.start()
     t_steps = timer.run(step, args.steps)
-    clocks = sampler.stop()
+    clocks = sampler.stop(busy=step)
     # end to end from pinned host buffers
     hq, hraw, hcmp, hidx = (x.cpu().pin_memory() for x in (q, raw, cmp, idx))
     dq, draw, dcmp, didx = (torch.empty_like(x, device=device) for x in (hq, hraw, hcmp, hidx))
@@ -464,15 +488,16 @@ def bench_train(args, torch, dist, rank, world, device) -> dict:
     fwd_flops, bwd_flops = c5_flops()
     timer = Timer(torch, device)
     step = lambda: c5_step(q, k, v, do)  # noqa: E731
+    sampler = ClockSampler(device.index)
+    sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    sampler.ready()
     if dist:
         dist.barrier()
-    sampler = ClockSampler(device.index)
-    sampler.start()
     t_steps = timer.run(step, args.steps)
-    clocks = sampler.stop()
+    clocks = sampler.stop(busy=step)
     # per-kernel legs for the roofline
     qf = quant.fake_quant_fp4_block(q, 32, rule="ocp")
     kf = quant.fake_quant_fp4_block(k, 32, rule="ocp")
@@ -674,12 +699,13 @@ def c4_bytes(lens_sub) -> float:
 def bench_decode(args, torch, dist, rank, world, device) -> dict:
     lens = c4_lens(torch)
     from mzoo_b200.sharding import shard_sequences
-    mine = shard_sequences(lens.tolist(), world)[rank]
+    parts = shard_sequences(lens.tolist(), world)
+    mine = parts[rank]
     x = c4_inputs(torch, device, mine, lens)
     nbytes = c4_bytes([lens[b] for b in mine])
     total_bytes = c4_bytes(lens.tolist())
     n_mine = len(mine)
-    shard = -(-C4["B"] // world)
+    shard = max(len(p) for p in parts)  # greedy-by-length shards differ in count
     gather_buf = torch.empty(world * shard, 128, 512, dtype=torch.bfloat16, device=device) if dist else None
 
     def step():
@@ -691,15 +717,16 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
         return o
 
     timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    sampler.ready()
     if dist:
         dist.barrier()
-    sampler = ClockSampler(device.index)
-    sampler.start()
     t_steps = timer.run(step, args.steps)
-    clocks = sampler.stop()
+    clocks = sampler.stop(busy=lambda: c4_step(x))  # no collective: ranks may loop unequally
     # dominant kernel legs
     from mzoo_b200 import indexer
     qp, kp, wp, sqp, skp, scale, dt = indexer._prep(x["q8"], x["k8"], x["w"], (x["sq"], x["sk"]), None)

@@ -15,8 +15,10 @@
 // query rows in N (up to 256 = T_q tokens x Hi heads), so the per-token head reduction is
 // a per-thread loop over TMEM columns.  Persistent CTAs, one per SM; warp 0 issues TMA
 // loads (K tiles in a 4-stage ring, Q tiles double-buffered), warp 1 issues tcgen05.mma
-// into two TMEM accumulators, warps 4-11 run the relu * weight reduction epilogue and
-// store fp32 scores.  The key loop stops at the block's causal frontier.
+// into two TMEM accumulators, warps 2-9 run the relu * weight reduction epilogue (each
+// warpgroup drains one accumulator, i.e. every other tile) and store fp32 scores.  The key
+// loop stops at the block's causal frontier; with few (batch, query block) pairs (decode)
+// the key range is split into chunks so every SM gets work.
 //
 // Kernel 2 (`topk_kernel`): one CTA per query row.  The fp32 tensor-core scores carry a
 // rounding error bounded by delta = eps * A_s * max_t B_t, with
@@ -30,14 +32,17 @@
 //   c_h = w*sq (exact), dot_h = sum_i q*k (fp64, sequential), p_h = c_h*max(dot_h, 0),
 //   acc = ((p_0 + p_1) + ...) + p_{Hi-1}, score = (acc * sk) * scale,
 // with ties to the lower index -- which is what the CPU oracle computes.
+#include <algorithm>
+
 #include "tc.cuh"
 
 namespace mzb {
 namespace idx {
 
 constexpr int BM = 128;  // keys per tile = MMA M
-constexpr int NTHREADS = 384;
-constexpr int EPI_WARP0 = 4;
+constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
+constexpr int EPI_WARP0 = 2;   // epilogue warp w reads TMEM lanes 32 * (w % 4): warps 2-5 and 6-9
+                               // each cover all four lane quarters
 constexpr int NEPI = 256;
 constexpr int KB_PARTS = 16;  // per-batch partial maxima of B_t
 
@@ -56,7 +61,7 @@ struct Cfg {
   static constexpr int KS_RAW = (BUDGET - Q_BUFS * Q_BYTES) / K_BYTES;
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
-  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + NMAX * 4 + 256 + 1024;
+  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
 };
@@ -72,6 +77,7 @@ struct ScoreArgs {
   long long q_offset;
   float scale;
   int write_tail;
+  int kc, n_kc;  // key tiles per chunk, chunks per (batch, query block)
   int* err;
 };
 
@@ -96,7 +102,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t* qs = smem;
   uint8_t* ks = qs + C::Q_BUFS * C::Q_BYTES;
   float* cw = reinterpret_cast<float*>(ks + C::K_STAGES * C::K_BYTES);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cw + C::NMAX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(cw + 8 * C::NMAX);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 2;
   uint64_t* k_full = bars + 4;
@@ -112,7 +118,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
       tc::mbar_init(&acc_full[i], 1);
-      tc::mbar_init(&acc_empty[i], NEPI / 32);
+      tc::mbar_init(&acc_empty[i], 4);  // the four warps of the warpgroup that owns buffer i
     }
     for (int i = 0; i < C::K_STAGES; ++i) {
       tc::mbar_init(&k_full[i], 1);
@@ -131,13 +137,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  // item = (key chunk, query block, batch); chunk-major so full chunks go first
   const int n_tb = (a.S + a.Tq - 1) / a.Tq;
-  const int items = a.B * n_tb;
-  auto item_tiles = [&](int tb, int b) {
+  const int items = a.B * n_tb * a.n_kc;
+  struct Item {
+    int tb, b, kc, k0, k1;
+  };
+  auto item_of = [&](int it) {
+    Item r;
+    r.kc = it / (a.B * n_tb);
+    const int rem = it % (a.B * n_tb);
+    r.tb = n_tb - 1 - rem / a.B;
+    r.b = rem % a.B;
     int vis = 0;
-    for (int s = tb * a.Tq; s < min((tb + 1) * a.Tq, a.S); ++s)
-      vis = max(vis, visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T));
-    return (vis + BM - 1) / BM;
+    for (int s = r.tb * a.Tq; s < min((r.tb + 1) * a.Tq, a.S); ++s)
+      vis = max(vis, visible_of(a.q_pos, a.q_offset, r.b, a.S, s, a.ratio, a.T));
+    const int n_kt = (vis + BM - 1) / BM;
+    r.k0 = r.kc * a.kc;
+    r.k1 = min(n_kt, r.k0 + a.kc);
+    return r;
   };
 
   if (warp == 0) {
@@ -147,22 +165,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       uint32_t k_issued = 0, k_par[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint32_t q_issued = 0, q_par[2] = {0, 0};
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const int tb = n_tb - 1 - it / a.B, b = it % a.B;
+        const Item m = item_of(it);
+        if (m.k0 >= m.k1) continue;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_empty[qb], qpar ^ 1, a.err, 101)) { *abort_flag = 1; break; }
         tc::mbar_expect_tx(&q_full[qb], uint32_t(a.N) * C::R);
         for (int cb = 0; cb < C::NCB; ++cb)
           tc::tma_load_3d(qs + qb * C::Q_BYTES + cb * C::NMAX * C::SW, &tq, &q_full[qb], cb * C::SW / C::EB,
-                          tb * a.Tq * a.Hi, b);
+                          m.tb * a.Tq * a.Hi, m.b);
         q_issued |= 1u << qb;
         q_par[qb] = qpar;
-        const int n_kt = item_tiles(tb, b);
-        for (int kt = 0; kt < n_kt; ++kt) {
+        for (int kt = m.k0; kt < m.k1; ++kt) {
           if (!tc::mbar_wait(&k_empty[ks_i], ks_ph ^ 1, a.err, 102)) { *abort_flag = 1; break; }
           tc::mbar_expect_tx(&k_full[ks_i], C::K_BYTES);
           for (int cb = 0; cb < C::NCB; ++cb)
             tc::tma_load_3d(ks + ks_i * C::K_BYTES + cb * BM * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB,
-                            kt * BM, b);
+                            kt * BM, m.b);
           k_issued |= 1u << ks_i;
           k_par[ks_i] = ks_ph;
           if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
@@ -183,12 +201,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t idesc = tc::make_idesc(BM, a.N, kFmt, kFmt);
       int ks_i = 0, ks_ph = 0, acc = 0, acc_ph = 0, qi = 0;
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const int tb = n_tb - 1 - it / a.B, b = it % a.B;
+        const Item m = item_of(it);
+        if (m.k0 >= m.k1) continue;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_full[qb], qpar, a.err, 103)) { *abort_flag = 1; break; }
         const uint32_t q_base = smem_u32(qs + qb * C::Q_BYTES);
-        const int n_kt = item_tiles(tb, b);
-        for (int kt = 0; kt < n_kt; ++kt) {
+        for (int kt = m.k0; kt < m.k1; ++kt) {
           if (!tc::mbar_wait(&acc_empty[acc], acc_ph ^ 1, a.err, 104)) { *abort_flag = 1; break; }
           if (!tc::mbar_wait(&k_full[ks_i], ks_ph, a.err, 105)) { *abort_flag = 1; break; }
           tc::fence_after_sync();
@@ -213,34 +231,85 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp >= EPI_WARP0) {
     // ---------------------------------------------------------------- epilogue
+    // Warpgroup g (warps 2-5 / 6-9) drains accumulator buffer g, i.e. every other tile,
+    // all tokens of it.  Each warp keeps its own copy of the item's weights c = w * sq.
     const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..255
-    const int quarter = warp & 3;
-    const int wg = (warp - EPI_WARP0) >> 2;  // 0/1: even / odd tokens
-    const int row = quarter * 32 + lane;     // key row inside the tile
-    int acc = 0, acc_ph = 0;
+    const int ew = warp - EPI_WARP0;
+    const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) ...
+    const int wg = ew >> 2;
+    const int row = quarter * 32 + lane;  // key row inside the tile
+    float* cwp = cw + ew * C::NMAX;
+    uint32_t tcount = 0;
+    int acc_ph = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-      const int tb = n_tb - 1 - it / a.B, b = it % a.B;
-      const int s0 = tb * a.Tq;
-      tc::bar_sync(1, NEPI);
-      for (int i = et; i < a.N; i += NEPI) {
+      const Item m = item_of(it);
+      const int s0 = m.tb * a.Tq;
+      if (a.write_tail && m.kc == 0) {  // keys no token of this block can see
+        int n_kt = 0;
+        for (int s = s0; s < min(s0 + a.Tq, a.S); ++s)
+          n_kt = max(n_kt, (visible_of(a.q_pos, a.q_offset, m.b, a.S, s, a.ratio, a.T) + BM - 1) / BM);
+        for (int t = 0; t < a.Tq; ++t) {
+          const int s = s0 + t;
+          if (s >= a.S) break;
+          float* rowp = a.scores + (size_t(m.b) * a.S + s) * a.T;
+          for (int j = n_kt * BM + et; j < a.T; j += NEPI) rowp[j] = -INFINITY;
+        }
+      }
+      if (m.k0 >= m.k1) continue;
+      const int tq_n = min(a.Tq, a.S - s0);  // real tokens in this block
+      for (int i = lane; i < a.N; i += 32) {
         const int s = s0 + i / a.Hi, h = i % a.Hi;
         float c = 0.0f;
         if (s < a.S) {
-          const size_t o = (size_t(b) * a.S + s) * a.Hi + h;
+          const size_t o = (size_t(m.b) * a.S + s) * a.Hi + h;
           c = a.w[o] * (a.sq ? a.sq[o] : 1.0f);
         }
-        cw[i] = c;
+        cwp[i] = c;
       }
-      tc::bar_sync(1, NEPI);
-      const int n_kt = item_tiles(tb, b);
-      for (int kt = 0; kt < n_kt; ++kt) {
-        if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { *abort_flag = 1; break; }
-        tc::fence_after_sync();
+      // visible keys of token t, held by lane t (Tq <= 16)
+      const int vis_l = lane < tq_n ? visible_of(a.q_pos, a.q_offset, m.b, a.S, s0 + lane, a.ratio, a.T) : 0;
+      __syncwarp();
+      bool ok = true;
+      for (int kt = m.k0; kt < m.k1; ++kt, ++tcount) {
+        const int acc = int(tcount & 1u);
+        if (acc != wg) continue;
+        // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
-        const float skj = (j < a.T) ? (a.sk ? a.sk[size_t(b) * a.T + j] : 1.0f) * a.scale : 0.0f;
+        const float skj = (j < a.T) ? (a.sk ? __ldg(a.sk + size_t(m.b) * a.T + j) : 1.0f) * a.scale : 0.0f;
+        if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
+        acc_ph ^= 1;
+        tc::fence_after_sync();
         const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * C::NMAX);
-        for (int t = wg; t < a.Tq; t += 2) {
-          float sum = 0.0f;
+        if (a.Hi == 64) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
+          for (int t = 0; t < tq_n; ++t) {
+            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // 8 independent fp32 sums
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+              uint32_t r[32];
+              tc::tmem_ld32(tbase + t * 64 + half * 32, r);
+              tc::tmem_wait_ld();
+              const float4* cq4 = reinterpret_cast<const float4*>(cwp + t * 64 + half * 32);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 cc = cq4[i];
+                const uint64_t x01 = pack_f32x2(fmaxf(__uint_as_float(r[4 * i + 0]), 0.0f),
+                                                fmaxf(__uint_as_float(r[4 * i + 1]), 0.0f));
+                const uint64_t x23 = pack_f32x2(fmaxf(__uint_as_float(r[4 * i + 2]), 0.0f),
+                                                fmaxf(__uint_as_float(r[4 * i + 3]), 0.0f));
+                acc[(i & 1) * 2 + 0] = ffma_f32x2(x01, pack_f32x2(cc.x, cc.y), acc[(i & 1) * 2 + 0]);
+                acc[(i & 1) * 2 + 1] = ffma_f32x2(x23, pack_f32x2(cc.z, cc.w), acc[(i & 1) * 2 + 1]);
+              }
+            }
+            const float2 p0 = unpack_f32x2(acc[0]), p1 = unpack_f32x2(acc[1]);
+            const float2 p2 = unpack_f32x2(acc[2]), p3 = unpack_f32x2(acc[3]);
+            const float sum = ((p0.x + p0.y) + (p1.x + p1.y)) + ((p2.x + p2.y) + (p3.x + p3.y));
+            const int vis = __shfl_sync(0xffffffffu, vis_l, t);
+            if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
+          }
+        } else
+        for (int t = 0; t < tq_n; ++t) {
+          // four independent partial sums (one per 16-head chunk) keep the FMA chains short
+          float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
           for (int h0 = 0; h0 < a.Hi; h0 += 64) {
             uint32_t r[4][16];
             const int nch = min(4, (a.Hi - h0) >> 4);
@@ -251,39 +320,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               if (c < nch) {
-                const float4* cwp = reinterpret_cast<const float4*>(cw + t * a.Hi + h0 + c * 16);
+                const float4* cq4 = reinterpret_cast<const float4*>(cwp + t * a.Hi + h0 + c * 16);
 #pragma unroll
                 for (int q4 = 0; q4 < 4; ++q4) {
-                  const float4 cc = cwp[q4];
-                  sum = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 0]), 0.0f), cc.x, sum);
-                  sum = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 1]), 0.0f), cc.y, sum);
-                  sum = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 2]), 0.0f), cc.z, sum);
-                  sum = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 3]), 0.0f), cc.w, sum);
+                  const float4 cc = cq4[q4];
+                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 0]), 0.0f), cc.x, part[c]);
+                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 1]), 0.0f), cc.y, part[c]);
+                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 2]), 0.0f), cc.z, part[c]);
+                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 3]), 0.0f), cc.w, part[c]);
                 }
               }
             }
           }
-          const int s = s0 + t;
-          if (s < a.S && j < a.T) {
-            const int vis = visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T);
-            a.scores[(size_t(b) * a.S + s) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
-          }
+          const float sum = (part[0] + part[1]) + (part[2] + part[3]);
+          const int vis = __shfl_sync(0xffffffffu, vis_l, t);
+          if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
         }
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
-        acc ^= 1;
-        if (acc == 0) acc_ph ^= 1;
       }
-      if (a.write_tail) {  // keys no token of this block can see
-        const int t0 = n_kt * BM;
-        for (int t = 0; t < a.Tq; ++t) {
-          const int s = s0 + t;
-          if (s >= a.S) break;
-          float* rowp = a.scores + (size_t(b) * a.S + s) * a.T;
-          for (int j = t0 + et; j < a.T; j += NEPI) rowp[j] = -INFINITY;
-        }
-      }
+      if (!ok) { *abort_flag = 1; break; }
+      __syncwarp();  // every lane is done with cwp before the next item rewrites it
     }
   }
 
@@ -314,8 +372,7 @@ struct TopkArgs {
   int* err;
 };
 
-constexpr int TK_THREADS = 256;
-constexpr int CAND_MAX = 2048;
+constexpr int CAND_MAX = 512;  // band keys re-scored exactly (the band holds ~0-2)
 
 __device__ __forceinline__ uint32_t f2key(float f) {
   uint32_t u = __float_as_uint(f);
@@ -330,37 +387,137 @@ __device__ __forceinline__ float elem_f(const uint8_t* p, int i, int fp8) {
   return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
 }
 
-// B_t = |scale| * sk_t * ||k_t||_2, partial maxima per (batch, part).
-__global__ void kbound_kernel(TopkArgs a) {
-  const int b = blockIdx.x, part = blockIdx.y;
-  const int eb = a.fp8 ? 1 : 2;
-  float m = 0.0f;
-  const int per = (a.T + KB_PARTS - 1) / KB_PARTS;
-  const int t_lo = part * per, t_hi = min(a.T, t_lo + per);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = t_lo + warp; t < t_hi; t += blockDim.x >> 5) {
-    const uint8_t* kr = a.k + (size_t(b) * a.T + t) * a.Di * eb;
-    float ss = 0.0f;
-    for (int i = lane; i < a.Di; i += 32) {
-      const float v = elem_f(kr, i, a.fp8);
-      ss = fmaf(v, v, ss);
+// sum of squares of the 16 bytes at p (16 e4m3 codes or 8 bf16 values)
+__device__ __forceinline__ float sumsq16(const uint4 v, int fp8) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (fp8) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> (16 * hh)), __NV_E4M3);
+        const float2 f = __half22float2(__half2(hr));
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+    } else {
+      const float lo = __uint_as_float(w[i] << 16), hi = __uint_as_float(w[i] & 0xFFFF0000u);
+      ss = fmaf(lo, lo, fmaf(hi, hi, ss));
     }
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float sk = a.sk ? a.sk[size_t(b) * a.T + t] : 1.0f;
-    m = fmaxf(m, fabsf(a.scale) * fabsf(sk) * sqrtf(ss));
   }
-  __shared__ float red[32];
+  return ss;
+}
+
+// Upper bound of B_t = |scale| * sk_t * ||k_t||_2 over the keys any query of batch b can
+// see, as partial maxima per (batch, part).  Exact norms (one 16-byte vector per lane) when
+// many queries share the keys; for one- or few-query rows (decode) with e4m3 keys, the
+// bound ||k_t|| <= 448 * sqrt(Di) (448 = largest finite e4m3) so that only the per-key
+// scales are read -- that widens the exactly re-scored band by at most sqrt(Di) times,
+// which costs little with so few rows.
+__global__ void __launch_bounds__(256) kbound_kernel(TopkArgs a) {
+  const int b = blockIdx.x, part = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float red[8];
+  __shared__ int red_v[8];
+  int tv = 0;
+  if (a.q_pos) {
+    for (int s = tid; s < a.S; s += blockDim.x) tv = max(tv, visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T));
+  } else {
+    tv = visible_keys(a.q_offset, a.S - 1, a.ratio, a.T);  // visibility grows with s
+  }
+  for (int o = 16; o; o >>= 1) tv = max(tv, __shfl_xor_sync(0xffffffffu, tv, o));
+  if (lane == 0) red_v[warp] = tv;
+  __syncthreads();
+  tv = 0;
+  for (int i = 0; i < 8; ++i) tv = max(tv, red_v[i]);
+  const int per = (tv + KB_PARTS - 1) / KB_PARTS;
+  const int t_lo = part * per, t_hi = min(tv, t_lo + per);
+  const float asc = fabsf(a.scale);
+  const int eb = a.fp8 ? 1 : 2;
+  const int rb = a.Di * eb;  // row bytes
+  const int lpr = rb / 16;   // lanes per row
+  float m = 0.0f;
+  if (a.fp8 && a.S <= 16) {
+    float mk = 0.0f;
+    for (int t = t_lo + tid; t < t_hi; t += blockDim.x) mk = fmaxf(mk, fabsf(a.sk[size_t(b) * a.T + t]));
+    m = asc * mk * (448.0f * sqrtf(float(a.Di))) * 1.0001f;
+  } else if (rb % 16 == 0 && lpr <= 32 && (lpr & (lpr - 1)) == 0) {
+    const int rows = blockDim.x / lpr;
+    for (int t0 = t_lo; t0 < t_hi; t0 += rows) {  // uniform trip count: shuffles see full warps
+      const int t = t0 + tid / lpr;
+      float ss = 0.0f;
+      if (t < t_hi) ss = sumsq16(*reinterpret_cast<const uint4*>(a.k + (size_t(b) * a.T + t) * rb + (tid % lpr) * 16),
+                                 a.fp8);
+      for (int o = lpr >> 1; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (t < t_hi) {
+        const float sk = a.sk ? fabsf(a.sk[size_t(b) * a.T + t]) : 1.0f;
+        m = fmaxf(m, asc * sk * sqrtf(ss));
+      }
+    }
+  } else {
+    for (int t = t_lo + warp; t < t_hi; t += blockDim.x >> 5) {
+      const uint8_t* kr = a.k + (size_t(b) * a.T + t) * rb;
+      float ss = 0.0f;
+      for (int i = lane; i < a.Di; i += 32) {
+        const float v = elem_f(kr, i, a.fp8);
+        ss = fmaf(v, v, ss);
+      }
+      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float sk = a.sk ? fabsf(a.sk[size_t(b) * a.T + t]) : 1.0f;
+      m = fmaxf(m, asc * sk * sqrtf(ss));
+    }
+  }
   for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     float r = 0.0f;
-    for (int i = 0; i < int(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+    for (int i = 0; i < 8; ++i) r = fmaxf(r, red[i]);
     const_cast<float*>(a.kbmax)[b * KB_PARTS + part] = r;
   }
 }
 
+// exact fp64 value of an e4m3 code pair (the low and high byte of a 16-bit word)
+__device__ __forceinline__ void e4m3x2_to_f64(uint32_t w16, double& lo, double& hi) {
+  const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w16 & 0xFFFFu), __NV_E4M3);
+  const float2 f = __half22float2(__half2(hr));
+  lo = double(f.x);
+  hi = double(f.y);
+}
+
+constexpr int BLIST = 256;  // keys of the selected linear bin ranked directly
+
+// exclusive prefix (over the block, in thread order) of `cnt`; also returns the total.
+// Uses sh[0..NW) and sh[32..32+NW], sh[64]; two __syncthreads.
+template <int NT>
+__device__ __forceinline__ int block_exclusive_scan(int cnt, int* sh, int& total) {
+  constexpr int NW = NT / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = cnt;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) sh[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v0 = lane < NW ? sh[lane] : 0;
+    int x = v0;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += v;
+    }
+    if (lane < NW) sh[32 + lane] = x - v0;
+    if (lane == NW - 1) sh[64] = x;
+  }
+  __syncthreads();
+  total = sh[64];
+  return sh[32 + warp] + incl - cnt;
+}
+
+template <int TK_THREADS>
 __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
+  constexpr int NW = TK_THREADS / 32;
   extern __shared__ uint8_t sm[];
   const int row = blockIdx.x;  // b * S + s
   const int b = row / a.S, s = row % a.S;
@@ -372,158 +529,324 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
     return;
   }
   const int eb = a.fp8 ? 1 : 2;
-  const int qstride = a.Di * eb + 4;  // padded rows: lane-varying heads hit different banks
+  const int rb = a.Di * eb;  // bytes per q head row / k row
   // smem carve-up
   uint32_t* keys = reinterpret_cast<uint32_t*>(sm);                        // V
   uint32_t* sel = keys + V;                                                // ceil(V/32)
   const int nsel = (V + 31) >> 5;
-  int* cand = reinterpret_cast<int*>(sel + nsel);                          // CAND_MAX
+  uint32_t* blist = sel + nsel;                                            // BLIST
+  int* cand = reinterpret_cast<int*>(blist + BLIST);                       // CAND_MAX
   double* exact = reinterpret_cast<double*>(                               // CAND_MAX
       (reinterpret_cast<uintptr_t>(cand + CAND_MAX) + 7) & ~uintptr_t(7));
   double* pbuf = exact + CAND_MAX;                                         // 8 warps x Hi
   double* cq = pbuf + 8 * a.Hi;                                            // Hi
-  uint8_t* qrow = reinterpret_cast<uint8_t*>(cq + a.Hi);                   // Hi x qstride
+  double* kdall = cq + a.Hi;                                               // 8 warps x Di
   __shared__ int hist[256];
-  __shared__ uint32_t sh_prefix, sh_kk;
-  __shared__ int n_in, n_cand, sh_scan[TK_THREADS];
+  __shared__ uint32_t sh_kk, sh_theta;
+  __shared__ int sh_bin, n_in, n_cand, n_bl, sh_scan[96];
   __shared__ float sh_A;
-
-  const float* srow = a.scores + size_t(row) * a.T;
-  for (int j = tid; j < V; j += TK_THREADS) keys[j] = f2key(srow[j]);
-  for (int i = tid; i < nsel; i += TK_THREADS) sel[i] = 0u;
-  // stage the query row and its exact weights; A_s = sum_h |c_h| ||q_h||
-  const uint8_t* qg = a.q + size_t(row) * a.Hi * a.Di * eb;
-  for (int i = tid; i < a.Hi * a.Di * eb; i += TK_THREADS) {
-    const int h = i / (a.Di * eb), o = i % (a.Di * eb);
-    qrow[h * qstride + o] = qg[i];
+  __shared__ uint32_t sh_kmin, sh_kmax, sh_bmin, sh_bmax;
+  if (tid == 0) {
+    sh_kmin = 0xFFFFFFFFu; sh_kmax = 0u; sh_bmin = 0xFFFFFFFFu; sh_bmax = 0u;
+    sh_A = 0.0f; n_in = 0; n_cand = 0; n_bl = 0;
   }
+  __syncthreads();
+
+  // pass 1: order-preserving keys, their range; exact head weights; A_s
+  const float* srow = a.scores + size_t(row) * a.T;
+  {
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int j = tid; j < V; j += TK_THREADS) {
+      const uint32_t kx = f2key(srow[j]);
+      keys[j] = kx;
+      kmin = min(kmin, kx);
+      kmax = max(kmax, kx);
+    }
+    for (int o = 16; o; o >>= 1) {
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) { atomicMin(&sh_kmin, kmin); atomicMax(&sh_kmax, kmax); }
+  }
+  for (int i = tid; i < nsel; i += TK_THREADS) sel[i] = 0u;
+  const uint8_t* qg = a.q + size_t(row) * a.Hi * rb;
   for (int h = tid; h < a.Hi; h += TK_THREADS) {
     const size_t o = size_t(row) * a.Hi + h;
     cq[h] = double(a.w[o]) * double(a.sq ? a.sq[o] : 1.0f);
   }
-  if (tid == 0) { sh_A = 0.0f; n_in = 0; n_cand = 0; }
-  __syncthreads();
   {
+    // A_s = sum_h |c_h| ||q_h||: one thread per head row, 16-byte loads (rows are 4-byte
+    // multiples; whole 16-byte vectors when they are 16-byte multiples)
     float part = 0.0f;
-    for (int h = warp; h < a.Hi; h += TK_THREADS / 32) {
+    for (int h = tid; h < a.Hi; h += TK_THREADS) {
+      const uint8_t* qh = qg + size_t(h) * rb;
       float ss = 0.0f;
-      for (int i = lane; i < a.Di; i += 32) {
-        const float v = elem_f(qrow + h * qstride, i, a.fp8);
-        ss = fmaf(v, v, ss);
+      if (rb % 16 == 0) {
+        for (int i = 0; i < rb; i += 16) ss += sumsq16(__ldg(reinterpret_cast<const uint4*>(qh + i)), a.fp8);
+      } else {
+        for (int i = 0; i < a.Di; ++i) {
+          const float v = elem_f(qh, i, a.fp8);
+          ss = fmaf(v, v, ss);
+        }
       }
-      for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      part += float(fabs(cq[h])) * sqrtf(ss);
+      const float ch = fabsf(a.w[size_t(row) * a.Hi + h] * (a.sq ? a.sq[size_t(row) * a.Hi + h] : 1.0f));
+      part += ch * sqrtf(ss);
     }
-    if (lane == 0) atomicAdd(&sh_A, part);
+    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+    if (lane == 0 && warp * 32 < a.Hi) atomicAdd(&sh_A, part);
   }
-  // radix select: the topk-th largest key (MSB-first, 8-bit digits)
-  uint32_t prefix = 0, mask = 0, kk = a.topk;
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
+  __syncthreads();
+
+  // The topk-th largest key, exactly.  Pass 2 histograms the scores into 256 linear bins
+  // over [min, max] -- a monotone map, so the k-th largest lies in one bin, and the bins
+  // spread any score distribution (keys of one row share their leading bits).  Pass 3
+  // gathers that bin's keys; up to BLIST of them are ranked directly, more fall back to a
+  // radix select (MSB first, 8-bit digits, below the bits the bin's keys share).
+  const float vmin = key2f(sh_kmin), vmax = key2f(sh_kmax);
+  const float inv = 256.0f / (vmax - vmin);
+  const bool binned = vmax > vmin && inv < 1e30f;
+  auto bin_of = [&](uint32_t kx) {  // monotone in the score; always in [0, 255]
+    const float f = (key2f(kx) - vmin) * inv;
+    return f >= 255.0f ? 255 : (f > 0.0f ? int(f) : 0);
+  };
+  // warp 0: the digit (bin) holding the kk-th largest of `hist`, counting from the top
+  auto pick = [&](uint32_t kk_in) {
+    int cnt[8], tot = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { cnt[i] = hist[255 - 8 * lane - i]; tot += cnt[i]; }
+    int incl = tot;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - tot;
+    if (excl < int(kk_in) && int(kk_in) <= incl) {
+      int run = excl;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (run < int(kk_in) && int(kk_in) <= run + cnt[i]) {
+          sh_bin = 255 - 8 * lane - i;
+          sh_kk = kk_in - run;
+        }
+        run += cnt[i];
+      }
+    }
+  };
+  uint32_t kk = a.topk;
+  uint32_t prefix = sh_kmin;  // all keys equal: that key
+  bool done = !binned;
+  if (binned) {
     for (int i = tid; i < 256; i += TK_THREADS) hist[i] = 0;
     __syncthreads();
-    for (int j = tid; j < V; j += TK_THREADS) {
-      const uint32_t kx = keys[j];
-      if ((kx & mask) == prefix) atomicAdd(&hist[(kx >> shift) & 255], 1);
-    }
+    for (int j = tid; j < V; j += TK_THREADS) atomicAdd(&hist[bin_of(keys[j])], 1);
     __syncthreads();
-    if (warp == 0) {
-      // lane l owns bins 255-8l .. 248-8l (descending)
-      int cnt[8], tot = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) { cnt[i] = hist[255 - 8 * lane - i]; tot += cnt[i]; }
-      int incl = tot;
-      for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const int excl = incl - tot;
-      if (excl < int(kk) && int(kk) <= incl) {
-        int run = excl;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (run < int(kk) && int(kk) <= run + cnt[i]) {
-            sh_prefix = prefix | (uint32_t(255 - 8 * lane - i) << shift);
-            sh_kk = kk - run;
-          }
-          run += cnt[i];
+    if (warp == 0) pick(kk);
+    __syncthreads();
+    const int bsel = sh_bin;
+    kk = sh_kk;
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int j0 = 0; j0 < V; j0 += TK_THREADS) {
+      const int j = j0 + tid;
+      const uint32_t kx = j < V ? keys[j] : 0u;
+      const bool in = j < V && bin_of(kx) == bsel;
+      const uint32_t wm = __ballot_sync(0xffffffffu, in);
+      if (wm) {
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&n_bl, __popc(wm));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int at = base + __popc(wm & ((1u << lane) - 1u));
+        if (in) {
+          if (at < BLIST) blist[at] = kx;
+          kmin = min(kmin, kx);
+          kmax = max(kmax, kx);
         }
       }
     }
+    for (int o = 16; o; o >>= 1) {
+      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
+    }
+    if (lane == 0) { atomicMin(&sh_bmin, kmin); atomicMax(&sh_bmax, kmax); }
     __syncthreads();
-    prefix = sh_prefix;
-    kk = sh_kk;
-    mask |= 255u << shift;
+    const int nb = n_bl;
+    if (nb <= BLIST) {
+      // rank directly: the kk-th largest has (#greater < kk <= #greater + #equal)
+      for (int i = tid; i < nb; i += TK_THREADS) {
+        const uint32_t kx = blist[i];
+        int gt = 0, eq = 0;
+        for (int o = 0; o < nb; ++o) {
+          const uint32_t y = blist[o];
+          gt += y > kx;
+          eq += y == kx;
+        }
+        if (gt < int(kk) && int(kk) <= gt + eq) sh_theta = kx;  // equal keys write equal values
+      }
+      __syncthreads();
+      prefix = sh_theta;
+      done = true;
+    } else {
+      prefix = sh_bmin;
+      const uint32_t kdiff = sh_bmin ^ sh_bmax;
+      int hi_bit = kdiff ? 31 - __clz(kdiff) : -1;
+      // bits above hi_bit are common to the bin's keys (all of them when they are equal)
+      uint32_t mask = hi_bit < 0 ? 0xFFFFFFFFu : (hi_bit >= 31 ? 0u : ~((2u << hi_bit) - 1u));
+      prefix &= mask;
+      while (hi_bit >= 0) {
+        const int width = min(8, hi_bit + 1);
+        const int shift = hi_bit - width + 1;
+        const uint32_t dmask = (1u << width) - 1u;
+        for (int i = tid; i < 256; i += TK_THREADS) hist[i] = 0;
+        __syncthreads();
+        for (int j = tid; j < V; j += TK_THREADS) {
+          const uint32_t kx = keys[j];
+          if ((kx & mask) == prefix && bin_of(kx) == bsel) atomicAdd(&hist[(kx >> shift) & dmask], 1);
+        }
+        __syncthreads();
+        if (warp == 0) pick(kk);
+        __syncthreads();
+        prefix |= uint32_t(sh_bin) << shift;
+        kk = sh_kk;
+        mask |= dmask << shift;
+        hi_bit -= width;
+      }
+      done = true;
+    }
   }
+  (void)done;
   const float theta = key2f(prefix);
   float kbm = 0.0f;
   for (int i = 0; i < KB_PARTS; ++i) kbm = fmaxf(kbm, a.kbmax[b * KB_PARTS + i]);
   const float delta = a.eps * sh_A * kbm * 1.0001f;
   const float hi_thr = __fadd_ru(theta, 2.0f * delta), lo_thr = __fsub_rd(theta, 2.0f * delta);
-  for (int j = tid; j < V; j += TK_THREADS) {
-    const float v = key2f(keys[j]);
-    if (v > hi_thr) {
-      atomicOr(&sel[j >> 5], 1u << (j & 31));
-      atomicAdd(&n_in, 1);
-    } else if (v >= lo_thr) {
-      const int c = atomicAdd(&n_cand, 1);
-      if (c < CAND_MAX) cand[c] = j;
+  // pass 4: certain keys into `sel` (one word per warp iteration, no atomics on sel); the
+  // band between the thresholds into `cand`
+  for (int j0 = 0; j0 < V; j0 += TK_THREADS) {
+    const int j = j0 + tid;
+    const float v = j < V ? key2f(keys[j]) : -INFINITY;
+    const uint32_t in_w = __ballot_sync(0xffffffffu, j < V && v > hi_thr);
+    const bool is_c = j < V && !(v > hi_thr) && v >= lo_thr;
+    const uint32_t c_w = __ballot_sync(0xffffffffu, is_c);
+    if (j - lane < V && lane == 0) {
+      sel[j >> 5] = in_w;
+      if (in_w) atomicAdd(&n_in, __popc(in_w));
+    }
+    if (c_w) {
+      int base = 0;
+      if (lane == 0) base = atomicAdd(&n_cand, __popc(c_w));
+      base = __shfl_sync(0xffffffffu, base, 0);
+      const int c = base + __popc(c_w & ((1u << lane) - 1u));
+      if (is_c && c < CAND_MAX) cand[c] = j;
     }
   }
   __syncthreads();
   const int nin = n_in, nc = n_cand;
   const int need = a.topk - nin;
-  if (nc > CAND_MAX || need < 0 || need > nc) {
+  if (need < 0 || need > nc || (nc > CAND_MAX && delta != 0.0f)) {
     if (tid == 0) atomicExch(a.err, MZB_ERR_BOUND);
     for (int i = tid; i < a.topk; i += TK_THREADS) out[i] = -1;
     return;
   }
-  // exact fp64 re-scoring, one warp per candidate; lane l owns heads l, l+32, ...
-  for (int c = warp; c < nc; c += TK_THREADS / 32) {
-    const int j = cand[c];
-    const uint8_t* kr = a.k + (size_t(b) * a.T + j) * a.Di * eb;
-    for (int h = lane; h < a.Hi; h += 32) {
-      const uint8_t* qh = qrow + h * qstride;
-      double dot = 0.0;
-      for (int i = 0; i < a.Di; ++i) dot = fma(double(elem_f(qh, i, a.fp8)), double(elem_f(kr, i, a.fp8)), dot);
-      pbuf[warp * a.Hi + h] = __dmul_rn(cq[h], dot > 0.0 ? dot : 0.0);
+  if (need == nc && nc <= CAND_MAX) {
+    // the whole band is selected: its exact order does not matter
+    for (int c = tid; c < nc; c += TK_THREADS) atomicOr(&sel[cand[c] >> 5], 1u << (cand[c] & 31));
+    __syncthreads();
+  } else if (nc > CAND_MAX) {
+    // delta == 0: every score is exactly 0 (all weights or all keys zero), so the band is
+    // one exact tie -- take its lowest indices.  Warp 0 walks the words in order.
+    if (warp == 0) {
+      int running = 0;
+      for (int w0 = 0; w0 < nsel; w0 += 32) {
+        const int w = w0 + lane;
+        uint32_t bits = 0;
+        if (w < nsel)
+          for (int bit = 0; bit < 32; ++bit) {
+            const int j = w * 32 + bit;
+            if (j < V) {
+              const float v = key2f(keys[j]);
+              if (!(v > hi_thr) && v >= lo_thr) bits |= 1u << bit;
+            }
+          }
+        const int c = __popc(bits);
+        int incl = c;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int v = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += v;
+        }
+        const int take = max(0, min(c, need - (running + incl - c)));
+        uint32_t kept = 0;
+        for (int t = 0; t < take; ++t) {
+          const uint32_t low = bits & (~bits + 1u);
+          kept |= low;
+          bits ^= low;
+        }
+        if (w < nsel) sel[w] |= kept;
+        running += __shfl_sync(0xffffffffu, incl, 31);
+      }
     }
-    __syncwarp();
-    if (lane == 0) {
-      double acc = 0.0;
-      for (int h = 0; h < a.Hi; ++h) acc = __dadd_rn(acc, pbuf[warp * a.Hi + h]);
-      const double skj = a.sk ? double(a.sk[size_t(b) * a.T + j]) : 1.0;
-      exact[c] = __dmul_rn(__dmul_rn(acc, skj), double(a.scale));
+    __syncthreads();
+  } else {
+    // exact fp64 re-scoring of the band, warps 0-7, one candidate per warp; lane l owns
+    // heads l, l+32, ...; q is read from global memory (L1-resident after the first use)
+    double* kd = kdall + warp * a.Di;
+    for (int c = warp; c < nc && warp < 8; c += 8) {
+      const int j = cand[c];
+      const uint8_t* kr = a.k + (size_t(b) * a.T + j) * rb;
+      __syncwarp();
+      for (int i = lane; i < a.Di; i += 32) kd[i] = double(elem_f(kr, i, a.fp8));
+      __syncwarp();
+      for (int h = lane; h < a.Hi; h += 32) {
+        const uint8_t* qh = qg + size_t(h) * rb;
+        double dot = 0.0;
+        if (a.fp8) {
+          // e4m3 products are multiples of 2^-18 below 2^18 and the sums stay below 2^53
+          // units: exact in any order, so two chains
+          double d0 = 0.0, d1 = 0.0;
+          for (int i = 0; i < a.Di; i += 4) {
+            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(qh + i));
+            double q0, q1, q2, q3;
+            e4m3x2_to_f64(w, q0, q1);
+            e4m3x2_to_f64(w >> 16, q2, q3);
+            d0 = fma(q0, kd[i], d0);
+            d1 = fma(q1, kd[i + 1], d1);
+            d0 = fma(q2, kd[i + 2], d0);
+            d1 = fma(q3, kd[i + 3], d1);
+          }
+          dot = d0 + d1;
+        } else {
+          for (int i = 0; i < a.Di; ++i) dot = fma(double(elem_f(qh, i, 0)), kd[i], dot);  // sequential
+        }
+        pbuf[warp * a.Hi + h] = __dmul_rn(cq[h], dot > 0.0 ? dot : 0.0);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        double acc = 0.0;
+        for (int h = 0; h < a.Hi; ++h) acc = __dadd_rn(acc, pbuf[warp * a.Hi + h]);
+        const double skj = a.sk ? double(a.sk[size_t(b) * a.T + j]) : 1.0;
+        exact[c] = __dmul_rn(__dmul_rn(acc, skj), double(a.scale));
+      }
+      __syncwarp();
     }
-    __syncwarp();
+    __syncthreads();
+    // rank candidates by (score desc, index asc); keep the best `need`
+    for (int c = tid; c < nc; c += TK_THREADS) {
+      const double e = exact[c];
+      const int j = cand[c];
+      int rank = 0;
+      for (int o = 0; o < nc; ++o) {
+        const double f = exact[o];
+        rank += (f > e) || (f == e && cand[o] < j);
+      }
+      if (rank < need) atomicOr(&sel[j >> 5], 1u << (j & 31));
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  // rank candidates by (score desc, index asc); keep the best `need`
-  for (int c = tid; c < nc; c += TK_THREADS) {
-    const double e = exact[c];
-    const int j = cand[c];
-    int rank = 0;
-    for (int o = 0; o < nc; ++o) {
-      const double f = exact[o];
-      rank += (f > e) || (f == e && cand[o] < j);
-    }
-    if (rank < need) atomicOr(&sel[j >> 5], 1u << (j & 31));
-  }
-  __syncthreads();
-  // ascending compaction of the selected bits
+  // ascending compaction of the selected bits (per-thread word ranges in thread order)
   const int per = (nsel + TK_THREADS - 1) / TK_THREADS;
   const int w0 = tid * per, w1 = min(nsel, w0 + per);
   int cnt = 0;
   for (int i = w0; i < w1; ++i) cnt += __popc(sel[i]);
-  sh_scan[tid] = cnt;
-  __syncthreads();
-  for (int o = 1; o < TK_THREADS; o <<= 1) {
-    const int v = tid >= o ? sh_scan[tid - o] : 0;
-    __syncthreads();
-    sh_scan[tid] += v;
-    __syncthreads();
-  }
-  int pos = sh_scan[tid] - cnt;
+  int total = 0;
+  int pos = block_exclusive_scan<TK_THREADS>(cnt, sh_scan, total);
   for (int i = w0; i < w1; ++i) {
     uint32_t bits = sel[i];
     while (bits) {
@@ -533,14 +856,15 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
       ++pos;
     }
   }
-  const int total = sh_scan[TK_THREADS - 1];
   for (int i = total + tid; i < a.topk; i += TK_THREADS) out[i] = -1;
 }
 
-static size_t topk_smem(int T, int Hi, int Di, int eb) {
+static size_t topk_smem(int T, int Hi, int Di, int eb, int threads) {
+  (void)eb;
+  (void)threads;
   size_t V = size_t(T);
-  size_t bytes = V * 4 + ((V + 31) / 32) * 4 + CAND_MAX * 4 + 8;
-  bytes += CAND_MAX * 8 + 8 * Hi * 8 + Hi * 8 + size_t(Hi) * (Di * eb + 4) + 16;
+  size_t bytes = V * 4 + ((V + 31) / 32) * 4 + BLIST * 4 + CAND_MAX * 4 + 8;
+  bytes += CAND_MAX * 8 + size_t(8) * Hi * 8 + size_t(Hi) * 8 + size_t(8) * Di * 8;
   return bytes;
 }
 
@@ -568,10 +892,24 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
   auto kern = score_kernel<FP8, DI>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return launch_status("indexer_scores(smem attr)");
+  // Few (batch, query block) pairs -- decode, short prefill -- would leave SMs idle while
+  // each walks its whole key range: split the keys into chunks so there are about 8 items
+  // per SM.  A chunk reloads its block's queries (one Q tile per chunk).
+  ScoreArgs b = a;
   const int n_tb = (a.S + a.Tq - 1) / a.Tq;
-  const int items = a.B * n_tb;
-  const int grid = items < num_sms() ? items : num_sms();
-  kern<<<grid, NTHREADS, C::SMEM, st>>>(tq, tk, a);
+  const long long base = (long long)a.B * n_tb;
+  const int sms = num_sms();
+  const int max_tiles = (a.T + BM - 1) / BM;
+  int n_kc = 1;
+  if (base < 2LL * sms && max_tiles > 1) n_kc = int(std::min<long long>(max_tiles, (8LL * sms + base - 1) / base));
+  b.kc = (max_tiles + n_kc - 1) / n_kc;
+  if (b.kc < 1) b.kc = 1;
+  b.n_kc = (max_tiles + b.kc - 1) / b.kc;
+  if (b.n_kc < 1) b.n_kc = 1;
+  const long long items = base * b.n_kc;
+  MZB_REQUIRE(items < (1LL << 31), MZB_ERR_SHAPE, "indexer: too many work items");
+  const int grid = items < sms ? int(items) : sms;
+  kern<<<grid, NTHREADS, C::SMEM, st>>>(tq, tk, b);
   return launch_status("indexer_scores");
 }
 
@@ -610,6 +948,7 @@ extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, 
   const int nmax = (Di * (dtype == MZB_E4M3 ? 1 : 2) <= 256) ? 256 : 128;
   a.Tq = nmax / Hi;
   MZB_REQUIRE(a.Tq >= 1, MZB_ERR_SHAPE, "indexer: Hi=%d too large for Di=%d", Hi, Di);
+  if (a.Tq > S) a.Tq = int(S);  // one-token decode: N = Hi columns, not a padded block
   a.N = a.Tq * Hi;
   a.ratio = ratio; a.q_offset = q_offset; a.scale = scale; a.write_tail = write_tail; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -642,7 +981,10 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   MZB_REQUIRE(err != nullptr, MZB_ERR_SHAPE, "indexer topk: needs an error word");
   MZB_REQUIRE(dtype == MZB_BF16 || (sq && sk), MZB_ERR_SHAPE, "indexer: fp8 inputs need sq and sk scales");
   const int eb = dtype == MZB_E4M3 ? 1 : 2;
-  const size_t smem = idx::topk_smem(int(T), Hi, Di, eb);
+  MZB_REQUIRE((Di * eb) % 4 == 0, MZB_ERR_UNSUPPORTED, "indexer topk: index rows must be a multiple of 4 bytes");
+  // few rows (decode: one query per sequence) -> wide blocks, else 256 threads per row
+  const bool wide = B * S < 2LL * num_sms();
+  const size_t smem = idx::topk_smem(int(T), Hi, Di, eb, wide ? 1024 : 256);
   MZB_REQUIRE(smem <= 200 * 1024, MZB_ERR_UNSUPPORTED, "indexer topk: T=%lld needs %zu B of shared memory",
               (long long)T, smem);
   idx::TopkArgs a{};
@@ -651,12 +993,14 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi; a.Di = Di; a.topk = topk; a.ratio = ratio;
   a.q_offset = q_offset; a.scale = scale; a.eps = eps; a.fp8 = dtype == MZB_E4M3; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B == 0 || S == 0) return MZB_OK;
   if (T > 0) {
     idx::kbound_kernel<<<dim3(unsigned(B), idx::KB_PARTS), 256, 0, st>>>(a);
     if (int r = launch_status("indexer_kbound")) return r;
   }
-  if (cudaFuncSetAttribute(idx::topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
+  auto kern = wide ? idx::topk_kernel<1024> : idx::topk_kernel<256>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return launch_status("indexer_topk(smem attr)");
-  idx::topk_kernel<<<unsigned(B * S), idx::TK_THREADS, smem, st>>>(a);
+  kern<<<unsigned(B * S), wide ? 1024 : 256, smem, st>>>(a);
   return launch_status("indexer_topk");
 }

@@ -145,6 +145,20 @@ def test_topk_bf16_exact(cuda, topk, T):
     assert np.array_equal(got, ref.astype(np.int32))
 
 
+@pytest.mark.gpu
+def test_topk_all_tied_rows(cuda):
+    """Zero head weights make every visible score exactly 0: the selection must fall back
+    to the lowest indices (the reference's tie rule), for rows shorter and longer than topk."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, Hi, Di, T, ratio, topk = 1, 64, 32, 128, 300, 1, 16
+    q, k, w = _bf16_inputs(torch, cuda, B, S, Hi, Di, T, seed=5)
+    got = indexer.attn(q, k, torch.zeros_like(w), compress_ratio=ratio, topk=topk).cpu().numpy()
+    for s in range(S):
+        n = min(topk, s + 1)
+        assert np.array_equal(got[0, s, :n], np.arange(n)) and (got[0, s, n:] == -1).all(), s
+
+
 def _fp8_case(torch, dev, B, S, Hi, Di, T, seed):
     from mzoo_b200 import indexer
     g = torch.Generator(device="cpu").manual_seed(seed)
@@ -169,6 +183,29 @@ def test_topk_fp8_exact(cuda, q_offset):
     kv = k8.float().cpu().numpy()
     canon = I.canonical_scores(qv, kv, w.cpu().numpy(), sq.cpu().numpy(), sk.cpu().numpy(), ratio, q_offset)
     assert np.array_equal(got.cpu().numpy(), I.canonical_topk(canon, topk, ratio, q_offset))
+
+
+@pytest.mark.gpu
+def test_decode_shaped_topk_fp8_exact(cuda):
+    """One query per sequence at its own position (paged decode, BASELINE config 4 at reduced
+    size): per-batch q_pos, few (batch, block) items, so the score kernel splits key ranges."""
+    import torch
+    from mzoo_b200 import indexer
+    B, Hi, Di, T, ratio, topk = 6, 64, 128, 4000, 4, 256
+    q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, 1, Hi, Di, T, 21)
+    lens = torch.tensor([16000, 1000, 9001, 4097, 15999, 777], dtype=torch.int32)
+    pos = (lens - 1).view(B, 1).to(cuda)
+    got = indexer.attn(q8, k8, w, compress_ratio=ratio, topk=topk, scales=(sq, sk), q_pos=pos).cpu().numpy()
+    sc = indexer.fwd(q8, k8, w, compress_ratio=ratio, scales=(sq, sk), q_pos=pos).cpu().numpy()
+    qv, kv, wn, sqn, skn = (x.float().cpu().numpy() for x in (q8, k8, w, sq, sk))
+    for b in range(B):
+        canon = I.canonical_scores(qv[b:b + 1], kv[b:b + 1], wn[b:b + 1], sqn[b:b + 1], skn[b:b + 1], ratio,
+                                   int(pos[b, 0]))
+        assert np.array_equal(got[b:b + 1], I.canonical_topk(canon, topk, ratio, int(pos[b, 0]))), b
+        vis = int(lens[b]) // ratio
+        assert np.isneginf(sc[b, 0, vis:]).all() and np.isfinite(sc[b, 0, :vis]).all()
+        rel = np.abs(sc[b, 0, :vis] - canon[0, 0, :vis]).max() / np.abs(canon[0, 0, :vis]).max()
+        assert rel < 1e-5, (b, rel)
 
 
 @pytest.mark.gpu
