@@ -191,17 +191,22 @@ __global__ void __launch_bounds__(256, 1)
           if (!tc::mbar_wait(&bars[QD_FULL + s], ph, a.err, 411)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
+          // descriptors once per tile; the unrolled loops add constant offsets
+          const uint64_t kd = tc::make_sdesc<128>(k_base, 16, 1024), vd = tc::make_sdesc<128>(v_base, 16, 1024);
+          const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
+          const uint64_t q_mn = tc::make_sdesc<128>(q_base, 16384, 1024);
+          const uint64_t do_mn = tc::make_sdesc<128>(do_base, 16384, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_S, tc::make_sdesc<128>(k_base + cb * 16384 + off, 16, 1024),
-                          tc::make_sdesc<128>(q_base + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+            tc::mma_ss<0>(tmem + C::C_S, tc::sdesc_add(kd, cb * 16384 + off), tc::sdesc_add(qd, cb * 16384 + off),
+                          idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_DP, tc::make_sdesc<128>(v_base + cb * 16384 + off, 16, 1024),
-                          tc::make_sdesc<128>(do_base + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+            tc::mma_ss<0>(tmem + C::C_DP, tc::sdesc_add(vd, cb * 16384 + off), tc::sdesc_add(dod, cb * 16384 + off),
+                          idesc_s, kk > 0);
           }
           tc::mma_commit(&bars[S_FULL]);
           if (i == 0 && !tc::mbar_wait(&bars[ACC_EMPTY], (ii & 1) ^ 1, a.err, 412)) { ok = false; break; }
@@ -210,10 +215,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // 128 query rows, 16 per step
             const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + kk * 8,
-                       tc::make_sdesc<128>(do_base + kk * 2048, 16384, 1024), idesc_acc, acc);
-            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8,
-                       tc::make_sdesc<128>(q_base + kk * 2048, 16384, 1024), idesc_acc, acc);
+            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + kk * 8, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
+            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8, tc::sdesc_add(q_mn, kk * 2048), idesc_acc, acc);
           }
           tc::mma_commit(&bars[QD_EMPTY + s]);
           if (i == m.nq - 1) {
@@ -460,17 +463,21 @@ __global__ void __launch_bounds__(384, 1)
           if (!tc::mbar_wait(&bars[(win ? KVW_FULL : KVG_FULL) + st], par, a.err, 511)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t kb = kv_base + st * C::KV_STAGE, vb = kb + (SEP_V ? C::T_BYTES : 0);
+          // descriptors once per tile; the unrolled loops add constant offsets
+          const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
+          const uint64_t kd = tc::make_sdesc<128>(kb, 16, 1024), vd = tc::make_sdesc<128>(vb, 16, 1024);
+          const uint64_t k_mn = tc::make_sdesc<128>(kb, 16384, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_S, tc::make_sdesc<128>(q_base + cb * 16384 + off, 16, 1024),
-                          tc::make_sdesc<128>(kb + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+            tc::mma_ss<0>(tmem + C::C_S, tc::sdesc_add(qd, cb * 16384 + off), tc::sdesc_add(kd, cb * 16384 + off),
+                          idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_DP, tc::make_sdesc<128>(do_base + cb * 16384 + off, 16, 1024),
-                          tc::make_sdesc<128>(vb + cb * 16384 + off, 16, 1024), idesc_s, kk > 0);
+            tc::mma_ss<0>(tmem + C::C_DP, tc::sdesc_add(dod, cb * 16384 + off), tc::sdesc_add(vd, cb * 16384 + off),
+                          idesc_s, kk > 0);
           }
           tc::mma_commit(&bars[S_FULL_Q]);
           if (j == 0 && !tc::mbar_wait(&bars[QACC_EMPTY], (ii & 1) ^ 1, a.err, 512)) { ok = false; break; }
@@ -478,16 +485,20 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per step: dQ += dS K
-            tc::mma_ts(tmem + C::C_DQ, tmem + C::C_S + kk * 8, tc::make_sdesc<128>(kb + kk * 2048, 16384, 1024),
-                       idesc_dq, (j == 0 && kk == 0) ? 0u : 1u);
+            tc::mma_ts(tmem + C::C_DQ, tmem + C::C_S + kk * 8, tc::sdesc_add(k_mn, kk * 2048), idesc_dq,
+                       (j == 0 && kk == 0) ? 0u : 1u);
           if (!win) {
             if (!tc::mbar_wait(&bars[DM_EMPTY], (gm & 1) ^ 1, a.err, 514)) { ok = false; break; }
+            const uint64_t ds_mn = tc::make_sdesc<128>(ds_base, 16384, 1024);
+            const uint64_t p_mn = tc::make_sdesc<128>(p_base, 16384, 1024);
+            const uint64_t q_mn = tc::make_sdesc<128>(q_base, 16384, 1024);
+            const uint64_t do_mn = tc::make_sdesc<128>(do_base, 16384, 1024);
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {  // 128 query rows: dM = dS^T Q + P^T dO
-              tc::mma_ss<0>(tmem + C::C_DM, tc::make_sdesc<128>(ds_base + kk * 2048, 16384, 1024),
-                            tc::make_sdesc<128>(q_base + kk * 2048, 16384, 1024), idesc_dm, kk > 0);
-              tc::mma_ss<0>(tmem + C::C_DM, tc::make_sdesc<128>(p_base + kk * 2048, 16384, 1024),
-                            tc::make_sdesc<128>(do_base + kk * 2048, 16384, 1024), idesc_dm, 1u);
+              tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(ds_mn, kk * 2048), tc::sdesc_add(q_mn, kk * 2048), idesc_dm,
+                            kk > 0);
+              tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(p_mn, kk * 2048), tc::sdesc_add(do_mn, kk * 2048), idesc_dm,
+                            1u);
             }
             tc::mma_commit(&bars[DM_FULL]);
             ++gm;

@@ -54,8 +54,10 @@ struct Args {
   int* err;
 };
 
+// O_FINAL: commit after an item's last PV, waited on by the epilogue with the item parity
+// (two PVs can still be in flight there, so O_DONE's parity would alias an older phase).
 enum Bar { Q_FULL = 0, Q_EMPTY, O_DONE, O_EMPTY, S_FULL, S_FULL1, S_EMPTY, S_EMPTY1, P_FULL, P_FULL1, KV_FULL_W,
-           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, NBAR = KV_EMPTY + 4 };
+           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, NBAR };
 
 __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -165,6 +167,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t idesc_qk = tc::make_idesc(128, NK, 1, 1);
       const uint32_t idesc_pv = tc::make_idesc(128, D, 1, 1, false, true);
       const uint32_t q_base = smem_u32(qs), kv_base = smem_u32(kvs), p_base = smem_u32(ps);
+      // descriptors built once per tile/buffer; unrolled loops add constant offsets (one
+      // thread issues every MMA, so per-MMA descriptor arithmetic would throttle issue)
+      const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024);
       int g = 0, ii = 0;
       int uses_w[4] = {0, 0, 0, 0}, uses_g[4] = {0, 0, 0, 0};
       auto pv = [&](int gg, bool first, int item) -> bool {
@@ -173,12 +178,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!tc::mbar_wait(&bars[P_FULL + pb], (gg >> 1) & 1, a.err, 312)) return false;
         tc::fence_after_sync();
         const uint32_t vb = kv_base + st * C::STAGE_BYTES + (SEP_V ? C::K_BYTES : 0);
+        const uint64_t pd = tc::make_sdesc<128>(p_base + pb * C::P_BYTES, 16, 1024);
+        const uint64_t vd = tc::make_sdesc<128>(vb, NK * 128, 1024);
 #pragma unroll
         for (int jj = 0; jj < NK / 16; ++jj) {
           const int cb = jj >> 2, off = (jj & 3) * 32;
-          const uint64_t ad = tc::make_sdesc<128>(p_base + pb * C::P_BYTES + cb * 128 * 128 + off, 16, 1024);
-          const uint64_t bd = tc::make_sdesc<128>(vb + jj * 16 * 128, NK * 128, 1024);
-          tc::mma_ss<0>(tmem, ad, bd, idesc_pv, (first && jj == 0) ? 0u : 1u);
+          tc::mma_ss<0>(tmem, tc::sdesc_add(pd, cb * 128 * 128 + off), tc::sdesc_add(vd, jj * 16 * 128), idesc_pv,
+                        (first && jj == 0) ? 0u : 1u);
         }
         tc::mma_commit(&bars[KV_EMPTY + st]);
         tc::mma_commit(&bars[O_DONE]);
@@ -197,18 +203,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               !tc::mbar_wait(&bars[S_EMPTY + sb], ((g >> 1) & 1) ^ 1, a.err, 314)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t kb = kv_base + st * C::STAGE_BYTES;
+          const uint64_t kd = tc::make_sdesc<128>(kb, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            const uint64_t ad = tc::make_sdesc<128>(q_base + cb * 128 * 128 + off, 16, 1024);
-            const uint64_t bd = tc::make_sdesc<128>(kb + cb * NK * 128 + off, 16, 1024);
-            tc::mma_ss<0>(tmem + C::S_COL0 + sb * NK, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            tc::mma_ss<0>(tmem + C::S_COL0 + sb * NK, tc::sdesc_add(qd, cb * 128 * 128 + off),
+                          tc::sdesc_add(kd, cb * NK * 128 + off), idesc_qk, kk > 0 ? 1u : 0u);
           }
           tc::mma_commit(&bars[S_FULL + sb]);
           if (j == n - 1) tc::mma_commit(&bars[Q_EMPTY]);
           if (j >= 1 && !pv(g - 1, j == 1, ii)) { ok = false; break; }
         }
         if (!ok || !pv(g - 1, n == 1, ii)) { *abort_flag = 1; break; }
+        tc::mma_commit(&bars[O_FINAL]);
       }
     }
   } else if (warp >= 4 && warp < 8) {
@@ -335,7 +342,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) tc::mbar_arrive(&bars[P_FULL + sb]);
       }
       if (!ok) { *abort_flag = 1; break; }
-      if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 322)) { *abort_flag = 1; break; }
+      if (!tc::mbar_wait(&bars[O_FINAL], ii & 1, a.err, 322)) { *abort_flag = 1; break; }
       tc::fence_after_sync();
       if (a.sinks) lsum += exp2f(a.sinks[h] * LOG2E - mrow * sl);
       const float inv = 1.0f / lsum;

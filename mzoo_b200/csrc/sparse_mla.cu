@@ -19,9 +19,16 @@
 // Warp roles per CTA (512 threads):
 //   0      TMA of this CTA's Q half (64 heads x 576, 9 swizzled 64-column blocks)
 //   1      TMEM allocation; in the leader CTA, the single MMA-issuing thread
+//   2      V copier: assembles the V tile from K tiles (below)
+//   3      V relay: waits for this CTA's V tile, tells the leader and the K-tile owners
 //   4-7    softmax / O correction / epilogue (thread = TMEM lane = (head, key half))
-//   8-11   K producers: gather + dequantise this CTA's 32 keys x 576 channels to bf16
-//   12-15  V producers: gather + dequantise all 64 keys x this CTA's 256 V channels
+//   8-11   K producers for even tiles, 12-15 for odd tiles: gather + dequantise this CTA's
+//          32 keys x 576 channels to bf16 (two groups, so each has two tile-times to hide
+//          the gather latency)
+// V is not dequantised again: V tile block (64 keys x 64 channels) = the same channel
+// block of both CTAs' K tiles (32 keys each, identical 128-byte swizzle), so the copier
+// pushes 4 KB blocks of its K tile into its own and the peer's V tile with
+// cp.async.bulk shared::cta -> shared::cluster, completing on the destination's V_FULL.
 // MMA order per item: QK_0, QK_1, PV_0, QK_2, PV_1, ...; tile g's S completion implies
 // PV_{g-2} finished (in-order tensor pipe), so P is double-buffered without extra waits.
 // The running max is only raised when it grows by more than 2^8 (in exp2 units), which
@@ -53,10 +60,17 @@ constexpr float LN2 = 0.6931471805599453f;
 enum Bar {
   Q_FULL = 0, Q_READY, Q_EMPTY,
   K_FULL, K_FULL1, K_EMPTY, K_EMPTY1,
-  V_FULL, V_FULL1, V_EMPTY, V_EMPTY1,
+  K_WRIT, K_WRIT1,    // local: this CTA's K tile written (its 4 producer warps)
+  K_CP, K_CP1,        // local: the copies out of this CTA's K tile have landed (2 relays)
+  V_FULL, V_FULL1,    // local: this CTA's V tile complete (32 KB of copies)
+  V_READY, V_READY1,  // leader: both CTAs' V tiles complete (2 relays)
+  V_EMPTY, V_EMPTY1,  // local (multicast commit): PV done
   S_FULL, S_FULL1, S_EMPTY, S_EMPTY1,
-  P_FULL, P_FULL1, O_DONE, O_EMPTY, XCH, XCH1, XL, NBAR
+  P_FULL, P_FULL1, O_DONE, O_EMPTY, XCH, XCH1, XL,
+  O_FINAL,            // multicast commit after an item's last PV (epilogue, item parity)
+  NBAR
 };
+static_assert(8 * NBAR + 8 <= 256, "barriers + TMEM slot + abort flag fit the first 256 misc bytes");
 
 struct Args {
   const uint8_t* raw;
@@ -155,6 +169,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     abort_flag = 1;                                                   \
     break;                                                            \
   }
+// barriers the peer CTA or the pair's MMA completions arrive on need a cluster-scope
+// acquire so that the peer's shared-memory writes / TMEM reads are ordered before what follows
+#define MLA_WAIT_CL(bar, par, code)                                   \
+  if (!tc::mbar_wait_cl(&bars[bar], (par), a.err, (code))) {          \
+    abort_flag = 1;                                                   \
+    break;                                                            \
+  }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     mla_fwd_kernel(const __grid_constant__ CUtensorMap tq, Args a) {
@@ -179,7 +200,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   const int pair = int(tc::cluster_id_x()), npairs = int(tc::nclusters_x());
 
   if (threadIdx.x == 0) {
-    const uint32_t counts[NBAR] = {1, 2, 1, 8, 8, 1, 1, 8, 8, 1, 1, 1, 1, 8, 8, 8, 8, 1, 8, 4, 4, 4};
+    const uint32_t counts[NBAR] = {1, 2, 1,           // Q_FULL, Q_READY, Q_EMPTY
+                                   8, 8, 1, 1,        // K_FULL x2, K_EMPTY x2
+                                   4, 4, 2, 2,        // K_WRIT x2, K_CP x2
+                                   1, 1, 2, 2, 1, 1,  // V_FULL x2, V_READY x2, V_EMPTY x2
+                                   1, 1, 8, 8,        // S_FULL x2, S_EMPTY x2
+                                   8, 8, 1, 8,        // P_FULL x2, O_DONE, O_EMPTY
+                                   4, 4, 4,           // XCH x2, XL
+                                   1};                // O_FINAL
     for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], counts[i]);
     abort_flag = 0;
     tc::fence_barrier_init();
@@ -192,6 +220,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
   auto leader_bar = [&](int i) { return tc::mapa(smem_u32(&bars[i]), 0); };
+  // arrive on a leader-CTA barrier: CTA scope from the leader itself (its waiters acquire at
+  // cluster scope, which covers it), a cluster-scope release from the peer
+  auto arrive_leader = [&](int i) {
+    if (rank == 0) tc::mbar_arrive(&bars[i]);
+    else tc::mbar_arrive_cluster(leader_bar(i));
+  };
   auto n_tiles = [&](int tk) { return (a.n_slots[tk] + NT - 1) / NT; };
 
   if (warp == 0) {
@@ -201,14 +235,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       bool issued = false;
       for (int it = pair; it < a.n_tok && !abort_flag; it += npairs, ++ii) {
         const int tk = a.n_tok - 1 - it;
-        MLA_WAIT(Q_EMPTY, (ii & 1) ^ 1, 201);
+        MLA_WAIT_CL(Q_EMPTY, (ii & 1) ^ 1, 201);
         tc::mbar_expect_tx(&bars[Q_FULL], Q_BYTES);
         for (int cb = 0; cb < QBLK; ++cb)
           tc::tma_load_2d(qs + cb * HC * 128, &tq, &bars[Q_FULL], cb * 64, tk * H + int(rank) * HC);
         issued = true;
         MLA_WAIT(Q_FULL, ii & 1, 202);
         issued = false;
-        tc::mbar_arrive_cluster(leader_bar(Q_READY));
+        arrive_leader(Q_READY);
       }
       if (issued) tc::mbar_wait(&bars[Q_FULL], (ii & 1), nullptr, 0);  // drain before exit
     }
@@ -217,22 +251,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_qk = tc::make_idesc(128, NT, 1, 1);
       const uint32_t idesc_pv = tc::make_idesc(128, 256, 1, 1, false, true);
-      const uint32_t q_base = smem_u32(qs), k_base = smem_u32(ks), v_base = smem_u32(vs), p_base = smem_u32(ps);
+      // descriptors built once; the unrolled loops add compile-time offsets (a single
+      // thread issues every MMA, so per-MMA descriptor arithmetic would throttle issue)
+      const uint64_t qd = tc::make_sdesc<128>(smem_u32(qs), 16, 1024);
+      const uint64_t kd[2] = {tc::make_sdesc<128>(smem_u32(ks), 16, 1024),
+                              tc::make_sdesc<128>(smem_u32(ks + K_BYTES), 16, 1024)};
+      const uint64_t pd[2] = {tc::make_sdesc<128>(smem_u32(ps), 16, 1024),
+                              tc::make_sdesc<128>(smem_u32(ps + P_BYTES), 16, 1024)};
+      const uint64_t vd[2] = {tc::make_sdesc<128>(smem_u32(vs), 8192, 1024),
+                              tc::make_sdesc<128>(smem_u32(vs + V_BYTES), 8192, 1024)};
       int g = 0, ii = 0;
       auto pv = [&](int gg, bool first, int item) -> bool {
         const int st = gg & 1, ph = (gg >> 1) & 1;
-        if (first && !tc::mbar_wait(&bars[O_EMPTY], (item & 1) ^ 1, a.err, 211)) return false;
-        if (!tc::mbar_wait(&bars[V_FULL + st], ph, a.err, 212)) return false;
-        if (!tc::mbar_wait(&bars[P_FULL + st], ph, a.err, 213)) return false;
+        if (first && !tc::mbar_wait_cl(&bars[O_EMPTY], (item & 1) ^ 1, a.err, 211)) return false;
+        if (!tc::mbar_wait_cl(&bars[V_READY + st], ph, a.err, 212)) return false;
+        if (!tc::mbar_wait_cl(&bars[P_FULL + st], ph, a.err, 213)) return false;
         tc::fence_after_sync();
+        const uint64_t ad0 = st ? pd[1] : pd[0], bd0 = st ? vd[1] : vd[0];
 #pragma unroll
         for (int i = 0; i < 2; ++i) {
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const uint64_t ad = tc::make_sdesc<128>(p_base + st * P_BYTES + jj * 32, 16, 1024);
-            const uint64_t bd = tc::make_sdesc<128>(v_base + st * V_BYTES + 2 * i * 8192 + jj * 2048, 8192, 1024);
-            tc::mma2_f16(tmem + i * 128, ad, bd, idesc_pv, (first && jj == 0) ? 0u : 1u);
-          }
+          for (int jj = 0; jj < 4; ++jj)
+            tc::mma2_f16(tmem + i * 128, tc::sdesc_add(ad0, jj * 32), tc::sdesc_add(bd0, 2 * i * 8192 + jj * 2048),
+                         idesc_pv, (first && jj == 0) ? 0u : 1u);
         }
         tc::mma2_commit_mc(&bars[V_EMPTY + st], 3);
         tc::mma2_commit_mc(&bars[O_DONE], 3);
@@ -241,20 +282,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       for (int it = pair; it < a.n_tok && !abort_flag; it += npairs, ++ii) {
         const int tk = a.n_tok - 1 - it;
         const int n = n_tiles(tk);
-        MLA_WAIT(Q_READY, ii & 1, 210);
+        MLA_WAIT_CL(Q_READY, ii & 1, 210);
         bool ok = true;
         for (int j = 0; j < n; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
-          if (!tc::mbar_wait(&bars[K_FULL + st], ph, a.err, 214) ||
-              !tc::mbar_wait(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
+          if (!tc::mbar_wait_cl(&bars[K_FULL + st], ph, a.err, 214) ||
+              !tc::mbar_wait_cl(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t d = tmem + S_COL0 + st * 32;
-#pragma unroll 4
+          const uint64_t kb = st ? kd[1] : kd[0];
+#pragma unroll
           for (int kk = 0; kk < 36; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            const uint64_t ad = tc::make_sdesc<128>(q_base + cb * 8192 + off, 16, 1024);
-            const uint64_t bd = tc::make_sdesc<128>(k_base + st * K_BYTES + cb * 4096 + off, 16, 1024);
-            tc::mma2_f16(d, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+            tc::mma2_f16(d, tc::sdesc_add(qd, cb * 8192 + off), tc::sdesc_add(kb, cb * 4096 + off), idesc_qk,
+                         kk > 0 ? 1u : 0u);
           }
           tc::mma2_commit_mc(&bars[K_EMPTY + st], 3);
           tc::mma2_commit_mc(&bars[S_FULL + st], 3);
@@ -262,6 +303,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           if (j >= 1 && !pv(g - 1, j == 1, ii)) { ok = false; break; }
         }
         if (!ok || !pv(g - 1, n == 1, ii)) { abort_flag = 1; break; }
+        tc::mma2_commit_mc(&bars[O_FINAL], 3);
       }
     }
   } else if (warp >= 4 && warp < 8) {
@@ -278,18 +320,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       const Slot s = item_info(a, tk);
       float m = -1e30f, lsum = 0.0f;
       bool ok = true;
+      // key validity: the index of this thread's key of tile j + 1 is loaded while tile j is
+      // processed (window slots need no load)
+      auto slot_code = [&](int p) -> int {
+        if (p < s.n_win) return 0;
+        const int c = p - s.n_win;
+        return c < a.topk ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
+      };
+      const int kofs = kh * NTH + lane;
+      int code_next = slot_code(kofs);
       for (int j = 0; j < n; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
-        // key validity (global index loads) before waiting on the MMA
-        const uint32_t vmask = __ballot_sync(0xffffffffu, slot_valid(a, s, tk, j * NT + kh * NTH + lane));
-        if (!tc::mbar_wait(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
+        const int code = code_next;
+        if (j + 1 < n) code_next = slot_code((j + 1) * NT + kofs);
+        const int p = j * NT + kofs;
+        const uint32_t vmask = __ballot_sync(0xffffffffu, p < s.n_win || (code >= 0 && code < s.g_lim));
+        if (!tc::mbar_wait_cl(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
         tc::fence_after_sync();
         uint32_t sr[32];
         tc::tmem_ld32(tc::taddr(tmem, sw * 32, S_COL0 + st * 32), sr);
         tc::tmem_wait_ld();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive_cluster(leader_bar(S_EMPTY + st));
+        if (lane == 0) arrive_leader(S_EMPTY + st);
         float sv[32];
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -324,7 +377,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         for (int c = 0; c < 4; ++c)
           st_shared16(prow + (((kh * 4 + c) ^ (hrow & 7)) * 16), make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
         if (j > 0 && __any_sync(0xffffffffu, need)) {
-          if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
+          if (!tc::mbar_wait_cl(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
           tc::fence_after_sync();
           for (int c0 = 0; c0 < 256; c0 += 32) {
             uint32_t ov[32];
@@ -340,11 +393,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tc::fence_async_smem();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive_cluster(leader_bar(P_FULL + st));
+        if (lane == 0) arrive_leader(P_FULL + st);
       }
       if (!ok) { abort_flag = 1; break; }
-      // epilogue: O / l, lse
-      MLA_WAIT(O_DONE, (g - 1) & 1, 222);
+      // epilogue: O / l, lse.  O_FINAL, not O_DONE: two PVs of this item can still be in
+      // flight here, and O_DONE's parity would alias the phase of an older PV.
+      MLA_WAIT_CL(O_FINAL, ii & 1, 222);
       tc::fence_after_sync();
       red_l[ii & 1][l] = lsum;
       __syncwarp();
@@ -371,11 +425,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       if (kh == 0) a.lse[(long long)tk * H + head] = (m * sl + log2f(ltot)) * LN2;
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive_cluster(leader_bar(O_EMPTY));
+      if (lane == 0) arrive_leader(O_EMPTY);
     }
-  } else if (warp >= 8 && warp < 12) {
+  } else if (warp >= 8) {
     // ------------------------------------------------------------------ K producers
-    const int t = threadIdx.x - 256;  // 0..127
+    // group 0 (warps 8-11) fills stage 0 (even tiles), group 1 (warps 12-15) stage 1
+    const int grp = (warp - 8) >> 2;
+    const int t = threadIdx.x - 256 - grp * 128;  // 0..127
     const int kk = t >> 2, sub = t & 3;
     int g = 0;
     for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
@@ -385,6 +441,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int j = 0; j < n; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
+        if (st != grp) continue;
         const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
         uint4 raw[10];
         float sc[8];
@@ -396,7 +453,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
 #pragma unroll
         for (int q = 0; q < 8; ++q) sc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
-        if (!tc::mbar_wait(&bars[K_EMPTY + st], ph ^ 1, a.err, 230)) { ok = false; break; }
+        // the stage is free once its QK MMA is done and the copies out of it have landed
+        if (!tc::mbar_wait_cl(&bars[K_EMPTY + st], ph ^ 1, a.err, 230) ||
+            !tc::mbar_wait_cl(&bars[K_CP + st], ph ^ 1, a.err, 231)) { ok = false; break; }
         uint8_t* kt = ks + st * K_BYTES + kk * 128;
 #pragma unroll
         for (int q = 0; q < 10; ++q) {
@@ -413,51 +472,65 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
         tc::fence_async_smem();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive_cluster(leader_bar(K_FULL + st));
+        if (lane == 0) {
+          tc::mbar_arrive(&bars[K_WRIT + st]);
+          arrive_leader(K_FULL + st);
+        }
       }
       if (!ok) { abort_flag = 1; break; }
     }
-  } else if (warp >= 12) {
-    // ------------------------------------------------------------------ V producers
-    const int t = threadIdx.x - 384;  // 0..127
-    const int key = t >> 1, sub = t & 1;
-    int g = 0;
-    for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
-      const int tk = a.n_tok - 1 - it;
-      const int n = n_tiles(tk);
-      const Slot s = item_info(a, tk);
-      bool ok = true;
-      for (int j = 0; j < n; ++j, ++g) {
-        const int st = g & 1, ph = (g >> 1) & 1;
-        const uint8_t* rp = slot_row(a, s, tk, j * NT + key);
-        uint4 raw[8];
-        float sc[8];
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ V copier
+    // V tile block lb (keys 0-31 | keys 32-63) of CTA r holds global channel block
+    // gb = (lb >> 1) * 4 + 2 r + (lb & 1); this CTA supplies its half of the keys.
+    if (lane == 0) {
+      int g = 0;
+      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
+        const int n = n_tiles(a.n_tok - 1 - it);
+        bool ok = true;
+        for (int j = 0; j < n; ++j, ++g) {
+          const int st = g & 1, ph = (g >> 1) & 1;
+          if (!tc::mbar_wait(&bars[K_WRIT + st], ph, a.err, 250) ||
+              !tc::mbar_wait_cl(&bars[V_EMPTY + st], ph ^ 1, a.err, 251)) { ok = false; break; }
+          const uint32_t k_base = smem_u32(ks + st * K_BYTES), v_base = smem_u32(vs + st * V_BYTES);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int cc = sub * 8 + q, lb = cc >> 2, w = cc & 3;
-          const int gb = (lb >> 1) * 4 + int(rank) * 2 + (lb & 1);
-          raw[q] = make_uint4(0, 0, 0, 0);
-          sc[q] = 0.0f;
-          if (rp) {
-            raw[q] = ld_nc16(rp + gb * 64 + w * 16);
-            sc[q] = __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + gb);
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t dst_bar = tc::mapa(smem_u32(&bars[V_FULL + st]), uint32_t(r));
+#pragma unroll
+            for (int lb = 0; lb < 4; ++lb) {
+              const int gb = (lb >> 1) * 4 + r * 2 + (lb & 1);
+              const uint32_t dst = tc::mapa(v_base + lb * 8192 + rank * 4096, uint32_t(r));
+              tc::bulk_copy_s2cluster(dst, k_base + gb * 4096, 4096, dst_bar);
+            }
           }
         }
-        if (!tc::mbar_wait(&bars[V_EMPTY + st], ph ^ 1, a.err, 240)) { ok = false; break; }
-        uint8_t* vt = vs + st * V_BYTES + key * 128;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int cc = sub * 8 + q, lb = cc >> 2, w = cc & 3;
-          uint4 lo, hi;
-          dequant16(raw[q], sc[q], lo, hi);
-          st_shared16(vt + lb * 8192 + (((2 * w) ^ (key & 7)) * 16), lo);
-          st_shared16(vt + lb * 8192 + (((2 * w + 1) ^ (key & 7)) * 16), hi);
-        }
-        tc::fence_async_smem();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive_cluster(leader_bar(V_FULL + st));
+        if (!ok) { abort_flag = 1; break; }
       }
-      if (!ok) { abort_flag = 1; break; }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------------ V relay
+    if (lane == 0) {
+      int g = 0;
+      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
+        const int n = n_tiles(a.n_tok - 1 - it);
+        bool ok = true;
+        for (int j = 0; j < n; ++j, ++g) {
+          const int st = g & 1, ph = (g >> 1) & 1;
+          tc::mbar_expect_tx(&bars[V_FULL + st], 2 * 4 * 4096);  // 4 blocks from each CTA
+          if (!tc::mbar_wait_cl(&bars[V_FULL + st], ph, a.err, 260)) { ok = false; break; }
+          arrive_leader(V_READY + st);
+          tc::mbar_arrive(&bars[K_CP + st]);
+          tc::mbar_arrive_cluster(tc::mapa(smem_u32(&bars[K_CP + st]), rank ^ 1u));
+        }
+        if (!ok) { abort_flag = 1; break; }
+      }
+      if (abort_flag) {
+        // copies already issued into this CTA land within microseconds; let them finish
+        // before the CTA (and its shared memory) goes away
+        const uint64_t t0 = tc::globaltimer_ns();
+        while (tc::globaltimer_ns() - t0 < 50000ull) {
+        }
+      }
     }
   }
 

@@ -191,6 +191,13 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t smem_addr, uint32_t lbo_
   return d;
 }
 
+// Descriptor of the same tile `byte_off` bytes further on: the start-address field holds
+// addr >> 4 in bits 0-13 and shared-memory addresses stay below 2^18, so a plain add never
+// carries out of the field.  Lets MMA loops build descriptors once and add constants.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_off) {
+  return desc + uint64_t(byte_off >> 4);
+}
+
 // ---------------------------------------------------------------- tcgen05: TMEM <-> registers
 
 // 32 lanes x 32-bit, `N` consecutive columns per thread (thread i of the warp <-> lane
@@ -274,6 +281,41 @@ __device__ __forceinline__ uint32_t mapa(uint32_t local_smem_addr, uint32_t rank
 // Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Wait (acquire, cluster scope) on a local mbarrier that CTAs of the cluster arrive on
+// remotely; bounded like mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t* bar, uint32_t parity, int* err, int code,
+                                             uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait_cl(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cl(bar, parity)) return true;
+    if ((i & 255) == 0 && globaltimer_ns() - t0 > limit_ns) break;
+  }
+  if (err) atomicExch(err, code);
+  return false;
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from this CTA's
+// shared memory to shared memory of a CTA in the cluster (this one or a peer); completes
+// as transaction bytes on the destination CTA's mbarrier; one destination per copy.
+__device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                    uint32_t mbar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_cluster), "r"(src_cta), "r"(bytes), "r"(mbar_cluster)
+               : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync() {
