@@ -49,7 +49,7 @@ constexpr int TILE_BYTES = Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES;  /
 // misc (barriers, exchange buffers) after the tiles; no static shared memory, so the
 // dynamic window starts 1024-aligned (checked at run time) and the total stays under the
 // 227 KB per-block limit.
-constexpr int MISC_BYTES = 256 + 2 * 2 * 128 * 4;
+constexpr int MISC_BYTES = 512 + 2 * 2 * 128 * 4;
 constexpr int SMEM_DYN = TILE_BYTES + MISC_BYTES;
 constexpr int NTHREADS = 512;
 constexpr int TMEM_COLS = 512;
@@ -66,11 +66,14 @@ enum Bar {
   V_READY, V_READY1,  // leader: both CTAs' V tiles complete (2 relays)
   V_EMPTY, V_EMPTY1,  // local (multicast commit): PV done
   S_FULL, S_FULL1, S_EMPTY, S_EMPTY1,
-  P_FULL, P_FULL1, O_DONE, O_EMPTY, XCH, XCH1, XL,
+  P_FULL, P_FULL1, O_DONE, O_EMPTY,
+  XCH, XCH1, XCH2, XCH3,  // row-max exchange per (S buffer, warp pair {4,6} / {5,7}), local
+  XL, XL1,                // row-sum exchange per warp pair, local
   O_FINAL,            // multicast commit after an item's last PV (epilogue, item parity)
   NBAR
 };
-static_assert(8 * NBAR + 8 <= 256, "barriers + TMEM slot + abort flag fit the first 256 misc bytes");
+static_assert(8 * NBAR + 8 <= 512, "barriers + TMEM slot + abort flag fit the first 512 misc bytes");
+static_assert(SMEM_DYN <= 232448, "shared memory budget");
 
 struct Args {
   const uint8_t* raw;
@@ -184,8 +187,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + TILE_BYTES);
   uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(sm + TILE_BYTES + 8 * NBAR);
   volatile int& abort_flag = *reinterpret_cast<volatile int*>(sm + TILE_BYTES + 8 * NBAR + 4);
-  float (*red_m)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 256);
-  float (*red_l)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 256 + 1024);
+  float (*red_m)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 512);
+  float (*red_l)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 512 + 1024);
   if (smem_u32(smem_raw) & 1023) {  // swizzled tiles need 1024-byte alignment
     if (threadIdx.x == 0) atomicExch(a.err, MZB_ERR_ALIGN);
     return;
@@ -206,7 +209,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                                    1, 1, 2, 2, 1, 1,  // V_FULL x2, V_READY x2, V_EMPTY x2
                                    1, 1, 8, 8,        // S_FULL x2, S_EMPTY x2
                                    8, 8, 1, 8,        // P_FULL x2, O_DONE, O_EMPTY
-                                   4, 4, 4,           // XCH x2, XL
+                                   2, 2, 2, 2, 2, 2,  // XCH x4, XL x2 (the two warps holding one head's key halves)
                                    1};                // O_FINAL
     for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], counts[i]);
     abort_flag = 0;
@@ -354,8 +357,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         // exchange with the thread holding the other key half of this head (mbarrier, bounded)
         red_m[st][l] = mt;
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bars[XCH + st]);
-        if (!tc::mbar_wait(&bars[XCH + st], ph, a.err, 223)) { ok = false; break; }
+        if (lane == 0) tc::mbar_arrive(&bars[XCH + 2 * st + (sw & 1)]);
+        if (!tc::mbar_wait(&bars[XCH + 2 * st + (sw & 1)], ph, a.err, 223)) { ok = false; break; }
         mt = fmaxf(mt, red_m[st][l ^ 64]);
         const bool need = mt * sl > m * sl + 8.0f;
         const float m_new = need ? mt : m;
@@ -402,8 +405,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::fence_after_sync();
       red_l[ii & 1][l] = lsum;
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars[XL]);
-      MLA_WAIT(XL, ii & 1, 224);
+      if (lane == 0) tc::mbar_arrive(&bars[XL + (sw & 1)]);
+      MLA_WAIT(XL + (sw & 1), ii & 1, 224);
       const float ltot = lsum + red_l[ii & 1][l ^ 64];
       const float inv = 1.0f / ltot;
       __nv_bfloat16* orow = a.o + ((long long)tk * H + head) * DV;
