@@ -119,6 +119,17 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+# DRAM bytes (read + write) of one full-size launch of each config's roofline kernel, from a
+# one-pass ncu capture of this build (dram__bytes_read.sum + dram__bytes_write.sum; the
+# command and per-kernel split are in profiles/traffic_full_size.md).
+TRAFFIC = {
+    "indexer": 72764928 + 69933824,
+    "prefill": 2535907584 + 2112252416,
+    "decode": 313127680 + 10324480,
+    "train": (4376674816 + 94292736) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
+}
+
+
 # ----------------------------------------------------------------------------- timing helpers
 
 class Timer:
@@ -244,7 +255,8 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
         "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128>", "achieved": achieved,
                      "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
                      "peak_note": f"dense FP8 = 2 x {pk['_source']} bf16 burst {pk['bf16_tflops']} TFLOP/s",
-                     "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_score, "traffic": None},
+                     "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_score,
+                     "traffic": TRAFFIC["indexer"], "traffic_unit": "bytes per launch (ncu)"},
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
     }
@@ -281,7 +293,7 @@ def reference_indexer(args, rank, world) -> dict:
     q, k, w = c2_inputs(torch, seed=0)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_indexer(torch, q, k, w, sample=min(args.cpu_sample, 256))
+        r = cpu_indexer(torch, q, k, w, sample=min(args.cpu_sample // 4, 1024))
         if i >= args.warmup:
             vals.append(r["value"])
     v = statistics.mean(vals)
@@ -388,12 +400,13 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
         "roofline": {"bound": "tensor", "kernel": "mzb::mla::mla_fwd_kernel", "achieved": achieved,
                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
                      "peak_note": f"{pk['_source']} bf16 burst", "algorithmic_flops_per_launch": flops,
-                     "ms_per_launch": ms, "traffic": None},
+                     "ms_per_launch": ms, "traffic": TRAFFIC["prefill"],
+                     "traffic_unit": "bytes per launch (ncu)"},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        toks = _prefill_sample(C3["S"], max(8, args.cpu_sample // 16))
+        toks = _prefill_sample(C3["S"], max(8, args.cpu_sample // 9))
         out["cpu_baseline"] = cpu_prefill(q[0, toks].float().cpu().numpy(), toks, raw[0].cpu().numpy(),
                                           cmp[0].cpu().numpy(), idx[0, toks].cpu().numpy())
     return out
@@ -428,7 +441,7 @@ def reference_prefill(args, rank, world) -> dict:
     if rank != 0:
         return None
     S = C3["S"]
-    n_tok = max(8, args.cpu_sample // 64)
+    n_tok = max(8, args.cpu_sample // 256)
     toks = _prefill_sample(S, n_tok)
     g = torch.Generator().manual_seed(0)
     q_rows = torch.randn(n_tok, 128, 576, generator=g).to(torch.bfloat16).float().numpy()
@@ -542,14 +555,15 @@ def bench_train(args, torch, dist, rank, world, device) -> dict:
         "roofline": {"bound": "tensor", "kernel": "mzb::attnb::dkv_kernel + dq_kernel (backward)",
                      "achieved": ach_bwd, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": ach_bwd / pk["bf16_tflops"], "peak_note": f"{pk['_source']} bf16 burst",
-                     "algorithmic_flops_per_launch": bwd_flops, "ms_per_launch": ms_bwd, "traffic": None},
+                     "algorithmic_flops_per_launch": bwd_flops, "ms_per_launch": ms_bwd,
+                     "traffic": TRAFFIC["train"], "traffic_unit": "bytes per launch (ncu, dkv + dq kernels)"},
         "legs": {"fwd_ms": ms_fwd, "fwd_tflops": fwd_flops / (ms_fwd * 1e-3) / 1e12, "bwd_ms": ms_bwd,
                  "fq_q_ms": ms_fq, "fq_q_gbs": fq_bytes / (ms_fq * 1e-3) / 1e9},
         "gpu_launches": 7 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 16))
+        out["cpu_baseline"] = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 2))
     return out
 
 
@@ -598,7 +612,7 @@ def reference_train(args, rank, world) -> dict:
     do = torch.randn(1, S, 64, 128, generator=g).to(torch.bfloat16)
     vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 32))
+        r = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 128))
         if i >= args.warmup:
             vals.append(r["value"])
     val = statistics.mean(vals)
@@ -768,12 +782,12 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
         "roofline": {"bound": "hbm", "kernel": "mzb::idx::score_kernel<fp8,128> (decode indexer)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                      "peak_note": f"{pk['_source']} HBM copy", "algorithmic_bytes_per_launch": score_bytes,
-                     "ms_per_launch": ms_score, "traffic": None},
+                     "ms_per_launch": ms_score, "traffic": TRAFFIC["decode"], "traffic_unit": "bytes per launch (ncu)"},
         "gpu_launches": 6 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_decode(max(1, args.cpu_sample // 256))
+        out["cpu_baseline"] = cpu_decode(min(C4["B"], max(1, args.cpu_sample // 32)))
     return out
 
 
@@ -817,7 +831,7 @@ def cpu_decode(n_seq: int) -> dict:
 def reference_decode(args, rank, world) -> dict:
     if rank != 0:
         return None
-    n = max(1, args.cpu_sample // 512)
+    n = max(1, args.cpu_sample // 2048)
     vals = []
     for i in range(args.warmup + args.steps):
         r = cpu_decode(n)
@@ -843,7 +857,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="indexer", choices=sorted(BENCHES))
     ap.add_argument("--impl", default="mzb", choices=["mzb", "reference"])
-    ap.add_argument("--cpu-sample", type=int, default=1024)
+    ap.add_argument("--cpu-sample", type=int, default=4096,
+                    help="size of the timed CPU baseline sample (about 10 s of host work at the default)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true",
                     help="shrunken workload (profiling captures only; not a bench number)")
