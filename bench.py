@@ -187,12 +187,19 @@ def c2_inputs(torch, seed: int):
 def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     from mzoo_b200 import indexer, _lib
 
-    q, k, w = c2_inputs(torch, seed=rank)
+    from mzoo_b200.sharding import shard_tokens
+    q, k, w = c2_inputs(torch, seed=0)  # the same workload on every rank
     q8, sq = indexer.quantize_fp8(q.to(device))
     k8, sk = indexer.quantize_fp8(k.to(device))
     w = w.to(device)
     B, S, T, Hi, Di = (C2[x] for x in ("B", "S", "T", "Hi", "Di"))
     kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk), check=False)
+    toks = list(range(S))
+    if world > 1:  # (batch x 128-query chunk) units, cyclic over ranks: the same chunks of every batch
+        toks = shard_tokens(S, world, 128)[rank]
+        tk = torch.tensor(toks, device=device)
+        q8, sq, w = q8[:, tk].contiguous(), sq[:, tk].contiguous(), w[:, tk].contiguous()
+        kw.update(scales=(sq, sk), q_pos=(tk + C2["q_offset"]).to(torch.int32).view(1, -1).expand(B, -1))
     step = lambda: indexer.attn(q8, k8, w, **kw)  # noqa: E731
     timer = Timer(torch, device)
     sampler = ClockSampler(device.index)
@@ -206,23 +213,23 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     t_steps = timer.run(step, args.steps)
     # the dominant kernel alone (score GEMM), for the roofline
     qp, kp, wp, sqp, skp, scale, dt = indexer._prep(q8, k8, w, (sq, sk), None)
-    err = torch.zeros(1, dtype=torch.int32, device=device)
+    qpos = kw.get("q_pos")
+    qpos = qpos.contiguous() if qpos is not None else None
     t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C2["ratio"], C2["q_offset"], scale, dt,
-                                                False, err), args.steps)
+                                                False, False, qpos), args.steps)
     # end to end through the public API from pinned host memory
     hq8 = q8.view(torch.uint8).cpu().pin_memory()
     hk8 = k8.view(torch.uint8).cpu().pin_memory()
     hsq, hsk, hw = (x.cpu().pin_memory() for x in (sq, sk, w))
     dq8, dk8 = torch.empty_like(hq8, device=device), torch.empty_like(hk8, device=device)
     dsq, dsk, dw = (torch.empty_like(x, device=device) for x in (hsq, hsk, hw))
-    hout = torch.empty(B, S, C2["topk"], dtype=torch.int32).pin_memory()
+    hout = torch.empty(B, len(toks), C2["topk"], dtype=torch.int32).pin_memory()
 
     def e2e():
         for d, h in ((dq8, hq8), (dk8, hk8), (dsq, hsq), (dsk, hsk), (dw, hw)):
             d.copy_(h, non_blocking=True)
         idx = indexer.attn(dq8.view(torch.float8_e4m3fn), dk8.view(torch.float8_e4m3fn), dw,
-                           compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"],
-                           scales=(dsq, dsk), check=False)
+                           **dict(kw, scales=(dsq, dsk)))
         hout.copy_(idx, non_blocking=True)
 
     for _ in range(2):
@@ -230,26 +237,28 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     t_e2e = timer.run(e2e, args.steps, flush=False)
     clocks = sampler.stop(busy=step)
     torch.cuda.synchronize()
-    code = int(err.item())
-    assert code == 0, f"device error word {code}"
+    indexer.attn(q8, k8, w, **dict(kw, check=True))  # one checked call: raises on a device error word
     h2d = sum(x.numel() * x.element_size() for x in (hq8, hk8, hsq, hsk, hw))
     d2h = hout.numel() * hout.element_size()
 
     ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
     ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
     ms_score = sum(t_score) / len(t_score)
-    queries = B * S * world
-    flops = 2.0 * B * c2_pairs() * Hi * Di
+    queries = B * S  # the whole job: every rank does its share of one workload
+    pairs_local = sum(min(T, (C2["q_offset"] + s + 1) // C2["ratio"]) for s in toks)
+    flops = 2.0 * B * pairs_local * Hi * Di
     pk = peaks()
     fp8_peak = 2.0 * pk["bf16_tflops"]
     achieved = flops / (ms_score * 1e-3) / 1e12
     out = {
         "metric": "indexer Mq/s", "value": queries / (ms * 1e-3) / 1e6, "unit": "Mq/s",
-        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3 (fp32 accumulate)", "data": "synthetic (seeded N(0,1), absmax fp8)",
         "config": {"workload": "C2 lightning indexer + top-k", "B": B, "queries": S, "keys": T, "Hi": Hi, "Di": Di,
                    "compress_ratio": C2["ratio"], "topk": C2["topk"], "q_offset": C2["q_offset"],
-                   "parallelism": f"independent instance per GPU x{world}", "l2": "flushed (256 MB write) per step"},
+                   "parallelism": (f"(batch x 128-query chunk) units cyclic over {world} GPUs, keys replicated, no "
+                                   "collective in the step" if world > 1 else "1 GPU"),
+                   "l2": "flushed (256 MB write) per step"},
         "e2e": {"value": queries / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128>", "achieved": achieved,
@@ -342,18 +351,28 @@ def c3_inputs(torch, device, seed: int):
     return q, raw, cmp, idx
 
 
-def c3_pairs(torch, idx) -> int:
-    S = idx.shape[1]
-    win = sum(min(C3["window"], t + 1) for t in range(S))
+def c3_pairs(torch, idx, positions=None) -> int:
+    """Selected (query, key) pairs: valid compressed indices + window keys of each query
+    (query i sits at positions[i], default i)."""
+    positions = range(idx.shape[1]) if positions is None else positions
+    win = sum(min(C3["window"], t + 1) for t in positions)
     return int((idx >= 0).sum().item()) + win
 
 
 def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     from mzoo_b200 import sparse_mla
-    q, raw, cmp, idx = c3_inputs(torch, device, seed=2 * rank)
-    pairs = c3_pairs(torch, idx)
-    flops = sparse_mla.pair_flops(pairs)
-    step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], check=False)  # noqa: E731
+    from mzoo_b200.sharding import shard_tokens
+    q, raw, cmp, idx = c3_inputs(torch, device, seed=0)  # the same workload on every rank
+    total_flops = sparse_mla.pair_flops(c3_pairs(torch, idx))
+    pos, toks = None, None
+    if world > 1:  # this rank's cyclic 128-token chunks of the query axis; KV replicated
+        toks = shard_tokens(C3["S"], world, 128)[rank]
+        tk = torch.tensor(toks, device=device)
+        q, idx = q[:, tk].contiguous(), idx[:, tk].contiguous()
+        pos = tk.to(torch.int32).view(1, -1)
+    flops = sparse_mla.pair_flops(c3_pairs(torch, idx, toks))
+    n_q = q.shape[1]
+    step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], q_pos=pos, check=False)  # noqa: E731
     timer = Timer(torch, device)
     sampler = ClockSampler(device.index)
     sampler.start()
@@ -368,13 +387,13 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     # end to end from pinned host buffers
     hq, hraw, hcmp, hidx = (x.cpu().pin_memory() for x in (q, raw, cmp, idx))
     dq, draw, dcmp, didx = (torch.empty_like(x, device=device) for x in (hq, hraw, hcmp, hidx))
-    ho = torch.empty(1, C3["S"], C3["H"], 512, dtype=torch.bfloat16).pin_memory()
-    hl = torch.empty(1, C3["H"], C3["S"], dtype=torch.float32).pin_memory()
+    ho = torch.empty(1, n_q, C3["H"], 512, dtype=torch.bfloat16).pin_memory()
+    hl = torch.empty(1, C3["H"], n_q, dtype=torch.float32).pin_memory()
 
     def e2e():
         for d, h in ((dq, hq), (draw, hraw), (dcmp, hcmp), (didx, hidx)):
             d.copy_(h, non_blocking=True)
-        o, lse = sparse_mla.prefill(dq, draw, dcmp, didx, window=C3["window"], check=False)
+        o, lse = sparse_mla.prefill(dq, draw, dcmp, didx, window=C3["window"], q_pos=pos, check=False)
         ho.copy_(o, non_blocking=True)
         hl.copy_(lse, non_blocking=True)
 
@@ -384,18 +403,31 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     d2h = ho.numel() * ho.element_size() + hl.numel() * hl.element_size()
     ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
     ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    gather_ms = None
+    if dist:  # optional output gather (o of every rank's shard to every rank), timed on its own
+        o_loc, _ = step()
+        width = max(len(p) for p in shard_tokens(C3["S"], world, 128))
+        pad = o_loc.new_zeros((width,) + tuple(o_loc.shape[2:]))
+        pad[:n_q] = o_loc[0]
+        buf = o_loc.new_empty((world * width,) + tuple(o_loc.shape[2:]))
+        t_g = timer.run(lambda: dist.all_gather_into_tensor(buf, pad), 3, flush=False)
+        gather_ms = max_over_ranks(torch, dist, sum(t_g) / len(t_g), device)
     pk = peaks()
-    tflops = flops * world / (ms * 1e-3) / 1e12
+    tflops = total_flops / (ms * 1e-3) / 1e12
     achieved = flops / (ms * 1e-3) / 1e12
     out = {
         "metric": "sparse-MLA prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp8 KV dequant, fp32 acc)",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "bf16 (fp8 KV dequant, fp32 acc)",
         "data": "synthetic (seeded N(0,1); FP8 no-rope rows with per-64 absmax scales)",
         "config": {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": C3["S"], "heads": C3["H"],
                    "d_qk": 576, "d_v": 512, "topk": C3["topk"], "window": C3["window"], "compressed": C3["G"],
-                   "selected_pairs": pairs, "parallelism": f"independent instance per GPU x{world}",
+                   "total_flops": total_flops,
+                   "parallelism": (f"query tokens sharded over {world} GPUs (cyclic 128-token chunks, KV replicated,"
+                                   " no collective in the step)" if world > 1 else "1 GPU"),
+                   "o_gather_ms": gather_ms,
                    "l2": "inputs (2.4 GB q) larger than L2; 256 MB flush per step"},
-        "e2e": {"value": flops * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": total_flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": "mzb::mla::mla_fwd_kernel", "achieved": achieved,
                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
@@ -744,9 +776,8 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
     # dominant kernel legs
     from mzoo_b200 import indexer
     qp, kp, wp, sqp, skp, scale, dt = indexer._prep(x["q8"], x["k8"], x["w"], (x["sq"], x["sk"]), None)
-    err = torch.zeros(1, dtype=torch.int32, device=device)
     qpos = x["pos"].to(torch.int32).contiguous()
-    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C4["ratio"], 0, scale, dt, False, err, qpos),
+    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C4["ratio"], 0, scale, dt, False, False, qpos),
                         args.steps)
     # e2e: queries / indexer queries / weights from pinned host memory, o back to the host
     hq, hq8, hw = x["q"].cpu().pin_memory(), x["q8"].view(torch.uint8).cpu().pin_memory(), x["w"].cpu().pin_memory()

@@ -3,8 +3,8 @@ words and the call into ``mzb_attn_fwd`` (packed BSHD rows, K == V latent)."""
 
 import torch
 
-from . import _lib
-from ._lib import call, ptr, require_cuda, stream_ptr
+from . import ops
+from ._lib import require_cuda
 
 SUPPORTED_D = (64, 128, 256)
 
@@ -23,16 +23,7 @@ def check_mqa(q: torch.Tensor, kv: torch.Tensor, what: str) -> tuple:
 def run_fwd(q, kv, v, main_kv, idx, sinks, window, scale, check=True):
     require_cuda(q, kv, v, main_kv, idx, sinks)
     B, S, H, D = q.shape
-    dev = q.device
-    o = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(B, S * H, dtype=torch.float32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    G = main_kv.shape[1] if main_kv is not None else 0
-    topk = idx.shape[2] if idx is not None else 0
-    call("mzb_attn_fwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(sinks), ptr(o), ptr(lse), B, S, H, D,
-         window, G, topk, float(scale), ptr(err), stream_ptr(dev))
-    if check and int(err.item()):
-        raise _lib.MzbError(f"attn_fwd: device error code {int(err.item())}")
+    o, lse = ops.attn_fwd(q, kv, v, main_kv, idx, sinks, window, float(scale), check)
     return o, lse.view(B, S, H).permute(0, 2, 1).contiguous()
 
 
@@ -41,25 +32,10 @@ def run_bwd(q, kv, v, main_kv, idx, o, lse, do, sinks, window, scale, check=True
     dmain [B,G,1,D] or None, dsinks [H] or None)."""
     require_cuda(q, kv, v, main_kv, idx, o, lse, do)
     B, S, H, D = q.shape
-    dev = q.device
-    rpad = -(-S * H // 128) * 128
     lse_packed = lse.permute(0, 2, 1).reshape(B, S * H).contiguous()  # [B,H,S] -> token-major rows
-    dq = torch.empty_like(q)
-    dk = torch.empty(B, S, 1, D, dtype=torch.bfloat16, device=dev)
-    dv = torch.empty_like(dk) if v is not None else None
     G = main_kv.shape[1] if main_kv is not None else 0
-    topk = idx.shape[2] if idx is not None else 0
-    dmain = torch.zeros(B, max(G, 1), D, dtype=torch.float32, device=dev) if G else None
-    delta = torch.empty(B, rpad, dtype=torch.float32, device=dev)
-    lse2 = torch.empty(B, rpad, dtype=torch.float32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    splits = _lib.lib().mzb_attn_bwd_splits(B, S, H, window)
-    part = torch.empty(splits * B * S * 2 * D, dtype=torch.float32, device=dev)
-    call("mzb_attn_bwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(o), ptr(lse_packed), ptr(do), ptr(dq),
-         ptr(dk), ptr(dv), ptr(dmain), ptr(delta), ptr(lse2), ptr(part), splits, B, S, H, D, window, G, topk,
-         float(scale), ptr(err), stream_ptr(dev))
-    if check and int(err.item()):
-        raise _lib.MzbError(f"attn_bwd: device error code {int(err.item())}")
+    dq, dk, dv, dmain, delta = ops.attn_bwd(q, kv, v, main_kv, idx, o, lse_packed, do, window, float(scale), check)
+    dv = dv if v is not None else None
     dsinks = None
     if sinks is not None:  # swa_attn/bwd.py, csa2_attn/bwd.py:123-127: a torch reduce over lse / delta
         d = delta[:, :S * H].view(B, S, H).permute(0, 2, 1)

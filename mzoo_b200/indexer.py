@@ -23,8 +23,8 @@ in ascending order, ``-1`` padded where fewer keys are visible.  (The reference 
 
 import torch
 
-from . import _lib
-from ._lib import call, ptr, require_cuda, stream_ptr
+from . import ops
+from ._lib import require_cuda
 
 KB_PARTS = 16
 # relative bound on the fp32 tensor-core score error: |approx - exact| <= EPS * A_s * B_t
@@ -60,13 +60,8 @@ def _prep(q, k, w, scales, softmax_scale):
     return q, k, w, sq, sk, float(scale), dt
 
 
-def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, err, q_pos=None):
-    B, S, Hi, Di = q.shape
-    T = k.shape[1]
-    out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
-    call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(out), B, S, T, Hi, Di, dt,
-         ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
-    return out
+def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, check, q_pos=None):
+    return ops.indexer_scores(q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dt, write_tail, check)
 
 
 def _positions(q_pos, B, S, device):
@@ -75,14 +70,6 @@ def _positions(q_pos, B, S, device):
     q_pos = q_pos.to(device=device, dtype=torch.int32).contiguous()
     assert q_pos.shape == (B, S), f"q_pos must be [B, S]={(B, S)}, got {tuple(q_pos.shape)}"
     return q_pos
-
-
-def _check_err(err: torch.Tensor, what: str) -> None:
-    code = int(err.item())
-    if code == _lib.MZB_ERR_BOUND:
-        raise _lib.MzbError(f"{what}: error bound left too many top-k candidates (raise EPS coverage)")
-    if code:
-        raise _lib.MzbError(f"{what}: device wait gave up (code {code})")
 
 
 def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, q_offset: int = 0,
@@ -96,11 +83,7 @@ def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: in
     B, S = q.shape[:2]
     if k.shape[1] == 0:
         return q.new_empty((B, S, 0), dtype=torch.float32)
-    err = torch.zeros(1, dtype=torch.int32, device=q.device)
-    out = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, err, _positions(q_pos, B, S, q.device))
-    if check:
-        _check_err(err, "indexer.fwd")
-    return out
+    return _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, check, _positions(q_pos, B, S, q.device))
 
 
 def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, topk: int, q_offset: int = 0,
@@ -115,15 +98,9 @@ def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: i
     out = torch.full((B, S, topk), -1, dtype=torch.int32, device=q.device)
     if topk == 0 or T == 0:
         return out
-    err = torch.zeros(1, dtype=torch.int32, device=q.device)
     qp = _positions(q_pos, B, S, q.device)
-    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, err, qp)
-    kb = torch.empty(B * KB_PARTS, dtype=torch.float32, device=q.device)
-    call("mzb_indexer_topk", ptr(sc), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(qp), ptr(kb), ptr(out), B, S,
-         T, Hi, Di, dt, compress_ratio, q_offset, scale, topk, EPS, ptr(err), stream_ptr(q.device))
-    if check:
-        _check_err(err, "indexer.attn")
-    return out
+    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, check, qp)
+    return ops.indexer_topk(sc, q, k, w, sq, sk, qp, compress_ratio, q_offset, scale, dt, topk, EPS, KB_PARTS, check)
 
 
 def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, compress_ratio: int,
@@ -147,15 +124,8 @@ def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, 
     if hp != Hi:  # pad heads to a power of two >= 16 with zero weights (their gradients are discarded)
         qp = torch.cat([qp, qp.new_zeros(B, S, hp - Hi, Di)], dim=2).contiguous()
         wp = torch.cat([wp, wp.new_zeros(B, S, hp - Hi)], dim=2).contiguous()
-    dq = torch.empty(B, S, hp, Di, dtype=torch.bfloat16, device=q.device)
-    dk = torch.empty(B, T, Di, dtype=torch.bfloat16, device=q.device)
-    dw = torch.empty(B, S, hp, dtype=torch.float32, device=q.device)
-    err = torch.zeros(1, dtype=torch.int32, device=q.device)
     scale = softmax_scale if softmax_scale is not None else Di**-0.5
-    call("mzb_indexer_bwd", ptr(qp), ptr(k.contiguous()), ptr(wp), ptr(dl.contiguous()), ptr(dq), ptr(dk), ptr(dw),
-         B, S, T, hp, Di, compress_ratio, q_offset, float(scale), ptr(err), stream_ptr(q.device))
-    if check:
-        _check_err(err, "indexer.bwd")
+    dq, dk, dw = ops.indexer_bwd(qp, k.contiguous(), wp, dl.contiguous(), compress_ratio, q_offset, float(scale), check)
     return dq[:, :, :Hi], dk, dw[:, :, :Hi]
 
 

@@ -49,3 +49,179 @@ def fq_fp8(x: torch.Tensor, block_size: int, rule: int) -> torch.Tensor:
 @fq_fp8.register_fake
 def _(x, block_size, rule):
     return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+def _err(dev) -> torch.Tensor:
+    return torch.zeros(1, dtype=torch.int32, device=dev)
+
+
+def _raise_on(err: torch.Tensor, what: str) -> None:
+    code = int(err.item())
+    if code == _lib.MZB_ERR_BOUND:
+        raise _lib.MzbError(f"{what}: error bound left too many top-k candidates")
+    if code:
+        raise _lib.MzbError(f"{what}: device error code {code} (a bounded device wait gave up)")
+
+
+# ----------------------------------------------------------------------------- indexer
+
+@torch.library.custom_op("mzb::indexer_scores", mutates_args=())
+def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, sq: torch.Tensor | None,
+                   sk: torch.Tensor | None, q_pos: torch.Tensor | None, ratio: int, q_offset: int, scale: float,
+                   dtype: int, write_tail: bool, check: bool) -> torch.Tensor:
+    """fp32 [B,S,T] scores of ``mzb_indexer_scores`` (q [B,S,Hi,Di], k [B,T,Di] contiguous)."""
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
+    err = _err(q.device)
+    call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(out), B, S, T, Hi, Di, dtype,
+         ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
+    if check:
+        _raise_on(err, "indexer scores")
+    return out
+
+
+@indexer_scores.register_fake
+def _(q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dtype, write_tail, check):
+    return q.new_empty((q.shape[0], q.shape[1], k.shape[1]), dtype=torch.float32)
+
+
+@torch.library.custom_op("mzb::indexer_topk", mutates_args=())
+def indexer_topk(scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, sq: torch.Tensor | None,
+                 sk: torch.Tensor | None, q_pos: torch.Tensor | None, ratio: int, q_offset: int, scale: float,
+                 dtype: int, topk: int, eps: float, kb_parts: int, check: bool) -> torch.Tensor:
+    """int32 [B,S,topk] exact top-k of ``mzb_indexer_topk`` (ascending, -1 padded)."""
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    out = torch.empty(B, S, topk, dtype=torch.int32, device=q.device)
+    kb = torch.empty(B * kb_parts, dtype=torch.float32, device=q.device)
+    err = _err(q.device)
+    call("mzb_indexer_topk", ptr(scores), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(kb), ptr(out),
+         B, S, T, Hi, Di, dtype, ratio, q_offset, scale, topk, eps, ptr(err), stream_ptr(q.device))
+    if check:
+        _raise_on(err, "indexer top-k")
+    return out
+
+
+@indexer_topk.register_fake
+def _(scores, q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dtype, topk, eps, kb_parts, check):
+    return q.new_empty((q.shape[0], q.shape[1], topk), dtype=torch.int32)
+
+
+@torch.library.custom_op("mzb::indexer_bwd", mutates_args=())
+def indexer_bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, ratio: int, q_offset: int,
+                scale: float, check: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dq bf16, dk bf16, dw fp32) of ``mzb_indexer_bwd`` (heads already padded to 2^n >= 16)."""
+    B, S, Hi, Di = q.shape
+    T = k.shape[1]
+    dq = torch.empty(B, S, Hi, Di, dtype=torch.bfloat16, device=q.device)
+    dk = torch.empty(B, T, Di, dtype=torch.bfloat16, device=q.device)
+    dw = torch.empty(B, S, Hi, dtype=torch.float32, device=q.device)
+    err = _err(q.device)
+    call("mzb_indexer_bwd", ptr(q), ptr(k), ptr(w), ptr(dl), ptr(dq), ptr(dk), ptr(dw), B, S, T, Hi, Di, ratio,
+         q_offset, scale, ptr(err), stream_ptr(q.device))
+    if check:
+        _raise_on(err, "indexer backward")
+    return dq, dk, dw
+
+
+@indexer_bwd.register_fake
+def _(q, k, w, dl, ratio, q_offset, scale, check):
+    B, S, Hi, Di = q.shape
+    return (q.new_empty((B, S, Hi, Di), dtype=torch.bfloat16), q.new_empty((B, k.shape[1], Di), dtype=torch.bfloat16),
+            q.new_empty((B, S, Hi), dtype=torch.float32))
+
+
+# ----------------------------------------------------------------------------- window / sparse attention
+
+@torch.library.custom_op("mzb::attn_fwd", mutates_args=())
+def attn_fwd(q: torch.Tensor, kv: torch.Tensor, v: torch.Tensor | None, main_kv: torch.Tensor | None,
+             idx: torch.Tensor | None, sinks: torch.Tensor | None, window: int, scale: float,
+             check: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o bf16 [B,S,H,D], lse fp32 [B,S*H] token-major) of ``mzb_attn_fwd``."""
+    B, S, H, D = q.shape
+    dev = q.device
+    o = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(B, S * H, dtype=torch.float32, device=dev)
+    err = _err(dev)
+    G = main_kv.shape[1] if main_kv is not None else 0
+    topk = idx.shape[2] if idx is not None else 0
+    call("mzb_attn_fwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(sinks), ptr(o), ptr(lse), B, S, H, D,
+         window, G, topk, scale, ptr(err), stream_ptr(dev))
+    if check:
+        _raise_on(err, "attention forward")
+    return o, lse
+
+
+@attn_fwd.register_fake
+def _(q, kv, v, main_kv, idx, sinks, window, scale, check):
+    B, S, H, D = q.shape
+    return q.new_empty((B, S, H, D), dtype=torch.bfloat16), q.new_empty((B, S * H), dtype=torch.float32)
+
+
+@torch.library.custom_op("mzb::attn_bwd", mutates_args=())
+def attn_bwd(q: torch.Tensor, kv: torch.Tensor, v: torch.Tensor | None, main_kv: torch.Tensor | None,
+             idx: torch.Tensor | None, o: torch.Tensor, lse_rows: torch.Tensor, do: torch.Tensor, window: int,
+             scale: float, check: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(dq, dk, dv, dmain fp32, delta) of ``mzb_attn_bwd``; ``lse_rows`` fp32 [B,S*H]
+    token-major.  dv is empty when v is None (dk then holds dK + dV), dmain empty without
+    gathered keys; delta = rowsum(dO * O) fp32 [B, S*H rounded up to 128]."""
+    B, S, H, D = q.shape
+    dev = q.device
+    rpad = -(-S * H // 128) * 128
+    dq = torch.empty_like(q)
+    dk = torch.empty(B, S, 1, D, dtype=torch.bfloat16, device=dev)
+    dv = torch.empty_like(dk) if v is not None else q.new_empty((0,), dtype=torch.bfloat16)
+    G = main_kv.shape[1] if main_kv is not None else 0
+    topk = idx.shape[2] if idx is not None else 0
+    dmain = torch.zeros(B, G, D, dtype=torch.float32, device=dev) if G else q.new_empty((0,), dtype=torch.float32)
+    delta = torch.empty(B, rpad, dtype=torch.float32, device=dev)
+    lse2 = torch.empty(B, rpad, dtype=torch.float32, device=dev)
+    err = _err(dev)
+    splits = _lib.lib().mzb_attn_bwd_splits(B, S, H, window)
+    part = torch.empty(splits * B * S * 2 * D, dtype=torch.float32, device=dev)
+    call("mzb_attn_bwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(o), ptr(lse_rows), ptr(do), ptr(dq),
+         ptr(dk), ptr(dv if v is not None else None), ptr(dmain if G else None), ptr(delta), ptr(lse2), ptr(part), splits,
+         B, S, H, D, window, G, topk, scale, ptr(err), stream_ptr(dev))
+    if check:
+        _raise_on(err, "attention backward")
+    return dq, dk, dv, dmain, delta
+
+
+@attn_bwd.register_fake
+def _(q, kv, v, main_kv, idx, o, lse_rows, do, window, scale, check):
+    B, S, H, D = q.shape
+    rpad = -(-S * H // 128) * 128
+    G = main_kv.shape[1] if main_kv is not None else 0
+    dv = q.new_empty((B, S, 1, D) if v is not None else (0,), dtype=torch.bfloat16)
+    dmain = q.new_empty((B, G, D) if G else (0,), dtype=torch.float32)
+    return (q.new_empty(q.shape, dtype=torch.bfloat16), q.new_empty((B, S, 1, D), dtype=torch.bfloat16), dv, dmain,
+            q.new_empty((B, rpad), dtype=torch.float32))
+
+
+# ----------------------------------------------------------------------------- sparse latent MLA
+
+@torch.library.custom_op("mzb::sparse_mla_fwd", mutates_args=())
+def sparse_mla_fwd(q: torch.Tensor, kv_raw: torch.Tensor, kv_cmp: torch.Tensor, idx: torch.Tensor,
+                   pos: torch.Tensor, raw_pt: torch.Tensor | None, cmp_pt: torch.Tensor | None,
+                   cmp_lens: torch.Tensor | None, n_tok: int, tok_per_seq: int, topk: int, window: int, raw_len: int,
+                   cmp_len: int, raw_ptw: int, cmp_ptw: int, scale: float,
+                   check: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o bf16 [n_tok,128,512], lse fp32 [n_tok,128]) of ``mzb_sparse_mla_fwd``."""
+    dev = q.device
+    o = torch.empty(n_tok, 128, 512, dtype=torch.bfloat16, device=dev)
+    lse = torch.empty(n_tok, 128, dtype=torch.float32, device=dev)
+    slots = torch.empty(max(n_tok, 1), dtype=torch.int32, device=dev)
+    err = _err(dev)
+    call("mzb_sparse_mla_fwd", ptr(q), ptr(kv_raw), ptr(kv_cmp), ptr(idx), ptr(pos), ptr(raw_pt), ptr(cmp_pt),
+         ptr(cmp_lens), ptr(slots), ptr(o), ptr(lse), n_tok, tok_per_seq, topk, window, raw_len, cmp_len, raw_ptw,
+         cmp_ptw, scale, ptr(err), stream_ptr(dev))
+    if check:
+        _raise_on(err, "sparse_mla")
+    return o, lse
+
+
+@sparse_mla_fwd.register_fake
+def _(q, kv_raw, kv_cmp, idx, pos, raw_pt, cmp_pt, cmp_lens, n_tok, tok_per_seq, topk, window, raw_len, cmp_len,
+      raw_ptw, cmp_ptw, scale, check):
+    return q.new_empty((n_tok, 128, 512), dtype=torch.bfloat16), q.new_empty((n_tok, 128), dtype=torch.float32)

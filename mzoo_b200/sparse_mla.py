@@ -15,8 +15,8 @@ lse in natural log.
 
 import torch
 
-from . import _lib
-from ._lib import call, ptr, require_cuda, stream_ptr
+from . import ops
+from ._lib import require_cuda
 
 H, DQK, DV, ROW_BYTES = 128, 576, 512, 672
 
@@ -41,26 +41,17 @@ def pack_kv(kv: torch.Tensor) -> torch.Tensor:
 
 def _run(q2, raw, cmp, idx, pos, raw_pt, cmp_pt, cmp_lens, n_tok, tok_per_seq, topk, window, raw_len, cmp_len,
          raw_ptw, cmp_ptw, scale, check):
-    dev = q2.device
-    o = torch.empty(n_tok, H, DV, dtype=torch.bfloat16, device=dev)
-    lse = torch.empty(n_tok, H, dtype=torch.float32, device=dev)
-    slots = torch.empty(max(n_tok, 1), dtype=torch.int32, device=dev)
-    err = torch.zeros(1, dtype=torch.int32, device=dev)
-    call("mzb_sparse_mla_fwd", ptr(q2), ptr(raw), ptr(cmp), ptr(idx), ptr(pos), ptr(raw_pt), ptr(cmp_pt),
-         ptr(cmp_lens), ptr(slots), ptr(o), ptr(lse), n_tok, tok_per_seq, topk, window, raw_len, cmp_len, raw_ptw,
-         cmp_ptw, scale, ptr(err), stream_ptr(dev))
-    if check:
-        code = int(err.item())
-        if code:
-            raise _lib.MzbError(f"sparse_mla: device error code {code}")
-    return o, lse
+    return ops.sparse_mla_fwd(q2, raw, cmp, idx, pos, raw_pt, cmp_pt, cmp_lens, n_tok, tok_per_seq, topk, window,
+                              raw_len, cmp_len, raw_ptw, cmp_ptw, scale, check)
 
 
 def prefill(q: torch.Tensor, kv: torch.Tensor, kv_cmp: torch.Tensor, indices: torch.Tensor, *, window: int = 128,
-            softmax_scale: float | None = None, q_offset: int = 0, check: bool = True):
+            softmax_scale: float | None = None, q_offset: int = 0, q_pos: torch.Tensor | None = None,
+            check: bool = True):
     """q bf16 [B,S,128,576]; kv uint8 [B,S_raw,672] raw latent rows (query s sits at
-    position s + q_offset < S_raw); kv_cmp uint8 [B,G,672]; indices int32 [B,S,topk]
-    -> (o bf16 [B,S,128,512], lse fp32 [B,128,S])."""
+    position s + q_offset < S_raw, or at ``q_pos[b, s]`` when given -- an arbitrary subset of
+    a sequence's queries, e.g. one rank's shard); kv_cmp uint8 [B,G,672]; indices int32
+    [B,S,topk] -> (o bf16 [B,S,128,512], lse fp32 [B,128,S])."""
     require_cuda(q, kv, kv_cmp, indices)
     assert q.dtype == torch.bfloat16 and q.dim() == 4 and q.shape[2:] == (H, DQK), \
         f"q must be bf16 [B, S, {H}, {DQK}], got {q.dtype} {tuple(q.shape)}"
@@ -69,10 +60,16 @@ def prefill(q: torch.Tensor, kv: torch.Tensor, kv_cmp: torch.Tensor, indices: to
     assert kv_cmp.dtype == torch.uint8 and kv_cmp.dim() == 3 and kv_cmp.shape[0] == B and kv_cmp.shape[2] == ROW_BYTES
     assert indices.dim() == 3 and indices.shape[:2] == (B, S), f"indices must be [B, S, topk], got {tuple(indices.shape)}"
     assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
-    assert q_offset >= 0 and S + q_offset <= kv.shape[1], "every query position must have its raw KV row"
     topk = indices.shape[2]
     idx = indices.to(torch.int32).contiguous()
-    pos = (torch.arange(S, device=q.device, dtype=torch.int32) + q_offset).repeat(B)
+    if q_pos is None:
+        assert q_offset >= 0 and S + q_offset <= kv.shape[1], "every query position must have its raw KV row"
+        pos = (torch.arange(S, device=q.device, dtype=torch.int32) + q_offset).repeat(B)
+    else:
+        assert q_pos.shape == (B, S), f"q_pos must be [B, S]={(B, S)}, got {tuple(q_pos.shape)}"
+        pos = q_pos.to(device=q.device, dtype=torch.int32).contiguous().view(B * S)
+        if check and S:
+            assert 0 <= int(pos.min()) and int(pos.max()) < kv.shape[1], "every query position must have its raw KV row"
     cmp = kv_cmp if kv_cmp.shape[1] else kv  # never dereferenced when G == 0
     scale = softmax_scale if softmax_scale is not None else DQK**-0.5
     o, lse = _run(q.contiguous(), kv.contiguous(), cmp.contiguous(), idx, pos, None, None, None, B * S, S, topk,

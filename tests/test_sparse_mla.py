@@ -146,3 +146,28 @@ def test_prefill_deterministic(cuda):
     a = sparse_mla.prefill(q, kv, cmp, idx)
     b = sparse_mla.prefill(q, kv, cmp, idx)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+@pytest.mark.gpu
+def test_prefill_token_shards_match_full(cuda):
+    """One rank's cyclic shard of query tokens (explicit q_pos) reproduces exactly the rows
+    of the full prefill: every token's attention is independent of the others."""
+    import torch
+    from mzoo_b200 import sparse_mla
+    from mzoo_b200.sharding import shard_tokens
+    rng = np.random.default_rng(11)
+    B, S, G, topk, window = 1, 256, 64, 32, 64
+    q = torch.from_numpy(rng.standard_normal((B, S, 128, 576)).astype(np.float32)).to(torch.bfloat16).to(cuda)
+    raw = sparse_mla.pack_kv(torch.from_numpy(rng.standard_normal((B, S, 576)).astype(np.float32)).to(cuda))
+    cmp = sparse_mla.pack_kv(torch.from_numpy(rng.standard_normal((B, G, 576)).astype(np.float32)).to(cuda))
+    idx = np.full((B, S, topk), -1, np.int32)
+    for s in range(S):
+        n = min(G, (s + 1) // 4)
+        sel = np.sort(rng.permutation(n)[:topk])
+        idx[0, s, :len(sel)] = sel
+    it = torch.from_numpy(idx).to(cuda)
+    o, lse = sparse_mla.prefill(q, raw, cmp, it, window=window)
+    for part in shard_tokens(S, 3, chunk=32):
+        tk = torch.tensor(part, device=cuda)
+        os_, ls_ = sparse_mla.prefill(q[:, tk], raw, cmp, it[:, tk], window=window, q_pos=tk.view(1, -1))
+        assert torch.equal(os_, o[:, tk]) and torch.equal(ls_, lse[:, :, tk])
