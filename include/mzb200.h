@@ -158,15 +158,21 @@ MZB_API int mzb_attn_bwd_splits(int64_t B, int64_t S, int H, int window);
  *   raw_page_table [B, raw_ptw] / cmp_page_table [B, cmp_ptw].  cmp_lens [B] (or NULL =
  *   cmp_len) bounds valid compressed indices.  Outputs o bf16 [n_tok, 128, 512] and
  *   lse fp32 [n_tok, 128] (natural log).  slots_ws: int32 workspace [n_tok].
+ *   splits: key-range splits per token (1, or mzb_sparse_mla_splits(n_tok) for calls with
+ *   few tokens such as decode); with splits > 1, part_ws holds splits * n_tok * 128 * 513
+ *   floats (each split's normalised output and lse, merged by a second kernel).
  */
 MZB_API int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void* kv_cmp, const int32_t* indices,
                                const int32_t* q_pos, const int32_t* raw_page_table, const int32_t* cmp_page_table,
                                const int32_t* cmp_lens, int32_t* slots_ws, void* o, float* lse, int64_t n_tok,
                                int tok_per_seq, int topk, int window, int64_t raw_len, int64_t cmp_len, int raw_ptw,
-                               int cmp_ptw, float softmax_scale, int* err, void* stream);
+                               int cmp_ptw, float softmax_scale, int splits, float* part_ws, int* err, void* stream);
+/* Key-range splits per token mzb_sparse_mla_fwd should use for n_tok tokens (1 unless the
+ * tokens alone leave SM pairs idle).  Host-only, no launch. */
+MZB_API int mzb_sparse_mla_splits(int64_t n_tok);
 
 /* mzb_sparse_mla_fwd_noalloc -- no counterpart in the reference.  Same arguments and
- *   result as mzb_sparse_mla_fwd minus `slots_ws`: for callers that cannot allocate device
+ *   result as mzb_sparse_mla_fwd minus `slots_ws`, `splits` and `part_ws` (one split): for callers that cannot allocate device
  *   memory at launch time (a serving engine whose free HBM all belongs to its KV-cache
  *   pool, or a host whose own memory manager must not be bypassed).  The workspace comes
  *   from a fixed 65536-entry (256 KB) array inside the library, present on every GPU that

@@ -45,7 +45,8 @@ SIGNATURES = {
                      _I32, _I64, _I32, _F32, _P, _P],
     "mzb_attn_bwd_splits": [_I64, _I64, _I32, _I32],
     "mzb_sparse_mla_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64, _I32,
-                           _I32, _F32, _P, _P],
+                           _I32, _F32, _I32, _P, _P, _P],
+    "mzb_sparse_mla_splits": [_I64],
     "mzb_sparse_mla_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64,
                                    _I32, _I32, _F32, _P, _P],
 }

@@ -33,8 +33,11 @@ struct Fp4Op {
       return e >= -126 ? __uint_as_float(uint32_t(e + 127) << 23) : __uint_as_float(1u << (e + 149));
     }
   }
-  __device__ __forceinline__ float apply(float x, float s) const {
-    float q = clamp_nan(__fdiv_rn(x, s), -6.0f, 6.0f);
+  // Power-of-two scales (ue8m0 and OCP rules, 2^-127..2^127): 1/s is an exactly
+  // representable float, so x * (1/s) is the same correctly rounded value as x / s.
+  __device__ __forceinline__ bool pow2() const { return rule != FP4_E4M3; }
+  __device__ __forceinline__ float apply(float x, float s, float inv) const {
+    float q = clamp_nan(pow2() ? __fmul_rn(x, inv) : __fdiv_rn(x, s), -6.0f, 6.0f);
     return __fmul_rn(e2m1_value(q), s);
   }
 };
@@ -46,8 +49,9 @@ struct Fp8Op {
     float s = __fdiv_rn(amax, 448.0f);
     return s > 0.0f ? s : 1.0f;
   }
-  __device__ __forceinline__ float apply(float x, float s) const {
-    float q = clamp_nan(__fdiv_rn(x, s), -448.0f, 448.0f);
+  __device__ __forceinline__ bool pow2() const { return rule == FP8_UE8M0; }
+  __device__ __forceinline__ float apply(float x, float s, float inv) const {
+    float q = clamp_nan(pow2() ? __fmul_rn(x, inv) : __fdiv_rn(x, s), -448.0f, 448.0f);
     return __fmul_rn(e4m3_round(q), s);
   }
 };
@@ -89,10 +93,11 @@ __global__ void __launch_bounds__(256) fq_vec_kernel(const void* __restrict__ x_
     }
     if (active) {
       const float s = op.scale(amax);
+      const float inv = op.pow2() ? __frcp_rn(s) : 0.0f;  // exact for a power of two
       uint4 out;
       T* o = reinterpret_cast<T*>(&out);
 #pragma unroll
-      for (int i = 0; i < V; ++i) o[i] = E::store(op.apply(v[i], s));
+      for (int i = 0; i < V; ++i) o[i] = E::store(op.apply(v[i], s, inv));
       reinterpret_cast<uint4*>(y)[t] = out;
     }
   }
@@ -112,7 +117,8 @@ __global__ void fq_scalar_kernel(const void* __restrict__ x_, void* __restrict__
     float amax = 0.0f;
     for (int i = 0; i < block; ++i) amax = amax_step(amax, E::load(xb[i]));
     const float s = op.scale(amax);
-    for (int i = 0; i < block; ++i) y[b * block + i] = E::store(op.apply(E::load(xb[i]), s));
+    const float inv = op.pow2() ? __frcp_rn(s) : 0.0f;
+    for (int i = 0; i < block; ++i) y[b * block + i] = E::store(op.apply(E::load(xb[i]), s, inv));
   }
 }
 

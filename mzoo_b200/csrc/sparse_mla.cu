@@ -90,6 +90,9 @@ struct Args {
   long long raw_len, cmp_len;  // rows per sequence of the dense layouts
   int raw_ptw, cmp_ptw;
   float scale_log2;
+  int n_split;      // key-range splits per token (1: write o/lse directly)
+  float* o_part;    // [n_split, n_tok, 128, 512] fp32, each split's normalised output
+  float* lse_part;  // [n_split, n_tok, 128] fp32 natural-log lse (-inf: empty split)
   int* err;
 };
 
@@ -230,14 +233,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     else tc::mbar_arrive_cluster(leader_bar(i));
   };
   auto n_tiles = [&](int tk) { return (a.n_slots[tk] + NT - 1) / NT; };
+  // work item = (token, key-range split), heaviest tokens first; tiles [t0, t1) of the
+  // token's key list (an empty range when the token has fewer tiles than splits)
+  const int items = a.n_tok * a.n_split;
+  auto item_range = [&](int it, int& tk, int& sp, int& t0, int& t1) {
+    tk = a.n_tok - 1 - it / a.n_split;
+    sp = it % a.n_split;
+    const int n = n_tiles(tk), per = (n + a.n_split - 1) / a.n_split;
+    t0 = sp * per;
+    t1 = min(n, t0 + per);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ Q loader
     if (lane == 0) {
       int ii = 0;
       bool issued = false;
-      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs, ++ii) {
-        const int tk = a.n_tok - 1 - it;
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
+        if (t0 >= t1) continue;
         MLA_WAIT_CL(Q_EMPTY, (ii & 1) ^ 1, 201);
         tc::mbar_expect_tx(&bars[Q_FULL], Q_BYTES);
         for (int cb = 0; cb < QBLK; ++cb)
@@ -246,6 +261,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         MLA_WAIT(Q_FULL, ii & 1, 202);
         issued = false;
         arrive_leader(Q_READY);
+        ++ii;
       }
       if (issued) tc::mbar_wait(&bars[Q_FULL], (ii & 1), nullptr, 0);  // drain before exit
     }
@@ -282,12 +298,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tc::mma2_commit_mc(&bars[O_DONE], 3);
         return true;
       };
-      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs, ++ii) {
-        const int tk = a.n_tok - 1 - it;
-        const int n = n_tiles(tk);
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
+        if (t0 >= t1) continue;
         MLA_WAIT_CL(Q_READY, ii & 1, 210);
         bool ok = true;
-        for (int j = 0; j < n; ++j, ++g) {
+        for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
           if (!tc::mbar_wait_cl(&bars[K_FULL + st], ph, a.err, 214) ||
               !tc::mbar_wait_cl(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
@@ -302,11 +319,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           }
           tc::mma2_commit_mc(&bars[K_EMPTY + st], 3);
           tc::mma2_commit_mc(&bars[S_FULL + st], 3);
-          if (j == n - 1) tc::mma2_commit_mc(&bars[Q_EMPTY], 3);
-          if (j >= 1 && !pv(g - 1, j == 1, ii)) { ok = false; break; }
+          if (j == t1 - 1) tc::mma2_commit_mc(&bars[Q_EMPTY], 3);
+          if (j > t0 && !pv(g - 1, j == t0 + 1, ii)) { ok = false; break; }
         }
-        if (!ok || !pv(g - 1, n == 1, ii)) { abort_flag = 1; break; }
+        if (!ok || !pv(g - 1, t1 - t0 == 1, ii)) { abort_flag = 1; break; }
         tc::mma2_commit_mc(&bars[O_FINAL], 3);
+        ++ii;
       }
     }
   } else if (warp >= 4 && warp < 8) {
@@ -317,9 +335,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     const int head = int(rank) * HC + hrow;
     const float sl = a.scale_log2;
     int g = 0, ii = 0;
-    for (int it = pair; it < a.n_tok && !abort_flag; it += npairs, ++ii) {
-      const int tk = a.n_tok - 1 - it;
-      const int n = n_tiles(tk);
+    for (int it = pair; it < items && !abort_flag; it += npairs) {
+      int tk, sp, t0, t1;
+      item_range(it, tk, sp, t0, t1);
+      if (t0 >= t1) {  // a split with no keys: an empty partial for the combine
+        float* orow = a.o_part + (((long long)sp * a.n_tok + tk) * H + head) * DV;
+        for (int c = kh * 128; c < DV; c += 256)
+          for (int q = 0; q < 128; q += 4) *reinterpret_cast<float4*>(orow + c + q) = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kh == 0) a.lse_part[((long long)sp * a.n_tok + tk) * H + head] = -INFINITY;
+        continue;
+      }
       const Slot s = item_info(a, tk);
       float m = -1e30f, lsum = 0.0f;
       bool ok = true;
@@ -331,11 +356,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         return c < a.topk ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
       };
       const int kofs = kh * NTH + lane;
-      int code_next = slot_code(kofs);
-      for (int j = 0; j < n; ++j, ++g) {
+      int code_next = slot_code(t0 * NT + kofs);
+      for (int j = t0; j < t1; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
         const int code = code_next;
-        if (j + 1 < n) code_next = slot_code((j + 1) * NT + kofs);
+        if (j + 1 < t1) code_next = slot_code((j + 1) * NT + kofs);
         const int p = j * NT + kofs;
         const uint32_t vmask = __ballot_sync(0xffffffffu, p < s.n_win || (code >= 0 && code < s.g_lim));
         if (!tc::mbar_wait_cl(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
@@ -379,7 +404,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           st_shared16(prow + (((kh * 4 + c) ^ (hrow & 7)) * 16), make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
-        if (j > 0 && __any_sync(0xffffffffu, need)) {
+        if (j > t0 && __any_sync(0xffffffffu, need)) {
           if (!tc::mbar_wait_cl(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
           tc::fence_after_sync();
           for (int c0 = 0; c0 < 256; c0 += 32) {
@@ -409,6 +434,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       MLA_WAIT(XL + (sw & 1), ii & 1, 224);
       const float ltot = lsum + red_l[ii & 1][l ^ 64];
       const float inv = 1.0f / ltot;
+      if (a.n_split > 1) {  // this split's normalised output and lse, merged by combine_kernel
+        float* orow = a.o_part + (((long long)sp * a.n_tok + tk) * H + head) * DV;
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          for (int c = 0; c < 4; ++c) {
+            uint32_t ov[32];
+            tc::tmem_ld32(tc::taddr(tmem, sw * 32, i * 128 + c * 32), ov);
+            tc::tmem_wait_ld();
+            float4* dst = reinterpret_cast<float4*>(orow + i * 256 + kh * 128 + c * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = make_float4(__uint_as_float(ov[4 * q + 0]) * inv, __uint_as_float(ov[4 * q + 1]) * inv,
+                                   __uint_as_float(ov[4 * q + 2]) * inv, __uint_as_float(ov[4 * q + 3]) * inv);
+          }
+        }
+        if (kh == 0) a.lse_part[((long long)sp * a.n_tok + tk) * H + head] = (m * sl + log2f(ltot)) * LN2;
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) arrive_leader(O_EMPTY);
+        ++ii;
+        continue;
+      }
       __nv_bfloat16* orow = a.o + ((long long)tk * H + head) * DV;
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
@@ -429,6 +476,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) arrive_leader(O_EMPTY);
+      ++ii;
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------------ K producers
@@ -437,12 +485,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     const int t = threadIdx.x - 256 - grp * 128;  // 0..127
     const int kk = t >> 2, sub = t & 3;
     int g = 0;
-    for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
-      const int tk = a.n_tok - 1 - it;
-      const int n = n_tiles(tk);
+    for (int it = pair; it < items && !abort_flag; it += npairs) {
+      int tk, sp, t0, t1;
+      item_range(it, tk, sp, t0, t1);
       const Slot s = item_info(a, tk);
       bool ok = true;
-      for (int j = 0; j < n; ++j, ++g) {
+      for (int j = t0; j < t1; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
         if (st != grp) continue;
         const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
@@ -488,10 +536,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     // gb = (lb >> 1) * 4 + 2 r + (lb & 1); this CTA supplies its half of the keys.
     if (lane == 0) {
       int g = 0;
-      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
-        const int n = n_tiles(a.n_tok - 1 - it);
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
         bool ok = true;
-        for (int j = 0; j < n; ++j, ++g) {
+        for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
           if (!tc::mbar_wait(&bars[K_WRIT + st], ph, a.err, 250) ||
               !tc::mbar_wait_cl(&bars[V_EMPTY + st], ph ^ 1, a.err, 251)) { ok = false; break; }
@@ -514,10 +563,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     // ------------------------------------------------------------------ V relay
     if (lane == 0) {
       int g = 0;
-      for (int it = pair; it < a.n_tok && !abort_flag; it += npairs) {
-        const int n = n_tiles(a.n_tok - 1 - it);
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
         bool ok = true;
-        for (int j = 0; j < n; ++j, ++g) {
+        for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
           tc::mbar_expect_tx(&bars[V_FULL + st], 2 * 4 * 4096);  // 4 blocks from each CTA
           if (!tc::mbar_wait_cl(&bars[V_FULL + st], ph, a.err, 260)) { ok = false; break; }
@@ -561,17 +611,70 @@ __global__ void slots_kernel(Args a) {
   if (lane == 0) const_cast<int32_t*>(a.n_slots)[warp] = s.n_win + last + 1;
 }
 
+// Merge the key-range splits of each (token, head): o = sum_i e^(lse_i) o_i / sum_i e^(lse_i),
+// lse = log sum_i e^(lse_i).  One warp per (token, head), 16 channels per lane.
+__global__ void __launch_bounds__(256) combine_kernel(Args a) {
+  const long long wid = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long long)a.n_tok * H) return;
+  const long long row = wid;  // tk * H + head
+  const long long stride = (long long)a.n_tok * H;
+  float mx = -INFINITY;
+  for (int sp = 0; sp < a.n_split; ++sp) mx = fmaxf(mx, a.lse_part[sp * stride + row]);
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+  float wsum = 0.0f;
+  for (int sp = 0; sp < a.n_split; ++sp) {
+    const float l = a.lse_part[sp * stride + row];
+    if (l == -INFINITY) continue;
+    const float wgt = __expf(l - mx);
+    wsum += wgt;
+    const float4* src = reinterpret_cast<const float4*>(a.o_part + (sp * stride + row) * DV + lane * 16);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = src[q];
+      acc[4 * q + 0] = fmaf(wgt, v.x, acc[4 * q + 0]);
+      acc[4 * q + 1] = fmaf(wgt, v.y, acc[4 * q + 1]);
+      acc[4 * q + 2] = fmaf(wgt, v.z, acc[4 * q + 2]);
+      acc[4 * q + 3] = fmaf(wgt, v.w, acc[4 * q + 3]);
+    }
+  }
+  const float inv = 1.0f / wsum;
+  uint4* dst = reinterpret_cast<uint4*>(a.o + row * DV + lane * 16);
+  dst[0] = make_uint4(pack_bf16(acc[0] * inv, acc[1] * inv), pack_bf16(acc[2] * inv, acc[3] * inv),
+                      pack_bf16(acc[4] * inv, acc[5] * inv), pack_bf16(acc[6] * inv, acc[7] * inv));
+  dst[1] = make_uint4(pack_bf16(acc[8] * inv, acc[9] * inv), pack_bf16(acc[10] * inv, acc[11] * inv),
+                      pack_bf16(acc[12] * inv, acc[13] * inv), pack_bf16(acc[14] * inv, acc[15] * inv));
+  if (lane == 0) a.lse[row] = mx + logf(wsum);
+}
+
+// Splits per token: only when the tokens alone would leave more than half of the SM pairs
+// idle (decode of a few sequences per GPU); then floor(pairs / n_tok), at most 8, so all
+// (token, split) items run in one wave.  A split costs a Q reload, an fp32 partial output
+// round trip through HBM and the combine kernel, which outweigh the gain otherwise.
+static int choose_splits(long long n_tok) {
+  const long long pairs = num_sms() / 2;
+  if (n_tok <= 0 || 2 * n_tok > pairs) return 1;
+  const long long s = pairs / n_tok;
+  return int(s > 8 ? 8 : (s < 1 ? 1 : s));
+}
+
 }  // namespace mla
 }  // namespace mzb
 
 using namespace mzb;
+
+extern "C" int mzb_sparse_mla_splits(int64_t n_tok) { return mla::choose_splits(n_tok); }
 
 extern "C" int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void* kv_cmp, const int32_t* indices,
                                   const int32_t* q_pos, const int32_t* raw_page_table,
                                   const int32_t* cmp_page_table, const int32_t* cmp_lens, int32_t* slots_ws,
                                   void* o, float* lse, int64_t n_tok, int tok_per_seq, int topk, int window,
                                   int64_t raw_len, int64_t cmp_len, int raw_ptw, int cmp_ptw, float softmax_scale,
-                                  int* err, void* stream) {
+                                  int splits, float* part_ws, int* err, void* stream) {
+  MZB_REQUIRE(splits >= 1 && splits <= 64 && (splits == 1 || part_ws != nullptr), MZB_ERR_SHAPE,
+              "sparse_mla: splits=%d needs 1..64 and a partial-output workspace when > 1", splits);
   MZB_REQUIRE(n_tok >= 0 && tok_per_seq >= 1 && topk >= 0 && window >= 1, MZB_ERR_SHAPE,
               "sparse_mla: bad sizes n_tok=%lld tok_per_seq=%d topk=%d window=%d", (long long)n_tok, tok_per_seq,
               topk, window);
@@ -591,6 +694,9 @@ extern "C" int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void*
   a.n_tok = int(n_tok); a.tok_per_seq = tok_per_seq; a.topk = topk; a.window = window;
   a.raw_len = raw_len; a.cmp_len = cmp_len; a.raw_ptw = raw_ptw; a.cmp_ptw = cmp_ptw;
   a.scale_log2 = softmax_scale * mla::LOG2E;
+  a.n_split = splits;
+  a.o_part = part_ws;
+  a.lse_part = part_ws ? part_ws + (long long)splits * n_tok * mla::H * mla::DV : nullptr;
   a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
@@ -607,9 +713,15 @@ extern "C" int mzb_sparse_mla_fwd(const void* q, const void* kv_raw, const void*
       cudaSuccess)
     return launch_status("sparse_mla(smem attr)");
   int pairs = num_sms() / 2;
-  if (pairs > n_tok) pairs = int(n_tok);
+  if (pairs > n_tok * splits) pairs = int(n_tok * splits);
   mla::mla_fwd_kernel<<<unsigned(2 * pairs), mla::NTHREADS, mla::SMEM_DYN, st>>>(tq, a);
-  return launch_status("sparse_mla_fwd");
+  if (int r = launch_status("sparse_mla_fwd")) return r;
+  if (splits > 1) {
+    const long long warps = n_tok * mla::H;
+    mla::combine_kernel<<<unsigned((warps * 32 + 255) / 256), 256, 0, st>>>(a);
+    return launch_status("sparse_mla_combine");
+  }
+  return MZB_OK;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -677,5 +789,5 @@ extern "C" int mzb_sparse_mla_fwd_noalloc(const void* q, const void* kv_raw, con
   if (int r = noalloc_scratch(&slots)) return r;
   return mzb_sparse_mla_fwd(q, kv_raw, kv_cmp, indices, q_pos, raw_page_table, cmp_page_table, cmp_lens, slots, o,
                             lse, n_tok, tok_per_seq, topk, window, raw_len, cmp_len, raw_ptw, cmp_ptw, softmax_scale,
-                            err, stream);
+                            1, nullptr, err, stream);
 }

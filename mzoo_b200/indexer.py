@@ -116,17 +116,21 @@ def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, 
     assert dl.shape == (B, S, T) and dl.dtype == torch.float32, \
         f"dl must be [B,S,T] fp32, got {tuple(dl.shape)} {dl.dtype}"
     assert T > 0, "bwd of an empty key axis is all zeros -- handle at the caller"
-    assert Di in (64, 128), f"indexer backward supports index head dim 64 / 128 here, got {Di}"
+    assert Di in (64, 96, 128), f"indexer backward supports index head dim 64 / 96 / 128 here, got {Di}"
     hp = 16
     while hp < Hi:
         hp *= 2
-    qp, wp = q.contiguous(), w.float().contiguous()
+    qp, wp, kp = q.contiguous(), w.float().contiguous(), k.contiguous()
+    Dk = 128 if Di == 96 else Di  # zero channels: same dot products, zero gradient channels
+    if Dk != Di:
+        qp = torch.nn.functional.pad(qp, (0, Dk - Di)).contiguous()
+        kp = torch.nn.functional.pad(kp, (0, Dk - Di)).contiguous()
     if hp != Hi:  # pad heads to a power of two >= 16 with zero weights (their gradients are discarded)
-        qp = torch.cat([qp, qp.new_zeros(B, S, hp - Hi, Di)], dim=2).contiguous()
+        qp = torch.cat([qp, qp.new_zeros(B, S, hp - Hi, Dk)], dim=2).contiguous()
         wp = torch.cat([wp, wp.new_zeros(B, S, hp - Hi)], dim=2).contiguous()
     scale = softmax_scale if softmax_scale is not None else Di**-0.5
-    dq, dk, dw = ops.indexer_bwd(qp, k.contiguous(), wp, dl.contiguous(), compress_ratio, q_offset, float(scale), check)
-    return dq[:, :, :Hi], dk, dw[:, :, :Hi]
+    dq, dk, dw = ops.indexer_bwd(qp, kp, wp, dl.contiguous(), compress_ratio, q_offset, float(scale), check)
+    return dq[:, :, :Hi, :Di].contiguous(), dk[..., :Di].contiguous(), dw[:, :, :Hi].contiguous()
 
 
 class _ScoresAutograd(torch.autograd.Function):

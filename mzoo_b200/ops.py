@@ -213,9 +213,11 @@ def sparse_mla_fwd(q: torch.Tensor, kv_raw: torch.Tensor, kv_cmp: torch.Tensor, 
     lse = torch.empty(n_tok, 128, dtype=torch.float32, device=dev)
     slots = torch.empty(max(n_tok, 1), dtype=torch.int32, device=dev)
     err = _err(dev)
+    splits = _lib.lib().mzb_sparse_mla_splits(n_tok)
+    part = torch.empty(splits * n_tok * 128 * 513, dtype=torch.float32, device=dev) if splits > 1 else None
     call("mzb_sparse_mla_fwd", ptr(q), ptr(kv_raw), ptr(kv_cmp), ptr(idx), ptr(pos), ptr(raw_pt), ptr(cmp_pt),
          ptr(cmp_lens), ptr(slots), ptr(o), ptr(lse), n_tok, tok_per_seq, topk, window, raw_len, cmp_len, raw_ptw,
-         cmp_ptw, scale, ptr(err), stream_ptr(dev))
+         cmp_ptw, scale, splits, ptr(part), ptr(err), stream_ptr(dev))
     if check:
         _raise_on(err, "sparse_mla")
     return o, lse

@@ -90,7 +90,7 @@ def _check(o, lse, ref_o, ref_lse, what):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("D", [64, 128, 256])
+@pytest.mark.parametrize("D", [64, 96, 128, 256])
 @pytest.mark.parametrize("H", [4, 16, 64])
 def test_swa_fwd(cuda, D, H):
     import torch
@@ -123,7 +123,8 @@ def test_swa_separate_v(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (64, 256, 70, 64), (4, 128, 50, 135)])
+@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (64, 256, 70, 64), (4, 128, 50, 135),
+                                         (16, 96, 40, 32)])
 def test_csa2_fwd(cuda, H, D, G, topk):
     import torch
     from mzoo_b200 import csa2_attn
@@ -211,7 +212,7 @@ def _do(torch, dev, shape, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("H,D,window", [(64, 128, 100), (16, 64, 37), (4, 128, 300)])
+@pytest.mark.parametrize("H,D,window", [(64, 128, 100), (16, 64, 37), (4, 128, 300), (16, 96, 100)])
 def test_swa_bwd(cuda, H, D, window):
     import torch
     from mzoo_b200 import swa_attn
@@ -242,7 +243,7 @@ def test_swa_bwd_separate_v(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48)])
+@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (16, 96, 40, 32)])
 def test_csa2_bwd(cuda, H, D, G, topk):
     import torch
     from mzoo_b200 import csa2_attn

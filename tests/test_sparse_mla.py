@@ -150,8 +150,10 @@ def test_prefill_deterministic(cuda):
 
 @pytest.mark.gpu
 def test_prefill_token_shards_match_full(cuda):
-    """One rank's cyclic shard of query tokens (explicit q_pos) reproduces exactly the rows
-    of the full prefill: every token's attention is independent of the others."""
+    """One rank's cyclic shard of query tokens (explicit q_pos) reproduces the rows of the
+    full prefill: every token's attention is independent of the others.  (A shard with few
+    tokens may run as key-range splits merged by the combine kernel, so the comparison is
+    to rounding, not bitwise.)"""
     import torch
     from mzoo_b200 import sparse_mla
     from mzoo_b200.sharding import shard_tokens
@@ -170,4 +172,14 @@ def test_prefill_token_shards_match_full(cuda):
     for part in shard_tokens(S, 3, chunk=32):
         tk = torch.tensor(part, device=cuda)
         os_, ls_ = sparse_mla.prefill(q[:, tk], raw, cmp, it[:, tk], window=window, q_pos=tk.view(1, -1))
-        assert torch.equal(os_, o[:, tk]) and torch.equal(ls_, lse[:, :, tk])
+        assert (os_.float() - o[:, tk].float()).abs().max() <= 1e-2
+        assert (ls_ - lse[:, :, tk]).abs().max() <= 1e-3
+
+
+@pytest.mark.gpu
+def test_prefill_few_tokens_key_splits(cuda):
+    """Few query tokens (fewer than half the SM pairs): each token's key list runs as
+    several key-range splits merged by the combine kernel, including splits left empty."""
+    import torch
+    r = _prefill_case(torch, cuda, B=1, S=12, G=40, topk=40, ratio=1, window=100, q_offset=150, seed=8)
+    _check(*r, "prefill few tokens")

@@ -44,12 +44,13 @@ def _call(torch, name, q, raw, cmp, idx, pos, S, G, topk, window=128):
     stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     common_head = [p(q), p(raw), p(cmp), p(idx), p(pos), None, None, None]
-    tail = [p(o), p(lse), S, S, topk, window, S, G, 0, 0, ctypes.c_float(576**-0.5), p(err), stream]
-    if name == "mzb_sparse_mla_fwd":
+    head = [p(o), p(lse), S, S, topk, window, S, G, 0, 0, ctypes.c_float(576**-0.5)]
+    tail = [p(err), stream]
+    if name == "mzb_sparse_mla_fwd":  # one key-range split, like the allocation-free entry point
         slots = torch.empty(S, dtype=torch.int32, device=dev)
-        status = lib.mzb_sparse_mla_fwd(*common_head, p(slots), *tail)
+        status = lib.mzb_sparse_mla_fwd(*common_head, p(slots), *head, 1, None, *tail)
     else:
-        status = lib.mzb_sparse_mla_fwd_noalloc(*common_head, *tail)
+        status = lib.mzb_sparse_mla_fwd_noalloc(*common_head, *head, *tail)
     assert status == 0, lib.mzb_last_error()
     torch.cuda.synchronize(dev)
     assert int(err.item()) == 0
