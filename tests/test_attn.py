@@ -102,6 +102,18 @@ def test_swa_fwd(cuda, D, H):
 
 
 @pytest.mark.gpu
+def test_swa_fwd_config1_shape(cuda):
+    """BASELINE config 1 (the reference's CPU case): B1, S=2048, 16 heads sharing one KV
+    head, D=128, window 128, scale 1/sqrt(128) -- on the bf16 kernel vs the fp64 oracle."""
+    import torch
+    from mzoo_b200 import swa_attn
+    q, kv, _, _, _, _ = _inputs(torch, cuda, 1, 2048, 16, 128, seed=1)
+    o, lse = swa_attn.fwd(q, kv, window=128)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=128)
+    _check(o, lse, ref_o, ref_lse, "swa config 1")
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("window", [1, 128, 513, 4096])
 def test_swa_windows_and_sinks(cuda, window):
     import torch
