@@ -87,7 +87,7 @@ MZB_API int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtyp
  *   Reads `scores` from mzb_indexer_scores (same arguments) and writes out [B,S,topk]
  *   int32: the top-k keys of the exact fp64 canonical score (ties to the lower index),
  *   ascending, -1 padded when fewer than topk keys are visible.  kbmax_ws is a float
- *   workspace of B*16 entries.  eps bounds the relative error of the fp32 scores (see
+ *   workspace of B*16 + B*S entries (key and query-row error-bound factors).  eps bounds the relative error of the fp32 scores (see
  *   indexer.cu); *err = MZB_ERR_BOUND if the bound leaves too many candidates.
  */
 MZB_API int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,

@@ -363,6 +363,7 @@ struct TopkArgs {
   const float* sq;
   const float* sk;
   const float* kbmax;  // [B, KB_PARTS]
+  const float* qnorm;  // [B * S]: A_s = sum_h |w_h sq_h| ||q_h||_2 per query row
   const int32_t* q_pos;
   int32_t* out;
   int B, S, T, Hi, Di, topk, ratio;
@@ -414,8 +415,7 @@ __device__ __forceinline__ float sumsq16(const uint4 v, int fp8) {
 // bound ||k_t|| <= 448 * sqrt(Di) (448 = largest finite e4m3) so that only the per-key
 // scales are read -- that widens the exactly re-scored band by at most sqrt(Di) times,
 // which costs little with so few rows.
-__global__ void __launch_bounds__(256) kbound_kernel(TopkArgs a) {
-  const int b = blockIdx.x, part = blockIdx.y;
+__device__ void key_bound(const TopkArgs& a, int b, int part) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   __shared__ float red[8];
   __shared__ int red_v[8];
@@ -477,6 +477,70 @@ __global__ void __launch_bounds__(256) kbound_kernel(TopkArgs a) {
   }
 }
 
+// A_s = sum_h |c_h| ||q_h||_2 (c_h = w_h sq_h) of one query row, by one warp, for the rows
+// whose selection can need the error bound (more visible keys than topk).  Rows of whole
+// 16-byte vectors: lpr = rb / 16 lanes per head row, QB vectors per lane in flight.
+__device__ void query_bound(const TopkArgs& a, int row) {
+  const int lane = threadIdx.x & 31;
+  const int b = row / a.S, s = row % a.S;
+  if (visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T) <= a.topk) return;
+  const int rb = a.Di * (a.fp8 ? 1 : 2);
+  const uint8_t* qg = a.q + size_t(row) * a.Hi * rb;
+  const float* wr = a.w + size_t(row) * a.Hi;
+  const float* sqr = a.sq ? a.sq + size_t(row) * a.Hi : nullptr;
+  const int lpr = rb >> 4;
+  float part = 0.0f;
+  if ((rb & 15) == 0 && lpr <= 32 && (lpr & (lpr - 1)) == 0) {
+    constexpr int QB = 4;
+    const int nv = a.Hi * lpr, sh = __ffs(lpr) - 1;
+    for (int v0 = 0; v0 < nv; v0 += 32 * QB) {  // warp-uniform trip count: full-warp shuffles
+      uint4 qv[QB];
+      float cabs[QB];
+#pragma unroll
+      for (int u = 0; u < QB; ++u) {
+        const int v = v0 + 32 * u + lane;
+        qv[u] = make_uint4(0u, 0u, 0u, 0u);
+        cabs[u] = 0.0f;
+        if (v < nv) {
+          const int h = v >> sh;
+          qv[u] = __ldg(reinterpret_cast<const uint4*>(qg + size_t(h) * rb + (v & (lpr - 1)) * 16));
+          if ((v & (lpr - 1)) == 0) cabs[u] = fabsf(__ldg(wr + h) * (sqr ? __ldg(sqr + h) : 1.0f));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < QB; ++u) {
+        float ss = sumsq16(qv[u], a.fp8);
+        for (int o = lpr >> 1; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        part += cabs[u] * sqrtf(ss);  // cabs is 0 off the head leaders
+      }
+    }
+  } else {
+    for (int h = lane; h < a.Hi; h += 32) {
+      const uint8_t* qh = qg + size_t(h) * rb;
+      float ss = 0.0f;
+      for (int i = 0; i < a.Di; ++i) {
+        const float v = elem_f(qh, i, a.fp8);
+        ss = fmaf(v, v, ss);
+      }
+      part += fabsf(wr[h] * (sqr ? sqr[h] : 1.0f)) * sqrtf(ss);
+    }
+  }
+  for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) const_cast<float*>(a.qnorm)[row] = part;
+}
+
+// The error-bound factors of the selection, one launch: blocks [0, B * KB_PARTS) bound
+// the keys (per batch and part), the rest the query rows (8 per block, one per warp).
+__global__ void __launch_bounds__(256) bound_kernel(TopkArgs a) {
+  const int nkb = a.B * KB_PARTS;
+  if (int(blockIdx.x) < nkb) {
+    key_bound(a, blockIdx.x / KB_PARTS, blockIdx.x % KB_PARTS);
+  } else {
+    const int row = (int(blockIdx.x) - nkb) * 8 + int(threadIdx.x >> 5);
+    if (row < a.B * a.S) query_bound(a, row);
+  }
+}
+
 // exact fp64 value of an e4m3 code pair (the low and high byte of a 16-bit word)
 __device__ __forceinline__ void e4m3x2_to_f64(uint32_t w16, double& lo, double& hi) {
   const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w16 & 0xFFFFu), __NV_E4M3);
@@ -486,6 +550,13 @@ __device__ __forceinline__ void e4m3x2_to_f64(uint32_t w16, double& lo, double& 
 }
 
 constexpr int BLIST = 256;  // keys of the selected linear bin ranked directly
+
+// bytes of the region shared by the bin bytes of V keys and the fp64 re-scoring buffers
+// (exact scores: CAND_MAX doubles, head weights: Hi doubles, per-warp key rows: rw x Di
+// floats), rounded up to 16
+__host__ __device__ constexpr int topk_region_bytes(int V, int Hi, int Di, int rw) {
+  return ((V > CAND_MAX * 8 + Hi * 8 + rw * Di * 4 ? V : CAND_MAX * 8 + Hi * 8 + rw * Di * 4) + 15) & ~15;
+}
 
 // exclusive prefix (over the block, in thread order) of `cnt`; also returns the total.
 // Uses sh[0..NW) and sh[32..32+NW], sh[64]; two __syncthreads.
@@ -516,8 +587,9 @@ __device__ __forceinline__ int block_exclusive_scan(int cnt, int* sh, int& total
 }
 
 template <int TK_THREADS>
-__global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
+__global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_kernel(TopkArgs a) {
   constexpr int NW = TK_THREADS / 32;
+  constexpr int RW = NW < 8 ? NW : 8;  // warps that re-score band keys
   extern __shared__ uint8_t sm[];
   const int row = blockIdx.x;  // b * S + s
   const int b = row / a.S, s = row % a.S;
@@ -530,83 +602,76 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
   }
   const int eb = a.fp8 ? 1 : 2;
   const int rb = a.Di * eb;  // bytes per q head row / k row
-  // smem carve-up
-  uint32_t* keys = reinterpret_cast<uint32_t*>(sm);                        // V
-  uint32_t* sel = keys + V;                                                // ceil(V/32)
+  // smem carve-up: one bin byte per key; the fp64 re-scoring buffers are used only once
+  // the bins are dead and share their region
+  const int region = topk_region_bytes(V, a.Hi, a.Di, RW);
+  uint8_t* bins = sm;                                                       // V (padded to 4)
+  double* exact = reinterpret_cast<double*>(sm);                            // CAND_MAX
+  double* cq = exact + CAND_MAX;                                            // Hi
+  float* kdall = reinterpret_cast<float*>(cq + a.Hi);                       // RW warps x Di
+  uint32_t* sel = reinterpret_cast<uint32_t*>(sm + region);                 // ceil(V/32)
   const int nsel = (V + 31) >> 5;
-  uint32_t* blist = sel + nsel;                                            // BLIST
-  int* cand = reinterpret_cast<int*>(blist + BLIST);                       // CAND_MAX
-  double* exact = reinterpret_cast<double*>(                               // CAND_MAX
-      (reinterpret_cast<uintptr_t>(cand + CAND_MAX) + 7) & ~uintptr_t(7));
-  double* pbuf = exact + CAND_MAX;                                         // 8 warps x Hi
-  double* cq = pbuf + 8 * a.Hi;                                            // Hi
-  double* kdall = cq + a.Hi;                                               // 8 warps x Di
+  uint32_t* bl_key = sel + nsel;                                            // BLIST
+  int* bl_idx = reinterpret_cast<int*>(bl_key + BLIST);                     // BLIST
+  int* cand = bl_idx + BLIST;                                               // CAND_MAX
   __shared__ int hist[256];
   __shared__ uint32_t sh_kk, sh_theta;
   __shared__ int sh_bin, n_in, n_cand, n_bl, sh_scan[96];
-  __shared__ float sh_A;
   __shared__ uint32_t sh_kmin, sh_kmax, sh_bmin, sh_bmax;
   if (tid == 0) {
     sh_kmin = 0xFFFFFFFFu; sh_kmax = 0u; sh_bmin = 0xFFFFFFFFu; sh_bmax = 0u;
-    sh_A = 0.0f; n_in = 0; n_cand = 0; n_bl = 0;
+    n_in = 0; n_cand = 0; n_bl = 0;
   }
+  for (int i = tid; i < 256; i += TK_THREADS) hist[i] = 0;
   __syncthreads();
 
-  // pass 1: order-preserving keys, their range; exact head weights; A_s
   const float* srow = a.scores + size_t(row) * a.T;
-  {
-    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-    for (int j = tid; j < V; j += TK_THREADS) {
-      const uint32_t kx = f2key(srow[j]);
-      keys[j] = kx;
-      kmin = min(kmin, kx);
-      kmax = max(kmax, kx);
-    }
+  const uint8_t* qg = a.q + size_t(row) * a.Hi * rb;
+  auto range_reduce = [&](uint32_t kmin, uint32_t kmax) {
     for (int o = 16; o; o >>= 1) {
       kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
       kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
     }
     if (lane == 0) { atomicMin(&sh_kmin, kmin); atomicMax(&sh_kmax, kmax); }
-  }
-  for (int i = tid; i < nsel; i += TK_THREADS) sel[i] = 0u;
-  const uint8_t* qg = a.q + size_t(row) * a.Hi * rb;
-  for (int h = tid; h < a.Hi; h += TK_THREADS) {
-    const size_t o = size_t(row) * a.Hi + h;
-    cq[h] = double(a.w[o]) * double(a.sq ? a.sq[o] : 1.0f);
-  }
+  };
+  // The bins' range comes from one strided sample per thread.  Any range is correct (keys
+  // outside it are clamped into the end bins, and the bin map stays monotone); a sample of
+  // TK_THREADS keys leaves ~V / TK_THREADS keys beyond either end.
   {
-    // A_s = sum_h |c_h| ||q_h||: one thread per head row, 16-byte loads (rows are 4-byte
-    // multiples; whole 16-byte vectors when they are 16-byte multiples)
-    float part = 0.0f;
-    for (int h = tid; h < a.Hi; h += TK_THREADS) {
-      const uint8_t* qh = qg + size_t(h) * rb;
-      float ss = 0.0f;
-      if (rb % 16 == 0) {
-        for (int i = 0; i < rb; i += 16) ss += sumsq16(__ldg(reinterpret_cast<const uint4*>(qh + i)), a.fp8);
-      } else {
-        for (int i = 0; i < a.Di; ++i) {
-          const float v = elem_f(qh, i, a.fp8);
-          ss = fmaf(v, v, ss);
-        }
-      }
-      const float ch = fabsf(a.w[size_t(row) * a.Hi + h] * (a.sq ? a.sq[size_t(row) * a.Hi + h] : 1.0f));
-      part += ch * sqrtf(ss);
-    }
-    for (int o = 16; o; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-    if (lane == 0 && warp * 32 < a.Hi) atomicAdd(&sh_A, part);
+    const int j = int((long long)tid * V / TK_THREADS);
+    const uint32_t kx = tid < V ? f2key(srow[j]) : 0u;
+    range_reduce(tid < V ? kx : 0xFFFFFFFFu, tid < V ? kx : 0u);
   }
   __syncthreads();
+  float vmin = key2f(sh_kmin), vmax = key2f(sh_kmax);
+  float inv = 256.0f / (vmax - vmin);
+  bool binned = vmax > vmin && inv < 1e30f;
+  if (!binned) {
+    // a flat sample: take the exact range (all keys equal -> no bins)
+    __syncthreads();
+    if (tid == 0) { sh_kmin = 0xFFFFFFFFu; sh_kmax = 0u; }
+    __syncthreads();
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
+    for (int j = tid; j < V; j += TK_THREADS) {
+      const uint32_t kx = f2key(srow[j]);
+      kmin = min(kmin, kx);
+      kmax = max(kmax, kx);
+    }
+    range_reduce(kmin, kmax);
+    __syncthreads();
+    vmin = key2f(sh_kmin);
+    vmax = key2f(sh_kmax);
+    inv = 256.0f / (vmax - vmin);
+    binned = vmax > vmin && inv < 1e30f;
+  }
 
-  // The topk-th largest key, exactly.  Pass 2 histograms the scores into 256 linear bins
-  // over [min, max] -- a monotone map, so the k-th largest lies in one bin, and the bins
-  // spread any score distribution (keys of one row share their leading bits).  Pass 3
-  // gathers that bin's keys; up to BLIST of them are ranked directly, more fall back to a
+  // The topk-th largest key, exactly.  Pass 1 histograms the scores into 256 linear bins
+  // over [vmin, vmax] -- a monotone map, so the k-th largest lies in one bin -- and keeps
+  // each key's bin.  Pass 2 writes the selection words of the bins above that bin and
+  // gathers the bin's keys; up to BLIST of them are ranked directly, more fall back to a
   // radix select (MSB first, 8-bit digits, below the bits the bin's keys share).
-  const float vmin = key2f(sh_kmin), vmax = key2f(sh_kmax);
-  const float inv = 256.0f / (vmax - vmin);
-  const bool binned = vmax > vmin && inv < 1e30f;
-  auto bin_of = [&](uint32_t kx) {  // monotone in the score; always in [0, 255]
-    const float f = (key2f(kx) - vmin) * inv;
+  auto bin_f = [&](float x) {  // monotone non-decreasing in x; always in [0, 255]
+    const float f = (x - vmin) * inv;
     return f >= 255.0f ? 255 : (f > 0.0f ? int(f) : 0);
   };
   // warp 0: the digit (bin) holding the kk-th largest of `hist`, counting from the top
@@ -634,48 +699,87 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
   };
   uint32_t kk = a.topk;
   uint32_t prefix = sh_kmin;  // all keys equal: that key
-  bool done = !binned;
+  int bsel = -1, nb = 0;
   if (binned) {
-    for (int i = tid; i < 256; i += TK_THREADS) hist[i] = 0;
-    __syncthreads();
-    for (int j = tid; j < V; j += TK_THREADS) atomicAdd(&hist[bin_of(keys[j])], 1);
+    // pass 1: global loads batched UNR vectors deep
+    if ((a.T & 3) == 0) {  // rows are 16-byte aligned; V rounded up to 4 stays in the row
+      constexpr int UNR = 4;
+      for (int j0 = 4 * tid; j0 < V; j0 += 4 * TK_THREADS * UNR) {
+        float4 f[UNR];
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const int j = j0 + 4 * TK_THREADS * u;
+          if (j < V) f[u] = __ldg(reinterpret_cast<const float4*>(srow + j));
+        }
+#pragma unroll
+        for (int u = 0; u < UNR; ++u) {
+          const int j = j0 + 4 * TK_THREADS * u;
+          if (j < V) {
+            const float fv[4] = {f[u].x, f[u].y, f[u].z, f[u].w};
+            uint32_t packed = 0u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if (j + e < V) {
+                const int bn = bin_f(fv[e]);
+                atomicAdd(&hist[bn], 1);
+                packed |= uint32_t(bn) << (8 * e);
+              }
+            }
+            *reinterpret_cast<uint32_t*>(bins + j) = packed;
+          }
+        }
+      }
+    } else {
+      for (int j = tid; j < V; j += TK_THREADS) {
+        const int bn = bin_f(srow[j]);
+        atomicAdd(&hist[bn], 1);
+        bins[j] = uint8_t(bn);
+      }
+    }
     __syncthreads();
     if (warp == 0) pick(kk);
     __syncthreads();
-    const int bsel = sh_bin;
+    bsel = sh_bin;
     kk = sh_kk;
-    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
-    for (int j0 = 0; j0 < V; j0 += TK_THREADS) {
-      const int j = j0 + tid;
-      const uint32_t kx = j < V ? keys[j] : 0u;
-      const bool in = j < V && bin_of(kx) == bsel;
-      const uint32_t wm = __ballot_sync(0xffffffffu, in);
-      if (wm) {
-        int base = 0;
-        if (lane == 0) base = atomicAdd(&n_bl, __popc(wm));
-        base = __shfl_sync(0xffffffffu, base, 0);
-        const int at = base + __popc(wm & ((1u << lane) - 1u));
-        if (in) {
-          if (at < BLIST) blist[at] = kx;
-          kmin = min(kmin, kx);
-          kmax = max(kmax, kx);
+    if (tid == 0) n_in = a.topk - int(kk);  // every key of the bins above bsel
+    // pass 2: selection words of the bins above bsel (a lane's 4 keys are a nibble of a
+    // word shared by 8 lanes); bin bsel's indices (its keys are re-read from the row after)
+    for (int j0 = 0; j0 < V; j0 += 4 * TK_THREADS) {  // block-uniform trip count
+      const int j = j0 + 4 * tid;
+      uint32_t nib = 0u;
+      if (j < V) {
+        const uint32_t b4 = *reinterpret_cast<const uint32_t*>(bins + j);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int bn = int((b4 >> (8 * e)) & 0xFFu);
+          if (j + e < V) {
+            if (bn > bsel) {
+              nib |= 1u << e;
+            } else if (bn == bsel) {
+              const int at = atomicAdd(&n_bl, 1);
+              if (at < BLIST) bl_idx[at] = j + e;
+            }
+          }
         }
       }
+      uint32_t word = nib << (4 * (lane & 7));
+      word |= __shfl_xor_sync(0xffffffffu, word, 1);
+      word |= __shfl_xor_sync(0xffffffffu, word, 2);
+      word |= __shfl_xor_sync(0xffffffffu, word, 4);
+      const int wi = j >> 5;
+      if ((lane & 7) == 0 && wi < nsel) sel[wi] = word;
     }
-    for (int o = 16; o; o >>= 1) {
-      kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
-      kmax = max(kmax, __shfl_xor_sync(0xffffffffu, kmax, o));
-    }
-    if (lane == 0) { atomicMin(&sh_bmin, kmin); atomicMax(&sh_bmax, kmax); }
     __syncthreads();
-    const int nb = n_bl;
+    nb = n_bl;
     if (nb <= BLIST) {
+      for (int i = tid; i < nb; i += TK_THREADS) bl_key[i] = f2key(srow[bl_idx[i]]);  // one round trip
+      __syncthreads();
       // rank directly: the kk-th largest has (#greater < kk <= #greater + #equal)
       for (int i = tid; i < nb; i += TK_THREADS) {
-        const uint32_t kx = blist[i];
+        const uint32_t kx = bl_key[i];
         int gt = 0, eq = 0;
         for (int o = 0; o < nb; ++o) {
-          const uint32_t y = blist[o];
+          const uint32_t y = bl_key[o];
           gt += y > kx;
           eq += y == kx;
         }
@@ -683,8 +787,23 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
       }
       __syncthreads();
       prefix = sh_theta;
-      done = true;
     } else {
+      {
+        uint32_t bmn = 0xFFFFFFFFu, bmx = 0u;
+        for (int j = tid; j < V; j += TK_THREADS) {
+          if (bins[j] == bsel) {
+            const uint32_t kx = f2key(srow[j]);
+            bmn = min(bmn, kx);
+            bmx = max(bmx, kx);
+          }
+        }
+        for (int o = 16; o; o >>= 1) {
+          bmn = min(bmn, __shfl_xor_sync(0xffffffffu, bmn, o));
+          bmx = max(bmx, __shfl_xor_sync(0xffffffffu, bmx, o));
+        }
+        if (lane == 0) { atomicMin(&sh_bmin, bmn); atomicMax(&sh_bmax, bmx); }
+        __syncthreads();
+      }
       prefix = sh_bmin;
       const uint32_t kdiff = sh_bmin ^ sh_bmax;
       int hi_bit = kdiff ? 31 - __clz(kdiff) : -1;
@@ -698,8 +817,10 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
         for (int i = tid; i < 256; i += TK_THREADS) hist[i] = 0;
         __syncthreads();
         for (int j = tid; j < V; j += TK_THREADS) {
-          const uint32_t kx = keys[j];
-          if ((kx & mask) == prefix && bin_of(kx) == bsel) atomicAdd(&hist[(kx >> shift) & dmask], 1);
+          if (bins[j] == bsel) {
+            const uint32_t kx = f2key(srow[j]);
+            if ((kx & mask) == prefix) atomicAdd(&hist[(kx >> shift) & dmask], 1);
+          }
         }
         __syncthreads();
         if (warp == 0) pick(kk);
@@ -709,33 +830,50 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
         mask |= dmask << shift;
         hi_bit -= width;
       }
-      done = true;
     }
   }
-  (void)done;
   const float theta = key2f(prefix);
   float kbm = 0.0f;
   for (int i = 0; i < KB_PARTS; ++i) kbm = fmaxf(kbm, a.kbmax[b * KB_PARTS + i]);
-  const float delta = a.eps * sh_A * kbm * 1.0001f;
+  const float delta = a.eps * a.qnorm[row] * kbm * 1.0001f;
   const float hi_thr = __fadd_ru(theta, 2.0f * delta), lo_thr = __fsub_rd(theta, 2.0f * delta);
-  // pass 4: certain keys into `sel` (one word per warp iteration, no atomics on sel); the
-  // band between the thresholds into `cand`
-  for (int j0 = 0; j0 < V; j0 += TK_THREADS) {
-    const int j = j0 + tid;
-    const float v = j < V ? key2f(keys[j]) : -INFINITY;
-    const uint32_t in_w = __ballot_sync(0xffffffffu, j < V && v > hi_thr);
-    const bool is_c = j < V && !(v > hi_thr) && v >= lo_thr;
-    const uint32_t c_w = __ballot_sync(0xffffffffu, is_c);
-    if (j - lane < V && lane == 0) {
-      sel[j >> 5] = in_w;
-      if (in_w) atomicAdd(&n_in, __popc(in_w));
+  // pass 3: certain keys into `sel`, the band between the thresholds into `cand`.  When the
+  // band lies in bin bsel and the list holds all of that bin, the keys above it are exactly
+  // the bins above bsel (written by pass 2: bin_f is monotone) plus the list's keys above
+  // hi_thr, and the band is in the list -- only the list is scanned.  Otherwise the row.
+  const bool in_bin = binned && nb <= BLIST && bin_f(lo_thr) == bsel && bin_f(hi_thr) == bsel;
+  if (in_bin) {
+    for (int i = tid; i < nb; i += TK_THREADS) {
+      const float v = key2f(bl_key[i]);
+      const int j = bl_idx[i];
+      if (v > hi_thr) {
+        atomicOr(&sel[j >> 5], 1u << (j & 31));
+        atomicAdd(&n_in, 1);
+      } else if (v >= lo_thr) {
+        const int c = atomicAdd(&n_cand, 1);
+        if (c < CAND_MAX) cand[c] = j;
+      }
     }
-    if (c_w) {
-      int base = 0;
-      if (lane == 0) base = atomicAdd(&n_cand, __popc(c_w));
-      base = __shfl_sync(0xffffffffu, base, 0);
-      const int c = base + __popc(c_w & ((1u << lane) - 1u));
-      if (is_c && c < CAND_MAX) cand[c] = j;
+  } else {
+    if (tid == 0) n_in = 0;
+    __syncthreads();
+    for (int j0 = 0; j0 < V; j0 += TK_THREADS) {  // one word per warp iteration, no atomics on sel
+      const int j = j0 + tid;
+      const float v = j < V ? srow[j] : -INFINITY;
+      const uint32_t in_w = __ballot_sync(0xffffffffu, j < V && v > hi_thr);
+      const bool is_c = j < V && !(v > hi_thr) && v >= lo_thr;
+      const uint32_t c_w = __ballot_sync(0xffffffffu, is_c);
+      if (j - lane < V && lane == 0) {
+        sel[j >> 5] = in_w;
+        if (in_w) atomicAdd(&n_in, __popc(in_w));
+      }
+      if (c_w) {
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&n_cand, __popc(c_w));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int c = base + __popc(c_w & ((1u << lane) - 1u));
+        if (is_c && c < CAND_MAX) cand[c] = j;
+      }
     }
   }
   __syncthreads();
@@ -762,7 +900,7 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
           for (int bit = 0; bit < 32; ++bit) {
             const int j = w * 32 + bit;
             if (j < V) {
-              const float v = key2f(keys[j]);
+              const float v = srow[j];
               if (!(v > hi_thr) && v >= lo_thr) bits |= 1u << bit;
             }
           }
@@ -785,46 +923,67 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
     }
     __syncthreads();
   } else {
-    // exact fp64 re-scoring of the band, warps 0-7, one candidate per warp; lane l owns
-    // heads l, l+32, ...; q is read from global memory (L1-resident after the first use)
-    double* kd = kdall + warp * a.Di;
-    for (int c = warp; c < nc && warp < 8; c += 8) {
+    // exact fp64 re-scoring of the band, RW warps, one candidate per warp; lane l owns
+    // heads l + 32 m; q is read from global memory (L1-resident after the first use).  The
+    // head products are summed in head order by lane 0, fetched by shuffles.
+    for (int h = tid; h < a.Hi; h += TK_THREADS) {
+      const size_t o = size_t(row) * a.Hi + h;
+      cq[h] = double(a.w[o]) * double(a.sq ? a.sq[o] : 1.0f);
+    }
+    __syncthreads();
+    float* kd = kdall + warp * a.Di;
+    for (int c = warp; c < nc && warp < RW; c += RW) {
       const int j = cand[c];
       const uint8_t* kr = a.k + (size_t(b) * a.T + j) * rb;
       __syncwarp();
-      for (int i = lane; i < a.Di; i += 32) kd[i] = double(elem_f(kr, i, a.fp8));
+      for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);  // exact in fp32
       __syncwarp();
-      for (int h = lane; h < a.Hi; h += 32) {
-        const uint8_t* qh = qg + size_t(h) * rb;
-        double dot = 0.0;
-        if (a.fp8) {
-          // e4m3 products are multiples of 2^-18 below 2^18 and the sums stay below 2^53
-          // units: exact in any order, so two chains
-          double d0 = 0.0, d1 = 0.0;
-          for (int i = 0; i < a.Di; i += 4) {
-            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(qh + i));
-            double q0, q1, q2, q3;
-            e4m3x2_to_f64(w, q0, q1);
-            e4m3x2_to_f64(w >> 16, q2, q3);
-            d0 = fma(q0, kd[i], d0);
-            d1 = fma(q1, kd[i + 1], d1);
-            d0 = fma(q2, kd[i + 2], d0);
-            d1 = fma(q3, kd[i + 3], d1);
+      double acc = 0.0;
+      for (int m = 0; 32 * m < a.Hi; ++m) {
+        const int h = 32 * m + lane;
+        double pv = 0.0;
+        if (h < a.Hi) {
+          const uint8_t* qh = qg + size_t(h) * rb;
+          double dot = 0.0;
+          if (a.fp8) {
+            // e4m3 products are multiples of 2^-18 below 2^18 and the sums stay below 2^53
+            // units: exact in any order, so two chains
+            double d0 = 0.0, d1 = 0.0;
+            auto word = [&](uint32_t w, int i) {
+              double q0, q1, q2, q3;
+              e4m3x2_to_f64(w, q0, q1);
+              e4m3x2_to_f64(w >> 16, q2, q3);
+              d0 = fma(q0, double(kd[i]), d0);
+              d1 = fma(q1, double(kd[i + 1]), d1);
+              d0 = fma(q2, double(kd[i + 2]), d0);
+              d1 = fma(q3, double(kd[i + 3]), d1);
+            };
+            if ((rb & 15) == 0) {
+              for (int i = 0; i < a.Di; i += 16) {
+                const uint4 w4 = __ldg(reinterpret_cast<const uint4*>(qh + i));
+                word(w4.x, i);
+                word(w4.y, i + 4);
+                word(w4.z, i + 8);
+                word(w4.w, i + 12);
+              }
+            } else {
+              for (int i = 0; i < a.Di; i += 4) word(__ldg(reinterpret_cast<const uint32_t*>(qh + i)), i);
+            }
+            dot = d0 + d1;
+          } else {
+            for (int i = 0; i < a.Di; ++i) dot = fma(double(elem_f(qh, i, 0)), double(kd[i]), dot);  // sequential
           }
-          dot = d0 + d1;
-        } else {
-          for (int i = 0; i < a.Di; ++i) dot = fma(double(elem_f(qh, i, 0)), kd[i], dot);  // sequential
+          pv = __dmul_rn(cq[h], dot > 0.0 ? dot : 0.0);
         }
-        pbuf[warp * a.Hi + h] = __dmul_rn(cq[h], dot > 0.0 ? dot : 0.0);
+        for (int l = 0; l < 32; ++l) {  // heads 32 m + l in order
+          const double v = __shfl_sync(0xffffffffu, pv, l);
+          if (32 * m + l < a.Hi) acc = __dadd_rn(acc, v);
+        }
       }
-      __syncwarp();
       if (lane == 0) {
-        double acc = 0.0;
-        for (int h = 0; h < a.Hi; ++h) acc = __dadd_rn(acc, pbuf[warp * a.Hi + h]);
         const double skj = a.sk ? double(a.sk[size_t(b) * a.T + j]) : 1.0;
         exact[c] = __dmul_rn(__dmul_rn(acc, skj), double(a.scale));
       }
-      __syncwarp();
     }
     __syncthreads();
     // rank candidates by (score desc, index asc); keep the best `need`
@@ -861,11 +1020,8 @@ __global__ void __launch_bounds__(TK_THREADS) topk_kernel(TopkArgs a) {
 
 static size_t topk_smem(int T, int Hi, int Di, int eb, int threads) {
   (void)eb;
-  (void)threads;
-  size_t V = size_t(T);
-  size_t bytes = V * 4 + ((V + 31) / 32) * 4 + BLIST * 4 + CAND_MAX * 4 + 8;
-  bytes += CAND_MAX * 8 + size_t(8) * Hi * 8 + size_t(Hi) * 8 + size_t(8) * Di * 8;
-  return bytes;
+  const int rw = std::min(threads / 32, 8);
+  return size_t(topk_region_bytes(T, Hi, Di, rw)) + size_t((T + 31) / 32) * 4 + BLIST * 8 + CAND_MAX * 4;
 }
 
 template <bool FP8, int DI>
@@ -984,23 +1140,25 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   MZB_REQUIRE((Di * eb) % 4 == 0, MZB_ERR_UNSUPPORTED, "indexer topk: index rows must be a multiple of 4 bytes");
   // few rows (decode: one query per sequence) -> wide blocks, else 256 threads per row
   const bool wide = B * S < 2LL * num_sms();
-  const size_t smem = idx::topk_smem(int(T), Hi, Di, eb, wide ? 1024 : 256);
+  const size_t smem = idx::topk_smem(int(T), Hi, Di, eb, wide ? 1024 : 128);
   MZB_REQUIRE(smem <= 200 * 1024, MZB_ERR_UNSUPPORTED, "indexer topk: T=%lld needs %zu B of shared memory",
               (long long)T, smem);
   idx::TopkArgs a{};
   a.scores = scores; a.q = static_cast<const uint8_t*>(q); a.k = static_cast<const uint8_t*>(k);
-  a.w = w; a.sq = sq; a.sk = sk; a.q_pos = q_pos; a.kbmax = kbmax_ws; a.out = out;
+  a.w = w; a.sq = sq; a.sk = sk; a.q_pos = q_pos; a.kbmax = kbmax_ws; a.qnorm = kbmax_ws + B * idx::KB_PARTS;
+  a.out = out;
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi; a.Di = Di; a.topk = topk; a.ratio = ratio;
   a.q_offset = q_offset; a.scale = scale; a.eps = eps; a.fp8 = dtype == MZB_E4M3; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0 || S == 0) return MZB_OK;
   if (T > 0) {
-    idx::kbound_kernel<<<dim3(unsigned(B), idx::KB_PARTS), 256, 0, st>>>(a);
-    if (int r = launch_status("indexer_kbound")) return r;
+    const long long blocks = B * idx::KB_PARTS + (B * S + 7) / 8;
+    idx::bound_kernel<<<unsigned(blocks), 256, 0, st>>>(a);
+    if (int r = launch_status("indexer_bound")) return r;
   }
-  auto kern = wide ? idx::topk_kernel<1024> : idx::topk_kernel<256>;
+  auto kern = wide ? idx::topk_kernel<1024> : idx::topk_kernel<128>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) != cudaSuccess)
     return launch_status("indexer_topk(smem attr)");
-  kern<<<unsigned(B * S), wide ? 1024 : 256, smem, st>>>(a);
+  kern<<<unsigned(B * S), wide ? 1024 : 128, smem, st>>>(a);
   return launch_status("indexer_topk");
 }

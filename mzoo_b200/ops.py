@@ -94,7 +94,7 @@ def indexer_topk(scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor, w: torc
     B, S, Hi, Di = q.shape
     T = k.shape[1]
     out = torch.empty(B, S, topk, dtype=torch.int32, device=q.device)
-    kb = torch.empty(B * kb_parts, dtype=torch.float32, device=q.device)
+    kb = torch.empty(B * kb_parts + B * S, dtype=torch.float32, device=q.device)  # key and query bounds
     err = _err(q.device)
     call("mzb_indexer_topk", ptr(scores), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(kb), ptr(out),
          B, S, T, Hi, Di, dtype, ratio, q_offset, scale, topk, eps, ptr(err), stream_ptr(q.device))

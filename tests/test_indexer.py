@@ -130,7 +130,7 @@ def test_empty_kv(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("topk,T", [(64, 128), (135, 128), (16, 400)])
+@pytest.mark.parametrize("topk,T", [(64, 128), (135, 128), (16, 400), (40, 397)])
 def test_topk_bf16_exact(cuda, topk, T):
     import torch
     from mzoo_b200 import indexer
@@ -157,6 +157,43 @@ def test_topk_all_tied_rows(cuda):
     for s in range(S):
         n = min(topk, s + 1)
         assert np.array_equal(got[0, s, :n], np.arange(n)) and (got[0, s, n:] == -1).all(), s
+
+
+@pytest.mark.gpu
+def test_topk_tied_block_exact(cuda):
+    """300 zero key rows score exactly 0 for every query; with positive head weights every
+    other key scores above 0 and the cut falls inside the tie: the selected bin holds more
+    keys than are ranked directly (radix select), and the exact re-scoring of the band
+    breaks the tie by the lower index."""
+    import torch
+    from mzoo_b200 import indexer
+    B, S, Hi, Di, T, ratio, topk = 1, 64, 64, 128, 1200, 1, 1000
+    q, k, w = _bf16_inputs(torch, cuda, B, S, Hi, Di, T, seed=9)
+    w = w.abs()
+    k[:, 500:800] = 0
+    got = indexer.attn(q, k, w, compress_ratio=ratio, topk=topk, q_offset=T).cpu().numpy()
+    qf, kf, wf = (x.float().cpu().numpy() for x in (q, k, w))
+    canon = I.canonical_scores(qf, kf, wf, None, None, ratio, T, scale=float(np.float32(Di**-0.5)), fp8=False)
+    pos = (canon[0] > 0).sum(axis=1)
+    assert ((pos < topk) & (pos + 300 >= topk)).all(), "the cut should fall in the tie"
+    assert np.array_equal(got, I.canonical_topk(canon, topk, ratio, T))
+
+
+@pytest.mark.gpu
+def test_topk_wide_band_exact(cuda):
+    """A band 2^10 times wider than the error bound needs (eps passed to the op) spans many
+    linear bins, so every key is scanned for it; exact re-scoring gives the same sets."""
+    import torch
+    from mzoo_b200 import indexer, ops
+    B, S, Hi, Di, T, ratio, topk = 2, 128, 64, 128, 1024, 1, 64
+    q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 11)
+    qp, kp, wp, sqp, skp, scale, dt = indexer._prep(q8, k8, w, (sq, sk), None)
+    sc = indexer._scores(qp, kp, wp, sqp, skp, ratio, T, scale, dt, False, True)
+    got = ops.indexer_topk(sc, qp, kp, wp, sqp, skp, None, ratio, T, scale, dt, topk, indexer.EPS * 1024,
+                           indexer.KB_PARTS, True).cpu().numpy()
+    qv, kv = q8.float().cpu().numpy(), k8.float().cpu().numpy()
+    canon = I.canonical_scores(qv, kv, w.cpu().numpy(), sq.cpu().numpy(), sk.cpu().numpy(), ratio, T)
+    assert np.array_equal(got, I.canonical_topk(canon, topk, ratio, T))
 
 
 def _fp8_case(torch, dev, B, S, Hi, Di, T, seed):
