@@ -26,7 +26,9 @@ constexpr int BM = 128;
 template <int DI>
 struct Cfg {
   static constexpr int DB = DI / 64;           // 64-channel column blocks of q / k rows
-  static constexpr int NMAX = 256;             // (token, head) rows per query block
+  // (token, head) rows per query block: 256, or 128 for Di = 256 (q, two k stages and dr
+  // then fill the shared memory, and dq's 256 fp32 columns the upper half of TMEM)
+  static constexpr int NMAX = DI == 256 ? 128 : 256;
   static constexpr int Q_BYTES = NMAX * DI * 2;
   static constexpr int K_BYTES = BM * DI * 2;
   static constexpr int DR_BYTES = BM * NMAX * 2;  // dr tile [key][(token, head)] bf16
@@ -101,6 +103,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     return (vis_keys(a, s_last) + BM - 1) / BM;
   };
   constexpr int C_R = 0, C_DQ = 256;
+  static_assert(C_DQ + (C::NMAX / 128) * DI <= 512, "TMEM");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -248,10 +251,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       } else {
         if (!tc::mbar_wait(&bars[A_DQ_DONE], ii & 1, a.err, 621)) { *abort_flag = 1; break; }
         tc::fence_after_sync();
-        // thread (quarter, lane) of warpgroup wg owns packed row wg*128 + row
+        // thread (quarter, lane) of warpgroup wg owns packed row wg*128 + row (the second
+        // warpgroup has no rows, and no accumulator columns, when NMAX = 128)
         const int rr = wg * 128 + row;
         const int s = s0 + rr / a.Hi;
-        if (rr < a.N || true) {
+        if (wg * 128 < C::NMAX) {
           for (int c0 = 0; c0 < DI; c0 += 16) {
             uint32_t v[16];
             tc::tmem_ld16(tc::taddr(tmem, quarter * 32, C_DQ + wg * DI + c0), v);
@@ -332,7 +336,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     return lo;
   };
-  constexpr int C_R = 0, C_DK = 256, C_DR = 384;  // R, dk accumulator, packed bf16 dr
+  // R (NMAX columns), dk accumulator (DI), packed bf16 dr (NMAX / 2): 0 / 256 / 384, or
+  // 0 / 256 / 128 when NMAX = 128 and DI = 256
+  constexpr int C_R = 0, C_DK = 256, C_DR = C::NMAX == 256 ? 384 : 128;
+  static_assert(C_DK + DI <= 512 && (C_DR + C::NMAX / 2 <= C_DK || C_DR >= C_DK + DI), "TMEM");
 
   if (warp == 0) {
     if (lane == 0) {
@@ -521,9 +528,12 @@ extern "C" int mzb_indexer_bwd(const void* q, const void* k, const float* w, con
                                float* dw, int64_t B, int64_t S, int64_t T, int Hi, int Di, int ratio, int64_t q_offset,
                                float scale, int* err, void* stream) {
   MZB_REQUIRE(B >= 1 && S >= 1 && T >= 1, MZB_ERR_SHAPE, "indexer_bwd: bad shape (an empty key axis is the caller's)");
-  MZB_REQUIRE(Hi >= 16 && Hi <= 256 && Hi % 16 == 0 && 256 % Hi == 0, MZB_ERR_SHAPE,
-              "indexer_bwd: index heads must divide 256 and be a multiple of 16 (pad with zero weights), got %d", Hi);
-  MZB_REQUIRE(Di == 64 || Di == 128, MZB_ERR_UNSUPPORTED, "indexer_bwd: index head dim %d not built (64, 128)", Di);
+  MZB_REQUIRE(Di == 64 || Di == 128 || Di == 256, MZB_ERR_UNSUPPORTED,
+              "indexer_bwd: index head dim %d not built (64, 128, 256)", Di);
+  const int nmax = Di == 256 ? 128 : 256;  // (token, head) rows per query block
+  MZB_REQUIRE(Hi >= 16 && Hi <= nmax && Hi % 16 == 0 && nmax % Hi == 0, MZB_ERR_SHAPE,
+              "indexer_bwd: index heads must divide %d and be a multiple of 16 (pad with zero weights), got %d", nmax,
+              Hi);
   MZB_REQUIRE(ratio >= 1 && err != nullptr, MZB_ERR_SHAPE, "indexer_bwd: bad ratio or missing error word");
   ibwd::Args a{};
   a.w = w; a.dl = dl;
@@ -531,8 +541,9 @@ extern "C" int mzb_indexer_bwd(const void* q, const void* k, const float* w, con
   a.dk = static_cast<__nv_bfloat16*>(dk);
   a.dw = dw;
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi;
-  a.Tq = 256 / Hi; a.N = 256;
+  a.Tq = nmax / Hi; a.N = nmax;
   a.ratio = ratio; a.q_offset = q_offset; a.scale = scale; a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return Di == 64 ? ibwd::launch<64>(q, k, a, st) : ibwd::launch<128>(q, k, a, st);
+  if (Di == 64) return ibwd::launch<64>(q, k, a, st);
+  return Di == 128 ? ibwd::launch<128>(q, k, a, st) : ibwd::launch<256>(q, k, a, st);
 }

@@ -116,10 +116,11 @@ def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, 
     assert dl.shape == (B, S, T) and dl.dtype == torch.float32, \
         f"dl must be [B,S,T] fp32, got {tuple(dl.shape)} {dl.dtype}"
     assert T > 0, "bwd of an empty key axis is all zeros -- handle at the caller"
-    assert Di in (64, 96, 128), f"indexer backward supports index head dim 64 / 96 / 128 here, got {Di}"
+    assert Di in (64, 96, 128, 256), f"indexer backward supports index head dim 64 / 96 / 128 / 256, got {Di}"
     hp = 16
     while hp < Hi:
         hp *= 2
+    assert hp <= (128 if Di == 256 else 256), f"indexer backward: {Hi} heads at Di={Di} not supported"
     qp, wp, kp = q.contiguous(), w.float().contiguous(), k.contiguous()
     Dk = 128 if Di == 96 else Di  # zero channels: same dot products, zero gradient channels
     if Dk != Di:

@@ -282,7 +282,8 @@ def _grad_close(got, ref, what, rel=1e-2, atol=2e-2):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("heads,dim,ratio", [(4, 64, 2), (32, 128, 4), (64, 128, 1), (16, 128, 2), (8, 96, 2)])
+@pytest.mark.parametrize("heads,dim,ratio", [(4, 64, 2), (32, 128, 4), (64, 128, 1), (16, 128, 2), (8, 96, 2),
+                                             (4, 256, 2), (32, 256, 2), (128, 256, 4)])
 def test_bwd_matches_oracle(cuda, heads, dim, ratio):
     """indexer/bwd_test.py:29-62: dq / dk / dw against autograd through the fp32 scores."""
     import torch
