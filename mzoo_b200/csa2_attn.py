@@ -49,7 +49,7 @@ def bwd(q, kv, main_kv, indices, o, lse, do, *, window: int, compress_ratio: int
     assert q.shape == o.shape == do.shape, "shape mismatch"
     assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
     B, S, H, D = check_mqa(q, kv, "csa2_attn")
-    assert D in (64, 96, 128), f"csa2_attn backward supports head dim 64 / 96 / 128 here, got {D}"
+    assert D in (64, 96, 128, 256), f"csa2_attn backward supports head dim 64 / 96 / 128 / 256, got {D}"
     G = main_kv.shape[1]
     scale = softmax_scale if softmax_scale is not None else D**-0.5
     main = main_kv.contiguous() if G else None

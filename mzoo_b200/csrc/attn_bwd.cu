@@ -77,11 +77,16 @@ struct KvCfg {
   static constexpr int DB = D / 64;
   static constexpr int T_BYTES = 128 * D * 2;  // one 128-row tile of Q, dO, K or V
   static constexpr int STAGE = 2 * T_BYTES + 1024;  // Q, dO, lse2[128], delta[128]
-  static constexpr int TILE_BYTES = (SEP_V ? 2 : 1) * T_BYTES + 2 * STAGE;
+  // D = 256 (K == V only): one Q/dO stage fits the shared memory, and dK and dV share one
+  // accumulator (scale * dS^T Q + P^T dO) so that S and dP still fit in TMEM
+  static constexpr bool MERGE = D == 256;
+  static constexpr int NST = MERGE ? 1 : 2;
+  static constexpr int TILE_BYTES = (SEP_V ? 2 : 1) * T_BYTES + NST * STAGE;
   static constexpr int SMEM = TILE_BYTES + 256;
-  static constexpr int C_DK = 0, C_DV = D, C_S = 2 * D, C_DP = 2 * D + 128;
+  static constexpr int C_DK = 0, C_DV = MERGE ? 0 : D, C_S = MERGE ? D : 2 * D, C_DP = C_S + 128;
   static_assert(C_DP + 128 <= 512, "TMEM");
   static_assert(SMEM <= 232448, "smem");
+  static_assert(!(MERGE && SEP_V), "a separate V needs D <= 128");
 };
 
 enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FULL, PT_FULL, O_DONE, ACC_EMPTY,
@@ -158,7 +163,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         bool ok = true;
         for (int i = 0; i < m.nq; ++i, ++g) {
-          const int s = g & 1, ph = (g >> 1) & 1;
+          const int s = g % C::NST, ph = (g / C::NST) & 1;
           if (!tc::mbar_wait(&bars[QD_EMPTY + s], ph ^ 1, a.err, 402)) { ok = false; break; }
           uint8_t* sp = stage(s);
           const int qt = m.qt0 + i;
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(256, 1)
         if (!tc::mbar_wait(&bars[KV_FULL], ii & 1, a.err, 410)) { *abort_flag = 1; break; }
         bool ok = true;
         for (int i = 0; i < m.nq; ++i, ++g) {
-          const int s = g & 1, ph = (g >> 1) & 1;
+          const int s = g % C::NST, ph = (g / C::NST) & 1;
           if (!tc::mbar_wait(&bars[QD_FULL + s], ph, a.err, 411)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
@@ -216,7 +221,8 @@ __global__ void __launch_bounds__(256, 1)
           for (int kk = 0; kk < 8; ++kk) {  // 128 query rows, 16 per step
             const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
             tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + kk * 8, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
-            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8, tc::sdesc_add(q_mn, kk * 2048), idesc_acc, acc);
+            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8, tc::sdesc_add(q_mn, kk * 2048), idesc_acc,
+                       C::MERGE ? 1u : acc);
           }
           tc::mma_commit(&bars[QD_EMPTY + s]);
           if (i == m.nq - 1) {
@@ -244,7 +250,7 @@ __global__ void __launch_bounds__(256, 1)
       ++ii;
       bool ok = true;
       for (int i = 0; i < m.nq; ++i, ++g) {
-        const int s = g & 1;
+        const int s = g % C::NST;
         if (!tc::mbar_wait(&bars[S_FULL], g & 1, a.err, 420)) { ok = false; break; }
         tc::fence_after_sync();
         const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
@@ -272,6 +278,7 @@ __global__ void __launch_bounds__(256, 1)
               }
               p2[e] = p;
               d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl[c]);
+              if (C::MERGE) d2[e] *= a.scale;  // the merged accumulator takes scale * dS
             }
             pp[q] = pack_bf16(p2[0], p2[1]);
             dd[q] = pack_bf16(d2[0], d2[1]);
@@ -291,9 +298,18 @@ __global__ void __launch_bounds__(256, 1)
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t kv[32], vv[32];
         tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DK + c0), kv);
-        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DV + c0), vv);
+        if (!C::MERGE) tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DV + c0), vv);
         tc::tmem_wait_ld();
-        if (j < a.S) {
+        if (C::MERGE) {  // dK + dV in one accumulator, the scale already applied: partial dV = 0
+          if (j < a.S) {
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+              *reinterpret_cast<float4*>(part + c0 + q) = make_float4(
+                  __uint_as_float(kv[q]), __uint_as_float(kv[q + 1]), __uint_as_float(kv[q + 2]), __uint_as_float(kv[q + 3]));
+              *reinterpret_cast<float4*>(part + D + c0 + q) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+          }
+        } else if (j < a.S) {
 #pragma unroll
           for (int q = 0; q < 32; q += 4) {
             *reinterpret_cast<float4*>(part + c0 + q) =
@@ -343,16 +359,23 @@ __global__ void dkv_finalize_kernel(Args a, int sep_v) {
 template <int D, bool SEP_V>
 struct QCfg {
   static constexpr int DB = D / 64;
-  static constexpr int T_BYTES = 128 * D * 2;
-  static constexpr int KV_STAGE = (SEP_V ? 2 : 1) * T_BYTES;
+  // D = 256: 64-key K/V tiles, and the gathered-row gradient is formed transposed (dM^T =
+  // Q^T dS + dO^T P, d in the TMEM lanes, two 128-channel halves of KT columns) so that
+  // the dQ accumulator (256 columns), S, dP and dM^T fit in TMEM together
+  static constexpr bool WIDE = D == 256;
+  static constexpr int KT = WIDE ? 64 : 128;     // keys per K/V tile
+  static constexpr int T_BYTES = 128 * D * 2;    // Q / dO tile (128 packed rows)
+  static constexpr int KV_BYTES = KT * D * 2;
+  static constexpr int KV_STAGE = (SEP_V ? 2 : 1) * KV_BYTES;
   static constexpr int STAGES = 2;
-  static constexpr int P_BYTES = 128 * 128 * 2;  // dS / P tile [rows][128 keys] bf16 (gathered tiles)
+  static constexpr int P_BYTES = 128 * KT * 2;   // dS / P tile [rows][KT keys] bf16 (gathered tiles)
   static constexpr int NP = SEP_V ? 0 : 2;       // dS and P copies (csa2 only)
   static constexpr int TILE_BYTES = 2 * T_BYTES + STAGES * KV_STAGE + NP * P_BYTES;
   static constexpr int SMEM = TILE_BYTES + 512;
-  static constexpr int C_DQ = 0, C_S = D, C_DP = D + 128, C_DM = D + 256;
-  static_assert(C_DP + 128 <= 512 && (SEP_V || C_DM + D <= 512), "TMEM");
+  static constexpr int C_DQ = 0, C_S = D, C_DP = D + KT, C_DM = D + 2 * KT;
+  static_assert(C_DP + KT <= 512 && (SEP_V || C_DM + (WIDE ? 2 * KT : D) <= 512), "TMEM");
   static_assert(SMEM <= 232448, "smem");
+  static_assert(!(WIDE && SEP_V), "a separate V needs D <= 128");
 };
 
 enum QBar { Q_FULL = 0, Q_EMPTY, S_FULL_Q, DS_FULL, DM_FULL, DM_EMPTY, QO_DONE, QACC_EMPTY, KVW_FULL,
@@ -362,6 +385,7 @@ struct QItem {
   int b, qt, t0, t1, kt0, n_win, n_gat, gtiles, tq_valid;
 };
 
+template <int KT>
 __device__ __forceinline__ QItem q_item(const Args& a, int it, int n_qt) {
   QItem m;
   m.b = it % a.B;
@@ -371,9 +395,9 @@ __device__ __forceinline__ QItem q_item(const Args& a, int it, int n_qt) {
   m.t1 = min(a.S, m.t0 + tq) - 1;
   m.tq_valid = m.t1 - m.t0 + 1;
   const int lo = max(0, m.t0 - a.window + 1);
-  m.kt0 = lo / 128;
-  m.n_win = m.t1 / 128 - m.kt0 + 1;
-  m.gtiles = (a.main_kv && a.topk > 0 && a.G > 0) ? (a.topk + 127) / 128 : 0;
+  m.kt0 = lo / KT;
+  m.n_win = m.t1 / KT - m.kt0 + 1;
+  m.gtiles = (a.main_kv && a.topk > 0 && a.G > 0) ? (a.topk + KT - 1) / KT : 0;
   m.n_gat = m.gtiles * m.tq_valid;
   return m;
 }
@@ -383,6 +407,8 @@ __global__ void __launch_bounds__(384, 1)
     dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
               const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Args a) {
   using C = QCfg<D, SEP_V>;
+  constexpr int KT = C::KT;
+  constexpr int KB = KT * 128;  // bytes of one 64-channel column block of a K/V tile
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* qs = smem;
   uint8_t* dos = smem + C::T_BYTES;
@@ -418,7 +444,7 @@ __global__ void __launch_bounds__(384, 1)
     if (lane == 0) {
       int g = 0, ii = 0;
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-        const QItem m = q_item(a, it, n_qt);
+        const QItem m = q_item<KT>(a, it, n_qt);
         if (!tc::mbar_wait(&bars[Q_EMPTY], (ii & 1) ^ 1, a.err, 501)) { *abort_flag = 1; break; }
         tc::mbar_expect_tx(&bars[Q_FULL], 2 * C::T_BYTES);
         for (int cb = 0; cb < C::DB; ++cb) {
@@ -433,10 +459,9 @@ __global__ void __launch_bounds__(384, 1)
           uint8_t* kt = kvs + st * C::KV_STAGE;
           tc::mbar_expect_tx(&bars[KVW_FULL + st], C::KV_STAGE);
           for (int cb = 0; cb < C::DB; ++cb) {
-            tc::tma_load_3d(kt + cb * 16384, &tk, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * 128, m.b);
+            tc::tma_load_3d(kt + cb * KB, &tk, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * KT, m.b);
             if (SEP_V)
-              tc::tma_load_3d(kt + C::T_BYTES + cb * 16384, &tv, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * 128,
-                              m.b);
+              tc::tma_load_3d(kt + C::KV_BYTES + cb * KB, &tv, &bars[KVW_FULL + st], cb * 64, (m.kt0 + j) * KT, m.b);
           }
         }
         if (!ok) { *abort_flag = 1; break; }
@@ -444,15 +469,15 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_s = tc::make_idesc(128, 128, 1, 1);
+      const uint32_t idesc_s = tc::make_idesc(128, KT, 1, 1);
       const uint32_t idesc_dq = tc::make_idesc(128, D, 1, 1, false, true);
-      const uint32_t idesc_dm = tc::make_idesc(128, D, 1, 1, true, true);
+      const uint32_t idesc_dm = tc::make_idesc(128, C::WIDE ? KT : D, 1, 1, true, true);
       const uint32_t q_base = smem_u32(qs), do_base = smem_u32(dos), kv_base = smem_u32(kvs);
       const uint32_t ds_base = smem_u32(dss), p_base = ds_base + C::P_BYTES;
       int g = 0, ii = 0, gm = 0;
       int uses_w[2] = {0, 0}, uses_g[2] = {0, 0};
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-        const QItem m = q_item(a, it, n_qt);
+        const QItem m = q_item<KT>(a, it, n_qt);
         const int n = m.n_win + m.n_gat;
         if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 510)) { *abort_flag = 1; break; }
         bool ok = true;
@@ -462,21 +487,21 @@ __global__ void __launch_bounds__(384, 1)
           const int par = win ? (uses_w[st]++ & 1) : (uses_g[st]++ & 1);
           if (!tc::mbar_wait(&bars[(win ? KVW_FULL : KVG_FULL) + st], par, a.err, 511)) { ok = false; break; }
           tc::fence_after_sync();
-          const uint32_t kb = kv_base + st * C::KV_STAGE, vb = kb + (SEP_V ? C::T_BYTES : 0);
+          const uint32_t kb = kv_base + st * C::KV_STAGE, vb = kb + (SEP_V ? C::KV_BYTES : 0);
           // descriptors once per tile; the unrolled loops add constant offsets
           const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
           const uint64_t kd = tc::make_sdesc<128>(kb, 16, 1024), vd = tc::make_sdesc<128>(vb, 16, 1024);
-          const uint64_t k_mn = tc::make_sdesc<128>(kb, 16384, 1024);
+          const uint64_t k_mn = tc::make_sdesc<128>(kb, KB, 1024);
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_S, tc::sdesc_add(qd, cb * 16384 + off), tc::sdesc_add(kd, cb * 16384 + off),
+            tc::mma_ss<0>(tmem + C::C_S, tc::sdesc_add(qd, cb * 16384 + off), tc::sdesc_add(kd, cb * KB + off),
                           idesc_s, kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_DP, tc::sdesc_add(dod, cb * 16384 + off), tc::sdesc_add(vd, cb * 16384 + off),
+            tc::mma_ss<0>(tmem + C::C_DP, tc::sdesc_add(dod, cb * 16384 + off), tc::sdesc_add(vd, cb * KB + off),
                           idesc_s, kk > 0);
           }
           tc::mma_commit(&bars[S_FULL_Q]);
@@ -484,7 +509,7 @@ __global__ void __launch_bounds__(384, 1)
           if (!tc::mbar_wait(&bars[DS_FULL], g & 1, a.err, 513)) { ok = false; break; }
           tc::fence_after_sync();
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)  // 128 keys, 16 per step: dQ += dS K
+          for (int kk = 0; kk < KT / 16; ++kk)  // KT keys, 16 per step: dQ += dS K
             tc::mma_ts(tmem + C::C_DQ, tmem + C::C_S + kk * 8, tc::sdesc_add(k_mn, kk * 2048), idesc_dq,
                        (j == 0 && kk == 0) ? 0u : 1u);
           if (!win) {
@@ -493,12 +518,27 @@ __global__ void __launch_bounds__(384, 1)
             const uint64_t p_mn = tc::make_sdesc<128>(p_base, 16384, 1024);
             const uint64_t q_mn = tc::make_sdesc<128>(q_base, 16384, 1024);
             const uint64_t do_mn = tc::make_sdesc<128>(do_base, 16384, 1024);
+            if (C::WIDE) {
+              // dM^T[d, key] for d in half h: A = Q^T / dO^T (channels 128h.., MN-major),
+              // B = dS / P [rows][keys] (MN-major), K = the 128 query rows
 #pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {  // 128 query rows: dM = dS^T Q + P^T dO
-              tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(ds_mn, kk * 2048), tc::sdesc_add(q_mn, kk * 2048), idesc_dm,
-                            kk > 0);
-              tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(p_mn, kk * 2048), tc::sdesc_add(do_mn, kk * 2048), idesc_dm,
-                            1u);
+              for (int h = 0; h < 2; ++h) {
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                  tc::mma_ss<0>(tmem + C::C_DM + h * KT, tc::sdesc_add(q_mn, 2 * h * 16384 + kk * 2048),
+                                tc::sdesc_add(ds_mn, kk * 2048), idesc_dm, kk > 0);
+                  tc::mma_ss<0>(tmem + C::C_DM + h * KT, tc::sdesc_add(do_mn, 2 * h * 16384 + kk * 2048),
+                                tc::sdesc_add(p_mn, kk * 2048), idesc_dm, 1u);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {  // 128 query rows: dM = dS^T Q + P^T dO
+                tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(ds_mn, kk * 2048), tc::sdesc_add(q_mn, kk * 2048), idesc_dm,
+                              kk > 0);
+                tc::mma_ss<0>(tmem + C::C_DM, tc::sdesc_add(p_mn, kk * 2048), tc::sdesc_add(do_mn, kk * 2048), idesc_dm,
+                              1u);
+              }
             }
             tc::mma_commit(&bars[DM_FULL]);
             ++gm;
@@ -517,7 +557,7 @@ __global__ void __launch_bounds__(384, 1)
     const float sl = a.scale_log2;
     int g = 0, ii = 0, gm = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
-      const QItem m = q_item(a, it, n_qt);
+      const QItem m = q_item<KT>(a, it, n_qt);
       const int n = m.n_win + m.n_gat;
       const int tr = r / a.H, t = m.t0 + tr;
       const bool row_ok = t < a.S;
@@ -528,18 +568,20 @@ __global__ void __launch_bounds__(384, 1)
       for (int j = 0; j < n; ++j, ++g) {
         const bool win = j < m.n_win;
         int k0 = 0, wlo = 0, whi = -1, gtok = -1, e0 = 0;
-        uint32_t gmask[4] = {0, 0, 0, 0};
+        uint32_t gmask[KT / 32];
+#pragma unroll
+        for (int w = 0; w < KT / 32; ++w) gmask[w] = 0u;
         if (win) {
-          k0 = (m.kt0 + j) * 128;
+          k0 = (m.kt0 + j) * KT;
           wlo = max(0, t - a.window + 1) - k0;
           whi = t - k0;
         } else {
           const int gj = j - m.n_win;
           gtok = gj / m.gtiles;
-          e0 = (gj % m.gtiles) * 128;
+          e0 = (gj % m.gtiles) * KT;
           const int32_t* irow = a.idx + ((long long)m.b * a.S + (m.t0 + gtok)) * a.topk;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
+          for (int w = 0; w < KT / 32; ++w) {
             const int e = e0 + w * 32 + lane;
             bool v = false;
             if (e < a.topk) {
@@ -549,11 +591,11 @@ __global__ void __launch_bounds__(384, 1)
             gmask[w] = __ballot_sync(0xffffffffu, v);
           }
         }
-        const bool full = row_ok && win && wlo <= 0 && whi >= 127;
+        const bool full = row_ok && win && wlo <= 0 && whi >= KT - 1;
         if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+        for (int c0 = 0; c0 < KT; c0 += 32) {
           uint32_t sv[32], dv[32];
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
@@ -593,22 +635,49 @@ __global__ void __launch_bounds__(384, 1)
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[DS_FULL]);
         if (!win) {
-          // dM rows (thread = key slot of the tile) -> fp32 atomics into dmain
           if (!tc::mbar_wait(&bars[DM_FULL], gm & 1, a.err, 521)) { ok = false; break; }
           tc::fence_after_sync();
-          const int e = e0 + r;
-          int gi = -1;
-          if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
-          const bool v = gi >= 0 && gi < a.G;
-          float* dst = a.dmain + ((long long)m.b * a.G + (v ? gi : 0)) * D;
-#pragma unroll 1
-          for (int c0 = 0; c0 < D; c0 += 32) {
-            uint32_t mv[32];
-            tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DM + c0), mv);
-            tc::tmem_wait_ld();
-            if (v) {
+          if (C::WIDE) {
+            // dM^T (thread = channel d of each half, column = key slot) -> fp32 atomics into
+            // dmain; the 32 lanes of a warp add to 32 consecutive channels of one row
+            const int32_t* irow = a.idx + ((long long)m.b * a.S + (m.t0 + gtok)) * a.topk;
+            int gl[KT / 32];
 #pragma unroll
-              for (int q = 0; q < 32; ++q) atomicAdd(dst + c0 + q, __uint_as_float(mv[q]));
+            for (int w = 0; w < KT / 32; ++w) {
+              const int e = e0 + w * 32 + lane;
+              gl[w] = e < a.topk ? irow[e] : -1;
+            }
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              const int d = h * 128 + sw * 32 + lane;
+#pragma unroll 1
+              for (int c0 = 0; c0 < KT; c0 += 32) {
+                uint32_t mv[32];
+                tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DM + h * KT + c0), mv);
+                tc::tmem_wait_ld();
+#pragma unroll
+                for (int q = 0; q < 32; ++q) {
+                  const int gi = __shfl_sync(0xffffffffu, gl[c0 >> 5], q);
+                  if (gi >= 0 && gi < a.G) atomicAdd(a.dmain + ((long long)m.b * a.G + gi) * D + d, __uint_as_float(mv[q]));
+                }
+              }
+            }
+          } else {
+            // dM rows (thread = key slot of the tile) -> fp32 atomics into dmain
+            const int e = e0 + r;
+            int gi = -1;
+            if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
+            const bool v = gi >= 0 && gi < a.G;
+            float* dst = a.dmain + ((long long)m.b * a.G + (v ? gi : 0)) * D;
+#pragma unroll 1
+            for (int c0 = 0; c0 < D; c0 += 32) {
+              uint32_t mv[32];
+              tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DM + c0), mv);
+              tc::tmem_wait_ld();
+              if (v) {
+#pragma unroll
+                for (int q = 0; q < 32; ++q) atomicAdd(dst + c0 + q, __uint_as_float(mv[q]));
+              }
             }
           }
           tc::fence_before_sync();
@@ -644,25 +713,30 @@ __global__ void __launch_bounds__(384, 1)
     const int t = threadIdx.x - 256, row = t;  // 128 rows, one per thread
     int g = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-      const QItem m = q_item(a, it, n_qt);
+      const QItem m = q_item<KT>(a, it, n_qt);
       const int n = m.n_win + m.n_gat;
       bool ok = true;
       for (int j = 0; j < n; ++j, ++g) {
         if (j < m.n_win) continue;
         const int st = g & 1, ph = (g >> 1) & 1;
-        const int gj = j - m.n_win, gtok = gj / m.gtiles, e = (gj % m.gtiles) * 128 + row;
+        // KT rows of D channels: 128 / KT threads per row, 16-byte vectors [q0, q0 + NQ)
+        constexpr int TPR = 128 / KT, NQ = D / 8 / TPR;
+        const int kr = row / TPR, q0 = (row % TPR) * NQ;
+        const int gj = j - m.n_win, gtok = gj / m.gtiles, e = (gj % m.gtiles) * KT + kr;
         int gi = -1;
         if (e < a.topk) gi = a.idx[((long long)m.b * a.S + (m.t0 + gtok)) * a.topk + e];
         const bool v = gi >= 0 && gi < a.G;
-        const uint4* src = reinterpret_cast<const uint4*>(a.main_kv + ((long long)m.b * a.G + (v ? gi : 0)) * D);
-        uint4 raw[D / 8];
+        const uint4* src = reinterpret_cast<const uint4*>(a.main_kv + ((long long)m.b * a.G + (v ? gi : 0)) * D) + q0;
+        uint4 raw[NQ];
 #pragma unroll
-        for (int q = 0; q < D / 8; ++q) raw[q] = v ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
+        for (int q = 0; q < NQ; ++q) raw[q] = v ? __ldg(src + q) : make_uint4(0, 0, 0, 0);
         if (!tc::mbar_wait(&bars[KVQ_EMPTY + st], ph ^ 1, a.err, 530)) { ok = false; break; }
         uint8_t* kt = kvs + st * C::KV_STAGE;
 #pragma unroll
-        for (int q = 0; q < D / 8; ++q)
-          st_shared16(kt + (q >> 3) * 16384 + row * 128 + (((q & 7) ^ (row & 7)) * 16), raw[q]);
+        for (int qq = 0; qq < NQ; ++qq) {
+          const int q = q0 + qq;
+          st_shared16(kt + (q >> 3) * KB + kr * 128 + (((q & 7) ^ (kr & 7)) * 16), raw[qq]);
+        }
         tc::fence_async_smem();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[KVG_FULL + st]);
@@ -721,6 +795,17 @@ int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStre
   auto kq = dq_kernel<D, SEP_V>;
   if (cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, QCfg<D, SEP_V>::SMEM) != cudaSuccess)
     return launch_status("attn_bwd_dq(smem attr)");
+  constexpr int KT = QCfg<D, SEP_V>::KT;
+  if (KT != 128) {  // the query-owner kernel reads KT-row K / V tiles
+    const uint32_t kbox[3] = {64, uint32_t(KT), 1};
+    const uint64_t dims[3] = {uint64_t(D), uint64_t(a.S), uint64_t(a.B)};
+    const uint64_t str[2] = {uint64_t(D) * 2, uint64_t(a.S) * D * 2};
+    if (int r = encode_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, kv, dims, str, kbox, CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+    if (int r = encode_tmap(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, SEP_V ? v : kv, dims, str, kbox,
+                            CU_TENSOR_MAP_SWIZZLE_128B))
+      return r;
+  }
   const int tqn = 128 / a.H;
   const int q_items = a.B * ((a.S + tqn - 1) / tqn);
   kq<<<q_items < num_sms() ? q_items : num_sms(), 384, QCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
@@ -751,8 +836,10 @@ extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const 
   MZB_REQUIRE(B >= 1 && S >= 1 && window >= 1 && topk >= 0 && G >= 0, MZB_ERR_SHAPE, "attn_bwd: bad sizes");
   MZB_REQUIRE(H >= 1 && H <= 128 && 128 % H == 0, MZB_ERR_UNSUPPORTED, "attn_bwd: heads must divide 128, got %d",
               H);
-  MZB_REQUIRE(D == 64 || D == 128, MZB_ERR_UNSUPPORTED, "attn_bwd: head dim %d not built (64, 128)", D);
+  MZB_REQUIRE(D == 64 || D == 128 || D == 256, MZB_ERR_UNSUPPORTED, "attn_bwd: head dim %d not built (64, 128, 256)",
+              D);
   const bool sep = v != nullptr && v != kv;
+  MZB_REQUIRE(!(sep && D == 256), MZB_ERR_UNSUPPORTED, "attn_bwd: a separate V needs head dim <= 128");
   const bool gathered = main_kv != nullptr && topk > 0 && G > 0;
   MZB_REQUIRE(!(sep && gathered), MZB_ERR_UNSUPPORTED, "attn_bwd: a separate V only for the window-only kernel");
   MZB_REQUIRE(!gathered || dmain_f32 != nullptr, MZB_ERR_SHAPE, "attn_bwd: gathered rows need a dmain accumulator");
@@ -781,5 +868,6 @@ extern "C" int mzb_attn_bwd(const void* q, const void* kv, const void* v, const 
   a.err = err;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (D == 64) return sep ? attnb::launch<64, true>(q, kv, v, a, st) : attnb::launch<64, false>(q, kv, v, a, st);
+  if (D == 256) return attnb::launch<256, false>(q, kv, v, a, st);
   return sep ? attnb::launch<128, true>(q, kv, v, a, st) : attnb::launch<128, false>(q, kv, v, a, st);
 }

@@ -40,7 +40,8 @@ def bwd(q, kv, o, lse, do, *, window: int, causal: bool = True, sinks=None, cfg=
     assert q.shape == o.shape == do.shape, "shape mismatch"
     assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
     B, S, H, D = check_mqa(q, kv, "swa_attn")
-    assert D in (64, 96, 128), f"swa_attn backward supports head dim 64 / 96 / 128 here, got {D}"
+    assert D in (64, 96, 128, 256), f"swa_attn backward supports head dim 64 / 96 / 128 / 256, got {D}"
+    assert v is None or D <= 128, "a separate v needs head dim <= 128 in backward"
     scale = softmax_scale if softmax_scale is not None else D**-0.5
     dq, dk, dv, _, dsinks = run_bwd(q.contiguous(), kv.contiguous(), None if v is None else v.contiguous(), None,
                                     None, o.contiguous(), lse.contiguous(), do.contiguous(), sinks, min(window, S),

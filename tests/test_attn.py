@@ -224,7 +224,8 @@ def _do(torch, dev, shape, seed):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("H,D,window", [(64, 128, 100), (16, 64, 37), (4, 128, 300), (16, 96, 100)])
+@pytest.mark.parametrize("H,D,window", [(64, 128, 100), (16, 64, 37), (4, 128, 300), (16, 96, 100), (4, 256, 100),
+                                        (16, 256, 37), (64, 256, 300)])
 def test_swa_bwd(cuda, H, D, window):
     import torch
     from mzoo_b200 import swa_attn
@@ -255,7 +256,8 @@ def test_swa_bwd_separate_v(cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (16, 96, 40, 32)])
+@pytest.mark.parametrize("H,D,G,topk", [(64, 128, 100, 100), (16, 64, 37, 48), (16, 96, 40, 32), (4, 256, 40, 64),
+                                        (16, 256, 100, 100), (64, 256, 70, 135)])
 def test_csa2_bwd(cuda, H, D, G, topk):
     import torch
     from mzoo_b200 import csa2_attn
