@@ -93,7 +93,9 @@ __device__ __forceinline__ int visible_of(const int32_t* q_pos, long long q_offs
   return visible_keys(q_offset, s, ratio, T);
 }
 
-template <bool FP8, int DI>
+// H64: the 64-head indexer's epilogue (packed FMAs, one TMEM wait per token) compiled
+// alone; otherwise the generic head loop.
+template <bool FP8, int DI, bool H64>
 __global__ void __launch_bounds__(NTHREADS, 1)
     score_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, ScoreArgs a) {
   using C = Cfg<FP8, DI>;
@@ -280,65 +282,94 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         acc_ph ^= 1;
         tc::fence_after_sync();
         const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * C::NMAX);
-        if (a.Hi == 64) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
-          for (int t = 0; t < tq_n; ++t) {
-            uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};  // 8 independent fp32 sums
+        bool released = false;
+        if constexpr (H64) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
+          // Per token, both 32-column TMEM loads go out behind one wait; the buffer is released
+          // as soon as the last token's columns are in registers, so the MMA can refill it
+          // while they are summed.
+          auto release = [&]() {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+            released = true;
+          };
+          uint64_t sum4[4];  // 8 independent fp32 sums of the current token
+          auto half = [&](const uint32_t (&r)[32], int u) {  // u = 2 t + (half of token t)
+            const int t = u >> 1;
+            if ((u & 1) == 0) sum4[0] = sum4[1] = sum4[2] = sum4[3] = 0ull;
+            const float4* cq4 = reinterpret_cast<const float4*>(cwp + u * 32);
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-              uint32_t r[32];
-              tc::tmem_ld32(tbase + t * 64 + half * 32, r);
-              tc::tmem_wait_ld();
-              const float4* cq4 = reinterpret_cast<const float4*>(cwp + t * 64 + half * 32);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 cc = cq4[i];
-                const uint64_t x01 = pack_f32x2(fmaxf(__uint_as_float(r[4 * i + 0]), 0.0f),
-                                                fmaxf(__uint_as_float(r[4 * i + 1]), 0.0f));
-                const uint64_t x23 = pack_f32x2(fmaxf(__uint_as_float(r[4 * i + 2]), 0.0f),
-                                                fmaxf(__uint_as_float(r[4 * i + 3]), 0.0f));
-                acc[(i & 1) * 2 + 0] = ffma_f32x2(x01, pack_f32x2(cc.x, cc.y), acc[(i & 1) * 2 + 0]);
-                acc[(i & 1) * 2 + 1] = ffma_f32x2(x23, pack_f32x2(cc.z, cc.w), acc[(i & 1) * 2 + 1]);
-              }
+            for (int i = 0; i < 4; ++i) {
+              const float4 c0 = cq4[2 * i], c1 = cq4[2 * i + 1];
+              sum4[0] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 0]), 0.0f),
+                                              fmaxf(__uint_as_float(r[8 * i + 1]), 0.0f)),
+                                   pack_f32x2(c0.x, c0.y), sum4[0]);
+              sum4[1] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 2]), 0.0f),
+                                              fmaxf(__uint_as_float(r[8 * i + 3]), 0.0f)),
+                                   pack_f32x2(c0.z, c0.w), sum4[1]);
+              sum4[2] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 4]), 0.0f),
+                                              fmaxf(__uint_as_float(r[8 * i + 5]), 0.0f)),
+                                   pack_f32x2(c1.x, c1.y), sum4[2]);
+              sum4[3] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 6]), 0.0f),
+                                              fmaxf(__uint_as_float(r[8 * i + 7]), 0.0f)),
+                                   pack_f32x2(c1.z, c1.w), sum4[3]);
             }
-            const float2 p0 = unpack_f32x2(acc[0]), p1 = unpack_f32x2(acc[1]);
-            const float2 p2 = unpack_f32x2(acc[2]), p3 = unpack_f32x2(acc[3]);
-            const float sum = ((p0.x + p0.y) + (p1.x + p1.y)) + ((p2.x + p2.y) + (p3.x + p3.y));
-            const int vis = __shfl_sync(0xffffffffu, vis_l, t);
-            if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
-          }
-        } else
-        for (int t = 0; t < tq_n; ++t) {
-          // four independent partial sums (one per 16-head chunk) keep the FMA chains short
-          float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-          for (int h0 = 0; h0 < a.Hi; h0 += 64) {
-            uint32_t r[4][16];
-            const int nch = min(4, (a.Hi - h0) >> 4);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              if (c < nch) tc::tmem_ld16(tbase + t * a.Hi + h0 + c * 16, r[c]);
+            if (u & 1) {
+              const float2 p0 = unpack_f32x2(sum4[0]), p1 = unpack_f32x2(sum4[1]);
+              const float2 p2 = unpack_f32x2(sum4[2]), p3 = unpack_f32x2(sum4[3]);
+              const float sum = ((p0.x + p0.y) + (p1.x + p1.y)) + ((p2.x + p2.y) + (p3.x + p3.y));
+              const int vis = __shfl_sync(0xffffffffu, vis_l, t);
+              if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
+            }
+          };
+          const int nu = 2 * tq_n;  // halves of this tile's tokens
+          for (int u = 0; u < nu; u += 2) {
+            uint32_t ra[32], rb[32];
+            tc::tmem_ld32(tbase + u * 32, ra);
+            tc::tmem_ld32(tbase + (u + 1) * 32, rb);
             tc::tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              if (c < nch) {
-                const float4* cq4 = reinterpret_cast<const float4*>(cwp + t * a.Hi + h0 + c * 16);
-#pragma unroll
-                for (int q4 = 0; q4 < 4; ++q4) {
-                  const float4 cc = cq4[q4];
-                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 0]), 0.0f), cc.x, part[c]);
-                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 1]), 0.0f), cc.y, part[c]);
-                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 2]), 0.0f), cc.z, part[c]);
-                  part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 3]), 0.0f), cc.w, part[c]);
+            tc::reg_after_wait(ra);
+            tc::reg_after_wait(rb);
+            if (u + 2 == nu) release();
+            half(ra, u);
+            half(rb, u + 1);
+          }
+        } else {
+          for (int t = 0; t < tq_n; ++t) {
+            // four independent partial sums (one per 16-head chunk) keep the FMA chains short
+            float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int h0 = 0; h0 < a.Hi; h0 += 64) {
+              uint32_t r[4][16];
+              const int nch = min(4, (a.Hi - h0) >> 4);
+  #pragma unroll
+              for (int c = 0; c < 4; ++c)
+                if (c < nch) tc::tmem_ld16(tbase + t * a.Hi + h0 + c * 16, r[c]);
+              tc::tmem_wait_ld();
+  #pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                if (c < nch) {
+                  const float4* cq4 = reinterpret_cast<const float4*>(cwp + t * a.Hi + h0 + c * 16);
+  #pragma unroll
+                  for (int q4 = 0; q4 < 4; ++q4) {
+                    const float4 cc = cq4[q4];
+                    part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 0]), 0.0f), cc.x, part[c]);
+                    part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 1]), 0.0f), cc.y, part[c]);
+                    part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 2]), 0.0f), cc.z, part[c]);
+                    part[c] = fmaf(fmaxf(__uint_as_float(r[c][q4 * 4 + 3]), 0.0f), cc.w, part[c]);
+                  }
                 }
               }
             }
+            const float sum = (part[0] + part[1]) + (part[2] + part[3]);
+            const int vis = __shfl_sync(0xffffffffu, vis_l, t);
+            if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
           }
-          const float sum = (part[0] + part[1]) + (part[2] + part[3]);
-          const int vis = __shfl_sync(0xffffffffu, vis_l, t);
-          if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
         }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+        if (!released) {
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&acc_empty[acc]);
+        }
       }
       if (!ok) { *abort_flag = 1; break; }
       __syncwarp();  // every lane is done with cwp before the next item rewrites it
@@ -1045,7 +1076,7 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
     int e = encode_tmap(&tk, dt, 3, k, dims, str, box, swz);
     if (e) return e;
   }
-  auto kern = score_kernel<FP8, DI>;
+  auto kern = a.Hi == 64 ? score_kernel<FP8, DI, true> : score_kernel<FP8, DI, false>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return launch_status("indexer_scores(smem attr)");
   // Few (batch, query block) pairs -- decode, short prefill -- would leave SMs idle while

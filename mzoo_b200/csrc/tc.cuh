@@ -243,6 +243,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Registers written by an asynchronous tcgen05.ld are defined only after tcgen05.wait::ld;
+// passing them through empty volatile asm placed after the wait keeps every use below it.
+template <int N>
+__device__ __forceinline__ void reg_after_wait(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMEM address: lane in bits [31:16], column in bits [15:0].
