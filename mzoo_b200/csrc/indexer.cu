@@ -43,7 +43,6 @@ constexpr int BM = 128;  // keys per tile = MMA M
 constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int EPI_WARP0 = 2;   // epilogue warp w reads TMEM lanes 32 * (w % 4): warps 2-5 and 6-9
                                // each cover all four lane quarters
-constexpr int NEPI = 256;
 constexpr int KB_PARTS = 16;  // per-batch partial maxima of B_t
 
 template <bool FP8, int DI>
@@ -93,10 +92,14 @@ __device__ __forceinline__ int visible_of(const int32_t* q_pos, long long q_offs
   return visible_keys(q_offset, s, ratio, T);
 }
 
-// H64: the 64-head indexer's epilogue (packed FMAs, one TMEM wait per token) compiled
-// alone; otherwise the generic head loop.
-template <bool FP8, int DI, bool H64>
-__global__ void __launch_bounds__(NTHREADS, 1)
+// Epilogue modes: 0 the generic head loop; 1 the 64-head indexer's (packed FMAs, one TMEM
+// wait per token) with warpgroup g draining accumulator buffer g, i.e. alternate tiles, all
+// tokens; 2 the same for four-token blocks with four warpgroups, two per buffer, each taking
+// two of its tokens (twice the warps to hide the epilogue's latencies).
+__host__ __device__ constexpr int score_nthreads(int mode) { return mode == 2 ? NTHREADS + 256 : NTHREADS; }
+
+template <bool FP8, int DI, int MODE>
+__global__ void __launch_bounds__(score_nthreads(MODE), 1)
     score_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, ScoreArgs a) {
   using C = Cfg<FP8, DI>;
   extern __shared__ uint8_t smem_raw[];
@@ -120,7 +123,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
       tc::mbar_init(&acc_full[i], 1);
-      tc::mbar_init(&acc_empty[i], 4);  // the four warps of the warpgroup that owns buffer i
+      tc::mbar_init(&acc_empty[i], MODE == 2 ? 8 : 4);  // the warps of the warpgroup(s) of buffer i
     }
     for (int i = 0; i < C::K_STAGES; ++i) {
       tc::mbar_init(&k_full[i], 1);
@@ -233,14 +236,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp >= EPI_WARP0) {
     // ---------------------------------------------------------------- epilogue
-    // Warpgroup g (warps 2-5 / 6-9) drains accumulator buffer g, i.e. every other tile,
-    // all tokens of it.  Each warp keeps its own copy of the item's weights c = w * sq.
-    const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..255
+    // Each warp keeps its own copy of the weights c = w * sq of the tokens it sums.
+    constexpr int NEPI_M = score_nthreads(MODE) - EPI_WARP0 * 32;
+    const int et = threadIdx.x - EPI_WARP0 * 32;  // 0..NEPI_M-1
     const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) ...
     const int wg = ew >> 2;
+    const int bwg = MODE == 2 ? wg >> 1 : wg;  // the accumulator buffer this warpgroup drains
+    const int th = MODE == 2 ? wg & 1 : 0;     // MODE 2: tokens [2 th, 2 th + 2) of the block
     const int row = quarter * 32 + lane;  // key row inside the tile
-    float* cwp = cw + ew * C::NMAX;
+    constexpr int CWN = MODE == 2 ? 128 : C::NMAX;  // weights per warp
+    float* cwp = cw + ew * CWN;
     uint32_t tcount = 0;
     int acc_ph = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
@@ -254,13 +260,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int s = s0 + t;
           if (s >= a.S) break;
           float* rowp = a.scores + (size_t(m.b) * a.S + s) * a.T;
-          for (int j = n_kt * BM + et; j < a.T; j += NEPI) rowp[j] = -INFINITY;
+          for (int j = n_kt * BM + et; j < a.T; j += NEPI_M) rowp[j] = -INFINITY;
         }
       }
       if (m.k0 >= m.k1) continue;
       const int tq_n = min(a.Tq, a.S - s0);  // real tokens in this block
-      for (int i = lane; i < a.N; i += 32) {
-        const int s = s0 + i / a.Hi, h = i % a.Hi;
+      const int t0 = MODE == 2 ? min(2 * th, tq_n) : 0, t1 = MODE == 2 ? min(2 * th + 2, tq_n) : tq_n;
+      for (int i = lane; i < (MODE == 2 ? 128 : a.N); i += 32) {
+        const int ci = (MODE == 2 ? th * 128 : 0) + i;  // column (token, head) of the block
+        const int s = s0 + ci / a.Hi, h = ci % a.Hi;
         float c = 0.0f;
         if (s < a.S) {
           const size_t o = (size_t(m.b) * a.S + s) * a.Hi + h;
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int kt = m.k0; kt < m.k1; ++kt, ++tcount) {
         const int acc = int(tcount & 1u);
-        if (acc != wg) continue;
+        if (acc != bwg) continue;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
         const float skj = (j < a.T) ? (a.sk ? __ldg(a.sk + size_t(m.b) * a.T + j) : 1.0f) * a.scale : 0.0f;
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc::fence_after_sync();
         const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * C::NMAX);
         bool released = false;
-        if constexpr (H64) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
+        if constexpr (MODE >= 1) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
           // Per token, both 32-column TMEM loads go out behind one wait; the buffer is released
           // as soon as the last token's columns are in registers, so the MMA can refill it
           // while they are summed.
@@ -297,7 +305,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           auto half = [&](const uint32_t (&r)[32], int u) {  // u = 2 t + (half of token t)
             const int t = u >> 1;
             if ((u & 1) == 0) sum4[0] = sum4[1] = sum4[2] = sum4[3] = 0ull;
-            const float4* cq4 = reinterpret_cast<const float4*>(cwp + u * 32);
+            const float4* cq4 = reinterpret_cast<const float4*>(cwp + (u - 2 * t0) * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float4 c0 = cq4[2 * i], c1 = cq4[2 * i + 1];
@@ -322,17 +330,28 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
             }
           };
-          const int nu = 2 * tq_n;  // halves of this tile's tokens
-          for (int u = 0; u < nu; u += 2) {
-            uint32_t ra[32], rb[32];
-            tc::tmem_ld32(tbase + u * 32, ra);
-            tc::tmem_ld32(tbase + (u + 1) * 32, rb);
-            tc::tmem_wait_ld();
-            tc::reg_after_wait(ra);
-            tc::reg_after_wait(rb);
-            if (u + 2 == nu) release();
-            half(ra, u);
-            half(rb, u + 1);
+          const int nu = 2 * t1;  // halves of this warp's tokens: [2 t0, 2 t1)
+          if constexpr (MODE == 2) {  // 96 registers a thread: one 32-column load at a time
+            for (int u = 2 * t0; u < nu; ++u) {
+              uint32_t r[32];
+              tc::tmem_ld32(tbase + u * 32, r);
+              tc::tmem_wait_ld();
+              tc::reg_after_wait(r);
+              if (u + 1 == nu) release();
+              half(r, u);
+            }
+          } else {
+            for (int u = 2 * t0; u < nu; u += 2) {
+              uint32_t ra[32], rb[32];
+              tc::tmem_ld32(tbase + u * 32, ra);
+              tc::tmem_ld32(tbase + (u + 1) * 32, rb);
+              tc::tmem_wait_ld();
+              tc::reg_after_wait(ra);
+              tc::reg_after_wait(rb);
+              if (u + 2 == nu) release();
+              half(ra, u);
+              half(rb, u + 1);
+            }
           }
         } else {
           for (int t = 0; t < tq_n; ++t) {
@@ -1076,7 +1095,8 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
     int e = encode_tmap(&tk, dt, 3, k, dims, str, box, swz);
     if (e) return e;
   }
-  auto kern = a.Hi == 64 ? score_kernel<FP8, DI, true> : score_kernel<FP8, DI, false>;
+  const int mode = a.Hi != 64 ? 0 : (a.Tq == 4 ? 2 : 1);
+  auto kern = mode == 2 ? score_kernel<FP8, DI, 2> : (mode == 1 ? score_kernel<FP8, DI, 1> : score_kernel<FP8, DI, 0>);
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
     return launch_status("indexer_scores(smem attr)");
   // Few (batch, query block) pairs -- decode, short prefill -- would leave SMs idle while
@@ -1096,7 +1116,7 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
   const long long items = base * b.n_kc;
   MZB_REQUIRE(items < (1LL << 31), MZB_ERR_SHAPE, "indexer: too many work items");
   const int grid = items < sms ? int(items) : sms;
-  kern<<<grid, NTHREADS, C::SMEM, st>>>(tq, tk, b);
+  kern<<<grid, score_nthreads(mode), C::SMEM, st>>>(tq, tk, b);
   return launch_status("indexer_scores");
 }
 
