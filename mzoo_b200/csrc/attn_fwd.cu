@@ -262,27 +262,48 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!tc::mbar_wait(&bars[S_FULL + sb], (g >> 1) & 1, a.err, 320)) { ok = false; break; }
         tc::fence_after_sync();
         const uint32_t sbase = tc::taddr(tmem, sw * 32, C::S_COL0 + sb * NK);
-        auto valid = [&](int c) -> bool {
-          if (!row_ok) return false;
-          if (win) return c >= wlo && c <= whi;
-          return tr == gtok && ((gm[c >> 5] >> (c & 31)) & 1u);
-        };
-        // a window tile this row sees completely needs no per-column mask
+        // column validity of this row as bits, built once per tile (window: the run
+        // [wlo, whi]; gathered: this token's valid slots); a warp whose rows all see the
+        // whole tile takes the mask-free loops
         const bool full = row_ok && win && wlo <= 0 && whi >= NK - 1;
+        const bool warp_full = __all_sync(0xffffffffu, full);
+        uint32_t mw[NK / 32];
+#pragma unroll
+        for (int q = 0; q < NK / 32; ++q) {
+          uint32_t w = 0u;
+          if (row_ok) {
+            if (win) {
+              const int lo = max(wlo - 32 * q, 0), hi = min(whi - 32 * q, 31);
+              w = lo > hi ? 0u : ((0xFFFFFFFFu >> (31 - (hi - lo))) << lo);
+            } else if (tr == gtok) {
+              w = gm[q];
+            }
+          }
+          mw[q] = w;
+        }
+        // the whole S row behind one TMEM wait; the S buffer is released as soon as it is in
+        // registers, so the next QK^T into it can start while this tile is exponentiated
+        uint32_t sv[NK / 32][32];
+#pragma unroll
+        for (int q = 0; q < NK / 32; ++q) tc::tmem_ld32(sbase + 32 * q, sv[q]);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < NK / 32; ++q) tc::reg_after_wait(sv[q]);
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[S_EMPTY + sb]);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (warp_full) {
 #pragma unroll
-        for (int c0 = 0; c0 < NK; c0 += 32) {
-          uint32_t sr[32];
-          tc::tmem_ld32(sbase + c0, sr);
-          tc::tmem_wait_ld();
-          if (full) {
+          for (int q = 0; q < NK / 32; ++q)
 #pragma unroll
-            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sr[i]));
-          } else {
+            for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sv[q][i]));
+        } else {
+#pragma unroll
+          for (int q = 0; q < NK / 32; ++q)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (valid(c0 + i)) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sr[i]));
-          }
+              mx[i & 3] = fmaxf(mx[i & 3], (mw[q] >> i) & 1u ? __uint_as_float(sv[q][i]) : -INFINITY);
         }
         const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         const bool need = mt * sl > mrow * sl + 8.0f;
@@ -292,18 +313,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         uint8_t* prow = ps + sb * C::P_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int c0 = 0; c0 < NK; c0 += 32) {
-          uint32_t sr[32];
-          tc::tmem_ld32(sbase + c0, sr);
-          tc::tmem_wait_ld();
+        for (int q = 0; q < NK / 32; ++q) {
+          const int c0 = 32 * q;
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * i]), sl, -ms));
-            float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * i + 1]), sl, -ms));
-            if (!full) {
-              p0 = valid(c0 + 2 * i) ? p0 : 0.0f;
-              p1 = valid(c0 + 2 * i + 1) ? p1 : 0.0f;
+            float p0 = fast_exp2(fmaf(__uint_as_float(sv[q][2 * i]), sl, -ms));
+            float p1 = fast_exp2(fmaf(__uint_as_float(sv[q][2 * i + 1]), sl, -ms));
+            if (!warp_full) {
+              p0 = (mw[q] >> (2 * i)) & 1u ? p0 : 0.0f;
+              p1 = (mw[q] >> (2 * i + 1)) & 1u ? p1 : 0.0f;
             }
             ps4[i & 3] += p0 + p1;
             pk[i] = pack_bf16(p0, p1);
@@ -311,15 +330,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // row r of column block c0/64: 4 chunks of 16 B (keys c0..c0+31 -> chunks (c0%64)/8 ..)
           uint8_t* blk = prow + (c0 >> 6) * 128 * 128;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int ch = ((c0 & 63) >> 3) + q;
-            st_shared16(blk + ((ch ^ (r & 7)) * 16), make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]));
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int ch = ((c0 & 63) >> 3) + q4;
+            st_shared16(blk + ((ch ^ (r & 7)) * 16),
+                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]));
           }
         }
         const float psum = (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bars[S_EMPTY + sb]);
         lsum = lsum * alpha + psum;
         if (j > 0 && __any_sync(0xffffffffu, need)) {
           if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 321)) { ok = false; break; }
