@@ -28,6 +28,12 @@ __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
+// bits [lo, hi] of a 32-bit word (empty when hi < lo; lo, hi clipped to [0, 31])
+__device__ __forceinline__ uint32_t run_bits(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 31);
+  return lo > hi ? 0u : ((0xFFFFFFFFu >> (31 - (hi - lo))) << lo);
+}
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -256,32 +262,44 @@ __global__ void __launch_bounds__(256, 1)
         const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
         const float* dl = l2 + 128;
         const int tb = ((m.qt0 + i) * 128) >> a.hshift;  // token of column 0
-        // key j sees every row of this tile: j <= tb and j > tb + tpt - 1 - window, tiles in range
-        const bool full = j < a.S && tb + tpt - 1 < a.S && j <= tb && j > tb + tpt - 1 - a.window;
+        // key j is seen by the tile's columns (packed rows of tokens t, j <= t < j + window,
+        // t < S): one run [clo, chi] of columns, turned into one mask word per 32 columns
+        int clo = 1, chi = 0;
+        if (j < a.S) {
+          clo = (j - tb) * a.H;
+          chi = (min(j + a.window - 1, a.S - 1) - tb + 1) * a.H - 1;
+        }
+        const bool warp_full = __all_sync(0xffffffffu, clo <= 0 && chi >= 127);
 #pragma unroll 1
         for (int c0 = 0; c0 < 128; c0 += 32) {
           uint32_t sv[32], dv[32];
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
+          const uint32_t mw = warp_full ? 0xFFFFFFFFu : run_bits(clo - c0, chi - c0);
+          const float4* l24 = reinterpret_cast<const float4*>(l2 + c0);
+          const float4* dl4 = reinterpret_cast<const float4*>(dl + c0);
           tc::tmem_wait_ld();
+          tc::reg_after_wait(sv);
+          tc::reg_after_wait(dv);
           uint32_t pp[16], dd[16];
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            float p2[2], d2[2];
+          for (int q4 = 0; q4 < 8; ++q4) {
+            const float4 L = l24[q4], Dl = dl4[q4];
+            const float lv[4] = {L.x, L.y, L.z, L.w}, dlv[4] = {Dl.x, Dl.y, Dl.z, Dl.w};
+            float p2[4], d2[4];
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int c = c0 + 2 * q + e;
-              float p = fast_exp2(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2[c]));
-              if (!full) {
-                const int t = tb + (c >> a.hshift);
-                p = (j < a.S && t < a.S && j <= t && j > t - a.window) ? p : 0.0f;
-              }
+            for (int e = 0; e < 4; ++e) {
+              const int c = 4 * q4 + e;  // column within the chunk
+              float p = fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -lv[e]));
+              if (!warp_full) p = (mw >> c) & 1u ? p : 0.0f;
               p2[e] = p;
-              d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl[c]);
+              d2[e] = p * (__uint_as_float(dv[c]) - dlv[e]);
               if (C::MERGE) d2[e] *= a.scale;  // the merged accumulator takes scale * dS
             }
-            pp[q] = pack_bf16(p2[0], p2[1]);
-            dd[q] = pack_bf16(d2[0], d2[1]);
+            pp[2 * q4] = pack_bf16(p2[0], p2[1]);
+            pp[2 * q4 + 1] = pack_bf16(p2[2], p2[3]);
+            dd[2 * q4] = pack_bf16(d2[0], d2[1]);
+            dd[2 * q4 + 1] = pack_bf16(d2[2], d2[3]);
           }
           tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), pp);
           tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_DP + c0 / 2), dd);
@@ -592,6 +610,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         const bool full = row_ok && win && wlo <= 0 && whi >= KT - 1;
+        const bool warp_full = __all_sync(0xffffffffu, full);
         if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
@@ -599,19 +618,25 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t sv[32], dv[32];
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
+          // this row's valid columns of the chunk as bits (window run, or its gathered slots)
+          uint32_t mw = 0xFFFFFFFFu;
+          if (!warp_full) {
+            mw = 0u;
+            if (row_ok) mw = win ? run_bits(wlo - c0, whi - c0) : (tr == gtok ? gmask[c0 >> 5] : 0u);
+          }
           tc::tmem_wait_ld();
+          tc::reg_after_wait(sv);
+          tc::reg_after_wait(dv);
           uint32_t dd[16], ds[16], pp[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             float d2[2], p2[2];
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const int c = c0 + 2 * q + e;
-              const bool valid = full || (row_ok && (win ? (c >= wlo && c <= whi)
-                                                          : (tr == gtok && ((gmask[c >> 5] >> (c & 31)) & 1u))));
-              const float p = valid ? fast_exp2(fmaf(__uint_as_float(sv[2 * q + e]), sl, -l2)) : 0.0f;
+              const int c = 2 * q + e;  // column within the chunk
+              const float p = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
               p2[e] = p;
-              d2[e] = p * (__uint_as_float(dv[2 * q + e]) - dl);
+              d2[e] = p * (__uint_as_float(dv[c]) - dl);
             }
             dd[q] = pack_bf16(d2[0], d2[1]);
             ds[q] = pack_bf16(d2[0] * a.scale, d2[1] * a.scale);  // dK carries the softmax scale
