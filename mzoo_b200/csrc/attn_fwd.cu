@@ -26,6 +26,14 @@ constexpr int NTHREADS = 384;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
+// Row finish, written with explicitly rounded operations so that the softmax warps and the
+// separate epilogue warps (window-only kernel) produce the same bits: msl = m * scale_log2,
+// optional sink term in the denominator, lse in natural log.
+__device__ __forceinline__ float row_sum_with_sink(float lsum, float msl, const float* sinks, int h) {
+  return sinks ? __fadd_rn(lsum, exp2f(__fsub_rn(__fmul_rn(sinks[h], LOG2E), msl))) : lsum;
+}
+__device__ __forceinline__ float row_lse(float msl, float lsum) { return __fmul_rn(__fadd_rn(msl, log2f(lsum)), LN2); }
+
 template <int D, bool SEP_V>
 struct Cfg {
   static constexpr int NK = D == 256 ? 64 : 128;  // keys per tile
@@ -36,7 +44,7 @@ struct Cfg {
   static constexpr int P_BYTES = 128 * NK * 2;
   static constexpr int STAGES = SEP_V ? 2 : 3;
   static constexpr int TILE_BYTES = Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES;
-  static constexpr int MISC = 512 + 2 * 128 * 4;
+  static constexpr int MISC = 512 + 4 * 128 * 4;  // barriers; 2 x (row max, row sum) handoff
   static constexpr int SMEM = TILE_BYTES + MISC;
   static constexpr int S_COL0 = D;  // O in columns [0, D), S buffers after it
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -57,7 +65,7 @@ struct Args {
 // O_FINAL: commit after an item's last PV, waited on by the epilogue with the item parity
 // (two PVs can still be in flight there, so O_DONE's parity would alias an older phase).
 enum Bar { Q_FULL = 0, Q_EMPTY, O_DONE, O_EMPTY, S_FULL, S_FULL1, S_EMPTY, S_EMPTY1, P_FULL, P_FULL1, KV_FULL_W,
-           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, NBAR };
+           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, EPI_FULL, NBAR };
 
 __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -103,8 +111,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 8 * NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::TILE_BYTES + 8 * NBAR + 4);
-  uint32_t* colmask = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 256);  // unused slot
-  (void)colmask;
+  // window-only kernel: the softmax warps hand each item's row statistics (max in the
+  // exp2 domain, sum) to warps 8-11, which write O and lse while the next item runs
+  float* stats = reinterpret_cast<float*>(smem + C::TILE_BYTES + 512);  // [2][2][128]
   if (smem_u32(smem) & 1023) {
     if (threadIdx.x == 0) atomicExch(a.err, MZB_ERR_ALIGN);
     return;
@@ -113,7 +122,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) {
       uint32_t c = 1;
-      if (i == O_EMPTY || i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1) c = 4;
+      if (i == O_EMPTY || i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1 || i == EPI_FULL) c = 4;
       if (i >= KV_FULL_G && i < KV_EMPTY) c = 4;
       tc::mbar_init(&bars[i], c);
     }
@@ -134,6 +143,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int tqn = 128 / a.H;
   const int n_qt = (a.S + tqn - 1) / tqn;
   const int items = a.B * n_qt;
+  const bool epi_warps = a.main_kv == nullptr;  // no gathered rows: warps 8-11 are free
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -359,9 +369,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) tc::mbar_arrive(&bars[P_FULL + sb]);
       }
       if (!ok) { *abort_flag = 1; break; }
+      if (epi_warps) {
+        float* st = stats + (ii & 1) * 256;
+        st[r] = __fmul_rn(mrow, sl);
+        st[128 + r] = lsum;
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bars[EPI_FULL]);
+        continue;
+      }
       if (!tc::mbar_wait(&bars[O_FINAL], ii & 1, a.err, 322)) { *abort_flag = 1; break; }
       tc::fence_after_sync();
-      if (a.sinks) lsum += exp2f(a.sinks[h] * LOG2E - mrow * sl);
+      const float msl = __fmul_rn(mrow, sl);
+      lsum = row_sum_with_sink(lsum, msl, a.sinks, h);
       const float inv = 1.0f / lsum;
       const long long grow = (long long)m.qt * 128 + r;  // packed row within the batch
       if (row_ok) {
@@ -379,7 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                 pack_bf16(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv),
                                 pack_bf16(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv));
         }
-        a.lse[(long long)m.b * a.S * a.H + grow] = (mrow * sl + log2f(lsum)) * LN2;
+        a.lse[(long long)m.b * a.S * a.H + grow] = row_lse(msl, lsum);
       } else {
         // keep the warp-collective TMEM loads uniform: rows past S read and discard
 #pragma unroll
@@ -389,6 +408,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           tc::tmem_wait_ld();
         }
       }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[O_EMPTY]);
+    }
+  } else if (warp >= 8 && epi_warps) {
+    // ---------------------------------------------------------------- epilogue (window-only)
+    const int sw = warp - 8, r = sw * 32 + lane;  // TMEM lane quarter warp % 4, as the softmax
+    int ii = 0;
+    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
+      const Item m = make_item<NK>(a, it, n_qt);
+      const int t = m.t0 + r / a.H, h = r % a.H;
+      const bool row_ok = t < a.S;
+      if (!tc::mbar_wait(&bars[EPI_FULL], ii & 1, a.err, 323) ||
+          !tc::mbar_wait(&bars[O_FINAL], ii & 1, a.err, 322)) { *abort_flag = 1; break; }
+      tc::fence_after_sync();
+      const float* st = stats + (ii & 1) * 256;
+      const float msl = st[r];
+      const float lsum = row_sum_with_sink(st[128 + r], msl, a.sinks, h);
+      const float inv = 1.0f / lsum;
+      const long long grow = (long long)m.qt * 128 + r;  // packed row within the batch
+      __nv_bfloat16* orow = a.o + ((long long)m.b * a.S * a.H + grow) * D;
+#pragma unroll
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t ov[32];
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
+        tc::tmem_wait_ld();
+        tc::reg_after_wait(ov);
+        if (row_ok) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16(__uint_as_float(ov[8 * q]) * inv, __uint_as_float(ov[8 * q + 1]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv),
+                                pack_bf16(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv));
+        }
+      }
+      if (row_ok) a.lse[(long long)m.b * a.S * a.H + grow] = row_lse(msl, lsum);
       tc::fence_before_sync();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bars[O_EMPTY]);
