@@ -100,6 +100,15 @@ def test_scores_match_reference(cuda, dim, heads):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("S", [253, 254, 255])
+def test_scores_partial_token_blocks(cuda, S):
+    """64 heads take four-token query blocks drained by four warpgroups, two tokens each:
+    a last block of one to three tokens leaves a warpgroup with nothing but its release."""
+    import torch
+    _check_scores(torch, cuda, 2, S, 64, 128, 160, 2, q_offset=64)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("ratio", [1, 2, 4])
 def test_compress_ratios(cuda, ratio):
     import torch
