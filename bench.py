@@ -261,7 +261,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
                    "l2": "flushed (256 MB write) per step"},
         "e2e": {"value": queries / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128>", "achieved": achieved,
+        "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128,2>", "achieved": achieved,
                      "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
                      "peak_note": f"dense FP8 = 2 x {pk['_source']} bf16 burst {pk['bf16_tflops']} TFLOP/s",
                      "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_score,
@@ -816,7 +816,7 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
         "e2e": {"value": total_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": hq.numel() * 2 + hq8.numel() + hw.numel() * 4,
                 "d2h_bytes_per_step": ho.numel() * 2},
-        "roofline": {"bound": "hbm", "kernel": "mzb::idx::score_kernel<fp8,128> (decode indexer)", "achieved": ach,
+        "roofline": {"bound": "hbm", "kernel": "mzb::idx::score_kernel<fp8,128,1> (decode indexer)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                      "peak_note": f"{pk['_source']} HBM copy", "algorithmic_bytes_per_launch": score_bytes,
                      "ms_per_launch": ms_score, "traffic": TRAFFIC["decode"], "traffic_unit": "bytes per launch (ncu)"},
