@@ -14,8 +14,10 @@ A "step" is one pass of the hot path over one batch.  ``value`` times the device
 inputs resident in HBM (L2 flushed with a 256 MB write before every timed step);
 ``e2e`` times the public API call with pinned host inputs, host->device copies, the
 kernels and the device->host copy of the result inside the timed region.  Multi-GPU:
-one process per GPU (torchrun), each rank runs its own independent instance (weak
-scaling, no data-path collective); timing is the max over ranks of CUDA-event time.
+one process per GPU (torchrun); the indexer, prefill and decode configs split one
+workload's independent units (query chunks, token chunks, sequences) over the ranks with
+no data-path collective (strong scaling), the training config runs one instance per rank
+(weak scaling); timing is the max over ranks of CUDA-event time.
 
 ``--impl reference`` times the reference's CPU path (the numpy restatement in
 ``oracle/``; the reference itself is Python and cannot travel to the GPU host) on a
@@ -120,8 +122,7 @@ class ClockSampler:
 
 
 # DRAM bytes (read + write) of one full-size launch of each config's roofline kernel, from a
-# one-pass ncu capture of this build (dram__bytes_read.sum + dram__bytes_write.sum; the
-# command and per-kernel split are in profiles/traffic_full_size.md).
+# one-pass ncu capture of this build (dram__bytes_read.sum + dram__bytes_write.sum).
 TRAFFIC = {
     "indexer": 72764928 + 69933824,
     "prefill": 2535907584 + 2112252416,

@@ -1,6 +1,6 @@
 """Work partitioning of the hot path across the GPUs of one node (one process per GPU).
 
-Every unit of this path is independent (SURVEY §8e): decode sequences, prefill query
+Every unit of this path is independent: decode sequences, prefill query
 tokens, indexer query blocks and training batch elements need nothing from each other, so
 there is no data-path collective.  The one collective is an optional output gather, done
 with ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink on GPUs, gloo on CPU).
