@@ -44,6 +44,7 @@ constexpr int NTHREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 epilogue
 constexpr int EPI_WARP0 = 2;   // epilogue warp w reads TMEM lanes 32 * (w % 4): warps 2-5 and 6-9
                                // each cover all four lane quarters
 constexpr int KB_PARTS = 16;  // per-batch partial maxima of B_t
+constexpr int BAL_MAX = 512;  // (batch, query block) units of the tile-balanced split
 
 template <bool FP8, int DI>
 struct Cfg {
@@ -60,7 +61,7 @@ struct Cfg {
   static constexpr int KS_RAW = (BUDGET - Q_BUFS * Q_BYTES) / K_BYTES;
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
-  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + 1024;
+  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + (BAL_MAX + 1) * 4 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
 };
@@ -77,6 +78,7 @@ struct ScoreArgs {
   float scale;
   int write_tail;
   int kc, n_kc;  // key tiles per chunk, chunks per (batch, query block)
+  int bal;       // 1: each CTA takes a contiguous 1/grid share of all key tiles (few units)
   int* err;
 };
 
@@ -116,6 +118,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [units + 1] tile prefix
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -137,13 +140,35 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     tc::prefetch_tmap(&tq);
     tc::prefetch_tmap(&tk);
   }
+  const int n_tb = (a.S + a.Tq - 1) / a.Tq;
+  const int units = a.B * n_tb;  // (batch, query block) pairs
+  auto unit_tiles = [&](int b, int tb) {  // key tiles a query block sees
+    int vis = 0;
+    for (int s = tb * a.Tq; s < min((tb + 1) * a.Tq, a.S); ++s)
+      vis = max(vis, visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T));
+    return (vis + BM - 1) / BM;
+  };
+  if (a.bal && warp == 2) {  // tile prefix over units (u = b * n_tb + tb): pref[u] tiles before u
+    int run = 0;
+    for (int u0 = 0; u0 < units; u0 += 32) {
+      const int u = u0 + lane;
+      const int nt = u < units ? unit_tiles(u / n_tb, u % n_tb) : 0;
+      int incl = nt;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (u < units) pref[u + 1] = run + incl;
+      run += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) pref[0] = 0;
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
   // item = (key chunk, query block, batch); chunk-major so full chunks go first
-  const int n_tb = (a.S + a.Tq - 1) / a.Tq;
   const int items = a.B * n_tb * a.n_kc;
   struct Item {
     int tb, b, kc, k0, k1;
@@ -154,13 +179,43 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     const int rem = it % (a.B * n_tb);
     r.tb = n_tb - 1 - rem / a.B;
     r.b = rem % a.B;
-    int vis = 0;
-    for (int s = r.tb * a.Tq; s < min((r.tb + 1) * a.Tq, a.S); ++s)
-      vis = max(vis, visible_of(a.q_pos, a.q_offset, r.b, a.S, s, a.ratio, a.T));
-    const int n_kt = (vis + BM - 1) / BM;
+    const int n_kt = unit_tiles(r.b, r.tb);
     r.k0 = r.kc * a.kc;
     r.k1 = min(n_kt, r.k0 + a.kc);
     return r;
+  };
+  // Tile-balanced split (few units, e.g. decode): this CTA takes key tiles [lo, hi) of the
+  // units' tiles laid end to end, as pieces (unit, k0, k1); units' lengths differ widely, so
+  // a round-robin of fixed chunks would leave some CTAs with far more tiles than others.
+  long long lo = 0, hi = 0;
+  int u_first = 0;
+  if (a.bal) {
+    const long long total = pref[units];
+    lo = total * blockIdx.x / gridDim.x;
+    hi = total * (blockIdx.x + 1) / gridDim.x;
+    int l = 0, h = units;  // first unit whose tiles end after lo
+    while (l < h) {
+      const int mid = (l + h) >> 1;
+      if (pref[mid + 1] > lo) h = mid; else l = mid + 1;
+    }
+    u_first = l;
+  }
+  // the k-th work item of this CTA
+  auto get_item = [&](int k, Item& r) -> bool {
+    if (!a.bal) {
+      const int it = blockIdx.x + k * gridDim.x;
+      if (it >= items) return false;
+      r = item_of(it);
+      return true;
+    }
+    const int u = u_first + k;
+    if (u >= units || pref[u] >= hi) return false;
+    r.b = u / n_tb;
+    r.tb = u % n_tb;
+    r.k0 = int((lo > pref[u] ? lo : (long long)pref[u]) - pref[u]);
+    r.k1 = int((hi < pref[u + 1] ? hi : (long long)pref[u + 1]) - pref[u]);
+    r.kc = 1;  // the -inf tail of a unit is written in a separate pass in this mode
+    return true;
   };
 
   if (warp == 0) {
@@ -169,8 +224,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       int ks_i = 0, ks_ph = 0, qi = 0;
       uint32_t k_issued = 0, k_par[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint32_t q_issued = 0, q_par[2] = {0, 0};
-      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const Item m = item_of(it);
+      for (int k = 0; !*abort_flag; ++k) {
+        Item m;
+        if (!get_item(k, m)) break;
         if (m.k0 >= m.k1) continue;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_empty[qb], qpar ^ 1, a.err, 101)) { *abort_flag = 1; break; }
@@ -205,8 +261,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       constexpr uint32_t kFmt = FP8 ? 0 : 1;
       const uint32_t idesc = tc::make_idesc(BM, a.N, kFmt, kFmt);
       int ks_i = 0, ks_ph = 0, acc = 0, acc_ph = 0, qi = 0;
-      for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-        const Item m = item_of(it);
+      for (int k = 0; !*abort_flag; ++k) {
+        Item m;
+        if (!get_item(k, m)) break;
         if (m.k0 >= m.k1) continue;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_full[qb], qpar, a.err, 103)) { *abort_flag = 1; break; }
@@ -249,20 +306,23 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     float* cwp = cw + ew * CWN;
     uint32_t tcount = 0;
     int acc_ph = 0;
-    for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
-      const Item m = item_of(it);
-      const int s0 = m.tb * a.Tq;
-      if (a.write_tail && m.kc == 0) {  // keys no token of this block can see
-        int n_kt = 0;
-        for (int s = s0; s < min(s0 + a.Tq, a.S); ++s)
-          n_kt = max(n_kt, (visible_of(a.q_pos, a.q_offset, m.b, a.S, s, a.ratio, a.T) + BM - 1) / BM);
-        for (int t = 0; t < a.Tq; ++t) {
-          const int s = s0 + t;
-          if (s >= a.S) break;
-          float* rowp = a.scores + (size_t(m.b) * a.S + s) * a.T;
-          for (int j = n_kt * BM + et; j < a.T; j += NEPI_M) rowp[j] = -INFINITY;
-        }
+    auto write_tail = [&](int b, int tb) {  // keys no token of this block can see
+      const int s0 = tb * a.Tq;
+      const int n_kt = unit_tiles(b, tb);
+      for (int t = 0; t < a.Tq; ++t) {
+        const int s = s0 + t;
+        if (s >= a.S) break;
+        float* rowp = a.scores + (size_t(b) * a.S + s) * a.T;
+        for (int j = n_kt * BM + et; j < a.T; j += NEPI_M) rowp[j] = -INFINITY;
       }
+    };
+    if (a.bal && a.write_tail)
+      for (int u = blockIdx.x; u < units; u += gridDim.x) write_tail(u / n_tb, u % n_tb);
+    for (int k = 0; !*abort_flag; ++k) {
+      Item m;
+      if (!get_item(k, m)) break;
+      const int s0 = m.tb * a.Tq;
+      if (a.write_tail && m.kc == 0) write_tail(m.b, m.tb);
       if (m.k0 >= m.k1) continue;
       const int tq_n = min(a.Tq, a.S - s0);  // real tokens in this block
       const int t0 = MODE == 2 ? min(2 * th, tq_n) : 0, t1 = MODE == 2 ? min(2 * th + 2, tq_n) : tq_n;
@@ -1115,7 +1175,9 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
   if (b.n_kc < 1) b.n_kc = 1;
   const long long items = base * b.n_kc;
   MZB_REQUIRE(items < (1LL << 31), MZB_ERR_SHAPE, "indexer: too many work items");
-  const int grid = items < sms ? int(items) : sms;
+  // few units: every CTA takes an equal share of all key tiles instead of whole chunks
+  b.bal = (n_kc > 1 && base <= BAL_MAX) ? 1 : 0;
+  const int grid = b.bal ? sms : (items < sms ? int(items) : sms);
   kern<<<grid, score_nthreads(mode), C::SMEM, st>>>(tq, tk, b);
   return launch_status("indexer_scores");
 }
