@@ -107,6 +107,22 @@ __device__ __forceinline__ float e2m1_value(float q) {
   return (signbit(q) && v != 0.0f) ? -v : v;
 }
 
+// Two values onto the e2m1 grid {0, .5, 1, 1.5, 2, 3, 4, 6} with the hardware conversion
+// (round to nearest, ties to the even code -- the same choices as the thresholds above: ties
+// at 0.25/1.25/2.5/5.0 go to codes 0/2/4/6 below, at 0.75/1.75/3.5 to codes 2/4/6 above --
+// saturating at 6), then back through f16x2.  mzoo's table gives +0.0 for -0 and its
+// thresholds give 0 for NaN; both are applied explicitly.  Inputs are pre-clamped to [-6, 6].
+__device__ __forceinline__ void e2m1_value2(float q0, float q1, float& r0, float& r1) {
+  uint32_t h2;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %2, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t;\n\t}"
+      : "=r"(h2)
+      : "f"(q0), "f"(q1));
+  const __half2 hh = *reinterpret_cast<const __half2*>(&h2);
+  const float2 f = __half22float2(hh);
+  r0 = isnan(q0) ? 0.0f : __fadd_rn(f.x, 0.0f);
+  r1 = isnan(q1) ? 0.0f : __fadd_rn(f.y, 0.0f);
+}
+
 // ---------------------------------------------------------------- PTX helpers
 
 // 2^x on the SFU (ex2.approx, relative error ~2^-22; -inf -> +0).  Softmax numerators only.

@@ -40,6 +40,14 @@ struct Fp4Op {
     float q = clamp_nan(pow2() ? __fmul_rn(x, inv) : __fdiv_rn(x, s), -6.0f, 6.0f);
     return __fmul_rn(e2m1_value(q), s);
   }
+  __device__ __forceinline__ void apply2(float x0, float x1, float s, float inv, float& r0, float& r1) const {
+    const float q0 = clamp_nan(pow2() ? __fmul_rn(x0, inv) : __fdiv_rn(x0, s), -6.0f, 6.0f);
+    const float q1 = clamp_nan(pow2() ? __fmul_rn(x1, inv) : __fdiv_rn(x1, s), -6.0f, 6.0f);
+    float v0, v1;
+    e2m1_value2(q0, q1, v0, v1);
+    r0 = __fmul_rn(v0, s);
+    r1 = __fmul_rn(v1, s);
+  }
 };
 
 struct Fp8Op {
@@ -53,6 +61,10 @@ struct Fp8Op {
   __device__ __forceinline__ float apply(float x, float s, float inv) const {
     float q = clamp_nan(pow2() ? __fmul_rn(x, inv) : __fdiv_rn(x, s), -448.0f, 448.0f);
     return __fmul_rn(e4m3_round(q), s);
+  }
+  __device__ __forceinline__ void apply2(float x0, float x1, float s, float inv, float& r0, float& r1) const {
+    r0 = apply(x0, s, inv);
+    r1 = apply(x1, s, inv);
   }
 };
 
@@ -97,7 +109,12 @@ __global__ void __launch_bounds__(256) fq_vec_kernel(const void* __restrict__ x_
       uint4 out;
       T* o = reinterpret_cast<T*>(&out);
 #pragma unroll
-      for (int i = 0; i < V; ++i) o[i] = E::store(op.apply(v[i], s, inv));
+      for (int i = 0; i < V; i += 2) {
+        float r0, r1;
+        op.apply2(v[i], v[i + 1], s, inv, r0, r1);
+        o[i] = E::store(r0);
+        o[i + 1] = E::store(r1);
+      }
       reinterpret_cast<uint4*>(y)[t] = out;
     }
   }
