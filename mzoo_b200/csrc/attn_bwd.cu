@@ -58,22 +58,43 @@ struct Args {
 };
 
 // ------------------------------------------------------------------ preprocess
-__global__ void preprocess_kernel(Args a) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const long long R = (long long)a.S * a.H;
-  if (warp >= (long long)a.B * a.Rpad) return;
-  const int b = warp / a.Rpad, r = warp % a.Rpad;
+// Four lanes per packed row, each reading D / 32 16-byte vectors of O and dO (all in flight).
+template <int D>
+__global__ void __launch_bounds__(256) preprocess_kernel(Args a) {
+  constexpr int NV = D / 8 / 4;  // 16-byte vectors per lane
+  const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 2;
+  const int sub = threadIdx.x & 3;
+  const long long R = (long long)a.S * a.H, nrows = (long long)a.B * a.Rpad;
+  const bool in = row < nrows;  // lanes past the end still take part in the shuffles
+  const long long b = in ? row / a.Rpad : 0, r = in ? row % a.Rpad : 0;
   float d = 0.0f, l2 = 0.0f;
-  if (r < R) {
-    const __nv_bfloat16* op = a.o + ((long long)b * R + r) * a.D;
-    const __nv_bfloat16* gp = a.dout + ((long long)b * R + r) * a.D;
-    for (int i = lane; i < a.D; i += 32) d = fmaf(__bfloat162float(op[i]), __bfloat162float(gp[i]), d);
-    for (int o = 16; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-    l2 = a.lse[(long long)b * R + r] * LOG2E;
+  if (in && r < R) {
+    const uint4* op = reinterpret_cast<const uint4*>(a.o + (b * R + r) * D);
+    const uint4* gp = reinterpret_cast<const uint4*>(a.dout + (b * R + r) * D);
+    uint4 ov[NV], gv[NV];
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      ov[v] = __ldg(op + sub + 4 * v);
+      gv[v] = __ldg(gp + sub + 4 * v);
+    }
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov[v]);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv[v]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 of = __bfloat1622float2(o2[i]), gf = __bfloat1622float2(g2[i]);
+        d = fmaf(of.x, gf.x, d);
+        d = fmaf(of.y, gf.y, d);
+      }
+    }
+    l2 = a.lse[b * R + r] * LOG2E;
   }
-  if (lane == 0) {
-    a.delta[(long long)b * a.Rpad + r] = d;
-    a.lse2[(long long)b * a.Rpad + r] = l2;
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
+  d += __shfl_xor_sync(0xffffffffu, d, 2);
+  if (in && sub == 0) {
+    a.delta[b * a.Rpad + r] = d;
+    a.lse2[b * a.Rpad + r] = l2;
   }
 }
 
@@ -800,7 +821,7 @@ int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStre
       return r;
   }
   const long long rows = (long long)a.B * a.Rpad;
-  preprocess_kernel<<<unsigned((rows * 32 + 255) / 256), 256, 0, st>>>(a);
+  preprocess_kernel<D><<<unsigned((rows * 4 + 255) / 256), 256, 0, st>>>(a);
   if (int r = launch_status("attn_bwd_preprocess")) return r;
 
   auto kkv = dkv_kernel<D, SEP_V>;
