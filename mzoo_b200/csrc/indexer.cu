@@ -15,16 +15,19 @@
 // query rows in N (up to 256 = T_q tokens x Hi heads), so the per-token head reduction is
 // a per-thread loop over TMEM columns.  Persistent CTAs, one per SM; warp 0 issues TMA
 // loads (K tiles in a 4-stage ring, Q tiles double-buffered), warp 1 issues tcgen05.mma
-// into two TMEM accumulators, warps 2-9 run the relu * weight reduction epilogue (each
-// warpgroup drains one accumulator, i.e. every other tile) and store fp32 scores.  The key
-// loop stops at the block's causal frontier; with few (batch, query block) pairs (decode)
-// the key range is split into chunks so every SM gets work.
+// into two TMEM accumulators, the epilogue warpgroups run the relu * weight reduction and
+// store fp32 scores (modes below: one warpgroup per accumulator, or with 64 heads and
+// four-token blocks two per accumulator, two tokens each).  The key loop stops at the
+// block's causal frontier; with few (batch, query block) pairs (decode) every CTA takes an
+// equal share of all visible key tiles so every SM gets the same work.
 //
 // Kernel 2 (`topk_kernel`): one CTA per query row.  The fp32 tensor-core scores carry a
 // rounding error bounded by delta = eps * A_s * max_t B_t, with
 // A_s = sum_h |w sq| * ||q_h||_2 and B_t = |scale| sk_t ||k_t||_2 (Cauchy-Schwarz on the
-// dot products plus the fp32 reductions).  A radix select finds the approximate k-th
-// score theta; keys above theta + 2 delta are certainly selected, keys below
+// dot products plus the fp32 reductions; both factors come from `bound_kernel`).  A
+// histogram over linear bins of a sampled score range, then an exact rank (or radix
+// select) inside the cut bin, finds the approximate k-th score theta; keys above
+// theta + 2 delta are certainly selected, keys below
 // theta - 2 delta certainly not, and the few in between are re-scored EXACTLY in fp64
 // (e4m3 and bf16 products are exact in fp64, the 8-bit-code sums are exact too) and
 // ranked by (score desc, index asc).  The selected indices are written in ascending
@@ -1251,7 +1254,7 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   MZB_REQUIRE(dtype == MZB_BF16 || (sq && sk), MZB_ERR_SHAPE, "indexer: fp8 inputs need sq and sk scales");
   const int eb = dtype == MZB_E4M3 ? 1 : 2;
   MZB_REQUIRE((Di * eb) % 4 == 0, MZB_ERR_UNSUPPORTED, "indexer topk: index rows must be a multiple of 4 bytes");
-  // few rows (decode: one query per sequence) -> wide blocks, else 256 threads per row
+  // few rows (decode: one query per sequence) -> wide blocks, else 128 threads per row
   const bool wide = B * S < 2LL * num_sms();
   const size_t smem = idx::topk_smem(int(T), Hi, Di, eb, wide ? 1024 : 128);
   MZB_REQUIRE(smem <= 200 * 1024, MZB_ERR_UNSUPPORTED, "indexer topk: T=%lld needs %zu B of shared memory",
