@@ -17,6 +17,10 @@
 //               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K); gathered tiles also
 //               keep dS and P in shared memory for dM = dS^T Q + P^T dO, scattered into
 //               dmain by the compute warps with fp32 atomics.
+// Column visibility (window run, or a token's valid gathered slots) is one mask word per
+// 32 columns, built per tile.  D = 256 (K == V): the key owner keeps one Q/dO stage and a
+// merged dK + dV accumulator; the query owner uses 64-key tiles and forms the gathered-row
+// gradient transposed (dM^T, channels in TMEM lanes).
 #include "tc.cuh"
 
 namespace mzb {

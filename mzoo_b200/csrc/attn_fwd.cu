@@ -13,8 +13,11 @@
 // tcgen05 kernel, one CTA per 128-row query tile, persistent over tiles:
 //   warp 0      TMA: Q tile, window K (and V) tiles into a ring of stages
 //   warp 1      TMEM allocation + the MMA-issuing thread
-//   warps 4-7   softmax, lazy O correction, epilogue (thread = row = TMEM lane)
-//   warps 8-11  gathered-tile producers (ld.global of main_kv rows -> swizzled smem)
+//   warps 4-7   softmax, lazy O correction, epilogue (thread = row = TMEM lane); column
+//               visibility as one mask word per 32 columns per tile
+//   warps 8-11  gathered-tile producers (ld.global of main_kv rows -> swizzled smem), or,
+//               without gathered rows, the O / lse epilogue while the softmax warps start
+//               the next tile
 // S = Q K^T (M=128 rows, N=NK keys) and O += P V (N=D) accumulate in TMEM; P goes through
 // shared memory as bf16.  MMA order QK_0, QK_1, PV_0, QK_2, PV_1, ... as in sparse_mla.cu.
 #include "tc.cuh"
