@@ -652,30 +652,30 @@ __global__ void __launch_bounds__(384, 1)
           tc::tmem_wait_ld();
           tc::reg_after_wait(sv);
           tc::reg_after_wait(dv);
-          uint32_t dd[16], ds[16], pp[16];
+          // P and dS overwrite S and dP in place; only gathered tiles pack the extra copies
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            float d2[2], p2[2];
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              const int c = 2 * q + e;  // column within the chunk
-              const float p = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
-              p2[e] = p;
-              d2[e] = p * (__uint_as_float(dv[c]) - dl);
-            }
-            dd[q] = pack_bf16(d2[0], d2[1]);
-            ds[q] = pack_bf16(d2[0] * a.scale, d2[1] * a.scale);  // dK carries the softmax scale
-            pp[q] = pack_bf16(p2[0], p2[1]);
+          for (int c = 0; c < 32; ++c) {
+            const float p = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
+            sv[c] = __float_as_uint(p);
+            dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - dl));
           }
+          uint32_t dd[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) dd[q] = pack_bf16(__uint_as_float(dv[2 * q]), __uint_as_float(dv[2 * q + 1]));
           tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), dd);
-          if (!win) {  // keep scale*dS and P in smem for the gathered-row gradient
+          if (!win) {  // keep scale*dS (dK carries the softmax scale) and P in smem for the gathered-row gradient
             uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
             uint8_t* pr = dsr + C::P_BYTES;
+            auto ds2 = [&](int c) {
+              return pack_bf16(__uint_as_float(dv[c]) * a.scale, __uint_as_float(dv[c + 1]) * a.scale);
+            };
+            auto pp2 = [&](int c) { return pack_bf16(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])); };
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
               const int ch = ((c0 & 63) >> 3) + q;
-              st_shared16(dsr + ((ch ^ (r & 7)) * 16), make_uint4(ds[4 * q], ds[4 * q + 1], ds[4 * q + 2], ds[4 * q + 3]));
-              st_shared16(pr + ((ch ^ (r & 7)) * 16), make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]));
+              const int c = 8 * q;
+              st_shared16(dsr + ((ch ^ (r & 7)) * 16), make_uint4(ds2(c), ds2(c + 2), ds2(c + 4), ds2(c + 6)));
+              st_shared16(pr + ((ch ^ (r & 7)) * 16), make_uint4(pp2(c), pp2(c + 2), pp2(c + 4), pp2(c + 6)));
             }
           }
         }
