@@ -416,7 +416,12 @@ struct QCfg {
   static constexpr int TILE_BYTES = 2 * T_BYTES + STAGES * KV_STAGE + NP * P_BYTES;
   static constexpr int SMEM = TILE_BYTES + 512;
   static constexpr int C_DQ = 0, C_S = D, C_DP = D + KT, C_DM = D + 2 * KT;
+  // window-only (separate V): warps 8-11 are free, so the columns of each key tile are split
+  // over two compute warpgroups; the second half's packed dS goes to the unused dM columns
+  static constexpr bool SPLIT = SEP_V;
+  static constexpr int C_DS2 = C_DM;
   static_assert(C_DP + KT <= 512 && (SEP_V || C_DM + (WIDE ? 2 * KT : D) <= 512), "TMEM");
+  static_assert(!SPLIT || C_DS2 + KT / 4 <= 512, "TMEM");
   static_assert(SMEM <= 232448, "smem");
   static_assert(!(WIDE && SEP_V), "a separate V needs D <= 128");
 };
@@ -468,7 +473,8 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Q_NBAR; ++i) {
       uint32_t c = 1;
-      if (i == DS_FULL || i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1) c = 4;
+      if (i == DS_FULL) c = C::SPLIT ? 8 : 4;
+      if (i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1) c = 4;
       tc::mbar_init(&bars[i], c);
     }
     *abort_flag = 0;
@@ -552,9 +558,11 @@ __global__ void __launch_bounds__(384, 1)
           if (!tc::mbar_wait(&bars[DS_FULL], g & 1, a.err, 513)) { ok = false; break; }
           tc::fence_after_sync();
 #pragma unroll
-          for (int kk = 0; kk < KT / 16; ++kk)  // KT keys, 16 per step: dQ += dS K
-            tc::mma_ts(tmem + C::C_DQ, tmem + C::C_S + kk * 8, tc::sdesc_add(k_mn, kk * 2048), idesc_dq,
+          for (int kk = 0; kk < KT / 16; ++kk) {  // KT keys, 16 per step: dQ += dS K
+            const uint32_t ds_col = (C::SPLIT && kk >= KT / 32) ? C::C_DS2 + (kk - KT / 32) * 8 : C::C_S + kk * 8;
+            tc::mma_ts(tmem + C::C_DQ, tmem + ds_col, tc::sdesc_add(k_mn, kk * 2048), idesc_dq,
                        (j == 0 && kk == 0) ? 0u : 1u);
+          }
           if (!win) {
             if (!tc::mbar_wait(&bars[DM_EMPTY], (gm & 1) ^ 1, a.err, 514)) { ok = false; break; }
             const uint64_t ds_mn = tc::make_sdesc<128>(ds_base, 16384, 1024);
@@ -595,8 +603,12 @@ __global__ void __launch_bounds__(384, 1)
         if (!ok) { *abort_flag = 1; break; }
       }
     }
-  } else if (warp >= 4 && warp < 8) {
-    const int sw = warp - 4, r = sw * 32 + lane;
+  } else if ((warp >= 4 && warp < 8) || (C::SPLIT && warp >= 8)) {
+    // compute warps: rows r of the tile (TMEM lane quarter = warp % 4); with SPLIT the first
+    // warpgroup takes key columns [0, KT/2) and the second [KT/2, KT)
+    const int sw = warp & 3, r = sw * 32 + lane;
+    const bool second = C::SPLIT && warp >= 8;
+    const int cbeg = second ? KT / 2 : 0, cend = (C::SPLIT && !second) ? KT / 2 : KT;
     const float sl = a.scale_log2;
     int g = 0, ii = 0, gm = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
@@ -639,7 +651,7 @@ __global__ void __launch_bounds__(384, 1)
         if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
-        for (int c0 = 0; c0 < KT; c0 += 32) {
+        for (int c0 = cbeg; c0 < cend; c0 += 32) {
           uint32_t sv[32], dv[32];
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
@@ -662,7 +674,7 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t dd[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) dd[q] = pack_bf16(__uint_as_float(dv[2 * q]), __uint_as_float(dv[2 * q + 1]));
-          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), dd);
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_DS2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
           if (!win) {  // keep scale*dS (dK carries the softmax scale) and P in smem for the gathered-row gradient
             uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
             uint8_t* pr = dsr + C::P_BYTES;
@@ -684,7 +696,7 @@ __global__ void __launch_bounds__(384, 1)
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[DS_FULL]);
-        if (!win) {
+        if (!win && !second) {
           if (!tc::mbar_wait(&bars[DM_FULL], gm & 1, a.err, 521)) { ok = false; break; }
           tc::fence_after_sync();
           if (C::WIDE) {
@@ -737,6 +749,7 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       if (!ok) { *abort_flag = 1; break; }
+      if (second) continue;  // the first warpgroup writes dQ
       if (!tc::mbar_wait(&bars[QO_DONE], ii & 1, a.err, 522)) { *abort_flag = 1; break; }
       tc::fence_after_sync();
 #pragma unroll 1
