@@ -120,6 +120,11 @@ struct KvCfg {
   static_assert(!(MERGE && SEP_V), "a separate V needs D <= 128");
 };
 
+// Packed bf16 column of query column c (even) of P^T / dS^T within the S / dP region: each
+// half of the 128 columns is packed into the front of its own 64 columns, so the two compute
+// warpgroups never store over columns the other one has still to read.
+__device__ __forceinline__ int pt_col(int c) { return c / 2 + (c >= 64 ? 32 : 0); }
+
 enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FULL, PT_FULL, O_DONE, ACC_EMPTY,
              KV_NBAR };
 
@@ -149,7 +154,7 @@ __device__ __forceinline__ KvItem kv_item(const Args& a, int it) {
 }
 
 template <int D, bool SEP_V>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(384, 1)
     dkv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
                const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, Args a) {
   using C = KvCfg<D, SEP_V>;
@@ -166,7 +171,7 @@ __global__ void __launch_bounds__(256, 1)
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < KV_NBAR; ++i) tc::mbar_init(&bars[i], (i == PT_FULL || i == ACC_EMPTY) ? 4 : 1);
+    for (int i = 0; i < KV_NBAR; ++i) tc::mbar_init(&bars[i], i == PT_FULL ? 8 : (i == ACC_EMPTY ? 4 : 1));
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -251,8 +256,9 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // 128 query rows, 16 per step
             const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + kk * 8, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
-            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + kk * 8, tc::sdesc_add(q_mn, kk * 2048), idesc_acc,
+            const int pc = pt_col(16 * kk);
+            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + pc, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
+            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + pc, tc::sdesc_add(q_mn, kk * 2048), idesc_acc,
                        C::MERGE ? 1u : acc);
           }
           tc::mma_commit(&bars[QD_EMPTY + s]);
@@ -265,7 +271,11 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   } else if (warp >= 4) {
-    const int sw = warp - 4, row = sw * 32 + lane;  // TMEM lane = key within the tile
+    // two compute warpgroups on the same keys (TMEM lane = key within the tile, quarter =
+    // warp % 4): warps 4-7 take query columns [0, 64), warps 8-11 [64, 128)
+    const int sw = warp & 3, row = sw * 32 + lane;
+    const bool second = warp >= 8;
+    const int cbeg = second ? 64 : 0, cend = cbeg + 64;
     const float sl = a.scale_log2;
     const int tpt = 128 >> a.hshift;  // tokens per query tile
     int g = 0, ii = -1;
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(256, 1)
       const int j = m.k0 + row;
       float* part = a.dkv_part + (((long long)m.sp * a.B + m.b) * a.S + j) * 2 * D;
       if (m.nq == 0) {  // this split has no query tiles: contribute zeros
-        if (j < a.S)
+        if (j < a.S && !second)
           for (int c = 0; c < 2 * D; c += 4) *reinterpret_cast<float4*>(part + c) = make_float4(0.f, 0.f, 0.f, 0.f);
         continue;
       }
@@ -296,7 +306,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         const bool warp_full = __all_sync(0xffffffffu, clo <= 0 && chi >= 127);
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+        for (int c0 = cbeg; c0 < cend; c0 += 32) {
           uint32_t sv[32], dv[32];
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
           tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
@@ -326,8 +336,8 @@ __global__ void __launch_bounds__(256, 1)
             dd[2 * q4] = pack_bf16(d2[0], d2[1]);
             dd[2 * q4 + 1] = pack_bf16(d2[2], d2[3]);
           }
-          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + c0 / 2), pp);
-          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_DP + c0 / 2), dd);
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_S + pt_col(c0)), pp);
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_DP + pt_col(c0)), dd);
         }
         tc::tmem_wait_st();
         tc::fence_before_sync();
@@ -335,6 +345,7 @@ __global__ void __launch_bounds__(256, 1)
         if (lane == 0) tc::mbar_arrive(&bars[PT_FULL]);
       }
       if (!ok) { *abort_flag = 1; break; }
+      if (second) continue;  // the first warpgroup writes the partial dK / dV
       if (!tc::mbar_wait(&bars[O_DONE], ii & 1, a.err, 421)) { *abort_flag = 1; break; }
       tc::fence_after_sync();
 #pragma unroll 1
@@ -845,7 +856,7 @@ int launch(const void* q, const void* kv, const void* v, const Args& a, cudaStre
   if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, KvCfg<D, SEP_V>::SMEM) != cudaSuccess)
     return launch_status("attn_bwd_dkv(smem attr)");
   const int kv_items = a.B * ((a.S + 127) / 128) * a.splits;
-  kkv<<<kv_items < num_sms() ? kv_items : num_sms(), 256, KvCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
+  kkv<<<kv_items < num_sms() ? kv_items : num_sms(), 384, KvCfg<D, SEP_V>::SMEM, st>>>(tq, tdo, tk, tv, a);
   if (int r = launch_status("attn_bwd_dkv")) return r;
   {
     const long long n = (long long)a.B * a.S * a.D;
