@@ -277,7 +277,6 @@ __global__ void __launch_bounds__(384, 1)
     const bool second = warp >= 8;
     const int cbeg = second ? 64 : 0, cend = cbeg + 64;
     const float sl = a.scale_log2;
-    const int tpt = 128 >> a.hshift;  // tokens per query tile
     int g = 0, ii = -1;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
       const KvItem m = kv_item(a, it);

@@ -25,7 +25,6 @@
 namespace mzb {
 namespace attn {
 
-constexpr int NTHREADS = 384;
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
@@ -50,6 +49,14 @@ struct Cfg {
   static constexpr int MISC = 512 + 4 * 128 * 4;  // barriers; 2 x (row max, row sum) handoff
   static constexpr int SMEM = TILE_BYTES + MISC;
   static constexpr int S_COL0 = D;  // O in columns [0, D), S buffers after it
+  // separate V (window only) at D <= 128: a second softmax warpgroup (warps 12-15) takes the
+  // upper half of every key tile's columns; the two halves exchange their row maxima, and
+  // hand the second half's row sum to the epilogue, through TMEM columns [X_COL, X_COL + 6)
+  static constexpr bool SPLIT = SEP_V && D <= 128;
+  static constexpr int NT = SPLIT ? 512 : 384;
+  static constexpr int NQ = SPLIT ? NK / 64 : NK / 32;  // 32-column chunks per softmax warp
+  static constexpr int X_COL = D + 2 * NK;
+  static_assert(!SPLIT || X_COL + 6 <= 512, "TMEM budget");
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(D + 2 * NK <= 512, "TMEM budget");
 };
@@ -68,7 +75,7 @@ struct Args {
 // O_FINAL: commit after an item's last PV, waited on by the epilogue with the item parity
 // (two PVs can still be in flight there, so O_DONE's parity would alias an older phase).
 enum Bar { Q_FULL = 0, Q_EMPTY, O_DONE, O_EMPTY, S_FULL, S_FULL1, S_EMPTY, S_EMPTY1, P_FULL, P_FULL1, KV_FULL_W,
-           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, EPI_FULL, NBAR };
+           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, EPI_FULL, MX, NBAR = MX + 4 };
 
 __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -102,7 +109,7 @@ __device__ __forceinline__ Item make_item(const Args& a, int it, int n_qt) {
 }
 
 template <int D, bool SEP_V>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, Args a) {
   using C = Cfg<D, SEP_V>;
@@ -125,7 +132,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NBAR; ++i) {
       uint32_t c = 1;
-      if (i == O_EMPTY || i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1 || i == EPI_FULL) c = 4;
+      if (i == O_EMPTY) c = 4;
+      if (i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1 || i == EPI_FULL) c = C::SPLIT ? 8 : 4;
+      if (i >= MX) c = 2;  // the two softmax warps of one TMEM lane quarter
       if (i >= KV_FULL_G && i < KV_EMPTY) c = 4;
       tc::mbar_init(&bars[i], c);
     }
@@ -231,9 +240,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc::mma_commit(&bars[O_FINAL]);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if ((warp >= 4 && warp < 8) || (C::SPLIT && warp >= 12)) {
     // ---------------------------------------------------------------- softmax / epilogue
-    const int sw = warp - 4, r = sw * 32 + lane;
+    const int sw = warp & 3, r = sw * 32 + lane;
+    const bool wg2 = C::SPLIT && warp >= 12;  // second softmax warpgroup: upper column half
+    const int q0 = wg2 ? C::NQ : 0;           // first 32-column chunk of this warp
+    const int oc0 = wg2 ? D / 2 : 0, oc1 = C::SPLIT ? oc0 + D / 2 : D;  // O columns it rescales
     const float sl = a.scale_log2;
     int g = 0, ii = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
@@ -280,15 +292,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         // whole tile takes the mask-free loops
         const bool full = row_ok && win && wlo <= 0 && whi >= NK - 1;
         const bool warp_full = __all_sync(0xffffffffu, full);
-        uint32_t mw[NK / 32];
+        uint32_t mw[C::NQ];
 #pragma unroll
-        for (int q = 0; q < NK / 32; ++q) {
+        for (int q = 0; q < C::NQ; ++q) {
+          const int qa = q0 + q;
           uint32_t w = 0u;
           if (row_ok) {
             if (win) {
-              const int lo = max(wlo - 32 * q, 0), hi = min(whi - 32 * q, 31);
+              const int lo = max(wlo - 32 * qa, 0), hi = min(whi - 32 * qa, 31);
               w = lo > hi ? 0u : ((0xFFFFFFFFu >> (31 - (hi - lo))) << lo);
-            } else if (tr == gtok) {
+            } else if (!C::SPLIT && tr == gtok) {  // (no gathered tiles with a separate V)
               w = gm[q];
             }
           }
@@ -296,29 +309,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         // the whole S row behind one TMEM wait; the S buffer is released as soon as it is in
         // registers, so the next QK^T into it can start while this tile is exponentiated
-        uint32_t sv[NK / 32][32];
+        uint32_t sv[C::NQ][32];
 #pragma unroll
-        for (int q = 0; q < NK / 32; ++q) tc::tmem_ld32(sbase + 32 * q, sv[q]);
+        for (int q = 0; q < C::NQ; ++q) tc::tmem_ld32(sbase + 32 * (q0 + q), sv[q]);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < NK / 32; ++q) tc::reg_after_wait(sv[q]);
+        for (int q = 0; q < C::NQ; ++q) tc::reg_after_wait(sv[q]);
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[S_EMPTY + sb]);
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
         if (warp_full) {
 #pragma unroll
-          for (int q = 0; q < NK / 32; ++q)
+          for (int q = 0; q < C::NQ; ++q)
 #pragma unroll
             for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], __uint_as_float(sv[q][i]));
         } else {
 #pragma unroll
-          for (int q = 0; q < NK / 32; ++q)
+          for (int q = 0; q < C::NQ; ++q)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
               mx[i & 3] = fmaxf(mx[i & 3], (mw[q] >> i) & 1u ? __uint_as_float(sv[q][i]) : -INFINITY);
         }
-        const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        if (C::SPLIT) {
+          // the pair's two partial maxima (double-buffered by tile parity) -> the same max in both
+          const uint32_t xa = tc::taddr(tmem, sw * 32, C::X_COL + (g & 1) * 2);
+          tc::tmem_st1(xa + (wg2 ? 1 : 0), __float_as_uint(mt));
+          tc::tmem_wait_st();
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bars[MX + sw]);
+          if (!tc::mbar_wait(&bars[MX + sw], g & 1, a.err, 324)) { ok = false; break; }
+          tc::fence_after_sync();
+          uint32_t other = tc::tmem_ld1(xa + (wg2 ? 0 : 1));
+          tc::tmem_wait_ld();
+          tc::reg_after_wait1(other);
+          mt = fmaxf(mt, __uint_as_float(other));
+        }
         const bool need = mt * sl > mrow * sl + 8.0f;
         const float m_new = need ? mt : mrow;
         const float alpha = fast_exp2((mrow - m_new) * sl);
@@ -326,8 +354,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
         uint8_t* prow = ps + sb * C::P_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int q = 0; q < NK / 32; ++q) {
-          const int c0 = 32 * q;
+        for (int q = 0; q < C::NQ; ++q) {
+          const int c0 = 32 * (q0 + q);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
@@ -355,7 +383,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 321)) { ok = false; break; }
           tc::fence_after_sync();
 #pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 32) {
+          for (int c0 = oc0; c0 < oc1; c0 += 32) {
             uint32_t ov[32];
             tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
             tc::tmem_wait_ld();
@@ -374,8 +402,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!ok) { *abort_flag = 1; break; }
       if (epi_warps) {
         float* st = stats + (ii & 1) * 256;
-        st[r] = __fmul_rn(mrow, sl);
-        st[128 + r] = lsum;
+        if (wg2) {  // the upper half's row sum goes through TMEM (item parity)
+          tc::tmem_st1(tc::taddr(tmem, sw * 32, C::X_COL + 4 + (ii & 1)), __float_as_uint(lsum));
+          tc::tmem_wait_st();
+          tc::fence_before_sync();
+        } else {
+          st[r] = __fmul_rn(mrow, sl);
+          st[128 + r] = lsum;
+        }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[EPI_FULL]);
         continue;
@@ -428,7 +462,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tc::fence_after_sync();
       const float* st = stats + (ii & 1) * 256;
       const float msl = st[r];
-      const float lsum = row_sum_with_sink(st[128 + r], msl, a.sinks, h);
+      float lraw = st[128 + r];
+      if (C::SPLIT) {  // add the upper column half's row sum (fixed order)
+        uint32_t l2 = tc::tmem_ld1(tc::taddr(tmem, sw * 32, C::X_COL + 4 + (ii & 1)));
+        tc::tmem_wait_ld();
+        tc::reg_after_wait1(l2);
+        lraw = __fadd_rn(lraw, __uint_as_float(l2));
+      }
+      const float lsum = row_sum_with_sink(lraw, msl, a.sinks, h);
       const float inv = 1.0f / lsum;
       const long long grow = (long long)m.qt * 128 + r;  // packed row within the batch
       __nv_bfloat16* orow = a.o + ((long long)m.b * a.S * a.H + grow) * D;
@@ -525,7 +566,7 @@ int launch(const void* q, const void* k, const void* v, const Args& a, cudaStrea
   const int n_qt = (a.S + 128 / a.H - 1) / (128 / a.H);
   const int items = a.B * n_qt;
   const int grid = items < num_sms() ? items : num_sms();
-  kern<<<grid, NTHREADS, C::SMEM, st>>>(tq, tk, tv, a);
+  kern<<<grid, C::NT, C::SMEM, st>>>(tq, tk, tv, a);
   return launch_status("attn_fwd");
 }
 

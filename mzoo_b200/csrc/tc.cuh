@@ -242,6 +242,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// One 32-bit value per lane of the warp's TMEM lane quarter (a per-row scalar).
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t tmem_ld1(uint32_t taddr) {
+  uint32_t v;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(v) : "r"(taddr) : "memory");
+  return v;
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Registers written by an asynchronous tcgen05.ld are defined only after tcgen05.wait::ld;
 // passing them through empty volatile asm placed after the wait keeps every use below it.
@@ -250,6 +259,7 @@ __device__ __forceinline__ void reg_after_wait(uint32_t (&r)[N]) {
 #pragma unroll
   for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
+__device__ __forceinline__ void reg_after_wait1(uint32_t& r) { asm volatile("" : "+r"(r)); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMEM address: lane in bits [31:16], column in bits [15:0].
