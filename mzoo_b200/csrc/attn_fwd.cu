@@ -18,8 +18,9 @@
 //   warps 8-11  gathered-tile producers (ld.global of main_kv rows -> swizzled smem), or,
 //               without gathered rows, the O / lse epilogue while the softmax warps start
 //               the next tile
-// S = Q K^T (M=128 rows, N=NK keys) and O += P V (N=D) accumulate in TMEM; P goes through
-// shared memory as bf16.  MMA order QK_0, QK_1, PV_0, QK_2, PV_1, ... as in sparse_mla.cu.
+// S = Q K^T (M=128 rows, N=NK keys) and O += P V (N=D) accumulate in TMEM; P (bf16) is
+// written back into its S buffer and read from there as the A operand of the PV MMA, so
+// shared memory carries only Q, K and V.  MMA order QK_0, QK_1, PV_0, QK_2, PV_1, ...
 #include "tc.cuh"
 
 namespace mzb {
@@ -43,9 +44,8 @@ struct Cfg {
   static constexpr int Q_BYTES = 128 * D * 2;
   static constexpr int K_BYTES = NK * D * 2;
   static constexpr int STAGE_BYTES = K_BYTES * (SEP_V ? 2 : 1);
-  static constexpr int P_BYTES = 128 * NK * 2;
-  static constexpr int STAGES = SEP_V ? 2 : 3;
-  static constexpr int TILE_BYTES = Q_BYTES + STAGES * STAGE_BYTES + 2 * P_BYTES;
+  static constexpr int STAGES = SEP_V ? (D == 256 ? 2 : 3) : 4;  // K (+ V) ring depth
+  static constexpr int TILE_BYTES = Q_BYTES + STAGES * STAGE_BYTES;
   static constexpr int MISC = 512 + 4 * 128 * 4;  // barriers; 2 x (row max, row sum) handoff
   static constexpr int SMEM = TILE_BYTES + MISC;
   static constexpr int S_COL0 = D;  // O in columns [0, D), S buffers after it
@@ -57,6 +57,10 @@ struct Cfg {
   static constexpr int NQ = SPLIT ? NK / 64 : NK / 32;  // 32-column chunks per softmax warp
   static constexpr int X_COL = D + 2 * NK;
   static_assert(!SPLIT || X_COL + 6 <= 512, "TMEM budget");
+  // P (bf16) goes back into its own S buffer: the 32-bit column of keys (c, c + 1) is
+  // pt_col(c); each column half [0, NK/2), [NK/2, NK) packs into the front of its own
+  // columns, so the two softmax warpgroups never store over S columns the other still reads
+  static __device__ __forceinline__ int pt_col(int c) { return c / 2 + (c >= NK / 2 ? NK / 4 : 0); }
   static_assert(SMEM <= 232448, "shared memory budget");
   static_assert(D + 2 * NK <= 512, "TMEM budget");
 };
@@ -117,7 +121,6 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* qs = smem;
   uint8_t* kvs = qs + C::Q_BYTES;
-  uint8_t* ps = kvs + C::STAGES * C::STAGE_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TILE_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::TILE_BYTES + 8 * NBAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::TILE_BYTES + 8 * NBAR + 4);
@@ -188,7 +191,7 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = tc::make_idesc(128, NK, 1, 1);
       const uint32_t idesc_pv = tc::make_idesc(128, D, 1, 1, false, true);
-      const uint32_t q_base = smem_u32(qs), kv_base = smem_u32(kvs), p_base = smem_u32(ps);
+      const uint32_t q_base = smem_u32(qs), kv_base = smem_u32(kvs);
       // descriptors built once per tile/buffer; unrolled loops add constant offsets (one
       // thread issues every MMA, so per-MMA descriptor arithmetic would throttle issue)
       const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024);
@@ -200,14 +203,11 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
         if (!tc::mbar_wait(&bars[P_FULL + pb], (gg >> 1) & 1, a.err, 312)) return false;
         tc::fence_after_sync();
         const uint32_t vb = kv_base + st * C::STAGE_BYTES + (SEP_V ? C::K_BYTES : 0);
-        const uint64_t pd = tc::make_sdesc<128>(p_base + pb * C::P_BYTES, 16, 1024);
         const uint64_t vd = tc::make_sdesc<128>(vb, NK * 128, 1024);
 #pragma unroll
-        for (int jj = 0; jj < NK / 16; ++jj) {
-          const int cb = jj >> 2, off = (jj & 3) * 32;
-          tc::mma_ss<0>(tmem, tc::sdesc_add(pd, cb * 128 * 128 + off), tc::sdesc_add(vd, jj * 16 * 128), idesc_pv,
-                        (first && jj == 0) ? 0u : 1u);
-        }
+        for (int jj = 0; jj < NK / 16; ++jj)  // O += P V, P (A operand) from the S buffer in TMEM
+          tc::mma_ts(tmem, tmem + C::S_COL0 + pb * NK + C::pt_col(16 * jj), tc::sdesc_add(vd, jj * 16 * 128),
+                     idesc_pv, (first && jj == 0) ? 0u : 1u);
         tc::mma_commit(&bars[KV_EMPTY + st]);
         tc::mma_commit(&bars[O_DONE]);
         return true;
@@ -307,8 +307,9 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
           }
           mw[q] = w;
         }
-        // the whole S row behind one TMEM wait; the S buffer is released as soon as it is in
-        // registers, so the next QK^T into it can start while this tile is exponentiated
+        // the whole S row (this warp's columns) behind one TMEM wait; P overwrites it in place
+        // below, and the next QK^T into this buffer is issued only after this tile's PV, which
+        // the in-order tensor pipe finishes first
         uint32_t sv[C::NQ][32];
 #pragma unroll
         for (int q = 0; q < C::NQ; ++q) tc::tmem_ld32(sbase + 32 * (q0 + q), sv[q]);
@@ -352,7 +353,6 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
         const float alpha = fast_exp2((mrow - m_new) * sl);
         const float ms = m_new * sl;
         float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint8_t* prow = ps + sb * C::P_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
         for (int q = 0; q < C::NQ; ++q) {
           const int c0 = 32 * (q0 + q);
@@ -368,14 +368,7 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
             ps4[i & 3] += p0 + p1;
             pk[i] = pack_bf16(p0, p1);
           }
-          // row r of column block c0/64: 4 chunks of 16 B (keys c0..c0+31 -> chunks (c0%64)/8 ..)
-          uint8_t* blk = prow + (c0 >> 6) * 128 * 128;
-#pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            const int ch = ((c0 & 63) >> 3) + q4;
-            st_shared16(blk + ((ch ^ (r & 7)) * 16),
-                        make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]));
-          }
+          tc::tmem_st16(sbase + C::pt_col(c0), pk);  // S of these keys is already in registers
         }
         const float psum = (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
         lsum = lsum * alpha + psum;
@@ -394,7 +387,7 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
           tc::tmem_wait_st();
         }
         mrow = m_new;
-        tc::fence_async_smem();
+        tc::tmem_wait_st();
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&bars[P_FULL + sb]);
