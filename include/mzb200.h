@@ -187,6 +187,27 @@ MZB_API int mzb_sparse_mla_fwd_noalloc(const void* q, const void* kv_raw, const 
                                        int64_t cmp_len, int raw_ptw, int cmp_ptw, float softmax_scale, int* err,
                                        void* stream);
 
+/* mzb_candidate_blocks -- replaces `select_candidate_blocks`
+ *   (src/mzoo/archs/dsv4/modeling_deepseek_v41.py:427-454, identical in
+ *   archs/owlet1/indexer.py:14-41), level one of the two-level indexer top-k.  logits fp32
+ *   [rows, T] with unreachable positions at -inf; compress_lens int32 [rows] (the query's
+ *   visible compressed length).  Block score = max of block_size consecutive logits; the block
+ *   (compress_len - 1) / block_size is pinned in; the top topk_blocks blocks with a score
+ *   above -inf are kept (ties to the lower block index).  blocks int32 [rows, topk_blocks]:
+ *   kept block indices ascending, -1 padded; mask uint8 [rows, T] (may be NULL): 1 where the
+ *   position's block is kept -- the reference's bool mask.  At most 16384 blocks per row.
+ * mzb_candidate_topk -- level two (modeling_deepseek_v41.py:566-578: scores outside the
+ *   candidates set to -inf, top-k, -inf picks dropped).  scores fp32 [rows, T]; candidates
+ *   as a block list int32 [rows, nblk] of block_size-position blocks (-1 = none; at most
+ *   16384 blocks per row) or as a uint8 mask [rows, T] -- exactly one of the two.  out int32
+ *   [rows, topk]: the candidate positions with the topk largest scores above -inf (ties to
+ *   the lower position), ascending, -1 padded.  NaN scores count as -inf in both calls.
+ */
+MZB_API int mzb_candidate_blocks(const float* logits, const int32_t* compress_lens, int32_t* blocks, uint8_t* mask,
+                                 int64_t rows, int64_t T, int block_size, int topk_blocks, void* stream);
+MZB_API int mzb_candidate_topk(const float* scores, const int32_t* blocks, const uint8_t* mask, int64_t rows,
+                               int64_t T, int block_size, int nblk, int topk, int32_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -49,6 +49,8 @@ SIGNATURES = {
     "mzb_sparse_mla_splits": [_I64],
     "mzb_sparse_mla_fwd_noalloc": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I64, _I64,
                                    _I32, _I32, _F32, _P, _P],
+    "mzb_candidate_blocks": [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _P],
+    "mzb_candidate_topk": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

@@ -1,0 +1,305 @@
+// Two-level (hierarchical) indexer selection: level-one candidate blocks and the level-two
+// top-k restricted to them.
+//
+// Reference: src/mzoo/archs/dsv4/modeling_deepseek_v41.py:427-454 `select_candidate_blocks`
+// (identical in src/mzoo/archs/owlet1/indexer.py:14-41) and its use in
+// `DeepseekV41Indexer.forward` :558-578:
+//   level one   block score = amax of `block_size` consecutive logits (the row padded with
+//               -inf to a multiple of block_size); the block holding the newest visible
+//               position, (compress_len - 1) // block_size, is pinned to +inf; keep the
+//               top `topk_blocks` blocks whose score is > -inf (fewer reachable blocks
+//               than topk_blocks is normal); the mask repeats each block's flag over its
+//               positions, truncated to T.
+//   level two   a later index source sets its scores outside the candidates to -inf and
+//               keeps its top `topk` positions, dropping picks whose score is -inf.
+// Ties: torch.topk leaves their order unspecified; here equal keys go to the lower index
+// (block index at level one, position at level two).  NaN scores count as -inf.
+//
+// One CTA of 1024 threads per query row.  Values become order-preserving uint32 keys (0 =
+// not selectable); a 4-pass radix select over 8-bit digits (shared-memory histograms, one
+// warp scanning the 256 bins) finds the K-th largest key, and one ordered pass keeps the
+// keys above it plus the lowest-index ties, writing ascending indices (-1 padded).  Level
+// one holds the row's block keys in shared memory (up to NB_MAX blocks); level two reads
+// the score row from global memory in every pass (HBM / L2 bound, no GEMM).
+#include "common.cuh"
+
+namespace mzb {
+namespace cand {
+
+constexpr int NT = 1024;
+constexpr int NW = NT / 32;
+constexpr int NB_MAX = 16384;  // blocks per row (level-one keys, level-two bitmap)
+
+// order-preserving float -> uint32 (larger value, larger key); -inf and NaN -> 0; -0 and +0
+// get the same key (they compare equal, so they are a tie)
+__device__ __forceinline__ uint32_t fkey(float x) {
+  if (!(x > -INFINITY)) return 0u;
+  uint32_t u = __float_as_uint(x);
+  if (u == 0x80000000u) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+constexpr uint32_t KEY_POS_INF = 0xFF800000u;  // fkey(+inf)
+
+struct Smem {
+  int hist[256];
+  int red[NW + 2];
+  int wsum[NW];
+  uint32_t bits[NB_MAX / 32];  // level one: kept blocks; level two: candidate blocks
+};
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ int block_sum(int v, Smem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_sum(v);
+  if (lane == 0) sm.red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    int t = lane < NW ? sm.red[lane] : 0;
+    t = warp_sum(t);
+    if (lane == 0) sm.red[NW] = t;
+  }
+  __syncthreads();
+  const int r = sm.red[NW];
+  __syncthreads();
+  return r;
+}
+
+// Exclusive prefix count of a per-thread flag over the CTA in thread order; returns the total.
+__device__ int block_scan(bool f, int& prefix, Smem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t b = __ballot_sync(0xffffffffu, f);
+  if (lane == 0) sm.wsum[warp] = __popc(b);
+  __syncthreads();
+  if (warp == 0) {
+    const int c = lane < NW ? sm.wsum[lane] : 0;
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    if (lane < NW) sm.wsum[lane] = inc - c;
+    if (lane == 31) sm.red[NW + 1] = inc;
+  }
+  __syncthreads();
+  prefix = sm.wsum[warp] + __popc(b & ((1u << lane) - 1u));
+  const int total = sm.red[NW + 1];
+  __syncthreads();
+  return total;
+}
+
+struct Sel {
+  uint32_t kth;  // keep keys > kth ...
+  int ties;      // ... and the first `ties` keys == kth in index order
+  bool all;      // every selectable key fits: keep all keys != 0
+};
+
+// K-th largest non-zero key of src.key(0..n) (K >= 1).
+template <class Src>
+__device__ Sel radix_select(const Src& src, int n, int K, Smem& sm) {
+  int cnt = 0;
+  for (int i = threadIdx.x; i < n; i += NT) cnt += src.key(i) != 0u;
+  cnt = block_sum(cnt, sm);
+  if (cnt <= K) return Sel{0u, 0, true};
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t prefix = 0u, pmask = 0u;
+  int k = K;
+#pragma unroll 1
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    if (threadIdx.x < 256) sm.hist[threadIdx.x] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += NT) {
+      const uint32_t key = src.key(i);
+      if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {  // lane l owns bins 255 - 8l down to 248 - 8l
+      int c[8], s = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = sm.hist[255 - (lane * 8 + j)];
+        s += c[j];
+      }
+      int inc = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      const int exc = inc - s;
+      if (exc < k && k <= inc) {  // exactly one lane: the bin holding the k-th key
+        int acc = exc, bin = -1, above = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (bin < 0 && acc + c[j] >= k) {
+            bin = 255 - (lane * 8 + j);
+            above = acc;
+          }
+          acc += c[j];
+        }
+        sm.red[0] = bin;
+        sm.red[1] = above;
+      }
+    }
+    __syncthreads();
+    prefix |= uint32_t(sm.red[0]) << shift;
+    pmask |= 0xFFu << shift;
+    k -= sm.red[1];
+    __syncthreads();
+  }
+  return Sel{prefix, k, false};
+}
+
+// Ordered pass: emit(rank, i) for every kept i, ranks ascending with i; returns the count.
+template <class Src, class Emit>
+__device__ int select_ordered(const Src& src, int n, const Sel& sel, Smem& sm, Emit emit) {
+  int kept = 0, ties_before = 0;
+  for (int t0 = 0; t0 < n; t0 += NT) {
+    const int i = t0 + threadIdx.x;
+    const uint32_t key = i < n ? src.key(i) : 0u;
+    const bool eq = !sel.all && key != 0u && key == sel.kth;
+    int er = 0;
+    const int et = sel.all ? 0 : block_scan(eq, er, sm);
+    const bool keep = key != 0u && (sel.all || key > sel.kth || (eq && ties_before + er < sel.ties));
+    int kr;
+    const int kt = block_scan(keep, kr, sm);
+    if (keep) emit(kept + kr, i);
+    kept += kt;
+    ties_before += et;
+  }
+  return kept;
+}
+
+// ------------------------------------------------------------------ level one
+struct BlockKeys {  // keys of the row's blocks, in shared memory
+  const uint32_t* k;
+  __device__ __forceinline__ uint32_t key(int i) const { return k[i]; }
+};
+
+__global__ void __launch_bounds__(NT) blocks_kernel(const float* __restrict__ logits, const int32_t* __restrict__ clens,
+                                                    int32_t* __restrict__ blocks, uint8_t* __restrict__ mask, int T,
+                                                    int bs, int nb, int topk_blocks) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ Smem sm;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(dsm);
+  const long long row = blockIdx.x;
+  const float* lrow = logits + row * T;
+  const int clen = clens[row];
+  const int last = clen >= 1 ? (clen - 1) / bs : -1;  // floor((clen - 1) / bs)
+  for (int b = threadIdx.x; b < nb; b += NT) {
+    const int t0 = b * bs, t1 = min(T, t0 + bs);
+    float m = -INFINITY;
+    for (int t = t0; t < t1; ++t) m = fmaxf(m, __ldg(lrow + t));  // fmaxf skips NaN
+    keys[b] = b == last ? KEY_POS_INF : fkey(m);
+  }
+  for (int w = threadIdx.x; w < (nb + 31) / 32; w += NT) sm.bits[w] = 0u;
+  __syncthreads();
+  const BlockKeys src{keys};
+  const Sel sel = radix_select(src, nb, topk_blocks, sm);
+  int32_t* brow = blocks + row * topk_blocks;
+  const int kept = select_ordered(src, nb, sel, sm, [&](int r, int i) {
+    brow[r] = i;
+    atomicOr(&sm.bits[i >> 5], 1u << (i & 31));
+  });
+  for (int r = kept + threadIdx.x; r < topk_blocks; r += NT) brow[r] = -1;
+  if (mask) {
+    __syncthreads();
+    uint8_t* mrow = mask + row * T;
+    for (int t = threadIdx.x; t < T; t += NT) {
+      const int b = t / bs;
+      mrow[t] = uint8_t((sm.bits[b >> 5] >> (b & 31)) & 1u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ level two
+struct MaskedScores {  // score of position i if it is a candidate, else not selectable
+  const float* s;
+  const uint8_t* m;       // bool mask row, or null
+  const uint32_t* bits;   // candidate-block bitmap (when m is null)
+  int bs;
+  __device__ __forceinline__ uint32_t key(int i) const {
+    bool c;
+    if (m) {
+      c = m[i] != 0;
+    } else {
+      const int b = i / bs;
+      c = (bits[b >> 5] >> (b & 31)) & 1u;
+    }
+    return c ? fkey(__ldg(s + i)) : 0u;
+  }
+};
+
+__global__ void __launch_bounds__(NT) topk_kernel(const float* __restrict__ scores, const int32_t* __restrict__ blocks,
+                                                  const uint8_t* __restrict__ mask, int32_t* __restrict__ out, int T,
+                                                  int bs, int nblk, int topk) {
+  __shared__ Smem sm;
+  const long long row = blockIdx.x;
+  if (!mask) {
+    const int nb = (T + bs - 1) / bs;
+    for (int w = threadIdx.x; w < (nb + 31) / 32; w += NT) sm.bits[w] = 0u;
+    __syncthreads();
+    const int32_t* brow = blocks + row * nblk;
+    for (int j = threadIdx.x; j < nblk; j += NT) {
+      const int b = brow[j];
+      if (b >= 0 && b < nb) atomicOr(&sm.bits[b >> 5], 1u << (b & 31));
+    }
+    __syncthreads();
+  }
+  const MaskedScores src{scores + row * T, mask ? mask + row * T : nullptr, sm.bits, bs};
+  const Sel sel = radix_select(src, T, topk, sm);
+  int32_t* orow = out + row * topk;
+  const int kept = select_ordered(src, T, sel, sm, [&](int r, int i) { orow[r] = i; });
+  for (int r = kept + threadIdx.x; r < topk; r += NT) orow[r] = -1;
+}
+
+}  // namespace cand
+}  // namespace mzb
+
+using namespace mzb;
+
+extern "C" int mzb_candidate_blocks(const float* logits, const int32_t* compress_lens, int32_t* blocks, uint8_t* mask,
+                                    int64_t rows, int64_t T, int block_size, int topk_blocks, void* stream) {
+  MZB_REQUIRE(rows >= 0 && T >= 0 && rows < (int64_t(1) << 31), MZB_ERR_SHAPE,
+              "candidate_blocks: bad sizes rows=%lld T=%lld", (long long)rows, (long long)T);
+  MZB_REQUIRE(block_size >= 1 && topk_blocks >= 1, MZB_ERR_SHAPE,
+              "candidate_blocks: block_size=%d and topk_blocks=%d must be >= 1", block_size, topk_blocks);
+  const int64_t nb = (T + block_size - 1) / block_size;
+  MZB_REQUIRE(nb <= cand::NB_MAX, MZB_ERR_UNSUPPORTED,
+              "candidate_blocks: %lld blocks per row exceed the %d this kernel holds on chip", (long long)nb,
+              cand::NB_MAX);
+  MZB_REQUIRE(rows == 0 || (logits && compress_lens && blocks), MZB_ERR_SHAPE,
+              "candidate_blocks: logits, compress_lens and blocks are required");
+  if (rows == 0) return MZB_OK;
+  const size_t dyn = size_t(nb > 0 ? nb : 1) * 4;
+  if (cudaFuncSetAttribute(cand::blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)) != cudaSuccess)
+    return launch_status("candidate_blocks(smem attr)");
+  cand::blocks_kernel<<<unsigned(rows), cand::NT, dyn, static_cast<cudaStream_t>(stream)>>>(
+      logits, compress_lens, blocks, mask, int(T), block_size, int(nb), topk_blocks);
+  return launch_status("candidate_blocks");
+}
+
+extern "C" int mzb_candidate_topk(const float* scores, const int32_t* blocks, const uint8_t* mask, int64_t rows,
+                                  int64_t T, int block_size, int nblk, int topk, int32_t* out, void* stream) {
+  MZB_REQUIRE(rows >= 0 && T >= 0 && rows < (int64_t(1) << 31) && T < (int64_t(1) << 31), MZB_ERR_SHAPE,
+              "candidate_topk: bad sizes rows=%lld T=%lld", (long long)rows, (long long)T);
+  MZB_REQUIRE(topk >= 1, MZB_ERR_SHAPE, "candidate_topk: topk=%d must be >= 1", topk);
+  MZB_REQUIRE((blocks == nullptr) != (mask == nullptr), MZB_ERR_SHAPE,
+              "candidate_topk: pass exactly one of a block list and a bool mask");
+  if (blocks) {
+    MZB_REQUIRE(block_size >= 1 && nblk >= 1, MZB_ERR_SHAPE, "candidate_topk: block_size=%d nblk=%d", block_size,
+                nblk);
+    MZB_REQUIRE((T + block_size - 1) / block_size <= cand::NB_MAX, MZB_ERR_UNSUPPORTED,
+                "candidate_topk: more than %d blocks per row", cand::NB_MAX);
+  }
+  MZB_REQUIRE(rows == 0 || (scores && out), MZB_ERR_SHAPE, "candidate_topk: scores and out are required");
+  if (rows == 0) return MZB_OK;
+  cand::topk_kernel<<<unsigned(rows), cand::NT, 0, static_cast<cudaStream_t>(stream)>>>(
+      scores, blocks, mask, out, int(T), blocks ? block_size : 1, blocks ? nblk : 0, topk);
+  return launch_status("candidate_topk");
+}

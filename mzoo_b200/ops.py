@@ -227,3 +227,44 @@ def sparse_mla_fwd(q: torch.Tensor, kv_raw: torch.Tensor, kv_cmp: torch.Tensor, 
 def _(q, kv_raw, kv_cmp, idx, pos, raw_pt, cmp_pt, cmp_lens, n_tok, tok_per_seq, topk, window, raw_len, cmp_len,
       raw_ptw, cmp_ptw, scale, check):
     return q.new_empty((n_tok, 128, 512), dtype=torch.bfloat16), q.new_empty((n_tok, 128), dtype=torch.float32)
+
+
+# ----------------------------------------------------------------------------- two-level indexer selection
+
+@torch.library.custom_op("mzb::candidate_blocks", mutates_args=())
+def candidate_blocks(logits: torch.Tensor, clens: torch.Tensor, topk_blocks: int, block_size: int,
+                     want_mask: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(blocks int32 [rows, topk_blocks], mask uint8 [rows, T] or [0]) of ``mzb_candidate_blocks``
+    (logits fp32 [rows, T], clens int32 [rows], both contiguous)."""
+    rows, T = logits.shape
+    dev = logits.device
+    blocks = torch.empty(rows, topk_blocks, dtype=torch.int32, device=dev)
+    mask = torch.empty((rows, T) if want_mask else (0,), dtype=torch.uint8, device=dev)
+    call("mzb_candidate_blocks", ptr(logits), ptr(clens), ptr(blocks), ptr(mask) if want_mask else None, rows, T,
+         block_size, topk_blocks, stream_ptr(dev))
+    return blocks, mask
+
+
+@candidate_blocks.register_fake
+def _(logits, clens, topk_blocks, block_size, want_mask):
+    rows, T = logits.shape
+    return (logits.new_empty((rows, topk_blocks), dtype=torch.int32),
+            logits.new_empty((rows, T) if want_mask else (0,), dtype=torch.uint8))
+
+
+@torch.library.custom_op("mzb::candidate_topk", mutates_args=())
+def candidate_topk(scores: torch.Tensor, blocks: torch.Tensor | None, mask: torch.Tensor | None, block_size: int,
+                   topk: int) -> torch.Tensor:
+    """int32 [rows, topk] of ``mzb_candidate_topk`` (scores fp32 [rows, T]; candidates as a block
+    list int32 [rows, nblk] or a uint8 mask [rows, T])."""
+    rows, T = scores.shape
+    out = torch.empty(rows, topk, dtype=torch.int32, device=scores.device)
+    nblk = blocks.shape[1] if blocks is not None else 0
+    call("mzb_candidate_topk", ptr(scores), ptr(blocks), ptr(mask), rows, T, block_size, nblk, topk, ptr(out),
+         stream_ptr(scores.device))
+    return out
+
+
+@candidate_topk.register_fake
+def _(scores, blocks, mask, block_size, topk):
+    return scores.new_empty((scores.shape[0], topk), dtype=torch.int32)

@@ -130,10 +130,54 @@ def make_indexer(golden_ref) -> None:
     np.savez_compressed(os.path.join(HERE, "indexer.npz"), **out)
 
 
+def make_candidates() -> None:
+    """Level one through the reference's ``select_candidate_blocks``
+    (archs/owlet1/indexer.py:14-41 = archs/dsv4/modeling_deepseek_v41.py:427-454); level two
+    as written in ``DeepseekV41Indexer.forward`` (modeling_deepseek_v41.py:566-578):
+    masked_fill(~candidates, -inf), topk(min(topk, T)), picks at -inf dropped."""
+    from mzoo.archs.owlet1.indexer import select_candidate_blocks  # noqa: E402
+    out = {}
+    g = torch.Generator().manual_seed(3)
+    # (rows, T, ratio, block_size, topk_blocks, topk, position offset)
+    cases = [(48, 45, 4, 8, 3, 10, 0),      # T not a multiple of 8; few reachable blocks early on
+             (40, 300, 2, 8, 16, 24, 100),  # more reachable blocks than topk_blocks
+             (16, 37, 1, 4, 64, 5, 0),      # topk_blocks > number of blocks
+             (24, 200, 1, 8, 5, 12, 150)]   # compress_len beyond T for the late rows: no pin
+    for c, (rows, T, ratio, bs, tb, topk, off) in enumerate(cases):
+        pos = off + torch.arange(rows) * max(1, (T * ratio) // rows)
+        clen = ((pos + 1) // ratio).unsqueeze(-1)  # [rows, 1], the reference's trailing axis
+        vis = torch.arange(T).view(1, -1) < clen
+        logits = torch.where(vis, torch.randn(rows, T, generator=g), torch.tensor(float("-inf")))
+        if c == 0:  # rows whose newest block also holds their best score
+            for r in range(0, rows, 5):
+                n = int(clen[r])
+                if n > 0:
+                    logits[r, n - 1] = 10.0
+        mask = select_candidate_blocks(logits, clen, tb, bs)
+        scores2 = torch.where(vis, torch.randn(rows, T, generator=g), torch.tensor(float("-inf")))
+        masked = scores2.masked_fill(~mask, float("-inf"))
+        top = masked.topk(min(topk, T), dim=-1, sorted=False)
+        picks = torch.where(top.values > float("-inf"), top.indices, torch.full_like(top.indices, T))
+        picks = picks.sort(dim=-1).values
+        picks = torch.where(picks == T, torch.full_like(picks, -1), picks)  # -1 padding at the end
+        key = f"c{c}."
+        out[key + "logits"], out[key + "clen"] = logits.numpy(), clen.squeeze(-1).numpy().astype(np.int64)
+        out[key + "mask"] = mask.numpy()
+        out[key + "scores2"], out[key + "topk_idx"] = scores2.numpy(), picks.numpy().astype(np.int64)
+        out[key + "params"] = np.array([bs, tb, topk], np.int64)
+    np.savez_compressed(os.path.join(HERE, "candidates.npz"), **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
     quant, golden_ref = _ref()
-    make_quant(quant)
-    make_attention(golden_ref)
-    make_indexer(golden_ref)
+    only = sys.argv[1:]
+    if not only or "quant" in only:
+        make_quant(quant)
+    if not only or "attention" in only:
+        make_attention(golden_ref)
+    if not only or "indexer" in only:
+        make_indexer(golden_ref)
+    if not only or "candidates" in only:
+        make_candidates()
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
