@@ -128,6 +128,7 @@ TRAFFIC = {
     "prefill": 2535907584 + 2112252416,
     "decode": 313127680 + 10324480,
     "train": (4376674816 + 94292736) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
+    "candidates": 381950464 + 3411200,  # level two (gathered): 32-byte blocks cost ~2.8x in DRAM bursts
 }
 
 
@@ -884,8 +885,143 @@ def reference_decode(args, rank, world) -> dict:
             "cpu_baseline": r, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ----------------------------------------------------------------------------- two-level selection
+
+# Level one over a candidate source's scores and level two over a later index source's, for
+# the model's defaults (blocks of 8 compressed positions, top-2048 blocks, top-512 positions)
+# at a context long enough for the block selection to bite: 65536 compressed positions
+# (262144 tokens at ratio 4), the last 2048 queries of the sequence.
+CF = dict(rows=2048, T=65536, block=8, topk_blocks=2048, topk=512)
+
+
+def cf_inputs(torch, seed: int, rows=None):
+    """Two score matrices [rows, T] ~ N(0,1), -inf past each query's compressed length, and
+    the lengths (query r sees T - rows + r + 1 positions)."""
+    rows = rows or CF["rows"]
+    g = torch.Generator().manual_seed(seed)
+    T = CF["T"]
+    clen = torch.arange(T - CF["rows"] + 1, T - CF["rows"] + 1 + rows, dtype=torch.int32)
+    vis = torch.arange(T).view(1, -1) < clen.view(-1, 1)
+    mats = [torch.randn(rows, T, generator=g).masked_fill_(~vis, float("-inf")) for _ in range(2)]
+    return mats[0], mats[1], clen
+
+
+def bench_candidates(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import candidates as K
+    lg_h, sc_h, cl_h = cf_inputs(torch, seed=0)
+    mine = torch.arange(rank, CF["rows"], world)  # rows cyclic over ranks, no collective
+    lg, sc, cl = (x[mine].contiguous().to(device) for x in (lg_h, sc_h, cl_h))
+    rows = lg.shape[0]
+    bs, tb, topk = CF["block"], CF["topk_blocks"], CF["topk"]
+
+    def step():
+        blocks = K.candidate_blocks(lg, cl, tb, bs)
+        return K.candidate_topk(sc, blocks, topk, block_size=bs)
+
+    timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler.ready()
+    if dist:
+        dist.barrier()
+    t_steps = timer.run(step, args.steps)
+    blocks = K.candidate_blocks(lg, cl, tb, bs)
+    t_l1 = timer.run(lambda: K.candidate_blocks(lg, cl, tb, bs), args.steps)
+    t_l2 = timer.run(lambda: K.candidate_topk(sc, blocks, topk, block_size=bs), args.steps)
+    # end to end through the public API from pinned host memory
+    hlg, hsc, hcl = (x[mine].contiguous().pin_memory() for x in (lg_h, sc_h, cl_h))
+    dlg, dsc, dcl = (torch.empty_like(x, device=device) for x in (hlg, hsc, hcl))
+    hout = torch.empty(rows, topk, dtype=torch.int32).pin_memory()
+
+    def e2e():
+        for d, h in ((dlg, hlg), (dsc, hsc), (dcl, hcl)):
+            d.copy_(h, non_blocking=True)
+        b = K.candidate_blocks(dlg, dcl, tb, bs)
+        hout.copy_(K.candidate_topk(dsc, b, topk, block_size=bs), non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    clocks = sampler.stop(busy=step)
+    torch.cuda.synchronize()
+    h2d = sum(x.numel() * x.element_size() for x in (hlg, hsc, hcl))
+    d2h = hout.numel() * hout.element_size()
+
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_l1, ms_l2 = sum(t_l1) / len(t_l1), sum(t_l2) / len(t_l2)
+    pk = peaks()
+    # dominant kernel: the level-two top-k, which reads only the listed blocks' scores (plus the
+    # block list) and writes the indices
+    alg2 = rows * (CF["topk_blocks"] * CF["block"] * 4 + CF["topk_blocks"] * 4 + CF["topk"] * 4)
+    achieved = alg2 / (ms_l2 * 1e-3) / 1e9
+    out = {
+        "metric": "two-level indexer selection Mq/s", "value": CF["rows"] / (ms * 1e-3) / 1e6, "unit": "Mq/s",
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 keys (radix select on order-preserving uint32)",
+        "data": "synthetic (seeded N(0,1) scores, -inf past each query's compressed length)",
+        "config": {"workload": "F1 two-level selection: level-one candidate blocks + level-two top-k",
+                   "queries": CF["rows"], "positions": CF["T"], "block_size": bs, "topk_blocks": tb, "topk": topk,
+                   "parallelism": (f"query rows cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
+                   "l2": "flushed (256 MB write) per step; inputs (2 x 512 MB) larger than L2"},
+        "legs": {"level_one_ms": ms_l1, "level_two_ms": ms_l2,
+                 "level_one_gbs": rows * CF["T"] * 4 / (ms_l1 * 1e-3) / 1e9},
+        "e2e": {"value": CF["rows"] / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": "mzb::cand::topk_gather_kernel (level two)", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_note": f"{pk['_source']} copy bandwidth", "algorithmic_bytes_per_launch": alg2,
+                     "ms_per_launch": ms_l2, "traffic": TRAFFIC.get("candidates"),
+                     "traffic_unit": "bytes per launch (ncu)"},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_candidates(lg_h, sc_h, cl_h, sample=max(1, min(CF["rows"], args.cpu_sample // 2)))
+    return out
+
+
+def cpu_candidates(lg, sc, cl, sample: int) -> dict:
+    """Oracle port on the host: both levels for the first `sample` query rows."""
+    from oracle import candidates as C
+    lgn, scn, cln = lg[:sample].numpy(), sc[:sample].numpy(), cl[:sample].numpy()
+    t0 = time.perf_counter()
+    mask = C.candidate_mask_ref(lgn, cln, CF["topk_blocks"], CF["block"])
+    C.candidate_topk_ref(scn, mask, CF["topk"])
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt / 1e6, "unit": "Mq/s", "cores": 1, "kind": "port",
+            "sample": f"{sample} query rows of {CF['T']} positions, numpy (lexsort per row), {dt:.2f} s"}
+
+
+def reference_candidates(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    n = max(1, args.cpu_sample // 16)
+    lg, sc, cl = cf_inputs(torch, seed=0, rows=n)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_candidates(lg, sc, cl, sample=n)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    r["value"] = v
+    return {"metric": "two-level indexer selection Mq/s", "value": v, "unit": "Mq/s", "impl": "reference",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": CF["rows"] / (v * 1e6) * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
+            "config": {"workload": "F1 two-level selection: level-one candidate blocks + level-two top-k",
+                       "queries": CF["rows"], "positions": CF["T"], "block_size": CF["block"],
+                       "topk_blocks": CF["topk_blocks"], "topk": CF["topk"]},
+            "cpu_baseline": r, "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
-           "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode)}
+           "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode),
+           "candidates": (bench_candidates, reference_candidates)}
 
 
 def main():
@@ -906,6 +1042,7 @@ def main():
         C3.update(S=2048)
         C5.update(B=1, S=2048)
         C4.update(B=8)
+        CF.update(rows=256)
         args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 

@@ -16,11 +16,13 @@
 // (block index at level one, position at level two).  NaN scores count as -inf.
 //
 // One CTA of 1024 threads per query row.  Values become order-preserving uint32 keys (0 =
-// not selectable); a 4-pass radix select over 8-bit digits (shared-memory histograms, one
-// warp scanning the 256 bins) finds the K-th largest key, and one ordered pass keeps the
-// keys above it plus the lowest-index ties, writing ascending indices (-1 padded).  Level
-// one holds the row's block keys in shared memory (up to NB_MAX blocks); level two reads
-// the score row from global memory in every pass (HBM / L2 bound, no GEMM).
+// not selectable); a 3-pass radix select over 12-, 10- and 10-bit digits (shared-memory
+// histograms scanned by the whole CTA) finds the K-th largest key, and one ordered pass keeps
+// the keys above it plus the lowest-index ties, writing ascending indices (-1 padded).  Level
+// one holds the row's block keys in shared memory (up to NB_MAX blocks).  Level two with a
+// block list gathers the listed blocks' scores into shared memory once (up to GK_MAX keys)
+// and selects there; with a bool mask, or a list too long for that, it reads the score row
+// from global memory in every pass.
 #include "common.cuh"
 
 namespace mzb {
@@ -40,8 +42,10 @@ __device__ __forceinline__ uint32_t fkey(float x) {
 }
 constexpr uint32_t KEY_POS_INF = 0xFF800000u;  // fkey(+inf)
 
+constexpr int NBIN = 4096;  // first radix digit: 12 bits (sign, exponent, 3 mantissa bits)
+
 struct Smem {
-  int hist[256];
+  int hist[NBIN];
   int red[NW + 2];
   int wsum[NW];
   uint32_t bits[NB_MAX / 32];  // level one: kept blocks; level two: candidate blocks
@@ -99,56 +103,83 @@ struct Sel {
   bool all;      // every selectable key fits: keep all keys != 0
 };
 
-// K-th largest non-zero key of src.key(0..n) (K >= 1).
+// Exclusive prefix sum of a per-thread count over the CTA in thread order; returns the total.
+__device__ int block_excl_sum(int v, int& prefix, Smem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int inc = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += y;
+  }
+  if (lane == 31) sm.wsum[warp] = inc;
+  __syncthreads();
+  if (warp == 0) {
+    const int c = lane < NW ? sm.wsum[lane] : 0;
+    int wi = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    if (lane < NW) sm.wsum[lane] = wi - c;
+    if (lane == 31) sm.red[NW + 1] = wi;
+  }
+  __syncthreads();
+  prefix = sm.wsum[warp] + inc - v;
+  const int total = sm.red[NW + 1];
+  __syncthreads();
+  return total;
+}
+
+// K-th largest non-zero key of src.key(0..n) (K >= 1): three digits of 12, 10 and 10 bits.
+// The 12-bit first digit spreads real scores (which share a handful of exponents) over many
+// bins, so the shared-memory histogram atomics rarely collide.
 template <class Src>
 __device__ Sel radix_select(const Src& src, int n, int K, Smem& sm) {
   int cnt = 0;
   for (int i = threadIdx.x; i < n; i += NT) cnt += src.key(i) != 0u;
   cnt = block_sum(cnt, sm);
   if (cnt <= K) return Sel{0u, 0, true};
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint32_t prefix = 0u, pmask = 0u;
   int k = K;
 #pragma unroll 1
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    if (threadIdx.x < 256) sm.hist[threadIdx.x] = 0;
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 20 : (pass == 1 ? 10 : 0);
+    const uint32_t dmask = pass == 0 ? 0xFFFu : 0x3FFu;
+    const int nbins = int(dmask) + 1, per = nbins / NT;  // bins per thread: 4, then 1
+    for (int b = threadIdx.x; b < nbins; b += NT) sm.hist[b] = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < n; i += NT) {
       const uint32_t key = src.key(i);
-      if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1);
+      if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & dmask], 1);
     }
     __syncthreads();
-    if (warp == 0) {  // lane l owns bins 255 - 8l down to 248 - 8l
-      int c[8], s = 0;
+    // thread t owns bins nbins-1-t*per .. nbins-(t+1)*per (descending)
+    int c[4], own = 0;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = sm.hist[255 - (lane * 8 + j)];
-        s += c[j];
-      }
-      int inc = s;
+    for (int j = 0; j < 4; ++j) {
+      c[j] = j < per ? sm.hist[nbins - 1 - (threadIdx.x * per + j)] : 0;
+      own += c[j];
+    }
+    int exc;
+    block_excl_sum(own, exc, sm);
+    if (exc < k && k <= exc + own) {  // exactly one thread: the bin holding the k-th key
+      int acc = exc, bin = -1, above = 0;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      const int exc = inc - s;
-      if (exc < k && k <= inc) {  // exactly one lane: the bin holding the k-th key
-        int acc = exc, bin = -1, above = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (bin < 0 && acc + c[j] >= k) {
-            bin = 255 - (lane * 8 + j);
-            above = acc;
-          }
-          acc += c[j];
+      for (int j = 0; j < 4; ++j) {
+        if (bin < 0 && j < per && acc + c[j] >= k) {
+          bin = nbins - 1 - (threadIdx.x * per + j);
+          above = acc;
         }
-        sm.red[0] = bin;
-        sm.red[1] = above;
+        acc += c[j];
       }
+      sm.red[0] = bin;
+      sm.red[1] = above;
     }
     __syncthreads();
     prefix |= uint32_t(sm.red[0]) << shift;
-    pmask |= 0xFFu << shift;
+    pmask |= dmask << shift;
     k -= sm.red[1];
     __syncthreads();
   }
@@ -183,7 +214,7 @@ struct BlockKeys {  // keys of the row's blocks, in shared memory
 
 __global__ void __launch_bounds__(NT) blocks_kernel(const float* __restrict__ logits, const int32_t* __restrict__ clens,
                                                     int32_t* __restrict__ blocks, uint8_t* __restrict__ mask, int T,
-                                                    int bs, int nb, int topk_blocks) {
+                                                    int bs, int nb, int topk_blocks, bool vec) {
   extern __shared__ __align__(16) uint8_t dsm[];
   __shared__ Smem sm;
   uint32_t* keys = reinterpret_cast<uint32_t*>(dsm);
@@ -193,8 +224,15 @@ __global__ void __launch_bounds__(NT) blocks_kernel(const float* __restrict__ lo
   const int last = clen >= 1 ? (clen - 1) / bs : -1;  // floor((clen - 1) / bs)
   for (int b = threadIdx.x; b < nb; b += NT) {
     const int t0 = b * bs, t1 = min(T, t0 + bs);
-    float m = -INFINITY;
-    for (int t = t0; t < t1; ++t) m = fmaxf(m, __ldg(lrow + t));  // fmaxf skips NaN
+    float m = -INFINITY;  // fmaxf skips NaN
+    if (vec) {  // host-checked: 16-byte aligned base, T and bs multiples of 4
+      for (int t = t0; t < t1; t += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(lrow + t));
+        m = fmaxf(fmaxf(m, fmaxf(v.x, v.y)), fmaxf(v.z, v.w));
+      }
+    } else {
+      for (int t = t0; t < t1; ++t) m = fmaxf(m, __ldg(lrow + t));
+    }
     keys[b] = b == last ? KEY_POS_INF : fkey(m);
   }
   for (int w = threadIdx.x; w < (nb + 31) / 32; w += NT) sm.bits[w] = 0u;
@@ -258,6 +296,62 @@ __global__ void __launch_bounds__(NT) topk_kernel(const float* __restrict__ scor
   for (int r = kept + threadIdx.x; r < topk; r += NT) orow[r] = -1;
 }
 
+// Level two from a block list, gathered: the candidate blocks (ascending, duplicates and
+// out-of-range entries dropped) are read once into shared memory as keys, in position order,
+// so the radix passes and the ordered pass never touch global memory again.
+constexpr int GK_MAX = 16384;   // gathered keys per row (64 KB)
+constexpr int GB_MAX = 4096;    // gathered blocks per row
+
+struct SmemKeys {
+  const uint32_t* k;
+  __device__ __forceinline__ uint32_t key(int i) const { return k[i]; }
+};
+
+__global__ void __launch_bounds__(NT) topk_gather_kernel(const float* __restrict__ scores,
+                                                         const int32_t* __restrict__ blocks, int32_t* __restrict__ out,
+                                                         int T, int bs, int nblk, int topk) {
+  extern __shared__ __align__(16) uint8_t dsm[];
+  __shared__ Smem sm;
+  uint32_t* keys = reinterpret_cast<uint32_t*>(dsm);
+  int32_t* blist = reinterpret_cast<int32_t*>(dsm + GK_MAX * 4);
+  const long long row = blockIdx.x;
+  const float* srow = scores + row * T;
+  const int nb = (T + bs - 1) / bs;
+  for (int w = threadIdx.x; w < (nb + 31) / 32; w += NT) sm.bits[w] = 0u;
+  __syncthreads();
+  const int32_t* brow = blocks + row * nblk;
+  for (int j = threadIdx.x; j < nblk; j += NT) {
+    const int b = brow[j];
+    if (b >= 0 && b < nb) atomicOr(&sm.bits[b >> 5], 1u << (b & 31));
+  }
+  __syncthreads();
+  // ascending list of the set blocks (the caller guarantees at most GB_MAX of them)
+  int nsel = 0;
+  for (int b0 = 0; b0 < nb; b0 += NT) {
+    const int b = b0 + threadIdx.x;
+    const bool set = b < nb && ((sm.bits[b >> 5] >> (b & 31)) & 1u);
+    int r;
+    const int tot = block_scan(set, r, sm);
+    if (set) blist[nsel + r] = b;
+    nsel += tot;
+  }
+  __syncthreads();
+  const int n = nsel * bs;
+  for (int j = threadIdx.x; j < n; j += NT) {
+    const int s = j / bs, t = blist[s] * bs + (j - s * bs);
+    keys[j] = t < T ? fkey(__ldg(srow + t)) : 0u;
+  }
+  __syncthreads();
+  const SmemKeys src{keys};
+  const Sel sel = radix_select(src, n, topk, sm);
+  int32_t* orow = out + row * topk;
+  const int kept = select_ordered(src, n, sel, sm, [&](int r, int j) {
+    const int s = j / bs;
+    orow[r] = blist[s] * bs + (j - s * bs);
+  });
+  for (int r = kept + threadIdx.x; r < topk; r += NT) orow[r] = -1;
+}
+
 }  // namespace cand
 }  // namespace mzb
 
@@ -279,8 +373,9 @@ extern "C" int mzb_candidate_blocks(const float* logits, const int32_t* compress
   const size_t dyn = size_t(nb > 0 ? nb : 1) * 4;
   if (cudaFuncSetAttribute(cand::blocks_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(dyn)) != cudaSuccess)
     return launch_status("candidate_blocks(smem attr)");
+  const bool vec = (T % 4) == 0 && (block_size % 4) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
   cand::blocks_kernel<<<unsigned(rows), cand::NT, dyn, static_cast<cudaStream_t>(stream)>>>(
-      logits, compress_lens, blocks, mask, int(T), block_size, int(nb), topk_blocks);
+      logits, compress_lens, blocks, mask, int(T), block_size, int(nb), topk_blocks, vec);
   return launch_status("candidate_blocks");
 }
 
@@ -299,6 +394,17 @@ extern "C" int mzb_candidate_topk(const float* scores, const int32_t* blocks, co
   }
   MZB_REQUIRE(rows == 0 || (scores && out), MZB_ERR_SHAPE, "candidate_topk: scores and out are required");
   if (rows == 0) return MZB_OK;
+  const int64_t nb = blocks ? (T + block_size - 1) / block_size : 0;
+  const int64_t gblocks = nb < nblk ? nb : nblk;  // distinct in-range blocks a row can list
+  if (blocks && gblocks <= cand::GB_MAX && gblocks * block_size <= cand::GK_MAX) {
+    const int dyn = cand::GK_MAX * 4 + cand::GB_MAX * 4;
+    if (cudaFuncSetAttribute(cand::topk_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) !=
+        cudaSuccess)
+      return launch_status("candidate_topk(smem attr)");
+    cand::topk_gather_kernel<<<unsigned(rows), cand::NT, dyn, static_cast<cudaStream_t>(stream)>>>(
+        scores, blocks, out, int(T), block_size, nblk, topk);
+    return launch_status("candidate_topk");
+  }
   cand::topk_kernel<<<unsigned(rows), cand::NT, 0, static_cast<cudaStream_t>(stream)>>>(
       scores, blocks, mask, out, int(T), blocks ? block_size : 1, blocks ? nblk : 0, topk);
   return launch_status("candidate_topk");

@@ -144,3 +144,34 @@ def test_kernels_reject_too_many_blocks(cuda):
     lg = torch.zeros(1, 16384 * 8 + 1, device=cuda)
     with pytest.raises(AssertionError, match="blocks per row"):
         K.candidate_blocks(lg, torch.ones(1, dtype=torch.int64, device=cuda), 8, 8)
+
+
+@pytest.mark.gpu
+def test_kernels_unaligned_rows(cuda):
+    """A logits view 4 bytes past an aligned address takes the scalar block-max path."""
+    import torch
+    from mzoo_b200 import candidates as K
+    rng = np.random.default_rng(11)
+    logits, clen = _rand_case(rng, 12, 4096, 1, 3000)
+    flat = torch.zeros(logits.size + 1, device=cuda)
+    flat[1:] = torch.from_numpy(logits.reshape(-1)).to(cuda)
+    lg = flat[1:].view(12, 4096)
+    assert lg.data_ptr() % 16 == 4
+    got = K.candidate_blocks(lg, torch.from_numpy(clen).to(cuda), 64, 8).cpu().numpy()
+    assert np.array_equal(got, C.candidate_blocks_ref(logits, clen, 64, 8))
+
+
+@pytest.mark.gpu
+def test_level_two_streaming_path(cuda):
+    """More listed blocks than the gathered kernel holds (5000 > 4096): the streaming kernel."""
+    import torch
+    from mzoo_b200 import candidates as K
+    rng = np.random.default_rng(12)
+    rows, T, bs, tb, topk = 6, 50000, 8, 5000, 300
+    logits, clen = _rand_case(rng, rows, T, 1, 40000)
+    blocks = C.candidate_blocks_ref(logits, clen, tb, bs)
+    mask = C.candidate_mask_ref(logits, clen, tb, bs)
+    scores2, _ = _rand_case(rng, rows, T, 1, 40000)
+    got = K.candidate_topk(torch.from_numpy(scores2).to(cuda), torch.from_numpy(blocks).to(cuda), topk,
+                           block_size=bs).cpu().numpy()
+    assert np.array_equal(got, C.candidate_topk_ref(scores2, mask, topk))
