@@ -10,11 +10,14 @@
 // Kernels (one CTA per tile, persistent):
 //   preprocess  delta and lse*log2(e) per packed row, into 128-row-padded buffers
 //   dkv         key owner: 128 window keys; loops over the query tiles that see them;
-//               S^T = K Q^T and dP^T = V dO^T in TMEM; the compute warps (thread = key)
-//               turn them into P^T, dS^T and store them back into TMEM as bf16, which the
-//               TS MMAs dV += P^T dO, dK += dS^T Q read as their A operand.
+//               S^T = K Q^T and dP^T = V dO^T in TMEM; two compute warpgroups (thread =
+//               key; warps 4-7 query columns [0, 64), warps 8-11 [64, 128)) turn them into
+//               P^T, dS^T and store them back into TMEM as bf16, each half packed into the
+//               front of its own columns, which the TS MMAs dV += P^T dO, dK += dS^T Q
+//               read as their A operand.
 //   dq          query owner: 128 rows; loops over window tiles then gathered tiles;
-//               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K); gathered tiles also
+//               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K; window-only: warps
+//               8-11 take the upper column half, its dS in the unused dM columns); gathered tiles also
 //               keep dS and P in shared memory for dM = dS^T Q + P^T dO, scattered into
 //               dmain by the compute warps with fp32 atomics.
 // Column visibility (window run, or a token's valid gathered slots) is one mask word per

@@ -10,7 +10,7 @@ M = dict(device="meta")
 
 def test_all_ops_registered():
     names = {"fq_fp4", "fq_fp8", "indexer_scores", "indexer_topk", "indexer_bwd", "attn_fwd", "attn_bwd",
-             "sparse_mla_fwd"}
+             "sparse_mla_fwd", "candidate_blocks", "candidate_topk"}
     assert names <= set(dir(torch.ops.mzb))
 
 
@@ -44,3 +44,11 @@ def test_fake_shapes():
     assert om.shape == (10, 128, 512) and lm.shape == (10, 128)
     x = torch.empty(4, 64, dtype=torch.bfloat16, **M)
     assert torch.ops.mzb.fq_fp4(x, 32, 0).shape == x.shape and torch.ops.mzb.fq_fp8(x, 32, 0).shape == x.shape
+    lg = torch.empty(12, 300, dtype=torch.float32, **M)
+    cl = torch.empty(12, dtype=torch.int32, **M)
+    blocks, mask = torch.ops.mzb.candidate_blocks(lg, cl, 16, 8, True)
+    assert blocks.shape == (12, 16) and blocks.dtype == torch.int32
+    assert mask.shape == (12, 300) and mask.dtype == torch.uint8
+    assert torch.ops.mzb.candidate_blocks(lg, cl, 16, 8, False)[1].shape == (0,)
+    top = torch.ops.mzb.candidate_topk(lg, blocks, None, 8, 24)
+    assert top.shape == (12, 24) and top.dtype == torch.int32
