@@ -97,6 +97,34 @@ __device__ int block_scan(bool f, int& prefix, Smem& sm) {
   return total;
 }
 
+// Exclusive prefix counts of two per-thread flags in one CTA scan (the counts share an int
+// as two 16-bit halves: a tile holds at most 1024 of each); totals through t0 / t1.
+__device__ void block_scan2(bool f0, bool f1, int& p0, int& p1, int& t0, int& t1, Smem& sm) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t b0 = __ballot_sync(0xffffffffu, f0), b1 = __ballot_sync(0xffffffffu, f1);
+  const uint32_t below = (1u << lane) - 1u;
+  if (lane == 0) sm.wsum[warp] = __popc(b0) | (__popc(b1) << 16);
+  __syncthreads();
+  if (warp == 0) {
+    const int c = lane < NW ? sm.wsum[lane] : 0;
+    int inc = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += y;
+    }
+    if (lane < NW) sm.wsum[lane] = inc - c;
+    if (lane == 31) sm.red[NW + 1] = inc;
+  }
+  __syncthreads();
+  const int base = sm.wsum[warp], tot = sm.red[NW + 1];
+  p0 = (base & 0xFFFF) + __popc(b0 & below);
+  p1 = (base >> 16) + __popc(b1 & below);
+  t0 = tot & 0xFFFF;
+  t1 = tot >> 16;
+  __syncthreads();
+}
+
 struct Sel {
   uint32_t kth;  // keep keys > kth ...
   int ties;      // ... and the first `ties` keys == kth in index order
@@ -137,10 +165,6 @@ __device__ int block_excl_sum(int v, int& prefix, Smem& sm) {
 // bins, so the shared-memory histogram atomics rarely collide.
 template <class Src>
 __device__ Sel radix_select(const Src& src, int n, int K, Smem& sm) {
-  int cnt = 0;
-  for (int i = threadIdx.x; i < n; i += NT) cnt += src.key(i) != 0u;
-  cnt = block_sum(cnt, sm);
-  if (cnt <= K) return Sel{0u, 0, true};
   uint32_t prefix = 0u, pmask = 0u;
   int k = K;
 #pragma unroll 1
@@ -150,11 +174,16 @@ __device__ Sel radix_select(const Src& src, int n, int K, Smem& sm) {
     const int nbins = int(dmask) + 1, per = nbins / NT;  // bins per thread: 4, then 1
     for (int b = threadIdx.x; b < nbins; b += NT) sm.hist[b] = 0;
     __syncthreads();
+    int cnt = 0;  // selectable keys (first pass)
     for (int i = threadIdx.x; i < n; i += NT) {
       const uint32_t key = src.key(i);
-      if (key != 0u && (key & pmask) == prefix) atomicAdd(&sm.hist[(key >> shift) & dmask], 1);
+      if (key != 0u && (key & pmask) == prefix) {
+        atomicAdd(&sm.hist[(key >> shift) & dmask], 1);
+        ++cnt;
+      }
     }
     __syncthreads();
+    if (pass == 0 && block_sum(cnt, sm) <= K) return Sel{0u, 0, true};  // every selectable key fits
     // thread t owns bins nbins-1-t*per .. nbins-(t+1)*per (descending)
     int c[4], own = 0;
 #pragma unroll
@@ -193,15 +222,14 @@ __device__ int select_ordered(const Src& src, int n, const Sel& sel, Smem& sm, E
   for (int t0 = 0; t0 < n; t0 += NT) {
     const int i = t0 + threadIdx.x;
     const uint32_t key = i < n ? src.key(i) : 0u;
+    const bool gt = key != 0u && (sel.all || key > sel.kth);
     const bool eq = !sel.all && key != 0u && key == sel.kth;
-    int er = 0;
-    const int et = sel.all ? 0 : block_scan(eq, er, sm);
-    const bool keep = key != 0u && (sel.all || key > sel.kth || (eq && ties_before + er < sel.ties));
-    int kr;
-    const int kt = block_scan(keep, kr, sm);
-    if (keep) emit(kept + kr, i);
-    kept += kt;
-    ties_before += et;
+    int pg, pe, tg, te;
+    block_scan2(gt, eq, pg, pe, tg, te, sm);
+    const int room = max(0, sel.ties - ties_before);  // ties still to take, lowest index first
+    if (gt || (eq && pe < room)) emit(kept + pg + min(pe, room), i);
+    kept += tg + min(te, room);
+    ties_before += te;
   }
   return kept;
 }
