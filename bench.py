@@ -129,6 +129,7 @@ TRAFFIC = {
     "decode": 313127680 + 10324480,
     "train": (4376674816 + 94292736) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
     "candidates": 381950464 + 3411200,  # level two (gathered): 32-byte blocks cost ~2.8x in DRAM bursts
+    "compressor": 612400896 + 68001536,
 }
 
 
@@ -1019,9 +1020,142 @@ def reference_candidates(args, rank, world) -> dict:
             "cpu_baseline": r, "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+# ----------------------------------------------------------------------------- compressor producer step
+
+# The compressor after its two fp32 projections, for a prefill batch: 8 sequences of 16384
+# tokens at ratio 4 (4096 groups each), the V4.1 latent (576 channels, 64 of them rope),
+# writing the pre-RoPE latent and the MXFP4 compressed-cache entry.
+CP = dict(B=8, S=16384, ratio=4, D=576, rope=64)
+
+
+def cp_inputs(torch, seed: int, B=None):
+    B = B or CP["B"]
+    g = torch.Generator().manual_seed(seed)
+    G = CP["S"] // CP["ratio"]
+    kv = torch.randn(B, CP["S"], CP["D"], generator=g)
+    gate = torch.randn(B, CP["S"], CP["D"], generator=g) * 2
+    w = (1 + 0.25 * torch.randn(CP["D"], generator=g)).to(torch.bfloat16)
+    ang = torch.rand(B, G, CP["rope"] // 2, generator=g) * 6
+    return kv, gate, w, ang.cos(), ang.sin()
+
+
+def cp_bytes(B: int) -> float:
+    """Algorithmic HBM bytes of one step: kv and gate read once, cos / sin read, two bf16 outputs."""
+    G = CP["S"] // CP["ratio"]
+    return B * (2 * CP["S"] * CP["D"] * 4 + 2 * G * (CP["rope"] // 2) * 4 + 2 * G * CP["D"] * 2)
+
+
+def bench_compressor(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import compressor as K
+    h = cp_inputs(torch, seed=0)
+    mine = torch.arange(rank, CP["B"], world)  # sequences cyclic over ranks, no collective
+    kv, gate, w, cos, sin = (x[mine].contiguous().to(device) if x.dim() > 1 else x.to(device) for x in h)
+    B = kv.shape[0]
+    step = lambda: K.compress(kv, gate, w, CP["ratio"], 1e-6, cos, sin)  # noqa: E731
+    timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler.ready()
+    if dist:
+        dist.barrier()
+    t_steps = timer.run(step, args.steps)
+    hkv, hgate, hcos, hsin = (x[mine].contiguous().pin_memory() for x in (h[0], h[1], h[3], h[4]))
+    dkv, dgate, dcos, dsin = (torch.empty_like(x, device=device) for x in (hkv, hgate, hcos, hsin))
+    G = CP["S"] // CP["ratio"]
+    hlat = torch.empty(B, G, CP["D"], dtype=torch.bfloat16).pin_memory()
+    hcache = torch.empty_like(hlat).pin_memory()
+
+    def e2e():
+        for d, x in ((dkv, hkv), (dgate, hgate), (dcos, hcos), (dsin, hsin)):
+            d.copy_(x, non_blocking=True)
+        lat, cache = K.compress(dkv, dgate, w, CP["ratio"], 1e-6, dcos, dsin)
+        hlat.copy_(lat, non_blocking=True)
+        hcache.copy_(cache, non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    clocks = sampler.stop(busy=step)
+    torch.cuda.synchronize()
+    h2d = sum(x.numel() * x.element_size() for x in (hkv, hgate, hcos, hsin))
+    d2h = 2 * hlat.numel() * hlat.element_size()
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    total = cp_bytes(CP["B"])  # the whole job
+    local = cp_bytes(B)
+    achieved = local / ((sum(t_steps) / len(t_steps)) * 1e-3) / 1e9
+    pk = peaks()
+    out = {
+        "metric": "compressor producer step HBM GB/s (algorithmic bytes)", "value": total / (ms * 1e-3) / 1e9,
+        "unit": "GB/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 pool, bf16 latent / cache", "data": "synthetic (seeded N(0,1) projections, random angles)",
+        "config": {"workload": "F3 compressor: gated softmax pool + RMSNorm + RoPE + MXFP4 cache entry",
+                   "B": CP["B"], "tokens": CP["S"], "compress_ratio": CP["ratio"], "head_dim": CP["D"],
+                   "rope_dim": CP["rope"],
+                   "parallelism": (f"sequences cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
+                   "l2": "flushed (256 MB write) per step; inputs (604 MB) larger than L2"},
+        "e2e": {"value": total / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "roofline": {"bound": "hbm", "kernel": "mzb::comp::compress_kernel", "achieved": achieved,
+                     "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "peak_note": f"{pk['_source']} copy bandwidth", "algorithmic_bytes_per_launch": local,
+                     "ms_per_launch": sum(t_steps) / len(t_steps), "traffic": TRAFFIC.get("compressor"),
+                     "traffic_unit": "bytes per launch (ncu)"},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_compressor(h, n_groups=max(1, args.cpu_sample))
+    return out
+
+
+def cpu_compressor(h, n_groups: int) -> dict:
+    """Oracle port on the host: latent + cache entry for the first n_groups groups of sequence 0."""
+    import numpy as np
+    import torch
+    from oracle import compressor as Cm
+    r = CP["ratio"]
+    n = min(n_groups, CP["S"] // r)
+    kv, gate = h[0][0:1, :n * r].numpy(), h[1][0:1, :n * r].numpy()
+    w = h[2].view(torch.int16).numpy().view(np.uint16)
+    cos, sin = h[3][0:1, :n].numpy(), h[4][0:1, :n].numpy()
+    t0 = time.perf_counter()
+    lat = Cm.latent_ref(kv, gate, w, 1e-6, r)
+    Cm.cache_ref(lat, cos, sin)
+    dt = time.perf_counter() - t0
+    return {"value": cp_bytes(1) * n / (CP["S"] // r) / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} groups of sequence 0, numpy, {dt:.2f} s"}
+
+
+def reference_compressor(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    h = cp_inputs(torch, seed=0, B=1)
+    vals = []
+    for i in range(args.warmup + args.steps):
+        r = cpu_compressor(h, n_groups=max(1, args.cpu_sample))
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.mean(vals)
+    r["value"] = v
+    return {"metric": "compressor producer step HBM GB/s (algorithmic bytes)", "value": v, "unit": "GB/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": cp_bytes(CP["B"]) / (v * 1e9) * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
+            "config": {"workload": "F3 compressor: gated softmax pool + RMSNorm + RoPE + MXFP4 cache entry",
+                       "B": CP["B"], "tokens": CP["S"], "compress_ratio": CP["ratio"], "head_dim": CP["D"],
+                       "rope_dim": CP["rope"]},
+            "cpu_baseline": r, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
            "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode),
-           "candidates": (bench_candidates, reference_candidates)}
+           "candidates": (bench_candidates, reference_candidates),
+           "compressor": (bench_compressor, reference_compressor)}
 
 
 def main():
@@ -1043,6 +1177,7 @@ def main():
         C5.update(B=1, S=2048)
         C4.update(B=8)
         CF.update(rows=256)
+        CP.update(B=1, S=4096)
         args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 

@@ -208,6 +208,21 @@ MZB_API int mzb_candidate_blocks(const float* logits, const int32_t* compress_le
 MZB_API int mzb_candidate_topk(const float* scores, const int32_t* blocks, const uint8_t* mask, int64_t rows,
                                int64_t T, int block_size, int nblk, int topk, int32_t* out, void* stream);
 
+/* mzb_compress -- replaces the elementwise part of `DeepseekV41Compressor.forward`
+ *   (src/mzoo/archs/dsv4/modeling_deepseek_v41.py:318-340) and of the compressed-cache
+ *   write (:745-753): per group of `ratio` tokens, latent = sum_r kv_r softmax_r(gate_r) (fp32),
+ *   cast to bf16, RMSNorm (:58-63; x * rsqrt(mean(x^2) + eps) -> bf16, times the bf16
+ *   weight) -> `latent` bf16 [B, G, D] (the pre-RoPE latent); optionally `cache` bf16
+ *   [B, G, D] = _fake_quant_fp4_block(apply_rotary_pos_emb(latent, cos, sin), 16,
+ *   e4m3_scales=True) (:405-425, :753).  kv, gate fp32 [B, G*ratio, D] (the projections;
+ *   gate NULL at ratio 1, where the latent is kv itself); norm_w bf16 [D]; cos, sin fp32
+ *   [B, G, rope_dim/2] (needed with `cache`).  D a multiple of 16, at most 4096; rope_dim a
+ *   multiple of 4; kv / gate 16-byte aligned, the bf16 buffers 8-byte aligned.
+ */
+MZB_API int mzb_compress(const float* kv, const float* gate, const void* norm_w, const float* cos_v,
+                         const float* sin_v, void* latent, void* cache, int64_t B, int64_t G, int ratio, int D,
+                         int rope_dim, float eps, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

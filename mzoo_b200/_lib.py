@@ -51,6 +51,7 @@ SIGNATURES = {
                                    _I32, _I32, _F32, _P, _P],
     "mzb_candidate_blocks": [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _P],
     "mzb_candidate_topk": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
+    "mzb_compress": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _F32, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

@@ -268,3 +268,29 @@ def candidate_topk(scores: torch.Tensor, blocks: torch.Tensor | None, mask: torc
 @candidate_topk.register_fake
 def _(scores, blocks, mask, block_size, topk):
     return scores.new_empty((scores.shape[0], topk), dtype=torch.int32)
+
+
+# ----------------------------------------------------------------------------- compressor producer step
+
+@torch.library.custom_op("mzb::compress", mutates_args=())
+def compress(kv: torch.Tensor, gate: torch.Tensor | None, norm_w: torch.Tensor, cos: torch.Tensor | None,
+             sin: torch.Tensor | None, ratio: int, rope_dim: int, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(latent bf16 [B,G,D], cache bf16 [B,G,D] or [0]) of ``mzb_compress`` (kv / gate fp32
+    [B, G*ratio, D] contiguous; cos / sin fp32 [B, G, rope_dim/2] or None: no cache entry)."""
+    B, N, D = kv.shape
+    G = N // ratio
+    dev = kv.device
+    latent = torch.empty(B, G, D, dtype=torch.bfloat16, device=dev)
+    want = cos is not None
+    cache = torch.empty((B, G, D) if want else (0,), dtype=torch.bfloat16, device=dev)
+    call("mzb_compress", ptr(kv), ptr(gate), ptr(norm_w), ptr(cos), ptr(sin), ptr(latent), ptr(cache) if want else None,
+         B, G, ratio, D, rope_dim, eps, stream_ptr(dev))
+    return latent, cache
+
+
+@compress.register_fake
+def _(kv, gate, norm_w, cos, sin, ratio, rope_dim, eps):
+    B, N, D = kv.shape
+    G = N // ratio
+    return (kv.new_empty((B, G, D), dtype=torch.bfloat16),
+            kv.new_empty((B, G, D) if cos is not None else (0,), dtype=torch.bfloat16))

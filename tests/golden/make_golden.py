@@ -168,6 +168,54 @@ def make_candidates() -> None:
     np.savez_compressed(os.path.join(HERE, "candidates.npz"), **out)
 
 
+def make_compressor() -> None:
+    """The reference's own ``DeepseekV41Compressor`` (modeling_deepseek_v41.py:295-340, bf16
+    module), ``apply_rotary_pos_emb`` (:405-425) and ``_fake_quant_fp4_block(..., 16,
+    e4m3_scales=True)`` (:753) on seeded inputs; the fp32 projections kv / gate are stored as
+    the kernel's inputs (the same F.linear calls the module makes)."""
+    from types import SimpleNamespace  # noqa: E402
+
+    import torch.nn.functional as F  # noqa: E402
+    from mzoo.archs.dsv4.modeling_deepseek_v41 import (  # noqa: E402
+        DeepseekV41Compressor, _fake_quant_fp4_block, apply_rotary_pos_emb)
+    out = {}
+    g = torch.Generator().manual_seed(4)
+    # (batch, tokens, hidden, head_dim, rope_dim, ratio): tokens past the last full group dropped
+    cases = [(2, 42, 256, 576, 64, 4), (1, 24, 128, 128, 32, 1), (2, 33, 192, 96, 16, 8)]
+    for c, (b, s, hid, d, rd, ratio) in enumerate(cases):
+        cfg = SimpleNamespace(compress_ratios=[ratio], head_dim=d, hidden_size=hid, rms_norm_eps=1e-6)
+        m = DeepseekV41Compressor(cfg, 0)
+        with torch.no_grad():
+            m.wkv.weight.copy_(torch.randn(d, hid, generator=g) * hid**-0.5)
+            if m.wgate is not None:
+                m.wgate.weight.copy_(torch.randn(d, hid, generator=g) * hid**-0.5)
+            m.norm.weight.copy_(1.0 + 0.25 * torch.randn(d, generator=g))
+        m = m.to(torch.bfloat16)
+        hs = torch.randn(b, s, hid, generator=g).to(torch.bfloat16)
+        with torch.no_grad():
+            latent, _ = m(hs, None)
+            usable = (s // ratio) * ratio
+            if ratio > 1:
+                kv = F.linear(hs.float(), m.wkv.weight.float())[:, :usable]
+                gate = F.linear(hs.float(), m.wgate.weight.float())[:, :usable]
+            else:  # no pooling: the projection in the model dtype
+                kv, gate = m.wkv(hs).float(), None
+            G = latent.shape[1]
+            ang = torch.rand(b, G, rd // 2, generator=g) * 6.0
+            cos, sin = ang.cos(), ang.sin()
+            rotated = apply_rotary_pos_emb(latent, cos, sin)
+            cache = _fake_quant_fp4_block(rotated, block_size=16, e4m3_scales=True)
+        key = f"c{c}."
+        out[key + "kv"] = kv.numpy()
+        if gate is not None:
+            out[key + "gate"] = gate.numpy()
+        out[key + "norm_w"] = bits(m.norm.weight.detach())
+        out[key + "cos"], out[key + "sin"] = cos.numpy(), sin.numpy()
+        out[key + "latent"], out[key + "rotated"], out[key + "cache"] = bits(latent), bits(rotated), bits(cache)
+        out[key + "params"] = np.array([ratio, rd], np.int64)
+    np.savez_compressed(os.path.join(HERE, "compressor.npz"), **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
     quant, golden_ref = _ref()
@@ -180,4 +228,6 @@ if __name__ == "__main__":
         make_indexer(golden_ref)
     if not only or "candidates" in only:
         make_candidates()
+    if not only or "compressor" in only:
+        make_compressor()
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))

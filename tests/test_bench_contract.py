@@ -16,7 +16,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("config", ["indexer", "prefill", "decode", "train", "candidates"])
+@pytest.mark.parametrize("config", ["indexer", "prefill", "decode", "train", "candidates", "compressor"])
 def test_reference_arm_json_line(config):
     cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", config,
            "--steps", "1", "--warmup", "1", "--cpu-sample", "64"]
