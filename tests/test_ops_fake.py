@@ -10,7 +10,7 @@ M = dict(device="meta")
 
 def test_all_ops_registered():
     names = {"fq_fp4", "fq_fp8", "indexer_scores", "indexer_topk", "indexer_bwd", "attn_fwd", "attn_bwd",
-             "sparse_mla_fwd", "candidate_blocks", "candidate_topk"}
+             "sparse_mla_fwd", "candidate_blocks", "candidate_topk", "compress"}
     assert names <= set(dir(torch.ops.mzb))
 
 
@@ -52,3 +52,9 @@ def test_fake_shapes():
     assert torch.ops.mzb.candidate_blocks(lg, cl, 16, 8, False)[1].shape == (0,)
     top = torch.ops.mzb.candidate_topk(lg, blocks, None, 8, 24)
     assert top.shape == (12, 24) and top.dtype == torch.int32
+    kv = torch.empty(2, 40, 576, dtype=torch.float32, **M)
+    nw = torch.empty(576, dtype=torch.bfloat16, **M)
+    cs = torch.empty(2, 10, 32, dtype=torch.float32, **M)
+    lat, cache = torch.ops.mzb.compress(kv, kv, nw, cs, cs, 4, 64, 1e-6)
+    assert lat.shape == (2, 10, 576) and cache.shape == (2, 10, 576) and lat.dtype == torch.bfloat16
+    assert torch.ops.mzb.compress(kv, kv, nw, None, None, 4, 0, 1e-6)[1].shape == (0,)
