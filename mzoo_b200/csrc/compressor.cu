@@ -16,7 +16,9 @@
 //
 // One CTA per group (batch, g); thread t owns channels [4t, 4t + 4) (16-byte loads of every
 // token row of the group), so a rope pair and a quarter of a 16-channel quant block stay in
-// one thread.  The softmax uses expf and a division, as torch's; the RMS variance is a CTA
+// one thread.  Groups of up to RMAX tokens load all their kv and gate rows into registers
+// first (one DRAM round trip); longer groups loop over the rows three times (max, sum,
+// weighted sum; the later passes hit L1).  The softmax uses expf and a division, as torch's; the RMS variance is a CTA
 // reduction in fp32.  Rope and fake quant use explicitly rounded operations, so they are
 // bit-exact given the bf16 latent.  Model dtype bf16 (latent, weight, outputs).
 #include "common.cuh"
@@ -25,6 +27,7 @@ namespace mzb {
 namespace comp {
 
 constexpr int MAXT = 1024;
+constexpr int RMAX = 4;  // groups up to this many tokens keep all their rows in registers
 
 __device__ __forceinline__ float bf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
@@ -53,6 +56,35 @@ __global__ void __launch_bounds__(MAXT) compress_kernel(Args a) {
     if (a.gate == nullptr) {
       const float4 x = *reinterpret_cast<const float4*>(a.kv + tok0 * a.D + c0);
       v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+    } else if (a.ratio <= RMAX) {
+      // short groups: every row of kv and gate loaded up front (one DRAM round trip), then
+      // the same operations in the same order as the general path below
+      float4 gr[RMAX], kr[RMAX];
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r) {
+        if (r < a.ratio) {
+          gr[r] = *reinterpret_cast<const float4*>(a.gate + (tok0 + r) * a.D + c0);
+          kr[r] = *reinterpret_cast<const float4*>(a.kv + (tok0 + r) * a.D + c0);
+        }
+      }
+      float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY}, s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r)
+        if (r < a.ratio) {
+          m[0] = fmaxf(m[0], gr[r].x); m[1] = fmaxf(m[1], gr[r].y); m[2] = fmaxf(m[2], gr[r].z); m[3] = fmaxf(m[3], gr[r].w);
+        }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r)
+        if (r < a.ratio) {
+          s[0] += expf(gr[r].x - m[0]); s[1] += expf(gr[r].y - m[1]); s[2] += expf(gr[r].z - m[2]); s[3] += expf(gr[r].w - m[3]);
+        }
+#pragma unroll
+      for (int r = 0; r < RMAX; ++r)
+        if (r < a.ratio) {
+          const float gg[4] = {gr[r].x, gr[r].y, gr[r].z, gr[r].w}, kk[4] = {kr[r].x, kr[r].y, kr[r].z, kr[r].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[j] = __fadd_rn(v[j], __fmul_rn(kk[j], expf(gg[j] - m[j]) / s[j]));
+        }
     } else {
       // softmax over the group's tokens per channel: max, exp(g - max), sum, divide
       float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
