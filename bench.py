@@ -9,14 +9,24 @@ distributions -- there is no dataset):
 - ``indexer`` (default, configs[1]): lightning indexer + top-512 over FP8 q/k, B=2,
   4096 queries at absolute positions 12288..16383 x 4096 compressed keys (ratio 4),
   Hi=64, Di=128.  Metric: indexer Mq/s (queries per second, whole job).
+- ``prefill``: sparse latent MQA over FP8 576/512 rows, 16384 tokens x 128
+  heads, top-2048 compressed entries + a 128-token window.  Metric: TFLOP/s.
+- ``decode``: paged decode of 128 sequences (lengths 8k..131k), decode indexer
+  + top-2048 + window 128.  Metric: algorithmic HBM GB/s.
+- ``train``: window attention training step, B=4, S=8192, 64 heads, D=128,
+  window 512, MXFP4 / FP8 fake quant of q, k, v.  Metric: TFLOP/s.
+- ``candidates`` (next row F1, not a BASELINE config): two-level indexer selection, 2048
+  queries x 65536 compressed positions.  Metric: Mq/s.
+- ``compressor`` (next row F3, not a BASELINE config): compressor pool + RMSNorm + RoPE +
+  MXFP4 cache entry, 8 x 16384 tokens at ratio 4, 576 channels.  Metric: algorithmic HBM GB/s.
 
 A "step" is one pass of the hot path over one batch.  ``value`` times the device path with
 inputs resident in HBM (L2 flushed with a 256 MB write before every timed step);
 ``e2e`` times the public API call with pinned host inputs, host->device copies, the
 kernels and the device->host copy of the result inside the timed region.  Multi-GPU:
-one process per GPU (torchrun); the indexer, prefill and decode configs split one
-workload's independent units (query chunks, token chunks, sequences) over the ranks with
-no data-path collective (strong scaling), the training config runs one instance per rank
+one process per GPU (torchrun); the indexer, prefill, decode, candidates and compressor
+configs split one workload's independent units (query chunks, token chunks, sequences,
+query rows, sequences) over the ranks with no data-path collective (strong scaling), the training config runs one instance per rank
 (weak scaling); timing is the max over ranks of CUDA-event time.
 
 ``--impl reference`` times the reference's CPU path (the numpy restatement in
