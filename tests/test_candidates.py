@@ -58,6 +58,35 @@ def test_oracle_pins_newest_block_and_drops_unreachable():
     assert np.array_equal(C.candidate_blocks_ref(logits, np.array([5]), 1, 2), [[2]])
 
 
+def test_oracle_tie_rule_brute_force():
+    """The reference's fixtures hold no ties; check the oracle's lower-index rule against a
+    plain-Python restatement on coarse (tie-heavy) rows, with -inf and pinned blocks."""
+    rng = np.random.default_rng(21)
+    for _ in range(60):
+        T, bs = int(rng.integers(1, 60)), int(rng.integers(1, 6))
+        tb, topk = int(rng.integers(1, 8)), int(rng.integers(1, 12))
+        clen = int(rng.integers(0, T + 3))
+        row = np.round(rng.standard_normal(T) * 2) / 2
+        row[np.arange(T) >= clen] = -np.inf
+        logits = row.astype(np.float32)[None]
+        nb = -(-T // bs)
+        score = [max([float(logits[0, t]) for t in range(b * bs, min(T, b * bs + bs))]) for b in range(nb)]
+        last = (clen - 1) // bs
+        if 0 <= last < nb:
+            score[last] = float("inf")
+        order = sorted(range(nb), key=lambda b: (-score[b], b))[:min(tb, nb)]
+        picks = sorted(b for b in order if score[b] > float("-inf"))
+        want = picks + [-1] * (tb - len(picks))
+        assert C.candidate_blocks_ref(logits, np.array([clen]), tb, bs).tolist() == [want]
+        mask = C.candidate_mask_ref(logits, np.array([clen]), tb, bs)
+        s2 = (np.round(rng.standard_normal(T) * 2) / 2).astype(np.float32)[None]
+        vals = [float(s2[0, t]) if mask[0, t] else float("-inf") for t in range(T)]
+        order = sorted(range(T), key=lambda t: (-vals[t], t))[:min(topk, T)]
+        picks = sorted(t for t in order if vals[t] > float("-inf"))
+        want = picks + [-1] * (min(topk, T) - len(picks))
+        assert C.candidate_topk_ref(s2, mask, topk).tolist() == [want]
+
+
 # ----------------------------------------------------------------------------- GPU: kernels
 
 def _rand_case(rng, rows, T, ratio, off, ties=False):
