@@ -6,11 +6,13 @@
 Configs (BASELINE.json ``configs``; synthetic seeded inputs with the stated shapes and
 distributions -- there is no dataset):
 
-- ``indexer`` (default, configs[1]): lightning indexer + top-512 over FP8 q/k, B=2,
-  4096 queries at absolute positions 12288..16383 x 4096 compressed keys (ratio 4),
-  Hi=64, Di=128.  Metric: indexer Mq/s (queries per second, whole job).
-- ``prefill``: sparse latent MQA over FP8 576/512 rows, 16384 tokens x 128
-  heads, top-2048 compressed entries + a 128-token window.  Metric: TFLOP/s.
+- ``prefill`` (default, configs[2]): sparse latent MQA over FP8 576/512 rows, 16384 tokens x
+  128 heads, top-2048 compressed entries + a 128-token window.  Metric: TFLOP/s.
+- ``window``: sliding-window MQA forward, B=1, S=2048, 16 heads, D=128,
+  window 128, fp32 inputs and outputs.  Metric: TFLOP/s.
+- ``indexer``: lightning indexer + top-512 over FP8 q/k, B=2, 4096 queries at
+  absolute positions 12288..16383 x 4096 compressed keys (ratio 4), Hi=64, Di=128.
+  Metric: indexer Mq/s (queries per second, whole job).
 - ``decode``: paged decode of 128 sequences (lengths 8k..131k), decode indexer
   + top-2048 + window 128.  Metric: algorithmic HBM GB/s.
 - ``train``: window attention training step, B=4, S=8192, 64 heads, D=128,
@@ -26,12 +28,18 @@ inputs resident in HBM (L2 flushed with a 256 MB write before every timed step);
 kernels and the device->host copy of the result inside the timed region.  Multi-GPU:
 one process per GPU (torchrun); the indexer, prefill, decode, candidates and compressor
 configs split one workload's independent units (query chunks, token chunks, sequences,
-query rows, sequences) over the ranks with no data-path collective (strong scaling), the training config runs one instance per rank
-(weak scaling); timing is the max over ranks of CUDA-event time.
+query rows, sequences) over the ranks with no data-path collective (strong scaling), the
+window and training configs run one instance per rank (weak scaling); timing is the max
+over ranks of CUDA-event time.
 
-``--impl reference`` times the reference's CPU path (the numpy restatement in
-``oracle/``; the reference itself is Python and cannot travel to the GPU host) on a
-bounded sample of the same workload, with all host threads, and prints the same metric.
+``--impl reference`` times the reference's CPU arithmetic -- its float32 PyTorch path
+(``golden_ref.py``, ``quant.py``) as restated in ``oracle/torch_ref.py``; the reference
+itself is Python and cannot travel to the GPU host -- on the host cores (all threads), one
+bounded sample of the same workload per step (stated in ``cpu_baseline.sample``; the
+printed ``ms_per_step`` is the time of that sample, ``value`` the metric over it), with the
+same ``config`` as this build's line.  The ``cpu_baseline`` of this build's line (rank 0,
+one GPU) times the same sample once and compares the GPU's rows for it with the CPU result
+(``cpu_baseline.parity``).
 """
 
 import argparse
@@ -131,9 +139,10 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
-# DRAM bytes (read + write) of one full-size launch of each config's roofline kernel, from a
-# one-pass ncu capture of this build (dram__bytes_read.sum + dram__bytes_write.sum).
-TRAFFIC = {
+# DRAM bytes (read + write) of one full-size launch of each config's roofline kernel at one
+# GPU, from a one-pass ncu capture of this build (dram__bytes_read.sum + dram__bytes_write.sum).
+# A rank of a multi-GPU run reports it scaled by its share of the work (``traffic_for``).
+TRAFFIC_N1 = {
     "indexer": 72764928 + 69933824,
     "prefill": 2535907584 + 2112252416,
     "decode": 313127680 + 10324480,
@@ -141,6 +150,24 @@ TRAFFIC = {
     "candidates": 381950464 + 3411200,  # level two (gathered): 32-byte blocks cost ~2.8x in DRAM bursts
     "compressor": 612400896 + 68001536,
 }
+
+
+def traffic_for(name: str, share: float) -> dict:
+    """The roofline's ``traffic`` fields: the N=1 capture scaled by this rank's share of the
+    job's algorithmic work (1.0 at one GPU)."""
+    t = TRAFFIC_N1.get(name)
+    if t is None:
+        return {"traffic": None}
+    note = "bytes per launch (ncu one-pass capture, full-size workload, 1 GPU)"
+    if abs(share - 1.0) > 1e-9:
+        note += f", scaled by this rank's {share:.4f} share of the work"
+    return {"traffic": t * share, "traffic_unit": note}
+
+
+def cpu_threads(torch) -> int:
+    """All host threads for the CPU arms."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    return torch.get_num_threads()
 
 
 # ----------------------------------------------------------------------------- timing helpers
@@ -178,6 +205,132 @@ def max_over_ranks(torch, dist, value: float, device) -> float:
     return float(t.item())
 
 
+# ----------------------------------------------------------------------------- window attention (C1)
+
+C1 = dict(B=1, S=2048, H=16, D=128, window=128)
+
+
+def c1_flops() -> float:
+    """Algorithmic forward FLOPs: 4 * B * H * D * sum_t min(t + 1, window)."""
+    band = sum(min(t + 1, C1["window"]) for t in range(C1["S"]))
+    return 4.0 * C1["B"] * C1["H"] * C1["D"] * band
+
+
+def c1_inputs(torch, seed: int = 0):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(C1["B"], C1["S"], C1["H"], C1["D"], generator=g)
+    kv = torch.randn(C1["B"], C1["S"], 1, C1["D"], generator=g)
+    return q, kv
+
+
+def c1_config(world: int) -> dict:
+    return {"workload": "C1 sliding-window MQA forward", "B": C1["B"], "S": C1["S"], "heads": C1["H"],
+            "head_dim": C1["D"], "window": C1["window"], "inputs": "fp32 q / kv, fp32 o + lse out",
+            "parallelism": f"x{world} independent" if world > 1 else "1 GPU",
+            "l2": "256 MB flush per step"}
+
+
+def bench_window(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import swa_attn
+    qh, kvh = c1_inputs(torch)
+    q, kv = qh.to(device), kvh.to(device)
+    W = C1["window"]
+
+    def step():  # fp32 in, bf16 kernel, fp32 out (o; lse is fp32 already)
+        o, lse = swa_attn.fwd(q.to(torch.bfloat16), kv.to(torch.bfloat16), window=W)
+        return o.float(), lse
+
+    timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler.ready()
+    if dist:
+        dist.barrier()
+    t_steps = timer.run(step, args.steps)
+    clocks = sampler.stop(busy=step, min_samples=2)
+    qb, kvb = q.to(torch.bfloat16), kv.to(torch.bfloat16)
+    t_k = timer.run(lambda: swa_attn.fwd(qb, kvb, window=W), args.steps)
+    hq, hkv = qh.pin_memory(), kvh.pin_memory()
+    dq, dkv = torch.empty_like(q), torch.empty_like(kv)
+    ho = torch.empty(qh.shape, dtype=torch.float32).pin_memory()
+    hl = torch.empty(C1["B"], C1["H"], C1["S"], dtype=torch.float32).pin_memory()
+
+    def e2e():
+        dq.copy_(hq, non_blocking=True)
+        dkv.copy_(hkv, non_blocking=True)
+        o, lse = swa_attn.fwd(dq.to(torch.bfloat16), dkv.to(torch.bfloat16), window=W)
+        ho.copy_(o, non_blocking=True)  # bf16 -> fp32 on the copy
+        hl.copy_(lse, non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    o_gpu, lse_gpu = step()
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_k = sum(t_k) / len(t_k)
+    flops = c1_flops()
+    pk = peaks()
+    ach = flops / (ms_k * 1e-3) / 1e12
+    out = {
+        "metric": "sliding-window MQA forward TFLOP/s", "value": flops * world / (ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 (fp32 inputs cast on the device, fp32 acc)", "data": "synthetic (seeded N(0,1) fp32)",
+        "config": c1_config(world),
+        "e2e": {"value": flops * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": (hq.numel() + hkv.numel()) * 4,
+                "d2h_bytes_per_step": (ho.numel() + hl.numel()) * 4},
+        "roofline": {"bound": "tensor", "kernel": "mzb::attn::attn_fwd_kernel<128>", "achieved": ach,
+                     "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+                     "peak_note": f"{pk['_source']} bf16 burst; 2 GFLOP per launch is latency-bound, not "
+                                  "tensor-bound", "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_k,
+                     "traffic": None},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_window(torch, qh, kvh)
+        ro, rl = r.pop("result")
+        eo = (o_gpu.cpu() - ro).abs().max().item()
+        el = (lse_gpu.cpu() - rl).abs().max().item()
+        r["parity"] = {"rows": "all", "max_abs_err_o": eo, "max_abs_err_lse": el, "atol": 2e-2,
+                       "ok": bool(eo <= 2e-2 and el <= 2e-2),
+                       "note": "GPU output (bf16 kernel) vs the CPU float32 reference on the whole config"}
+        out["cpu_baseline"] = r
+    return out
+
+
+def cpu_window(torch, q, kv) -> dict:
+    """The reference's CPU path for this config, ``golden(q, kv, level="window", window=128)``
+    (its float32 ``_attend`` with the band mask), on the whole config, all host threads."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    t0 = time.perf_counter()
+    o, lse = R.window_attention(q, kv, C1["window"])
+    dt = time.perf_counter() - t0
+    return {"value": c1_flops() / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"the whole config: torch float32 golden(level='window') arithmetic (dense masked "
+                      f"_attend), {dt:.3f} s; FLOPs counted for the visible band only",
+            "result": (o, lse)}
+
+
+def reference_window(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    q, kv = c1_inputs(torch)
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_window(torch, q, kv)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "sliding-window MQA forward TFLOP/s", "TFLOP/s", c1_config(world), runs,
+                           "f32 (reference CPU path)", "synthetic (seeded N(0,1) fp32)", scaling="weak")
+
+
 # ----------------------------------------------------------------------------- indexer (C2)
 
 C2 = dict(B=2, S=4096, T=4096, Hi=64, Di=128, ratio=4, topk=512, q_offset=12288)
@@ -197,8 +350,17 @@ def c2_inputs(torch, seed: int):
     return q, k, w
 
 
+def c2_config(world: int) -> dict:
+    return {"workload": "C2 lightning indexer + top-k", "B": C2["B"], "queries": C2["S"], "keys": C2["T"],
+            "Hi": C2["Hi"], "Di": C2["Di"], "compress_ratio": C2["ratio"], "topk": C2["topk"],
+            "q_offset": C2["q_offset"],
+            "parallelism": (f"(batch x 128-query chunk) units cyclic over {world} GPUs, keys replicated, no "
+                            "collective in the step" if world > 1 else "1 GPU"),
+            "l2": "flushed (256 MB write) per step"}
+
+
 def bench_indexer(args, torch, dist, rank, world, device) -> dict:
-    from mzoo_b200 import indexer, _lib
+    from mzoo_b200 import indexer
 
     from mzoo_b200.sharding import shard_tokens
     q, k, w = c2_inputs(torch, seed=0)  # the same workload on every rank
@@ -206,7 +368,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     k8, sk = indexer.quantize_fp8(k.to(device))
     w = w.to(device)
     B, S, T, Hi, Di = (C2[x] for x in ("B", "S", "T", "Hi", "Di"))
-    kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk), check=False)
+    kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk))
     toks = list(range(S))
     if world > 1:  # (batch x 128-query chunk) units, cyclic over ranks: the same chunks of every batch
         toks = shard_tokens(S, world, 128)[rank]
@@ -250,7 +412,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     t_e2e = timer.run(e2e, args.steps, flush=False)
     clocks = sampler.stop(busy=step)
     torch.cuda.synchronize()
-    indexer.attn(q8, k8, w, **dict(kw, check=True))  # one checked call: raises on a device error word
+    out_idx = indexer.attn(q8, k8, w, **dict(kw, check=True))  # one checked call: raises on a device error word
     h2d = sum(x.numel() * x.element_size() for x in (hq8, hk8, hsq, hsk, hw))
     d2h = hout.numel() * hout.element_size()
 
@@ -267,45 +429,77 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
         "metric": "indexer Mq/s", "value": queries / (ms * 1e-3) / 1e6, "unit": "Mq/s",
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3 (fp32 accumulate)", "data": "synthetic (seeded N(0,1), absmax fp8)",
-        "config": {"workload": "C2 lightning indexer + top-k", "B": B, "queries": S, "keys": T, "Hi": Hi, "Di": Di,
-                   "compress_ratio": C2["ratio"], "topk": C2["topk"], "q_offset": C2["q_offset"],
-                   "parallelism": (f"(batch x 128-query chunk) units cyclic over {world} GPUs, keys replicated, no "
-                                   "collective in the step" if world > 1 else "1 GPU"),
-                   "l2": "flushed (256 MB write) per step"},
+        "config": c2_config(world),
         "e2e": {"value": queries / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": "mzb::idx::score_kernel<fp8,128,2>", "achieved": achieved,
                      "peak": fp8_peak, "unit": "TFLOP/s", "frac": achieved / fp8_peak,
                      "peak_note": f"dense FP8 = 2 x {pk['_source']} bf16 burst {pk['bf16_tflops']} TFLOP/s",
                      "algorithmic_flops_per_launch": flops, "ms_per_launch": ms_score,
-                     "traffic": TRAFFIC["indexer"], "traffic_unit": "bytes per launch (ncu)"},
+                     **traffic_for("indexer", len(toks) / S)},
         "gpu_launches": 3 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_indexer(torch, q, k, w, sample=args.cpu_sample)
+        r = cpu_indexer(torch, q, k, w)
+        got = out_idx[0, C2["S"] - r.pop("n"):].cpu()
+        ref = r.pop("result")
+        r["parity"] = {"rows": int(got.shape[0]), "equal_sets": int(_set_equal_rows(torch, got, ref)),
+                       "note": "GPU index sets vs the CPU float32 reference's top-k sets on the sample rows"}
+        out["cpu_baseline"] = r
     return out
 
 
-def cpu_indexer(torch, q, k, w, sample: int) -> dict:
-    """Oracle port on the host: canonical fp64 scores + exact top-k for `sample` queries
-    (the last ones of batch 0, every key visible to most of them)."""
-    import numpy as np
-    from oracle import indexer as I
-    from oracle import quant as Q
-    qn = q[0:1, -sample:].numpy()
-    kn = k[0:1].numpy()
-    wn = w[0:1, -sample:].cpu().numpy()
-    qv, sq = Q.quantize_fp8_rows(qn, C2["Di"])
-    kv, sk = Q.quantize_fp8_rows(kn, C2["Di"])
-    off = C2["q_offset"] + C2["S"] - sample
+def _set_equal_rows(torch, a, b) -> int:
+    """Rows of two [rows, topk] index lists that hold the same set (-1 = empty)."""
+    big = 1 << 30
+    sa = torch.where(a < 0, big, a.long()).sort(-1).values
+    sb = torch.where(b < 0, big, b.long()).sort(-1).values
+    return int((sa == sb).all(-1).sum())
+
+
+def cpu_indexer(torch, q, k, w, n: int = 512) -> dict:
+    """The reference's float32 CPU path (``indexer_scores`` + ``topk_indices``) on the last
+    ``n`` queries of batch 0, with the FP8 inputs dequantised (q * s_q, k * s_k), all host
+    threads.  Returns the metric over the sample and the sample's index sets."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    q8, sq = _fp8_absmax_cpu(torch, q[0:1, -n:])
+    k8, sk = _fp8_absmax_cpu(torch, k[0:1])
+    off = C2["q_offset"] + C2["S"] - n
     t0 = time.perf_counter()
-    sc = I.canonical_scores(qv, kv, wn, sq[..., 0], sk[..., 0], C2["ratio"], off)
-    I.canonical_topk(sc, C2["topk"], C2["ratio"], off)
+    qd = q8.float() * sq.unsqueeze(-1)
+    kd = k8.float() * sk.unsqueeze(-1)
+    sc = R.indexer_scores(qd, kd, w[0:1, -n:], C2["ratio"], off, scale=1.0)
+    idx = R.topk_indices(sc, C2["topk"])
     dt = time.perf_counter() - t0
-    return {"value": sample / dt / 1e6, "unit": "Mq/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{sample} queries of batch 0 (positions {off}..{off + sample - 1}), numpy fp64 canonical "
-                      f"scores + top-{C2['topk']}, {dt:.2f} s"}
+    return {"value": n / dt / 1e6, "unit": "Mq/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"{n} queries of batch 0 (positions {off}..{off + n - 1}) x {C2['T']} keys: torch float32 "
+                      f"indexer_scores + topk_indices (the reference's CPU arithmetic), {dt:.2f} s",
+            "n": n, "result": idx[0]}
+
+
+def _fp8_absmax_cpu(torch, x):
+    """Absmax e4m3 codes and fp32 scales per row of the last dim (the synthetic inputs' rule)."""
+    xf = x.float()
+    amax = xf.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    return (xf / scale.unsqueeze(-1)).clamp(-448, 448).to(torch.float8_e4m3fn), scale
+
+
+def _reference_line(args, world, metric, unit, cfg, runs, dtype, data, scaling="strong") -> dict:
+    """The reference arm's JSON line from per-step CPU-sample results ``runs`` (the last
+    ``args.steps`` are timed; ``ms_per_step`` is the sample's own time)."""
+    timed = runs[args.warmup:]
+    v = statistics.mean(r["value"] for r in timed)
+    ms = statistics.mean(r["ms"] for r in timed)
+    cb = {k: timed[-1][k] for k in ("unit", "cores", "kind", "sample")}
+    cb["value"] = v
+    return {"metric": metric, "value": v, "unit": unit, "impl": "reference", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None,
+            "dtype": dtype, "data": data, "config": cfg, "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def reference_indexer(args, rank, world) -> dict:
@@ -313,22 +507,14 @@ def reference_indexer(args, rank, world) -> dict:
     if rank != 0:
         return None
     q, k, w = c2_inputs(torch, seed=0)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_indexer(torch, q, k, w, sample=min(args.cpu_sample // 4, 1024))
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
-    r["value"] = v
-    return {"metric": "indexer Mq/s", "value": v, "unit": "Mq/s", "impl": "reference", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": C2["B"] * C2["S"] / (v * 1e6) * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (oracle port)",
-            "data": "synthetic (seeded N(0,1), absmax fp8)",
-            "config": {"workload": "C2 lightning indexer + top-k", "B": C2["B"], "queries": C2["S"], "keys": C2["T"],
-                       "Hi": C2["Hi"], "Di": C2["Di"], "compress_ratio": C2["ratio"], "topk": C2["topk"],
-                       "q_offset": C2["q_offset"]},
-            "cpu_baseline": r,
-            "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_indexer(torch, q, k, w)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "indexer Mq/s", "Mq/s", c2_config(world), runs,
+                           "f32 (reference CPU arithmetic, FP8 inputs dequantised)",
+                           "synthetic (seeded N(0,1), absmax fp8)")
 
 
 # ----------------------------------------------------------------------------- sparse MLA prefill (C3)
@@ -336,15 +522,19 @@ def reference_indexer(args, rank, world) -> dict:
 C3 = dict(B=1, S=16384, H=128, G=4096, ratio=4, topk=2048, window=128)
 
 
-def sorted_causal_indices(torch, S, G, topk, ratio, gen, device, q_offset=0, chunk=2048):
+def sorted_causal_indices(torch, S, G, topk, ratio, gen, device, q_offset=0, chunk=2048, positions=None):
     """Per query t: seeded random distinct compressed indices from [0, (t+q_offset+1)//ratio),
-    the first topk of a random permutation, sorted ascending, -1 padded."""
+    the first topk of a random permutation, sorted ascending, -1 padded.  ``positions``
+    (a list) gives the query positions explicitly instead of q_offset..q_offset+S-1."""
+    pos_all = (torch.arange(S, device=device) + q_offset if positions is None
+               else torch.tensor(positions, device=device))
+    S = pos_all.shape[0]
     out = torch.empty(S, topk, dtype=torch.int32, device=device)
     cols = torch.arange(G, device=device)
     for s0 in range(0, S, chunk):
         s1 = min(S, s0 + chunk)
         r = torch.rand(s1 - s0, G, generator=gen, device=device)
-        vis = (torch.arange(s0, s1, device=device) + q_offset + 1) // ratio
+        vis = (pos_all[s0:s1] + 1) // ratio
         r.masked_fill_(cols[None, :] >= vis[:, None], 2.0)
         vals, ind = r.topk(topk, dim=1, largest=False)
         ind = torch.where(vals < 2.0, ind, torch.full_like(ind, 1 << 30)).sort(dim=1).values
@@ -372,12 +562,21 @@ def c3_pairs(torch, idx, positions=None) -> int:
     return int((idx >= 0).sum().item()) + win
 
 
+def c3_config(world: int) -> dict:
+    return {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": C3["S"], "heads": C3["H"], "d_qk": 576,
+            "d_v": 512, "topk": C3["topk"], "window": C3["window"], "compressed": C3["G"],
+            "parallelism": (f"query tokens sharded over {world} GPUs (cyclic 128-token chunks, KV replicated,"
+                            " no collective in the step)" if world > 1 else "1 GPU"),
+            "l2": "inputs (2.4 GB q) larger than L2; 256 MB flush per step"}
+
+
 def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     from mzoo_b200 import sparse_mla
     from mzoo_b200.sharding import shard_tokens
     q, raw, cmp, idx = c3_inputs(torch, device, seed=0)  # the same workload on every rank
     total_flops = sparse_mla.pair_flops(c3_pairs(torch, idx))
     pos, toks = None, None
+    q_full, idx_full = q, idx
     if world > 1:  # this rank's cyclic 128-token chunks of the query axis; KV replicated
         toks = shard_tokens(C3["S"], world, 128)[rank]
         tk = torch.tensor(toks, device=device)
@@ -385,7 +584,7 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
         pos = tk.to(torch.int32).view(1, -1)
     flops = sparse_mla.pair_flops(c3_pairs(torch, idx, toks))
     n_q = q.shape[1]
-    step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], q_pos=pos, check=False)  # noqa: E731
+    step = lambda: sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], q_pos=pos)  # noqa: E731
     timer = Timer(torch, device)
     sampler = ClockSampler(device.index)
     sampler.start()
@@ -406,7 +605,7 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     def e2e():
         for d, h in ((dq, hq), (draw, hraw), (dcmp, hcmp), (didx, hidx)):
             d.copy_(h, non_blocking=True)
-        o, lse = sparse_mla.prefill(dq, draw, dcmp, didx, window=C3["window"], q_pos=pos, check=False)
+        o, lse = sparse_mla.prefill(dq, draw, dcmp, didx, window=C3["window"], q_pos=pos)
         ho.copy_(o, non_blocking=True)
         hl.copy_(lse, non_blocking=True)
 
@@ -416,9 +615,9 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
     d2h = ho.numel() * ho.element_size() + hl.numel() * hl.element_size()
     ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
     ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    o_loc, lse_loc = sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], q_pos=pos, check=True)
     gather_ms = None
     if dist:  # optional output gather (o of every rank's shard to every rank), timed on its own
-        o_loc, _ = step()
         width = max(len(p) for p in shard_tokens(C3["S"], world, 128))
         pad = o_loc.new_zeros((width,) + tuple(o_loc.shape[2:]))
         pad[:n_q] = o_loc[0]
@@ -428,86 +627,100 @@ def bench_prefill(args, torch, dist, rank, world, device) -> dict:
         gather_ms = max_over_ranks(torch, dist, sum(t_g) / len(t_g), device)
     pk = peaks()
     tflops = total_flops / (ms * 1e-3) / 1e12
-    achieved = flops / (ms * 1e-3) / 1e12
+    ms_local = sum(t_steps) / len(t_steps)
+    achieved = flops / (ms_local * 1e-3) / 1e12
     out = {
         "metric": "sparse-MLA prefill TFLOP/s", "value": tflops, "unit": "TFLOP/s", "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "bf16 (fp8 KV dequant, fp32 acc)",
         "data": "synthetic (seeded N(0,1); FP8 no-rope rows with per-64 absmax scales)",
-        "config": {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": C3["S"], "heads": C3["H"],
-                   "d_qk": 576, "d_v": 512, "topk": C3["topk"], "window": C3["window"], "compressed": C3["G"],
-                   "total_flops": total_flops,
-                   "parallelism": (f"query tokens sharded over {world} GPUs (cyclic 128-token chunks, KV replicated,"
-                                   " no collective in the step)" if world > 1 else "1 GPU"),
-                   "o_gather_ms": gather_ms,
-                   "l2": "inputs (2.4 GB q) larger than L2; 256 MB flush per step"},
+        "config": c3_config(world),
+        "legs": {"total_flops": total_flops, "o_gather_ms": gather_ms},
         "e2e": {"value": total_flops / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": "mzb::mla::mla_fwd_kernel", "achieved": achieved,
                      "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / pk["bf16_tflops"],
                      "peak_note": f"{pk['_source']} bf16 burst", "algorithmic_flops_per_launch": flops,
-                     "ms_per_launch": ms, "traffic": TRAFFIC["prefill"],
-                     "traffic_unit": "bytes per launch (ncu)"},
+                     "ms_per_launch": ms_local, **traffic_for("prefill", flops / total_flops)},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        toks = _prefill_sample(C3["S"], max(8, args.cpu_sample // 9))
-        out["cpu_baseline"] = cpu_prefill(q[0, toks].float().cpu().numpy(), toks, raw[0].cpu().numpy(),
-                                          cmp[0].cpu().numpy(), idx[0, toks].cpu().numpy())
+        toks_s = _prefill_sample(C3["S"], 256)
+        tk = torch.tensor(toks_s, device=device)
+        r = cpu_prefill(torch, q_full[0, tk].cpu(), toks_s, raw[0].cpu(), cmp[0].cpu(), idx_full[0, tk].cpu())
+        ro, rl = r.pop("result")
+        eo = (o_loc[0, tk].float().cpu() - ro).abs().max().item()
+        el = (lse_loc[0, :, tk].cpu().T - rl).abs().max().item()
+        r["parity"] = {"tokens": len(toks_s), "max_abs_err_o": eo, "max_abs_err_lse": el, "atol": 2e-2,
+                       "ok": bool(eo <= 2e-2 and el <= 2e-2),
+                       "note": "GPU rows vs the CPU float32 reference on the sampled tokens"}
+        out["cpu_baseline"] = r
     return out
 
 
-def cpu_prefill(q_rows, toks, raw_rows, cmp_rows, idx_rows) -> dict:
-    """Oracle port: sparse attention for the sampled query tokens (all 128 heads), reported
-    as TFLOP/s of the sample's selected pairs (extrapolation to the full config is by
-    selected-pair count)."""
-    from oracle import mla as M
+def cpu_prefill(torch, q_rows, toks, raw_rows, cmp_rows, idx_rows, chunk: int = 32) -> dict:
+    """The reference's float32 CPU arithmetic (``_attend`` over each token's gathered rows:
+    the 128-token window then the listed compressed entries, rows dequantised from FP8) for
+    the sampled query tokens, all 128 heads, all host threads.  Metric: TFLOP/s of the
+    sample's selected pairs.  q_rows [n,128,576] bf16, raw_rows [S,672], cmp_rows [G,672],
+    idx_rows [n,topk] (CPU tensors)."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    n, W = len(toks), C3["window"]
+    S, G = raw_rows.shape[0], cmp_rows.shape[0]
     t0 = time.perf_counter()
-    pairs = 0
-    for i, t in enumerate(toks):
-        keys = M.unpack_rows(M.token_keys(raw_rows, cmp_rows, idx_rows[i], int(t), C3["window"]))
-        pairs += keys.shape[0]
-        M.attend_rows(q_rows[i], keys, 576**-0.5)
+    table = torch.cat([raw_rows, cmp_rows])           # compressed entry g is row S + g
+    pos = torch.tensor(toks).view(-1, 1)
+    wrow = pos - W + 1 + torch.arange(W).view(1, -1)   # window rows, -ve = empty
+    ci = idx_rows.long()
+    crow = torch.where((ci >= 0) & (ci < G), ci + S, torch.full_like(ci, -1))
+    rows = torch.cat([wrow.masked_fill(wrow < 0, -1), crow], 1)
+    counts = (rows >= 0).sum(1)
+    order = torch.sort((rows < 0).to(torch.int8), dim=1, stable=True).indices  # valid rows first, in order
+    rows = torch.gather(rows, 1, order)
+    o = torch.empty(n, 128, 512)
+    lse = torch.empty(n, 128)
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        tmax = int(counts[c0:c1].max())
+        keys = R.unpack_rows(table[rows[c0:c1, :tmax].clamp_min(0)])
+        o[c0:c1], lse[c0:c1] = R.gathered_attention(q_rows[c0:c1].float(), keys, counts[c0:c1], 576 ** -0.5)
     dt = time.perf_counter() - t0
+    pairs = int(counts.sum())
     flops = 2.0 * 128 * 1088 * pairs
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{len(toks)} evenly spaced query tokens x 128 heads ({pairs} selected pairs), numpy fp64, "
-                      f"{dt:.2f} s, extrapolated by selected-pair count"}
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"{n} evenly spaced query tokens x 128 heads ({pairs} selected pairs): torch float32 "
+                      f"_attend over the gathered, dequantised rows (the reference's CPU arithmetic), {dt:.2f} s",
+            "result": (o, lse)}
 
 
 def _prefill_sample(S, n_tok):
     import numpy as np
-    return [int(t) for t in np.linspace(S // n_tok, S - 1, n_tok)]
+    return [int(t) for t in np.linspace(0, S - 1, n_tok)]
 
 
 def reference_prefill(args, rank, world) -> dict:
     import torch
-    from oracle import mla as M
+    from oracle import torch_ref as R
     if rank != 0:
         return None
-    S = C3["S"]
-    n_tok = max(8, args.cpu_sample // 256)
-    toks = _prefill_sample(S, n_tok)
+    S, G = C3["S"], C3["G"]
+    toks = _prefill_sample(S, 256)
     g = torch.Generator().manual_seed(0)
-    q_rows = torch.randn(n_tok, 128, 576, generator=g).to(torch.bfloat16).float().numpy()
-    raw = M.pack_rows(torch.randn(S, 576, generator=g).numpy())
-    cmp = M.pack_rows(torch.randn(C3["G"], 576, generator=g).numpy())
-    idx = sorted_causal_indices(torch, S, C3["G"], C3["topk"], C3["ratio"], torch.Generator().manual_seed(1),
-                                torch.device("cpu"))[toks].numpy()
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_prefill(q_rows, toks, raw, cmp, idx)
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
-    r["value"] = v
-    return {"metric": "sparse-MLA prefill TFLOP/s", "value": v, "unit": "TFLOP/s", "impl": "reference",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
-            "config": {"workload": "C3 sparse latent-MQA prefill", "B": 1, "S": S, "heads": 128, "topk": C3["topk"],
-                       "window": C3["window"]},
-            "cpu_baseline": r, "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    q_rows = torch.randn(len(toks), 128, 576, generator=g).to(torch.bfloat16)
+    raw = R.pack_rows(torch.randn(S, 576, generator=g))
+    cmp = R.pack_rows(torch.randn(G, 576, generator=g))
+    idx = sorted_causal_indices(torch, 0, G, C3["topk"], C3["ratio"], torch.Generator().manual_seed(1),
+                                torch.device("cpu"), positions=toks)
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_prefill(torch, q_rows, toks, raw, cmp, idx)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "sparse-MLA prefill TFLOP/s", "TFLOP/s", c3_config(world), runs,
+                           "f32 (reference CPU arithmetic, FP8 KV dequantised)",
+                           "synthetic (seeded N(0,1); FP8 no-rope rows with per-64 absmax scales)")
 
 # ----------------------------------------------------------------------------- SWA train + fake quant (C5)
 
@@ -534,6 +747,12 @@ def c5_step(q, k, v, do):
     o, lse = swa_attn.fwd(qf, kf, window=C5["window"], v=vf)
     dq, dk, _, dv = swa_attn.bwd(qf, kf, o, lse, do, window=C5["window"], v=vf)
     return dq, dk, dv  # STE: gradients w.r.t. the pre-quant inputs
+
+
+def c5_config(world: int) -> dict:
+    return {"workload": "C5 SWA train + fake quant", "B": C5["B"], "S": C5["S"], "heads": C5["H"],
+            "head_dim": C5["D"], "window": C5["window"], "fq": "Q,K OCP MXFP4 block 32; V FP8 absmax per 128; STE",
+            "parallelism": f"x{world} independent" if world > 1 else "1 GPU", "l2": "256 MB flush per step"}
 
 
 def bench_train(args, torch, dist, rank, world, device) -> dict:
@@ -593,57 +812,69 @@ def bench_train(args, torch, dist, rank, world, device) -> dict:
         "metric": "SWA train fwd+bwd TFLOP/s (fake-quant Q/K MXFP4, V FP8)", "value": total * world / (ms * 1e-3) / 1e12,
         "unit": "TFLOP/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (fp32 acc)", "data": "synthetic (seeded N(0,1) bf16 inputs and dO)",
-        "config": {"workload": "C5 SWA train + fake quant", "B": B, "S": S, "heads": H, "head_dim": D, "window": W,
-                   "fq": "Q,K OCP MXFP4 block 32; V FP8 absmax per 128; STE", "parallelism": f"x{world} independent",
-                   "l2": "256 MB flush per step"},
+        "config": c5_config(world),
         "e2e": {"value": total * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "tensor", "kernel": "mzb::attnb::dkv_kernel + dq_kernel (backward)",
                      "achieved": ach_bwd, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": ach_bwd / pk["bf16_tflops"], "peak_note": f"{pk['_source']} bf16 burst",
-                     "algorithmic_flops_per_launch": bwd_flops, "ms_per_launch": ms_bwd,
-                     "traffic": TRAFFIC["train"], "traffic_unit": "bytes per launch (ncu, dkv + dq kernels)"},
+                     "algorithmic_flops_per_launch": bwd_flops, "ms_per_launch": ms_bwd, **traffic_for("train", 1.0)},
         "legs": {"fwd_ms": ms_fwd, "fwd_tflops": fwd_flops / (ms_fwd * 1e-3) / 1e12, "bwd_ms": ms_bwd,
                  "fq_q_ms": ms_fq, "fq_q_gbs": fq_bytes / (ms_fq * 1e-3) / 1e9},
         "gpu_launches": 7 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 2))
+        toks = _train_sample()
+        dq_gpu = c5_step(q, k, v, do)[0][0, torch.tensor(toks, device=device)].float().cpu()
+        r = cpu_train(torch, q[0, toks].cpu(), k[0, :, 0].cpu(), v[0, :, 0].cpu(), do[0, toks].cpu(), toks)
+        dq_ref = r.pop("result")
+        err = (dq_gpu - dq_ref).abs().max().item()
+        tol = 2e-2 + 1e-2 * dq_ref.abs().max().item()
+        r["parity"] = {"tokens": len(toks), "max_abs_err_dq": err, "tol": tol, "ok": bool(err <= tol),
+                       "note": "GPU dq rows vs the CPU float32 reference (STE fake quant + autograd) on the "
+                               "sampled tokens"}
+        out["cpu_baseline"] = r
     return out
 
 
-def cpu_train(q, k, v, do, n_tok: int) -> dict:
-    """Oracle port: fake quant + window attention fwd/bwd (fp64 numpy) for n_tok query tokens
-    of batch 0 (all 64 heads, full 512-key window each), as TFLOP/s of their band pairs."""
+def _train_sample(n: int = 512):
     import numpy as np
-    from oracle import quant as Q
-    S, W, D = C5["S"], C5["window"], C5["D"]
-    toks = [int(t) for t in np.linspace(W, S - 1, n_tok)]
-    qs = q[0].float().cpu().numpy()
-    ks = k[0, :, 0].float().cpu().numpy()
-    vs = v[0, :, 0].float().cpu().numpy()
-    dos = do[0].float().cpu().numpy().astype(np.float64)
+    return [int(t) for t in np.linspace(0, C5["S"] - 1, n)]
+
+
+def cpu_train(torch, q_rows, k_seq, v_seq, do_rows, toks) -> dict:
+    """The reference's float32 CPU arithmetic for the sampled query tokens of one sequence:
+    STE fake quant (``x - x.detach() + fq(x)``, ``indexer/attn.py:29-34``; Q, K OCP MXFP4 per
+    32, V FP8 absmax per 128), ``_attend`` over each token's window with autograd, backward
+    from dO.  q_rows / do_rows [n,H,D], k_seq / v_seq [S,D].  Metric: TFLOP/s of the sample's
+    band pairs (forward + 2.5x backward)."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    W, D = C5["window"], C5["D"]
+    n = len(toks)
     t0 = time.perf_counter()
-    pairs = 0
-    for t in toks:
-        lo = t - W + 1
-        qq = Q.fake_quant_fp4(qs[t], 32, "ocp").astype(np.float64)
-        kk = Q.fake_quant_fp4(ks[lo:t + 1], 32, "ocp").astype(np.float64)
-        vv = Q.fake_quant_fp8(vs[lo:t + 1], 128, "absmax").astype(np.float64)
-        z = qq @ kk.T * D**-0.5
-        p = np.exp(z - z.max(1, keepdims=True))
-        p /= p.sum(1, keepdims=True)
-        o = p @ vv
-        dp = dos[t] @ vv.T
-        ds = p * (dp - (dos[t] * o).sum(1, keepdims=True))
-        _ = (ds @ kk * D**-0.5, ds.T @ qq * D**-0.5, p.T @ dos[t])
-        pairs += 64 * W
+    qx = q_rows.float().requires_grad_()
+    kx = k_seq.float().requires_grad_()
+    vx = v_seq.float().requires_grad_()
+    qf = qx - qx.detach() + R.fake_quant_fp4_ocp(qx.detach(), 32)
+    kf = kx - kx.detach() + R.fake_quant_fp4_ocp(kx.detach(), 32)
+    vf = vx - vx.detach() + R.fake_quant_fp8_absmax(vx.detach(), 128)
+    pos = torch.tensor(toks).view(-1, 1)
+    rows = pos - W + 1 + torch.arange(W).view(1, -1)             # [n, W] window positions
+    valid = rows >= 0
+    rc = rows.clamp_min(0)
+    bias = torch.zeros(n, W).masked_fill_(~valid, float("-inf")).view(n, 1, 1, W)
+    o, _ = R.attend(qf.unsqueeze(1), kf[rc].unsqueeze(1), vf[rc].unsqueeze(1), bias, D ** -0.5)
+    o.backward(do_rows.float().unsqueeze(2))        # o is [n, H, 1, D]
     dt = time.perf_counter() - t0
+    pairs = int(valid.sum()) * q_rows.shape[1]
     flops = 4.0 * D * pairs * 3.5
-    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n_tok} query tokens x 64 heads x {W}-key window, numpy fp64 fake quant + fwd + bwd, "
-                      f"{dt:.2f} s, extrapolated by band pairs"}
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"{n} evenly spaced query tokens of one sequence x {q_rows.shape[1]} heads x their {W}-key "
+                      f"windows: torch float32 STE fake quant + _attend forward + autograd backward (the "
+                      f"reference's CPU arithmetic), {dt:.2f} s",
+            "result": qx.grad}
 
 
 def reference_train(args, rank, world) -> dict:
@@ -651,23 +882,20 @@ def reference_train(args, rank, world) -> dict:
     if rank != 0:
         return None
     g = torch.Generator().manual_seed(10)
-    S = C5["S"]
-    q = torch.randn(1, S, 64, 128, generator=g).to(torch.bfloat16)
-    k = torch.randn(1, S, 1, 128, generator=g).to(torch.bfloat16)
-    v = torch.randn(1, S, 1, 128, generator=g).to(torch.bfloat16)
-    do = torch.randn(1, S, 64, 128, generator=g).to(torch.bfloat16)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_train(q, k, v, do, n_tok=max(16, args.cpu_sample // 128))
-        if i >= args.warmup:
-            vals.append(r["value"])
-    val = statistics.mean(vals)
-    r["value"] = val
-    return {"metric": "SWA train fwd+bwd TFLOP/s (fake-quant Q/K MXFP4, V FP8)", "value": val, "unit": "TFLOP/s",
-            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64 (oracle port)",
-            "data": "synthetic", "config": {"workload": "C5 SWA train + fake quant", **C5},
-            "cpu_baseline": r, "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    toks = _train_sample()
+    H, D = C5["H"], C5["D"]
+    q = torch.randn(len(toks), H, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(C5["S"], D, generator=g).to(torch.bfloat16)
+    v = torch.randn(C5["S"], D, generator=g).to(torch.bfloat16)
+    do = torch.randn(len(toks), H, D, generator=g).to(torch.bfloat16)
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_train(torch, q, k, v, do, toks)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "SWA train fwd+bwd TFLOP/s (fake-quant Q/K MXFP4, V FP8)", "TFLOP/s",
+                           c5_config(world), runs, "f32 (reference CPU arithmetic)",
+                           "synthetic (seeded N(0,1) bf16 inputs and dO)", scaling="weak")
 
 
 # ----------------------------------------------------------------------------- paged decode + indexer (C4)
@@ -739,9 +967,9 @@ def c4_inputs(torch, device, seqs, lens):
 def c4_step(x):
     from mzoo_b200 import indexer, sparse_mla
     idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"], scales=(x["sq"], x["sk"]),
-                       q_pos=x["pos"], check=False)
+                       q_pos=x["pos"])
     return sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"], idx[:, 0],
-                             window=C4["window"], check=False)
+                             window=C4["window"])
 
 
 def c4_bytes(lens_sub) -> float:
@@ -756,13 +984,20 @@ def c4_bytes(lens_sub) -> float:
     return tot
 
 
+def c4_config(world: int) -> dict:
+    return {"workload": "C4 paged decode + indexer", "sequences": C4["B"], "context": "U[8192,131072] seed 1",
+            "heads": 128, "topk": C4["topk"], "window": C4["window"], "page": 64,
+            "parallelism": (f"sequences sharded over {world} GPUs (greedy by length), no collective in the "
+                            "step" if world > 1 else "1 GPU"),
+            "l2": "caches (~8 GB) larger than L2; 256 MB flush per step"}
+
+
 def bench_decode(args, torch, dist, rank, world, device) -> dict:
     lens = c4_lens(torch)
     from mzoo_b200.sharding import shard_sequences
     parts = shard_sequences(lens.tolist(), world)
     mine = parts[rank]
     x = c4_inputs(torch, device, mine, lens)
-    nbytes = c4_bytes([lens[b] for b in mine])
     total_bytes = c4_bytes(lens.tolist())
     n_mine = len(mine)
     shard = max(len(p) for p in parts)  # greedy-by-length shards differ in count
@@ -814,86 +1049,140 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
     ms_score = sum(t_score) / len(t_score)
     pk = peaks()
     score_bytes = sum((int(lens[b]) // 4) * (C4["Di"] + 4) + C4["Hi"] * (C4["Di"] + 8) for b in mine)
+    score_bytes_all = sum((int(L) // 4) * (C4["Di"] + 4) + C4["Hi"] * (C4["Di"] + 8) for L in lens.tolist())
     ach = score_bytes / (ms_score * 1e-3) / 1e9
     out = {
         "metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)", "value": total_bytes / (ms * 1e-3) / 1e9,
         "unit": "GB/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3 KV / bf16 q (fp32 acc)", "data": "synthetic (seeded lengths, random page tables, random FP8 rows)",
-        "config": {"workload": "C4 paged decode + indexer", "sequences": C4["B"], "context": "U[8192,131072] seed 1",
-                   "mean_context": float(lens.float().mean()), "heads": 128, "topk": C4["topk"],
-                   "window": C4["window"], "page": 64, "algorithmic_bytes_per_step": total_bytes,
-                   "parallelism": (f"sequences sharded over {world} GPUs (greedy by length), no collective in the "
-                                   "step" if world > 1 else "1 GPU"),
-                   "o_gather_ms": gather_ms,
-                   "l2": "caches (~8 GB) larger than L2; 256 MB flush per step"},
+        "config": c4_config(world),
+        "legs": {"algorithmic_bytes_per_step": total_bytes, "mean_context": float(lens.float().mean()),
+                 "o_gather_ms": gather_ms},
         "e2e": {"value": total_bytes / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
                 "h2d_bytes_per_step": hq.numel() * 2 + hq8.numel() + hw.numel() * 4,
                 "d2h_bytes_per_step": ho.numel() * 2},
         "roofline": {"bound": "hbm", "kernel": "mzb::idx::score_kernel<fp8,128,1> (decode indexer)", "achieved": ach,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
                      "peak_note": f"{pk['_source']} HBM copy", "algorithmic_bytes_per_launch": score_bytes,
-                     "ms_per_launch": ms_score, "traffic": TRAFFIC["decode"], "traffic_unit": "bytes per launch (ncu)"},
+                     "ms_per_launch": ms_score, **traffic_for("decode", score_bytes / score_bytes_all)},
         "gpu_launches": 6 * args.steps,
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_decode(min(C4["B"], max(1, args.cpu_sample // 32)))
+        from mzoo_b200 import sparse_mla
+        idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"],
+                           scales=(x["sq"], x["sk"]), q_pos=x["pos"], check=True)
+        o, lse = sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"],
+                                   idx[:, 0], window=C4["window"], check=True)
+        sample = _decode_sample(lens)
+        items = [_decode_item_from_device(torch, x, b, int(lens[b])) for b in sample]
+        r = cpu_decode(torch, items)
+        res = r.pop("result")
+        same = sum(_set_equal_rows(torch, idx[b, 0:1].cpu(), ri.view(1, -1)) for b, (ri, _, _) in zip(sample, res))
+        eo = max((o[b].float().cpu() - ro).abs().max().item() for b, (_, ro, _) in zip(sample, res))
+        el = max((lse[b].cpu() - rl).abs().max().item() for b, (_, _, rl) in zip(sample, res))
+        r["parity"] = {"sequences": len(sample), "equal_index_sets": int(same), "max_abs_err_o": eo,
+                       "max_abs_err_lse": el, "atol": 2e-2,
+                       "note": "GPU index sets and rows vs the CPU float32 reference on the sampled sequences (the "
+                               "attention check holds where the sets agree)"}
+        out["cpu_baseline"] = r
     return out
 
 
-def cpu_decode(n_seq: int) -> dict:
-    """Oracle port of one decode step for n_seq sequences (the first of the seeded lengths):
-    canonical fp64 indexer scores over L/4 FP8 keys -> exact top-2048 -> sparse attention
-    over window + selected latent rows (numpy fp64), as GB/s of their algorithmic bytes."""
-    import numpy as np
-    import torch
-    from oracle import indexer as I
-    from oracle import mla as M
-    lens = c4_lens(torch)[:n_seq].tolist()
-    rng = np.random.default_rng(5)
-    t_total = 0.0
-    for L in lens:
-        T = L // C4["ratio"]
-        codes = rng.integers(0, 255, (T, C4["Di"]), dtype=np.uint8)
-        codes[(codes & 0x7F) == 0x7F] -= 1
-        kv = M.e4m3_values(codes)[None]
-        qc = rng.integers(0, 255, (1, 1, C4["Hi"], C4["Di"]), dtype=np.uint8)
-        qc[(qc & 0x7F) == 0x7F] -= 1
-        qv = M.e4m3_values(qc)
-        sk = ((rng.random((1, T)) * 3 + 1) / 448).astype(np.float32)
-        sq = ((rng.random((1, 1, C4["Hi"])) * 3 + 1) / 448).astype(np.float32)
-        w = (rng.standard_normal((1, 1, C4["Hi"])) / 8).astype(np.float32)
-        raw_rows = M.pack_rows(rng.standard_normal((C4["window"], 576)).astype(np.float32))
-        cmp_rows = M.pack_rows(rng.standard_normal((min(T, C4["topk"]), 576)).astype(np.float32))
-        q = rng.standard_normal((128, 576)).astype(np.float32)
-        t0 = time.perf_counter()
-        sc = I.canonical_scores(qv, kv, w, sq, sk, C4["ratio"], L - 1)
-        sel = I.canonical_topk(sc, C4["topk"], C4["ratio"], L - 1)[0, 0]
-        keys = M.unpack_rows(np.concatenate([raw_rows, cmp_rows[:int((sel >= 0).sum())]], 0))
-        M.attend_rows(q, keys, 576**-0.5)
-        t_total += time.perf_counter() - t0
+def _decode_sample(lens, n: int = 32) -> list:
+    """n sequences spread over the length distribution (every len/n-th in length order)."""
+    order = sorted(range(len(lens)), key=lambda b: int(lens[b]))
+    step = max(1, len(order) // n)
+    return [order[i] for i in range(step // 2, len(order), step)][:n]
+
+
+def _window_pages(L: int):
+    """Raw pages the 128-token window of a query at position L-1 reads."""
+    return range(max(0, L - C4["window"]) // 64, (L - 1) // 64 + 1)
+
+
+def _decode_item_from_device(torch, x, b: int, L: int) -> dict:
+    """One sequence's decode inputs moved to the host: indexer tensors, its compressed pages
+    (compacted, page table 0..n-1) and the raw pages its window reads (other entries of the
+    raw page table are never read)."""
+    T = L // C4["ratio"]
+    ncp = -(-T // 64)
+    wp = list(_window_pages(L))
+    raw_pt = torch.zeros(-(-L // 64), dtype=torch.int64)
+    raw_pt[wp] = torch.arange(len(wp))
+    return {"L": L, "q8": x["q8"][b, 0].cpu(), "sq": x["sq"][b, 0].cpu(), "w": x["w"][b, 0].cpu(),
+            "k8": x["k8"][b, :T].cpu(), "sk": x["sk"][b, :T].cpu(), "q": x["q"][b].cpu(),
+            "cmp": x["cmp"][x["cpt"][b, :ncp].long()].cpu(), "cpt": torch.arange(ncp),
+            "raw": x["raw"][x["pt"][b, wp].long()].cpu(), "pt": raw_pt}
+
+
+def _decode_item_cpu(torch, L: int, gen) -> dict:
+    """One sequence's decode inputs generated on the host with the bench's distributions."""
+    T = L // C4["ratio"]
+    ncp = -(-T // 64)
+    wp = list(_window_pages(L))
+    raw_pt = torch.zeros(-(-L // 64), dtype=torch.int64)
+    raw_pt[wp] = torch.arange(len(wp))
+
+    def codes(*shape):
+        c = torch.randint(0, 255, shape, generator=gen, dtype=torch.int32)
+        return torch.where((c & 0x7F) == 0x7F, c - 1, c).to(torch.uint8).view(torch.float8_e4m3fn)
+    return {"L": L, "q8": codes(C4["Hi"], C4["Di"]), "sq": (torch.rand(C4["Hi"], generator=gen) * 3 + 1) / 448.0,
+            "w": torch.randn(C4["Hi"], generator=gen) / 8, "k8": codes(T, C4["Di"]),
+            "sk": (torch.rand(T, generator=gen) * 3 + 1) / 448.0,
+            "q": torch.randn(128, 576, generator=gen).to(torch.bfloat16),
+            "cmp": _random_rows(torch, ncp * 64, torch.device("cpu"), gen).view(ncp, 64, 672), "cpt": torch.arange(ncp),
+            "raw": _random_rows(torch, len(wp) * 64, torch.device("cpu"), gen).view(len(wp), 64, 672), "pt": raw_pt}
+
+
+def cpu_decode(torch, items) -> dict:
+    """The reference's float32 CPU arithmetic for one decode step of the given sequences:
+    ``indexer_scores`` of the one query over the sequence's L/4 dequantised FP8 keys
+    (position L-1), ``topk_indices`` (top-2048), then ``_attend`` over the window and the
+    selected compressed rows, read through the page tables and dequantised.  Metric: GB/s
+    of the sequences' algorithmic bytes."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    W = C4["window"]
+    res = []
+    t0 = time.perf_counter()
+    for it in items:
+        L = it["L"]
+        qd = (it["q8"].float() * it["sq"].view(-1, 1)).view(1, 1, C4["Hi"], C4["Di"])
+        kd = (it["k8"].float() * it["sk"].view(-1, 1)).unsqueeze(0)
+        sc = R.indexer_scores(qd, kd, it["w"].view(1, 1, -1), C4["ratio"], L - 1, scale=1.0)
+        idx = R.topk_indices(sc, C4["topk"])[0, 0]
+        sel = idx[idx >= 0]
+        pos = torch.arange(max(0, L - W), L)
+        rows = torch.cat([it["raw"][it["pt"][pos // 64], pos % 64], it["cmp"][it["cpt"][sel // 64], sel % 64]])
+        keys = R.unpack_rows(rows).unsqueeze(0)
+        o, lse = R.gathered_attention(it["q"].float().unsqueeze(0), keys, torch.tensor([rows.shape[0]]),
+                                      576 ** -0.5)
+        res.append((idx, o[0], lse[0]))
+    dt = time.perf_counter() - t0
+    lens = [it["L"] for it in items]
     nbytes = c4_bytes(lens)
-    return {"value": nbytes / t_total / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n_seq} sequences (L = {lens}), numpy fp64 canonical indexer + exact top-2048 + sparse "
-                      f"attention, {t_total:.2f} s"}
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"{len(items)} of the 128 sequences ({sum(lens)} tokens of context): torch float32 indexer_scores + topk_indices + _attend over the paged, dequantised "
+                      f"rows (the reference's CPU arithmetic), {dt:.2f} s",
+            "result": res}
 
 
 def reference_decode(args, rank, world) -> dict:
+    import torch
     if rank != 0:
         return None
-    n = max(1, args.cpu_sample // 2048)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_decode(n)
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
-    r["value"] = v
-    return {"metric": "paged sparse-MLA decode HBM GB/s (indexer + attention)", "value": v, "unit": "GB/s",
-            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64 (oracle port)",
-            "data": "synthetic", "config": {"workload": "C4 paged decode + indexer", "sequences": C4["B"]},
-            "cpu_baseline": r, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    lens = c4_lens(torch)
+    g = torch.Generator().manual_seed(5)
+    items = [_decode_item_cpu(torch, int(lens[b]), g) for b in range(C4["B"])]  # the whole config
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_decode(torch, items)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "paged sparse-MLA decode HBM GB/s (indexer + attention)", "GB/s",
+                           c4_config(world), runs, "f32 (reference CPU arithmetic, FP8 dequantised)",
+                           "synthetic (seeded lengths, random page tables, random FP8 rows)")
 
 
 # ----------------------------------------------------------------------------- two-level selection
@@ -915,6 +1204,14 @@ def cf_inputs(torch, seed: int, rows=None):
     vis = torch.arange(T).view(1, -1) < clen.view(-1, 1)
     mats = [torch.randn(rows, T, generator=g).masked_fill_(~vis, float("-inf")) for _ in range(2)]
     return mats[0], mats[1], clen
+
+
+def cf_config(world: int) -> dict:
+    return {"workload": "F1 two-level selection: level-one candidate blocks + level-two top-k",
+            "queries": CF["rows"], "positions": CF["T"], "block_size": CF["block"], "topk_blocks": CF["topk_blocks"],
+            "topk": CF["topk"],
+            "parallelism": (f"query rows cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
+            "l2": "flushed (256 MB write) per step; inputs (2 x 512 MB) larger than L2"}
 
 
 def bench_candidates(args, torch, dist, rank, world, device) -> dict:
@@ -974,10 +1271,7 @@ def bench_candidates(args, torch, dist, rank, world, device) -> dict:
         "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32 keys (radix select on order-preserving uint32)",
         "data": "synthetic (seeded N(0,1) scores, -inf past each query's compressed length)",
-        "config": {"workload": "F1 two-level selection: level-one candidate blocks + level-two top-k",
-                   "queries": CF["rows"], "positions": CF["T"], "block_size": bs, "topk_blocks": tb, "topk": topk,
-                   "parallelism": (f"query rows cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
-                   "l2": "flushed (256 MB write) per step; inputs (2 x 512 MB) larger than L2"},
+        "config": cf_config(world),
         "legs": {"level_one_ms": ms_l1, "level_two_ms": ms_l2,
                  "level_one_gbs": rows * CF["T"] * 4 / (ms_l1 * 1e-3) / 1e9},
         "e2e": {"value": CF["rows"] / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
@@ -985,8 +1279,7 @@ def bench_candidates(args, torch, dist, rank, world, device) -> dict:
         "roofline": {"bound": "hbm", "kernel": "mzb::cand::topk_gather_kernel (level two)", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_note": f"{pk['_source']} copy bandwidth", "algorithmic_bytes_per_launch": alg2,
-                     "ms_per_launch": ms_l2, "traffic": TRAFFIC.get("candidates"),
-                     "traffic_unit": "bytes per launch (ncu)"},
+                     "ms_per_launch": ms_l2, **traffic_for("candidates", rows / CF["rows"])},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
     }
@@ -1003,7 +1296,7 @@ def cpu_candidates(lg, sc, cl, sample: int) -> dict:
     mask = C.candidate_mask_ref(lgn, cln, CF["topk_blocks"], CF["block"])
     C.candidate_topk_ref(scn, mask, CF["topk"])
     dt = time.perf_counter() - t0
-    return {"value": sample / dt / 1e6, "unit": "Mq/s", "cores": 1, "kind": "port",
+    return {"value": sample / dt / 1e6, "unit": "Mq/s", "cores": 1, "kind": "port", "ms": dt * 1e3,
             "sample": f"{sample} query rows of {CF['T']} positions, numpy (lexsort per row), {dt:.2f} s"}
 
 
@@ -1013,21 +1306,9 @@ def reference_candidates(args, rank, world) -> dict:
         return None
     n = max(1, args.cpu_sample // 16)
     lg, sc, cl = cf_inputs(torch, seed=0, rows=n)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_candidates(lg, sc, cl, sample=n)
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
-    r["value"] = v
-    return {"metric": "two-level indexer selection Mq/s", "value": v, "unit": "Mq/s", "impl": "reference",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": CF["rows"] / (v * 1e6) * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
-            "config": {"workload": "F1 two-level selection: level-one candidate blocks + level-two top-k",
-                       "queries": CF["rows"], "positions": CF["T"], "block_size": CF["block"],
-                       "topk_blocks": CF["topk_blocks"], "topk": CF["topk"]},
-            "cpu_baseline": r, "e2e": {"value": v, "unit": "Mq/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    runs = [cpu_candidates(lg, sc, cl, sample=n) for _ in range(args.warmup + args.steps)]
+    return _reference_line(args, world, "two-level indexer selection Mq/s", "Mq/s", cf_config(world), runs,
+                           "f32 keys (oracle port, numpy)", "synthetic")
 
 
 # ----------------------------------------------------------------------------- compressor producer step
@@ -1053,6 +1334,14 @@ def cp_bytes(B: int) -> float:
     """Algorithmic HBM bytes of one step: kv and gate read once, cos / sin read, two bf16 outputs."""
     G = CP["S"] // CP["ratio"]
     return B * (2 * CP["S"] * CP["D"] * 4 + 2 * G * (CP["rope"] // 2) * 4 + 2 * G * CP["D"] * 2)
+
+
+def cp_config(world: int) -> dict:
+    return {"workload": "F3 compressor: gated softmax pool + RMSNorm + RoPE + MXFP4 cache entry",
+            "B": CP["B"], "tokens": CP["S"], "compress_ratio": CP["ratio"], "head_dim": CP["D"],
+            "rope_dim": CP["rope"],
+            "parallelism": (f"sequences cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
+            "l2": "flushed (256 MB write) per step; inputs (604 MB) larger than L2"}
 
 
 def bench_compressor(args, torch, dist, rank, world, device) -> dict:
@@ -1102,18 +1391,13 @@ def bench_compressor(args, torch, dist, rank, world, device) -> dict:
         "metric": "compressor producer step HBM GB/s (algorithmic bytes)", "value": total / (ms * 1e-3) / 1e9,
         "unit": "GB/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32 pool, bf16 latent / cache", "data": "synthetic (seeded N(0,1) projections, random angles)",
-        "config": {"workload": "F3 compressor: gated softmax pool + RMSNorm + RoPE + MXFP4 cache entry",
-                   "B": CP["B"], "tokens": CP["S"], "compress_ratio": CP["ratio"], "head_dim": CP["D"],
-                   "rope_dim": CP["rope"],
-                   "parallelism": (f"sequences cyclic over {world} GPUs, no collective" if world > 1 else "1 GPU"),
-                   "l2": "flushed (256 MB write) per step; inputs (604 MB) larger than L2"},
+        "config": cp_config(world),
         "e2e": {"value": total / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "kernel": "mzb::comp::compress_kernel", "achieved": achieved,
                      "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "peak_note": f"{pk['_source']} copy bandwidth", "algorithmic_bytes_per_launch": local,
-                     "ms_per_launch": sum(t_steps) / len(t_steps), "traffic": TRAFFIC.get("compressor"),
-                     "traffic_unit": "bytes per launch (ncu)"},
+                     "ms_per_launch": sum(t_steps) / len(t_steps), **traffic_for("compressor", B / CP["B"])},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
@@ -1137,7 +1421,7 @@ def cpu_compressor(h, n_groups: int) -> dict:
     Cm.cache_ref(lat, cos, sin)
     dt = time.perf_counter() - t0
     return {"value": cp_bytes(1) * n / (CP["S"] // r) / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
-            "sample": f"{n} groups of sequence 0, numpy, {dt:.2f} s"}
+            "ms": dt * 1e3, "sample": f"{n} groups of sequence 0, numpy, {dt:.2f} s"}
 
 
 def reference_compressor(args, rank, world) -> dict:
@@ -1145,24 +1429,16 @@ def reference_compressor(args, rank, world) -> dict:
     if rank != 0:
         return None
     h = cp_inputs(torch, seed=0, B=1)
-    vals = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_compressor(h, n_groups=max(1, args.cpu_sample))
-        if i >= args.warmup:
-            vals.append(r["value"])
-    v = statistics.mean(vals)
-    r["value"] = v
-    return {"metric": "compressor producer step HBM GB/s (algorithmic bytes)", "value": v, "unit": "GB/s",
-            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": cp_bytes(CP["B"]) / (v * 1e9) * 1e3, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f64 (oracle port)", "data": "synthetic",
-            "config": {"workload": "F3 compressor: gated softmax pool + RMSNorm + RoPE + MXFP4 cache entry",
-                       "B": CP["B"], "tokens": CP["S"], "compress_ratio": CP["ratio"], "head_dim": CP["D"],
-                       "rope_dim": CP["rope"]},
-            "cpu_baseline": r, "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    runs = [cpu_compressor(h, n_groups=max(1, args.cpu_sample)) for _ in range(args.warmup + args.steps)]
+    return _reference_line(args, world, "compressor producer step HBM GB/s (algorithmic bytes)", "GB/s",
+                           cp_config(world), runs, "f32 (oracle port, numpy)", "synthetic")
 
 
-BENCHES = {"indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
+CONFIGS = {"window": c1_config, "indexer": c2_config, "prefill": c3_config, "decode": c4_config,
+           "train": c5_config, "candidates": cf_config, "compressor": cp_config}
+
+BENCHES = {"window": (bench_window, reference_window),
+           "indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
            "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode),
            "candidates": (bench_candidates, reference_candidates),
            "compressor": (bench_compressor, reference_compressor)}
@@ -1173,7 +1449,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="indexer", choices=sorted(BENCHES))
+    ap.add_argument("--config", default="prefill", choices=sorted(BENCHES))
     ap.add_argument("--impl", default="mzb", choices=["mzb", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=4096,
                     help="size of the timed CPU baseline sample (about 10 s of host work at the default)")

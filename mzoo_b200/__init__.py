@@ -10,6 +10,18 @@ Drop-in modules mirroring the reference's call signatures:
 
 All compute runs in ``libmzb200.so`` (hand-written CUDA for sm_100a) behind the C ABI
 of ``include/mzb200.h``; there is no CPU fallback.
+
+The wrappers never block the host (like the reference's): a device-side failure (a
+bounded wait that gave up, a top-k error band too wide) is recorded in a per-device error
+word that ``check_errors()`` reads and clears; ``check=True`` on a wrapper reads it right
+after that launch instead.
 """
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
+
+
+def check_errors(device=None) -> None:
+    """Raise ``mzoo_b200._lib.MzbError`` if a kernel recorded a device-side failure since
+    the last call (synchronises with the device)."""
+    from .ops import check_errors as _check
+    _check(device)

@@ -30,7 +30,7 @@ def check_mqa(q: torch.Tensor, kv: torch.Tensor, what: str) -> tuple:
     return batch, seq_len, heads, dim
 
 
-def run_fwd(q, kv, v, main_kv, idx, sinks, window, scale, check=True):
+def run_fwd(q, kv, v, main_kv, idx, sinks, window, scale, check=False):
     require_cuda(q, kv, v, main_kv, idx, sinks)
     B, S, H, D = q.shape
     Dk = KERNEL_D[D]
@@ -41,7 +41,7 @@ def run_fwd(q, kv, v, main_kv, idx, sinks, window, scale, check=True):
     return o, lse.view(B, S, H).permute(0, 2, 1).contiguous()
 
 
-def run_bwd(q, kv, v, main_kv, idx, o, lse, do, sinks, window, scale, check=True):
+def run_bwd(q, kv, v, main_kv, idx, o, lse, do, sinks, window, scale, check=False):
     """-> (dq [B,S,H,D], dkv [B,S,1,D] (dK+dV when v is None, else dK), dv or None,
     dmain [B,G,1,D] or None, dsinks [H] or None)."""
     require_cuda(q, kv, v, main_kv, idx, o, lse, do)

@@ -74,7 +74,7 @@ def _positions(q_pos, B, S, device):
 
 def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, q_offset: int = 0,
         scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
-        check: bool = True) -> torch.Tensor:
+        check: bool = False) -> torch.Tensor:
     """Lightning-indexer score matrix (``indexer/fwd.py:112``): q bf16 [B,S,Hi,Di], k bf16
     [B,T,Di], w fp32 [B,S,Hi] (already scaled by Hi**-0.5) -> fp32 [B,S,T], ``-inf`` where
     ``t >= (q_offset + s + 1) // compress_ratio``."""
@@ -88,7 +88,7 @@ def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: in
 
 def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, topk: int, q_offset: int = 0,
          scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
-         check: bool = True) -> torch.Tensor:
+         check: bool = False) -> torch.Tensor:
     """``indexer/attn.py:67``: -> ``Indices`` int32 [B,S,topk] (``-1`` = empty slot)."""
     assert topk >= 0, f"topk must be >= 0, got {topk}"
     assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
@@ -104,7 +104,7 @@ def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: i
 
 
 def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, compress_ratio: int,
-        q_offset: int = 0, softmax_scale: float | None = None, check: bool = True):
+        q_offset: int = 0, softmax_scale: float | None = None, check: bool = False):
     """``indexer/bwd.py:104``: q bf16 [B,S,Hi,Di], k bf16 [B,T,Di], w fp32 [B,S,Hi], dl fp32
     [B,S,T] -> (dq bf16 [B,S,Hi,Di], dk bf16 [B,T,Di], dw fp32 [B,S,Hi]).  Entries of ``dl`` at
     group-causally masked positions are ignored, whatever they hold."""

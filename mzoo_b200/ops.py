@@ -51,16 +51,52 @@ def _(x, block_size, rule):
     return torch.empty_like(x, memory_format=torch.contiguous_format)
 
 
-def _err(dev) -> torch.Tensor:
-    return torch.zeros(1, dtype=torch.int32, device=dev)
+# Per-device persistent error words.  Kernels only ever set their error word (on a failure:
+# a bounded wait that gave up, a top-k error band too wide), never clear it, so one word per
+# device keeps the first failure of every launch made with check=False until
+# ``check_errors`` reads it.  Launches made with check=True get a fresh word that is read
+# (a host synchronisation) right after the launch.
+_ERR_WORDS: dict = {}
 
 
-def _raise_on(err: torch.Tensor, what: str) -> None:
-    code = int(err.item())
+def _err(dev, check: bool) -> torch.Tensor:
+    if check:
+        return torch.zeros(1, dtype=torch.int32, device=dev)
+    i = dev.index if dev.index is not None else torch.cuda.current_device()
+    w = _ERR_WORDS.get(i)
+    if w is None:
+        w = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", i))
+        _ERR_WORDS[i] = w
+    return w
+
+
+def _raise_code(code: int, what: str) -> None:
     if code == _lib.MZB_ERR_BOUND:
         raise _lib.MzbError(f"{what}: error bound left too many top-k candidates")
     if code:
         raise _lib.MzbError(f"{what}: device error code {code} (a bounded device wait gave up)")
+
+
+def _raise_on(err: torch.Tensor, what: str) -> None:
+    _raise_code(int(err.item()), what)
+
+
+def check_errors(device=None) -> None:
+    """Raise ``MzbError`` if a kernel launched with ``check=False`` (the wrappers' default)
+    on ``device`` (every device used so far when None) recorded a device-side failure since
+    the last call; the word is cleared either way.  Reading it waits for the device's
+    pending work, so call it where the caller synchronises anyway (end of a step)."""
+    idx = list(_ERR_WORDS) if device is None else [torch.device(device).index or 0]
+    first = 0
+    for i in idx:
+        w = _ERR_WORDS.get(i)
+        if w is None:
+            continue
+        code = int(w.item())
+        if code:
+            w.zero_()
+            first = first or code
+    _raise_code(first, "deferred kernel check")
 
 
 # ----------------------------------------------------------------------------- indexer
@@ -73,7 +109,7 @@ def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, sq: torch.
     B, S, Hi, Di = q.shape
     T = k.shape[1]
     out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
-    err = _err(q.device)
+    err = _err(q.device, check)
     call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(out), B, S, T, Hi, Di, dtype,
          ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
     if check:
@@ -95,7 +131,7 @@ def indexer_topk(scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor, w: torc
     T = k.shape[1]
     out = torch.empty(B, S, topk, dtype=torch.int32, device=q.device)
     kb = torch.empty(B * kb_parts + B * S, dtype=torch.float32, device=q.device)  # key and query bounds
-    err = _err(q.device)
+    err = _err(q.device, check)
     call("mzb_indexer_topk", ptr(scores), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(kb), ptr(out),
          B, S, T, Hi, Di, dtype, ratio, q_offset, scale, topk, eps, ptr(err), stream_ptr(q.device))
     if check:
@@ -117,7 +153,7 @@ def indexer_bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Ten
     dq = torch.empty(B, S, Hi, Di, dtype=torch.bfloat16, device=q.device)
     dk = torch.empty(B, T, Di, dtype=torch.bfloat16, device=q.device)
     dw = torch.empty(B, S, Hi, dtype=torch.float32, device=q.device)
-    err = _err(q.device)
+    err = _err(q.device, check)
     call("mzb_indexer_bwd", ptr(q), ptr(k), ptr(w), ptr(dl), ptr(dq), ptr(dk), ptr(dw), B, S, T, Hi, Di, ratio,
          q_offset, scale, ptr(err), stream_ptr(q.device))
     if check:
@@ -143,7 +179,7 @@ def attn_fwd(q: torch.Tensor, kv: torch.Tensor, v: torch.Tensor | None, main_kv:
     dev = q.device
     o = torch.empty(B, S, H, D, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(B, S * H, dtype=torch.float32, device=dev)
-    err = _err(dev)
+    err = _err(dev, check)
     G = main_kv.shape[1] if main_kv is not None else 0
     topk = idx.shape[2] if idx is not None else 0
     call("mzb_attn_fwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(sinks), ptr(o), ptr(lse), B, S, H, D,
@@ -177,7 +213,7 @@ def attn_bwd(q: torch.Tensor, kv: torch.Tensor, v: torch.Tensor | None, main_kv:
     dmain = torch.zeros(B, G, D, dtype=torch.float32, device=dev) if G else q.new_empty((0,), dtype=torch.float32)
     delta = torch.empty(B, rpad, dtype=torch.float32, device=dev)
     lse2 = torch.empty(B, rpad, dtype=torch.float32, device=dev)
-    err = _err(dev)
+    err = _err(dev, check)
     splits = _lib.lib().mzb_attn_bwd_splits(B, S, H, window)
     part = torch.empty(splits * B * S * 2 * D, dtype=torch.float32, device=dev)
     call("mzb_attn_bwd", ptr(q), ptr(kv), ptr(v), ptr(main_kv), ptr(idx), ptr(o), ptr(lse_rows), ptr(do), ptr(dq),
@@ -212,7 +248,7 @@ def sparse_mla_fwd(q: torch.Tensor, kv_raw: torch.Tensor, kv_cmp: torch.Tensor, 
     o = torch.empty(n_tok, 128, 512, dtype=torch.bfloat16, device=dev)
     lse = torch.empty(n_tok, 128, dtype=torch.float32, device=dev)
     slots = torch.empty(max(n_tok, 1), dtype=torch.int32, device=dev)
-    err = _err(dev)
+    err = _err(dev, check)
     splits = _lib.lib().mzb_sparse_mla_splits(n_tok)
     part = torch.empty(splits * n_tok * 128 * 513, dtype=torch.float32, device=dev) if splits > 1 else None
     call("mzb_sparse_mla_fwd", ptr(q), ptr(kv_raw), ptr(kv_cmp), ptr(idx), ptr(pos), ptr(raw_pt), ptr(cmp_pt),

@@ -47,7 +47,7 @@ def _run(q2, raw, cmp, idx, pos, raw_pt, cmp_pt, cmp_lens, n_tok, tok_per_seq, t
 
 def prefill(q: torch.Tensor, kv: torch.Tensor, kv_cmp: torch.Tensor, indices: torch.Tensor, *, window: int = 128,
             softmax_scale: float | None = None, q_offset: int = 0, q_pos: torch.Tensor | None = None,
-            check: bool = True):
+            check: bool = False):
     """q bf16 [B,S,128,576]; kv uint8 [B,S_raw,672] raw latent rows (query s sits at
     position s + q_offset < S_raw, or at ``q_pos[b, s]`` when given -- an arbitrary subset of
     a sequence's queries, e.g. one rank's shard); kv_cmp uint8 [B,G,672]; indices int32
@@ -79,7 +79,7 @@ def prefill(q: torch.Tensor, kv: torch.Tensor, kv_cmp: torch.Tensor, indices: to
 
 def decode(q: torch.Tensor, kv_pages: torch.Tensor, page_table: torch.Tensor, seq_lens: torch.Tensor,
            cmp_pages: torch.Tensor, cmp_page_table: torch.Tensor, cmp_lens: torch.Tensor, indices: torch.Tensor, *,
-           window: int = 128, softmax_scale: float | None = None, check: bool = True):
+           window: int = 128, softmax_scale: float | None = None, check: bool = False):
     """One new token per sequence at position ``seq_lens[b] - 1``.
 
     q bf16 [B,128,576]; kv_pages uint8 [P,64,672] raw latent pages with page_table int32

@@ -9,14 +9,17 @@ pmonad/mzoo's pure-PyTorch reference for the path the CUDA library replaces:
                        (``src/mzoo/layers/attn/golden_ref.py``);
 - ``oracle.indexer``   lightning-indexer scores and top-k
                        (``golden_ref.py:213-243``, ``indexer/fwd.py``, ``indexer/bwd.py``);
-- ``oracle.mla``       576/512 latent sparse prefill and paged decode over FP8 rows.
+- ``oracle.mla``       576/512 latent sparse prefill and paged decode over FP8 rows;
+- ``oracle.torch_ref`` the same reference arithmetic in torch float32 (the CPU path the
+                       benchmark's reference arm times on the host cores).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg may
 import it, and only as the checker.  The product path (``mzoo_b200``) never imports
 anything from here and has no CPU fallback.
 
 Pinning: ``tests/golden/`` holds input/output vectors produced by importing the
-reference itself (``tests/golden/make_golden.py``); ``tests/test_oracle.py`` checks
-this oracle against them bit-for-bit (quant, top-k sets) or to fp32 rounding
-(attention, scores).
+reference itself (``tests/golden/make_golden.py``); the CPU tests of ``tests/test_quant.py``,
+``test_attn.py``, ``test_indexer.py``, ``test_sparse_mla.py``, ``test_candidates.py``,
+``test_compressor.py`` and ``test_torch_ref.py`` check this oracle against them
+bit-for-bit (quant, row packing, top-k sets) or to fp32 rounding (attention, scores).
 """

@@ -130,6 +130,155 @@ def make_indexer(golden_ref) -> None:
     np.savez_compressed(os.path.join(HERE, "indexer.npz"), **out)
 
 
+def _fp8_absmax(x: torch.Tensor, tile: int):
+    """Absmax e4m3 quantisation in torch (the synthetic inputs' rule): per ``tile`` elements
+    of the last axis scale = amax / 448 (1 where amax is 0), codes = e4m3(x / scale) with
+    torch's own float8_e4m3fn cast (round to nearest even).  -> (uint8 codes, fp32 scales)."""
+    lead = x.shape[:-1]
+    blk = x.float().reshape(*lead, x.shape[-1] // tile, tile)
+    amax = blk.abs().amax(-1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    codes = (blk / scale.unsqueeze(-1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+    return codes.view(torch.uint8).reshape(x.shape), scale
+
+
+def _e4m3_dequant(codes: torch.Tensor, scale: torch.Tensor, tile: int) -> torch.Tensor:
+    lead = codes.shape[:-1]
+    vals = codes.view(torch.float8_e4m3fn).float().reshape(*lead, codes.shape[-1] // tile, tile)
+    return (vals * scale.unsqueeze(-1)).reshape(codes.shape)
+
+
+def _pack_latent(x: torch.Tensor) -> torch.Tensor:
+    """[..., 576] fp32 -> [..., 672] uint8 latent rows: 512 e4m3 codes (absmax/448 per 64),
+    the 8 fp32 scales, the 64 rope channels as bf16."""
+    lead = x.shape[:-1]
+    codes, scale = _fp8_absmax(x[..., :512], 64)
+    rows = torch.empty(*lead, 672, dtype=torch.uint8)
+    rows[..., :512] = codes
+    rows[..., 512:544] = scale.contiguous().view(torch.uint8).reshape(*lead, 32)
+    rows[..., 544:] = x[..., 512:].to(torch.bfloat16).contiguous().view(torch.uint8).reshape(*lead, 128)
+    return rows
+
+
+def _unpack_latent(rows: torch.Tensor) -> torch.Tensor:
+    """[..., 672] uint8 -> [..., 576] fp32 (nope = code * tile scale, rope = bf16 value)."""
+    lead = rows.shape[:-1]
+    scale = rows[..., 512:544].contiguous().view(torch.float32).reshape(*lead, 8)
+    nope = _e4m3_dequant(rows[..., :512].contiguous(), scale, 64)
+    rope = rows[..., 544:].contiguous().view(torch.bfloat16).float().reshape(*lead, 64)
+    return torch.cat([nope, rope], -1)
+
+
+def _attend_rows(golden_ref, q_tok: torch.Tensor, keys: torch.Tensor):
+    """The reference's ``_attend`` (golden_ref.py:83-100) for one query token over its
+    gathered key rows: K = the 576-wide rows, V = their first 512 channels, scale
+    576**-0.5 (``_attend`` scales by q's last dim), no mask, no sink, fp32."""
+    q = q_tok.float().view(1, q_tok.shape[0], 1, 576)      # [B=1, H, S=1, D]
+    k = keys.float().view(1, 1, keys.shape[0], 576)         # [B=1, Hk=1, T, D]
+    o, lse = golden_ref._attend(q, k, k[..., :512], None, None, torch.float32)
+    return o.view(q_tok.shape[0], 512), lse.view(q_tok.shape[0])
+
+
+def make_mla(golden_ref) -> None:
+    """576/512 FP8-latent sparse attention (BASELINE configs 3 and 4) through the
+    reference's ``_attend`` on the rows each query gathers: the causal window of ``window``
+    raw tokens ending at the query position, then the listed compressed entries in order
+    (duplicates kept, ``-1`` and out-of-range entries dropped -- the reference kernels'
+    rule, ``csa2_attn/fwd.py:1-16``, ``bwd_dq.py:33-37``).  The FP8 rows are packed and
+    dequantised here with torch's own e4m3 cast, independently of the oracle.  Heads = 8:
+    the oracle is head-generic (the kernels' 128 heads are covered by the GPU tests)."""
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    H = 8
+    # prefill: S queries at positions q_offset..q_offset+S-1
+    S, q_offset, G, topk, window = 16, 8, 14, 10, 6
+    q = torch.randn(S, H, 576, generator=g).to(torch.bfloat16)
+    kv = torch.randn(S + q_offset, 576, generator=g) * 1.5
+    cmp = torch.randn(G, 576, generator=g)
+    kv[3, :64] = 0.0  # an all-zero 64-channel tile (scale 1, all codes 0)
+    raw_rows, cmp_rows = _pack_latent(kv), _pack_latent(cmp)
+    raw_f, cmp_f = _unpack_latent(raw_rows), _unpack_latent(cmp_rows)
+    idx = torch.full((S, topk), -1, dtype=torch.int32)
+    for s in range(S):
+        vis = min(G, (s + q_offset + 1) // 2)
+        sel = torch.randperm(vis, generator=g)[:topk].sort().values if vis else torch.zeros(0, dtype=torch.int64)
+        idx[s, :len(sel)] = sel.to(torch.int32)
+        if s % 3 == 0 and len(sel) >= 2:
+            idx[s, 1] = idx[s, 0]      # duplicate: counted twice
+        if s % 4 == 1 and len(sel) >= 3:
+            idx[s, 2] = G + 5          # out of range: empty slot
+    o = torch.empty(S, H, 512)
+    lse = torch.empty(H, S)
+    for s in range(S):
+        pos = s + q_offset
+        sel = [int(i) for i in idx[s] if 0 <= int(i) < G]
+        keys = torch.cat([raw_f[max(0, pos - window + 1):pos + 1], cmp_f[sel]], 0)
+        o[s], lse[:, s] = _attend_rows(golden_ref, q[s], keys)
+    out.update({"pre.q": bits(q), "pre.kv": kv.numpy(), "pre.cmp": cmp.numpy(), "pre.raw_rows": raw_rows.numpy(),
+                "pre.cmp_rows": cmp_rows.numpy(), "pre.idx": idx.numpy(), "pre.o": o.numpy(), "pre.lse": lse.numpy(),
+                "pre.params": np.array([q_offset, window], np.int64)})
+    # paged decode: one token per sequence at position L-1, rows through 64-token page tables
+    lens = torch.tensor([70, 200, 9], dtype=torch.int32)
+    B, topk, window, ratio = 3, 12, 16, 4
+    n_pages = int(((lens + 63) // 64).sum())
+    clens = lens // ratio
+    n_cpages = int(((clens + 63) // 64).sum())
+    raw_pages = _pack_latent(torch.randn(n_pages, 64, 576, generator=g))
+    cmp_pages = _pack_latent(torch.randn(n_cpages, 64, 576, generator=g))
+    rperm, cperm = torch.randperm(n_pages, generator=g), torch.randperm(n_cpages, generator=g)
+    pt = torch.zeros(B, 4, dtype=torch.int32)
+    cpt = torch.zeros(B, 1, dtype=torch.int32)
+    ro = co = 0
+    for b in range(B):
+        npg, ncp = int((lens[b] + 63) // 64), int((clens[b] + 63) // 64)
+        pt[b, :npg] = rperm[ro:ro + npg].to(torch.int32)
+        cpt[b, :ncp] = cperm[co:co + ncp].to(torch.int32)
+        ro, co = ro + npg, co + ncp
+    didx = torch.full((B, topk), -1, dtype=torch.int32)
+    for b in range(B):
+        sel = torch.randperm(int(clens[b]), generator=g)[:topk].sort().values
+        didx[b, :len(sel)] = sel.to(torch.int32)
+    didx[1, 3] = didx[1, 2]  # duplicate
+    qd = torch.randn(B, H, 576, generator=g).to(torch.bfloat16)
+    od = torch.empty(B, H, 512)
+    lsed = torch.empty(B, H)
+    for b in range(B):
+        L = int(lens[b])
+        pos = torch.arange(max(0, L - window), L)
+        sel = torch.tensor([int(i) for i in didx[b] if 0 <= int(i) < int(clens[b])], dtype=torch.int64)
+        rows = torch.cat([raw_pages[pt[b, pos // 64].long(), pos % 64], cmp_pages[cpt[b, sel // 64].long(), sel % 64]])
+        od[b], lsed[b] = _attend_rows(golden_ref, qd[b], _unpack_latent(rows))
+    out.update({"dec.q": bits(qd), "dec.raw_pages": raw_pages.numpy(), "dec.cmp_pages": cmp_pages.numpy(),
+                "dec.pt": pt.numpy(), "dec.cpt": cpt.numpy(), "dec.lens": lens.numpy(), "dec.clens": clens.numpy(),
+                "dec.idx": didx.numpy(), "dec.o": od.numpy(), "dec.lse": lsed.numpy(),
+                "dec.params": np.array([window], np.int64)})
+    np.savez_compressed(os.path.join(HERE, "mla.npz"), **out)
+
+
+def make_indexer_fp8(golden_ref) -> None:
+    """The FP8 indexer (BASELINE config 2's numerics) through the reference's
+    ``indexer_scores`` / ``topk_indices`` (golden_ref.py:213-243): q quantised per
+    (token, head) and k per token to e4m3 with absmax / 448 scales (torch's cast), the
+    reference fed the dequantised values q * s_q and k * s_k.  The reference's score
+    carries Di**-0.5 (the kernel's ``softmax_scale``) and no position offset."""
+    out = {}
+    g = torch.Generator().manual_seed(6)
+    b, s, hi, di, t, ratio = 2, 48, 16, 64, 24, 2
+    q = torch.randn(b, s, hi, di, generator=g)
+    k = torch.randn(b, t, di, generator=g)
+    w = torch.randn(b, s, hi, generator=g) / 8
+    qc, sq = _fp8_absmax(q, di)
+    kc, sk = _fp8_absmax(k, di)
+    qd, kd = _e4m3_dequant(qc, sq, di), _e4m3_dequant(kc, sk, di)
+    sc = golden_ref.indexer_scores(qd, kd, w, ratio)
+    out.update({"q": q.numpy(), "k": k.numpy(), "w": w.numpy(), "q_codes": qc.numpy(), "k_codes": kc.numpy(),
+                "sq": sq[..., 0].numpy(), "sk": sk[..., 0].numpy(), "scores": sc.numpy(),
+                "params": np.array([ratio], np.int64)})
+    for topk in (5, 12, 30):
+        out[f"topk{topk}"] = golden_ref.topk_indices(sc, topk).numpy()
+    np.savez_compressed(os.path.join(HERE, "indexer_fp8.npz"), **out)
+
+
 def make_candidates() -> None:
     """Level one through the reference's ``select_candidate_blocks``
     (archs/owlet1/indexer.py:14-41 = archs/dsv4/modeling_deepseek_v41.py:427-454); level two
@@ -226,6 +375,10 @@ if __name__ == "__main__":
         make_attention(golden_ref)
     if not only or "indexer" in only:
         make_indexer(golden_ref)
+    if not only or "mla" in only:
+        make_mla(golden_ref)
+    if not only or "indexer_fp8" in only:
+        make_indexer_fp8(golden_ref)
     if not only or "candidates" in only:
         make_candidates()
     if not only or "compressor" in only:

@@ -287,3 +287,34 @@ def test_swa_attn_autograd(cuda):
     ref = A.attend_bwd(_np(q.detach()), _np(kv.detach())[:, :, 0], _np(do), window=50)
     _check_grad(q.grad, ref["dq"], "autograd dq")
     _check_grad(kv.grad[:, :, 0], ref["dkv"], "autograd dkv")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("sinks", [False, True])
+def test_csa2_attn_autograd(cuda, sinks):
+    """csa2_attn/attn_test.py:98-152 through the autograd wrapper (``csa2_attn/attn.py:20-55``):
+    q, kv, main_kv (and sinks) receive the gradients ``csa2_attn.bwd`` gives, which match the
+    oracle's closed form; duplicate and -1 indices; indices get no gradient."""
+    import torch
+    from mzoo_b200 import csa2_attn
+    q, kv, _, main, idx, sk = _inputs(torch, cuda, 2, 160, 16, 128, G=48, topk=40, seed=21, dup=True, holes=True,
+                                      sinks=sinks)
+    do = _do(torch, cuda, q.shape, 13)
+    leaves = [x.detach().clone().requires_grad_() for x in (q, kv, main)]
+    sl = sk.detach().clone().requires_grad_() if sinks else None
+    o = csa2_attn.attn(*leaves, idx, window=64, compress_ratio=4, sinks=sl)
+    o.backward(do)
+    o_ref, lse = csa2_attn.fwd(q, kv, main, idx, window=64, compress_ratio=4, sinks=sk)
+    assert torch.equal(o.detach(), o_ref)
+    dq, dkv, dmain, dsinks = csa2_attn.bwd(q, kv, main, idx, o_ref, lse, do, window=64, compress_ratio=4, sinks=sk)
+    assert torch.equal(leaves[0].grad, dq) and torch.equal(leaves[1].grad, dkv)
+    # dmain is accumulated by fp32 atomics (order varies run to run): compare to rounding
+    assert (leaves[2].grad.float() - dmain.float()).abs().max() <= 2e-2
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=64, main_kv=_np(main)[:, :, 0],
+                       indices=idx.cpu().numpy(), sinks=_np(sk) if sinks else None)
+    _check_grad(leaves[0].grad, ref["dq"], "autograd csa2 dq")
+    _check_grad(leaves[1].grad[:, :, 0], ref["dkv"], "autograd csa2 dkv")
+    _check_grad(leaves[2].grad[:, :, 0], ref["dmain"], "autograd csa2 dmain")
+    if sinks:
+        assert torch.equal(sl.grad, dsinks)
+        _check_grad(sl.grad, ref["dsinks"], "autograd csa2 dsinks")

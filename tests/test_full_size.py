@@ -1,0 +1,117 @@
+"""Parity at the BASELINE configs' full sizes (the workloads ``bench.py`` times, built by the
+bench's own input generators): every output row is checked for the size-independent
+properties (ascending distinct in-range indices, finite outputs), and a sample of rows
+against the CPU oracle -- bit-exact index sets for the indexer, max-abs 2e-2 for attention
+outputs and lse.
+
+- C2: B=2, 4096 queries at positions 12288..16383 x 4096 compressed keys, Hi=64, Di=128,
+  FP8, top-512: 256 sampled query rows (four 64-row chunks over both batches).
+- C3: 16384 tokens x 128 heads, top-2048 compressed + 128-token window: 32 sampled tokens.
+- C4: 128 sequences with lengths in [8192, 131072], paged FP8 latent caches, decode indexer
+  top-2048 + window 128: 8 sampled sequences (indexer sets and attention).
+"""
+
+import numpy as np
+import pytest
+
+import bench
+from oracle import indexer as I
+from oracle import mla as M
+
+ATOL = 2e-2
+
+
+def _check_index_rows(idx: np.ndarray, vis: np.ndarray, topk: int) -> None:
+    """Every row: ascending, distinct, in [0, vis), exactly min(topk, vis) entries, -1 after."""
+    n = (idx >= 0).sum(-1)
+    assert np.array_equal(n, np.minimum(topk, vis)), "wrong number of selected keys"
+    first_pad = np.where(idx < 0, 1, 0).argmax(-1)
+    ok_pad = np.where(n < topk, first_pad == n, True)
+    assert ok_pad.all(), "-1 padding not at the end"
+    d = np.diff(np.where(idx < 0, np.iinfo(np.int32).max, idx), axis=-1)
+    assert (d > 0).all(), "indices not strictly ascending"
+    assert (idx.max(-1) < vis).all(), "index beyond the visible range"
+
+
+@pytest.mark.gpu
+def test_c2_indexer_full_size(cuda):
+    import torch
+    from mzoo_b200 import indexer
+    C2 = bench.C2
+    q, k, w = bench.c2_inputs(torch, seed=0)
+    q8, sq = indexer.quantize_fp8(q.to(cuda))
+    k8, sk = indexer.quantize_fp8(k.to(cuda))
+    wd = w.to(cuda)
+    got = indexer.attn(q8, k8, wd, compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"],
+                       scales=(sq, sk), check=True).cpu().numpy()
+    B, S, T = C2["B"], C2["S"], C2["T"]
+    vis = np.minimum(T, (C2["q_offset"] + np.arange(S) + 1) // C2["ratio"])
+    _check_index_rows(got, np.broadcast_to(vis, (B, S)), C2["topk"])
+    qv, kv = q8.float().cpu().numpy(), k8.float().cpu().numpy()
+    sqn, skn, wn = sq.cpu().numpy(), sk.cpu().numpy(), w.numpy()
+    for b, s0 in ((0, 0), (0, 2048), (1, 1000), (1, S - 64)):
+        s1 = s0 + 64
+        off = C2["q_offset"] + s0
+        canon = I.canonical_scores(qv[b:b + 1, s0:s1], kv[b:b + 1], wn[b:b + 1, s0:s1], sqn[b:b + 1, s0:s1],
+                                   skn[b:b + 1], C2["ratio"], off)
+        ref = I.canonical_topk(canon, C2["topk"], C2["ratio"], off)
+        assert np.array_equal(got[b:b + 1, s0:s1], ref), (b, s0)
+
+
+@pytest.mark.gpu
+def test_c3_prefill_full_size(cuda):
+    import torch
+    from mzoo_b200 import sparse_mla
+    C3 = bench.C3
+    q, raw, cmp, idx = bench.c3_inputs(torch, cuda, seed=0)
+    o, lse = sparse_mla.prefill(q, raw, cmp, idx, window=C3["window"], check=True)
+    assert torch.isfinite(lse).all() and not torch.isnan(o).any()
+    S = C3["S"]
+    toks = [0, 1, 3, 127, 128, 4095, 4096, 8191] + [int(t) for t in np.linspace(200, S - 1, 24)]
+    raw_h, cmp_h = raw[0].cpu().numpy(), cmp[0].cpu().numpy()
+    idx_h = idx[0].cpu().numpy()
+    tk = torch.tensor(toks, device=cuda)
+    qs = q[0, tk].float().cpu().numpy()
+    os_, ls_ = o[0, tk].float().cpu().numpy(), lse[0, :, tk].cpu().numpy()
+    for i, t in enumerate(toks):
+        keys = M.unpack_rows(M.token_keys(raw_h, cmp_h, idx_h[t], t, C3["window"]))
+        ro, rl = M.attend_rows(qs[i], keys, 576**-0.5)
+        eo, el = np.abs(os_[i] - ro).max(), np.abs(ls_[:, i] - rl).max()
+        assert eo <= ATOL and el <= ATOL, (t, eo, el)
+
+
+@pytest.mark.gpu
+def test_c4_decode_full_size(cuda):
+    import torch
+    from mzoo_b200 import indexer, sparse_mla
+    C4 = bench.C4
+    lens = bench.c4_lens(torch)
+    seqs = list(range(C4["B"]))
+    x = bench.c4_inputs(torch, cuda, seqs, lens)
+    idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"],
+                       scales=(x["sq"], x["sk"]), q_pos=x["pos"], check=True)
+    o, lse = sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"], idx[:, 0],
+                               window=C4["window"], check=True)
+    idx_h = idx[:, 0].cpu().numpy()
+    L = lens.numpy()
+    _check_index_rows(idx_h, L // C4["ratio"], C4["topk"])
+    assert torch.isfinite(lse).all() and not torch.isnan(o).any()
+    order = np.argsort(L)
+    sample = sorted({int(order[0]), int(order[-1]), *[int(order[i]) for i in (16, 40, 64, 90, 110)], 0})
+    for b in sample:
+        T = int(L[b]) // C4["ratio"]
+        qv = x["q8"][b:b + 1].float().cpu().numpy()
+        kv = x["k8"][b:b + 1, :T].float().cpu().numpy()
+        canon = I.canonical_scores(qv, kv, x["w"][b:b + 1].cpu().numpy(), x["sq"][b:b + 1].cpu().numpy(),
+                                   x["sk"][b:b + 1, :T].cpu().numpy(), C4["ratio"], int(L[b]) - 1)
+        ref_idx = I.canonical_topk(canon, C4["topk"], C4["ratio"], int(L[b]) - 1)[0, 0]
+        assert np.array_equal(idx_h[b], ref_idx), b
+        # attention over the window + selected rows, gathered through the page tables on the GPU
+        pos = torch.arange(max(0, int(L[b]) - C4["window"]), int(L[b]), device=cuda)
+        sel = idx[b, 0][idx[b, 0] >= 0].long()
+        rows = torch.cat([x["raw"][x["pt"][b, pos // 64].long(), pos % 64],
+                          x["cmp"][x["cpt"][b, sel // 64].long(), sel % 64]])
+        ro, rl = M.attend_rows(x["q"][b].float().cpu().numpy(), M.unpack_rows(rows.cpu().numpy()), 576**-0.5)
+        eo = np.abs(o[b].float().cpu().numpy() - ro).max()
+        el = np.abs(lse[b].cpu().numpy() - rl).max()
+        assert eo <= ATOL and el <= ATOL, (b, eo, el)

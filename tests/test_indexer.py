@@ -51,6 +51,44 @@ def test_canonical_topk_equals_reference_sets():
         assert np.array_equal(I.canonical_topk(c, topk, 2), ref.astype(np.int32))
 
 
+def _golden_fp8():
+    return np.load(os.path.join(GOLDEN, "indexer_fp8.npz"))
+
+
+def test_oracle_fp8_quantiser_matches_reference_fixture():
+    """The oracle's absmax e4m3 quantiser equals torch's float8_e4m3fn cast (codes, scales)."""
+    from oracle import mla as M
+    d = _golden_fp8()
+    di = d["q"].shape[-1]
+    for x, codes, sc in ((d["q"], d["q_codes"], d["sq"]), (d["k"], d["k_codes"], d["sk"])):
+        v, s = Q.quantize_fp8_rows(x, di)
+        assert np.array_equal(s[..., 0], sc)
+        assert np.array_equal(v, M.e4m3_values(codes))
+
+
+def test_oracle_fp8_scores_and_sets_match_reference():
+    """FP8 indexer numerics: the reference's fp32 ``indexer_scores`` on the dequantised
+    q * s_q, k * s_k (golden_ref.py:213-227) equals the oracle's, and the canonical exact
+    definition the kernel selects against (scale = Di**-0.5) picks the reference's sets."""
+    from oracle import mla as M
+    d = _golden_fp8()
+    ratio = int(d["params"][0])
+    qv, kv = M.e4m3_values(d["q_codes"]), M.e4m3_values(d["k_codes"])
+    di = qv.shape[-1]
+    qd = (qv * d["sq"][..., None]).astype(np.float32)
+    kd = (kv * d["sk"][..., None]).astype(np.float32)
+    got = I.scores_ref(qd, kd, d["w"], ratio)
+    ref = d["scores"]
+    fin = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), fin)
+    np.testing.assert_allclose(got[fin], ref[fin], rtol=0, atol=1e-5)
+    canon = I.canonical_scores(qv, kv, d["w"], d["sq"], d["sk"], ratio, 0, scale=float(np.float32(di**-0.5)))
+    for topk in (5, 12, 30):
+        r = np.sort(np.where(d[f"topk{topk}"] < 0, 1 << 30, d[f"topk{topk}"]), -1)
+        r = np.where(r == 1 << 30, -1, r)
+        assert np.array_equal(I.canonical_topk(canon, topk, ratio), r.astype(np.int32)), topk
+
+
 def test_canonical_fp8_dot_is_order_independent():
     """e4m3 products are multiples of 2^-18 below 2^17.6: any fp64 summation order is exact."""
     rng = np.random.default_rng(0)
@@ -229,6 +267,24 @@ def test_topk_fp8_exact(cuda, q_offset):
     kv = k8.float().cpu().numpy()
     canon = I.canonical_scores(qv, kv, w.cpu().numpy(), sq.cpu().numpy(), sk.cpu().numpy(), ratio, q_offset)
     assert np.array_equal(got.cpu().numpy(), I.canonical_topk(canon, topk, ratio, q_offset))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("topk", [5, 12, 30])
+def test_topk_fp8_matches_reference_fixture(cuda, topk):
+    """The FP8 kernel path (e4m3 codes + scales, softmax_scale = Di**-0.5) on the reference
+    fixture's own inputs selects the reference's index sets."""
+    import torch
+    from mzoo_b200 import indexer
+    d = _golden_fp8()
+    ratio = int(d["params"][0])
+    di = d["q"].shape[-1]
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)  # noqa: E731
+    q8, k8 = t(d["q_codes"]).view(torch.float8_e4m3fn), t(d["k_codes"]).view(torch.float8_e4m3fn)
+    got = indexer.attn(q8, k8, t(d["w"]), compress_ratio=ratio, topk=topk, scales=(t(d["sq"]), t(d["sk"])),
+                       softmax_scale=di**-0.5).cpu().numpy()
+    r = np.sort(np.where(d[f"topk{topk}"] < 0, 1 << 30, d[f"topk{topk}"]), -1)
+    assert np.array_equal(got, np.where(r == 1 << 30, -1, r).astype(np.int32))
 
 
 @pytest.mark.gpu

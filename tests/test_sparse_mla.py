@@ -6,10 +6,14 @@ same packed rows.  Cases mirror the reference's csa2 test matrix
 window, duplicate indices (counted twice), and a window-only degenerate case.
 """
 
+import os
+
 import numpy as np
 import pytest
 
+from conftest import GOLDEN
 from oracle import mla as M
+from oracle.quant import bf16_to_f32
 
 ATOL = 2e-2
 
@@ -34,6 +38,42 @@ def test_oracle_attend_matches_dense_softmax():
     p = np.exp(z) / np.exp(z).sum(-1, keepdims=True)
     np.testing.assert_allclose(o, p @ k[:, :512], rtol=1e-12)
     np.testing.assert_allclose(lse, np.log(np.exp(z).sum(-1)), rtol=1e-12)
+
+
+def _golden():
+    return np.load(os.path.join(GOLDEN, "mla.npz"))
+
+
+def test_oracle_pack_matches_reference_fixture():
+    """The oracle's row packing (absmax/448 per 64 channels, e4m3 round to nearest even,
+    bf16 rope) equals torch's float8_e4m3fn / bfloat16 casts bit for bit."""
+    d = _golden()
+    assert np.array_equal(M.pack_rows(d["pre.kv"]), d["pre.raw_rows"])
+    assert np.array_equal(M.pack_rows(d["pre.cmp"]), d["pre.cmp_rows"])
+
+
+def test_oracle_prefill_matches_reference_attend():
+    """oracle.mla.sparse_prefill against the reference's ``_attend`` (golden_ref.py:83-100)
+    on each query's gathered rows: window, duplicates counted twice, -1 and out-of-range
+    slots empty, absolute positions (q_offset)."""
+    d = _golden()
+    q_offset, window = (int(x) for x in d["pre.params"])
+    q = bf16_to_f32(d["pre.q"])[None]
+    o, lse = M.sparse_prefill(q, d["pre.raw_rows"][None], d["pre.cmp_rows"][None], d["pre.idx"][None], window,
+                              q_offset=q_offset)
+    np.testing.assert_allclose(o[0], d["pre.o"], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(lse[0], d["pre.lse"], rtol=0, atol=2e-5)
+
+
+def test_oracle_decode_matches_reference_attend():
+    """oracle.mla.sparse_decode (page tables, window over the last tokens, compressed entries
+    below each sequence's compressed length) against the reference's ``_attend``."""
+    d = _golden()
+    window = int(d["dec.params"][0])
+    o, lse = M.sparse_decode(bf16_to_f32(d["dec.q"]), d["dec.raw_pages"], d["dec.pt"], d["dec.lens"],
+                             d["dec.cmp_pages"], d["dec.cpt"], d["dec.clens"], d["dec.idx"], window)
+    np.testing.assert_allclose(o, d["dec.o"], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(lse, d["dec.lse"], rtol=0, atol=2e-5)
 
 
 # ----------------------------------------------------------------------------- GPU helpers
