@@ -246,13 +246,33 @@ def bench_window(args, torch, dist, rank, world, device) -> dict:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # A step is ~2 GFLOP: launched one op at a time it is bound by the host's launch rate,
+    # so the timed step replays a CUDA graph of the same launches (captured after warm-up).
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        step()
+        with torch.cuda.graph(graph, stream=cap):
+            o_graph, lse_graph = step()
+    torch.cuda.current_stream(device).wait_stream(cap)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
     sampler.ready()
     if dist:
         dist.barrier()
-    t_steps = timer.run(step, args.steps)
-    clocks = sampler.stop(busy=step, min_samples=2)
+    t_steps = timer.run(graph.replay, args.steps)
+    clocks = sampler.stop(busy=graph.replay, min_samples=2)
     qb, kvb = q.to(torch.bfloat16), kv.to(torch.bfloat16)
-    t_k = timer.run(lambda: swa_attn.fwd(qb, kvb, window=W), args.steps)
+    kgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        swa_attn.fwd(qb, kvb, window=W)
+        with torch.cuda.graph(kgraph, stream=cap):
+            swa_attn.fwd(qb, kvb, window=W)
+    torch.cuda.current_stream(device).wait_stream(cap)
+    kgraph.replay()
+    t_k = timer.run(kgraph.replay, args.steps)
     hq, hkv = qh.pin_memory(), kvh.pin_memory()
     dq, dkv = torch.empty_like(q), torch.empty_like(kv)
     ho = torch.empty(qh.shape, dtype=torch.float32).pin_memory()
@@ -269,6 +289,8 @@ def bench_window(args, torch, dist, rank, world, device) -> dict:
         e2e()
     t_e2e = timer.run(e2e, args.steps, flush=False)
     o_gpu, lse_gpu = step()
+    torch.cuda.synchronize()
+    assert torch.equal(o_gpu, o_graph) and torch.equal(lse_gpu, lse_graph), "graph replay differs from the step"
     ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
     ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
     ms_k = sum(t_k) / len(t_k)
@@ -280,6 +302,8 @@ def bench_window(args, torch, dist, rank, world, device) -> dict:
         "unit": "TFLOP/s", "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16 (fp32 inputs cast on the device, fp32 acc)", "data": "synthetic (seeded N(0,1) fp32)",
         "config": c1_config(world),
+        "timing": "value: CUDA-graph replay of the step's launches (casts, window kernel, cast back); e2e: the "
+                  "public API called op by op with host copies",
         "e2e": {"value": flops * world / (ms_e2e * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": (hq.numel() + hkv.numel()) * 4,
                 "d2h_bytes_per_step": (ho.numel() + hl.numel()) * 4},
@@ -363,10 +387,10 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     from mzoo_b200 import indexer
 
     from mzoo_b200.sharding import shard_tokens
-    q, k, w = c2_inputs(torch, seed=0)  # the same workload on every rank
+    q, k, w_host = c2_inputs(torch, seed=0)  # the same workload on every rank
     q8, sq = indexer.quantize_fp8(q.to(device))
     k8, sk = indexer.quantize_fp8(k.to(device))
-    w = w.to(device)
+    w = w_host.to(device)
     B, S, T, Hi, Di = (C2[x] for x in ("B", "S", "T", "Hi", "Di"))
     kw = dict(compress_ratio=C2["ratio"], topk=C2["topk"], q_offset=C2["q_offset"], scales=(sq, sk))
     toks = list(range(S))
@@ -441,7 +465,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
         "clocks": clocks,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        r = cpu_indexer(torch, q, k, w)
+        r = cpu_indexer(torch, q, k, w_host)
         got = out_idx[0, C2["S"] - r.pop("n"):].cpu()
         ref = r.pop("result")
         r["parity"] = {"rows": int(got.shape[0]), "equal_sets": int(_set_equal_rows(torch, got, ref)),

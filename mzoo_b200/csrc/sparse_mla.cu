@@ -18,9 +18,10 @@
 //
 // Warp roles per CTA (512 threads):
 //   0      TMA of this CTA's Q half (64 heads x 576, 9 swizzled 64-column blocks)
-//   1      TMEM allocation; in the leader CTA, the single MMA-issuing thread
-//   2      V copier: assembles the V tile from K tiles (below)
-//   3      V relay: waits for this CTA's V tile, tells the leader and the K-tile owners
+//   1      TMEM allocation; in the leader CTA, the thread issuing the QK^T MMAs
+//   2      V copier: assembles the V tile from K tiles (below), waits for this CTA's V
+//          tile and tells the leader and the K-tile owners
+//   3      in the leader CTA, the thread issuing the PV MMAs
 //   4-7    softmax / O correction / epilogue (thread = TMEM lane = (head, key half))
 //   8-11   K producers for even tiles, 12-15 for odd tiles: gather + dequantise this CTA's
 //          32 keys x 576 channels to bf16 (two groups, so each has two tile-times to hide
@@ -29,10 +30,13 @@
 // block of both CTAs' K tiles (32 keys each, identical 128-byte swizzle), so the copier
 // pushes 4 KB blocks of its K tile into its own and the peer's V tile with
 // cp.async.bulk shared::cta -> shared::cluster, completing on the destination's V_FULL.
-// MMA order per item: QK_0, QK_1, PV_0, QK_2, PV_1, ...; tile g's S completion implies
-// PV_{g-2} finished (in-order tensor pipe), so P is double-buffered without extra waits.
-// The running max is only raised when it grows by more than 2^8 (in exp2 units), which
-// skips most O corrections.
+// QK^T and PV are issued by two threads: a tcgen05.mma issue blocks until the tensor pipe
+// takes the instruction, so one thread alternating QK_j, PV_{j-1} and their barrier waits
+// left the pipe idle between the bursts (measured: ~4500 cycles per 64-key tile against
+// ~2150 of MMA work); with two issuers one thread's waits overlap the other's MMAs.  The
+// softmax then waits P_EMPTY (PV of the tile two back done) before it rewrites a P buffer
+// or rescales O.  The running max is only raised when it grows by more than 2^8 (in exp2
+// units), which skips most O corrections.
 #include "tc.cuh"
 
 namespace mzb {
@@ -66,7 +70,7 @@ enum Bar {
   V_READY, V_READY1,  // leader: both CTAs' V tiles complete (2 relays)
   V_EMPTY, V_EMPTY1,  // local (multicast commit): PV done
   S_FULL, S_FULL1, S_EMPTY, S_EMPTY1,
-  P_FULL, P_FULL1, O_DONE, O_EMPTY,
+  P_FULL, P_FULL1, P_EMPTY, P_EMPTY1, O_DONE, O_EMPTY,
   XCH, XCH1, XCH2, XCH3,  // row-max exchange per (S buffer, warp pair {4,6} / {5,7}), local
   XL, XL1,                // row-sum exchange per warp pair, local
   O_FINAL,            // multicast commit after an item's last PV (epilogue, item parity)
@@ -170,15 +174,13 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// Every wait is CTA-scope, including on barriers the peer CTA or the pair's MMA commits
+// arrive on: the operands behind them sit in each CTA's own shared memory / TMEM (written
+// by its own threads and fenced to the async proxy, or by bulk copies and TMA that complete
+// on the barrier's transaction count), never read by the other CTA's threads.  A
+// cluster-scope acquire costs ~130 cycles per check on the MMA issuers' critical path.
 #define MLA_WAIT(bar, par, code)                                      \
   if (!tc::mbar_wait(&bars[bar], (par), a.err, (code))) {             \
-    abort_flag = 1;                                                   \
-    break;                                                            \
-  }
-// barriers the peer CTA or the pair's MMA completions arrive on need a cluster-scope
-// acquire so that the peer's shared-memory writes / TMEM reads are ordered before what follows
-#define MLA_WAIT_CL(bar, par, code)                                   \
-  if (!tc::mbar_wait_cl(&bars[bar], (par), a.err, (code))) {          \
     abort_flag = 1;                                                   \
     break;                                                            \
   }
@@ -211,7 +213,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                                    4, 4, 2, 2,        // K_WRIT x2, K_CP x2
                                    1, 1, 2, 2, 1, 1,  // V_FULL x2, V_READY x2, V_EMPTY x2
                                    1, 1, 8, 8,        // S_FULL x2, S_EMPTY x2
-                                   8, 8, 1, 8,        // P_FULL x2, O_DONE, O_EMPTY
+                                   8, 8, 1, 1, 1, 8,  // P_FULL x2, P_EMPTY x2, O_DONE, O_EMPTY
                                    2, 2, 2, 2, 2, 2,  // XCH x4, XL x2 (the two warps holding one head's key halves)
                                    1};                // O_FINAL
     for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], counts[i]);
@@ -226,11 +228,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   tc::fence_after_sync();
   const uint32_t tmem = tmem_slot;
   auto leader_bar = [&](int i) { return tc::mapa(smem_u32(&bars[i]), 0); };
-  // arrive on a leader-CTA barrier: CTA scope from the leader itself (its waiters acquire at
-  // cluster scope, which covers it), a cluster-scope release from the peer
+  // arrive on a leader-CTA barrier: a local arrive from the leader itself, a remote one
+  // (CTA-scope release, see tc::mbar_arrive_remote) from the peer
   auto arrive_leader = [&](int i) {
     if (rank == 0) tc::mbar_arrive(&bars[i]);
-    else tc::mbar_arrive_cluster(leader_bar(i));
+    else tc::mbar_arrive_remote(leader_bar(i));
   };
   auto n_tiles = [&](int tk) { return (a.n_slots[tk] + NT - 1) / NT; };
   // work item = (token, key-range split), heaviest tokens first; tiles [t0, t1) of the
@@ -253,7 +255,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         int tk, sp, t0, t1;
         item_range(it, tk, sp, t0, t1);
         if (t0 >= t1) continue;
-        MLA_WAIT_CL(Q_EMPTY, (ii & 1) ^ 1, 201);
+        MLA_WAIT(Q_EMPTY, (ii & 1) ^ 1, 201);
         tc::mbar_expect_tx(&bars[Q_FULL], Q_BYTES);
         for (int cb = 0; cb < QBLK; ++cb)
           tc::tma_load_2d(qs + cb * HC * 128, &tq, &bars[Q_FULL], cb * 64, tk * H + int(rank) * HC);
@@ -266,48 +268,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       if (issued) tc::mbar_wait(&bars[Q_FULL], (ii & 1), nullptr, 0);  // drain before exit
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (leader)
+    // ------------------------------------------------------------------ QK^T issuer (leader)
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_qk = tc::make_idesc(128, NT, 1, 1);
-      const uint32_t idesc_pv = tc::make_idesc(128, 256, 1, 1, false, true);
-      // descriptors built once; the unrolled loops add compile-time offsets (a single
+      // descriptors built once; the unrolled loop adds compile-time offsets (a single
       // thread issues every MMA, so per-MMA descriptor arithmetic would throttle issue)
       const uint64_t qd = tc::make_sdesc<128>(smem_u32(qs), 16, 1024);
       const uint64_t kd[2] = {tc::make_sdesc<128>(smem_u32(ks), 16, 1024),
                               tc::make_sdesc<128>(smem_u32(ks + K_BYTES), 16, 1024)};
-      const uint64_t pd[2] = {tc::make_sdesc<128>(smem_u32(ps), 16, 1024),
-                              tc::make_sdesc<128>(smem_u32(ps + P_BYTES), 16, 1024)};
-      const uint64_t vd[2] = {tc::make_sdesc<128>(smem_u32(vs), 8192, 1024),
-                              tc::make_sdesc<128>(smem_u32(vs + V_BYTES), 8192, 1024)};
       int g = 0, ii = 0;
-      auto pv = [&](int gg, bool first, int item) -> bool {
-        const int st = gg & 1, ph = (gg >> 1) & 1;
-        if (first && !tc::mbar_wait_cl(&bars[O_EMPTY], (item & 1) ^ 1, a.err, 211)) return false;
-        if (!tc::mbar_wait_cl(&bars[V_READY + st], ph, a.err, 212)) return false;
-        if (!tc::mbar_wait_cl(&bars[P_FULL + st], ph, a.err, 213)) return false;
-        tc::fence_after_sync();
-        const uint64_t ad0 = st ? pd[1] : pd[0], bd0 = st ? vd[1] : vd[0];
-#pragma unroll
-        for (int i = 0; i < 2; ++i) {
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj)
-            tc::mma2_f16(tmem + i * 128, tc::sdesc_add(ad0, jj * 32), tc::sdesc_add(bd0, 2 * i * 8192 + jj * 2048),
-                         idesc_pv, (first && jj == 0) ? 0u : 1u);
-        }
-        tc::mma2_commit_mc(&bars[V_EMPTY + st], 3);
-        tc::mma2_commit_mc(&bars[O_DONE], 3);
-        return true;
-      };
       for (int it = pair; it < items && !abort_flag; it += npairs) {
         int tk, sp, t0, t1;
         item_range(it, tk, sp, t0, t1);
         if (t0 >= t1) continue;
-        MLA_WAIT_CL(Q_READY, ii & 1, 210);
+        MLA_WAIT(Q_READY, ii & 1, 210);
         bool ok = true;
         for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
-          if (!tc::mbar_wait_cl(&bars[K_FULL + st], ph, a.err, 214) ||
-              !tc::mbar_wait_cl(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[K_FULL + st], ph, a.err, 214) ||
+              !tc::mbar_wait(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
           tc::fence_after_sync();
           const uint32_t d = tmem + S_COL0 + st * 32;
           const uint64_t kb = st ? kd[1] : kd[0];
@@ -320,9 +299,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
           tc::mma2_commit_mc(&bars[K_EMPTY + st], 3);
           tc::mma2_commit_mc(&bars[S_FULL + st], 3);
           if (j == t1 - 1) tc::mma2_commit_mc(&bars[Q_EMPTY], 3);
-          if (j > t0 && !pv(g - 1, j == t0 + 1, ii)) { ok = false; break; }
         }
-        if (!ok || !pv(g - 1, t1 - t0 == 1, ii)) { abort_flag = 1; break; }
+        if (!ok) { abort_flag = 1; break; }
+        ++ii;
+      }
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------------ PV issuer (leader)
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc_pv = tc::make_idesc(128, 256, 1, 1, false, true);
+      const uint64_t pd[2] = {tc::make_sdesc<128>(smem_u32(ps), 16, 1024),
+                              tc::make_sdesc<128>(smem_u32(ps + P_BYTES), 16, 1024)};
+      const uint64_t vd[2] = {tc::make_sdesc<128>(smem_u32(vs), 8192, 1024),
+                              tc::make_sdesc<128>(smem_u32(vs + V_BYTES), 8192, 1024)};
+      int g = 0, ii = 0;
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
+        if (t0 >= t1) continue;
+        // the previous item's epilogue has read O
+        MLA_WAIT(O_EMPTY, (ii & 1) ^ 1, 211);
+        bool ok = true;
+        for (int j = t0; j < t1; ++j, ++g) {
+          const int st = g & 1, ph = (g >> 1) & 1;
+          if (!tc::mbar_wait(&bars[V_READY + st], ph, a.err, 212) ||
+              !tc::mbar_wait(&bars[P_FULL + st], ph, a.err, 213)) { ok = false; break; }
+          tc::fence_after_sync();
+          const uint64_t ad0 = st ? pd[1] : pd[0], bd0 = st ? vd[1] : vd[0];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj)
+              tc::mma2_f16(tmem + i * 128, tc::sdesc_add(ad0, jj * 32), tc::sdesc_add(bd0, 2 * i * 8192 + jj * 2048),
+                           idesc_pv, (j == t0 && jj == 0) ? 0u : 1u);
+          }
+          tc::mma2_commit_mc(&bars[V_EMPTY + st], 3);
+          tc::mma2_commit_mc(&bars[P_EMPTY + st], 3);
+          tc::mma2_commit_mc(&bars[O_DONE], 3);
+        }
+        if (!ok) { abort_flag = 1; break; }
         tc::mma2_commit_mc(&bars[O_FINAL], 3);
         ++ii;
       }
@@ -363,7 +378,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         if (j + 1 < t1) code_next = slot_code((j + 1) * NT + kofs);
         const int p = j * NT + kofs;
         const uint32_t vmask = __ballot_sync(0xffffffffu, p < s.n_win || (code >= 0 && code < s.g_lim));
-        if (!tc::mbar_wait_cl(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
+        if (!tc::mbar_wait(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
         tc::fence_after_sync();
         uint32_t sr[32];
         tc::tmem_ld32(tc::taddr(tmem, sw * 32, S_COL0 + st * 32), sr);
@@ -386,6 +401,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         if (!tc::mbar_wait(&bars[XCH + 2 * st + (sw & 1)], ph, a.err, 223)) { ok = false; break; }
         mt = fmaxf(mt, red_m[st][l ^ 64]);
         const bool need = mt * sl > m * sl + 8.0f;
+        // PV of the tile two back (same P buffer) is done: P may be rewritten, and O_DONE's
+        // phase below cannot alias an older PV
+        if (!tc::mbar_wait(&bars[P_EMPTY + st], ph ^ 1, a.err, 225)) { ok = false; break; }
         const float m_new = need ? mt : m;
         const float alpha = fast_exp2((m - m_new) * sl);
         const float ms = m_new * sl;
@@ -405,7 +423,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         for (int c = 0; c < 4; ++c)
           st_shared16(prow + (((kh * 4 + c) ^ (hrow & 7)) * 16), make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
         if (j > t0 && __any_sync(0xffffffffu, need)) {
-          if (!tc::mbar_wait_cl(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
           tc::fence_after_sync();
           for (int c0 = 0; c0 < 256; c0 += 32) {
             uint32_t ov[32];
@@ -426,7 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       if (!ok) { abort_flag = 1; break; }
       // epilogue: O / l, lse.  O_FINAL, not O_DONE: two PVs of this item can still be in
       // flight here, and O_DONE's parity would alias the phase of an older PV.
-      MLA_WAIT_CL(O_FINAL, ii & 1, 222);
+      MLA_WAIT(O_FINAL, ii & 1, 222);
       tc::fence_after_sync();
       red_l[ii & 1][l] = lsum;
       __syncwarp();
@@ -505,8 +523,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int q = 0; q < 8; ++q) sc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
         // the stage is free once its QK MMA is done and the copies out of it have landed
-        if (!tc::mbar_wait_cl(&bars[K_EMPTY + st], ph ^ 1, a.err, 230) ||
-            !tc::mbar_wait_cl(&bars[K_CP + st], ph ^ 1, a.err, 231)) { ok = false; break; }
+        if (!tc::mbar_wait(&bars[K_EMPTY + st], ph ^ 1, a.err, 230) ||
+            !tc::mbar_wait(&bars[K_CP + st], ph ^ 1, a.err, 231)) { ok = false; break; }
         uint8_t* kt = ks + st * K_BYTES + kk * 128;
 #pragma unroll
         for (int q = 0; q < 10; ++q) {
@@ -531,9 +549,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       if (!ok) { abort_flag = 1; break; }
     }
   } else if (warp == 2) {
-    // ------------------------------------------------------------------ V copier
+    // ------------------------------------------------------------------ V copier + relay
     // V tile block lb (keys 0-31 | keys 32-63) of CTA r holds global channel block
-    // gb = (lb >> 1) * 4 + 2 r + (lb & 1); this CTA supplies its half of the keys.
+    // gb = (lb >> 1) * 4 + 2 r + (lb & 1); this CTA supplies its half of the keys.  Once
+    // both CTAs' copies into this CTA's V tile have landed, it tells the leader (V_READY)
+    // and both K-tile owners (K_CP: the stage may be overwritten).
     if (lane == 0) {
       int g = 0;
       for (int it = pair; it < items && !abort_flag; it += npairs) {
@@ -543,7 +563,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
           if (!tc::mbar_wait(&bars[K_WRIT + st], ph, a.err, 250) ||
-              !tc::mbar_wait_cl(&bars[V_EMPTY + st], ph ^ 1, a.err, 251)) { ok = false; break; }
+              !tc::mbar_wait(&bars[V_EMPTY + st], ph ^ 1, a.err, 251)) { ok = false; break; }
           const uint32_t k_base = smem_u32(ks + st * K_BYTES), v_base = smem_u32(vs + st * V_BYTES);
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
@@ -555,31 +575,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
               tc::bulk_copy_s2cluster(dst, k_base + gb * 4096, 4096, dst_bar);
             }
           }
-        }
-        if (!ok) { abort_flag = 1; break; }
-      }
-    }
-  } else if (warp == 3) {
-    // ------------------------------------------------------------------ V relay
-    if (lane == 0) {
-      int g = 0;
-      for (int it = pair; it < items && !abort_flag; it += npairs) {
-        int tk, sp, t0, t1;
-        item_range(it, tk, sp, t0, t1);
-        bool ok = true;
-        for (int j = t0; j < t1; ++j, ++g) {
-          const int st = g & 1, ph = (g >> 1) & 1;
           tc::mbar_expect_tx(&bars[V_FULL + st], 2 * 4 * 4096);  // 4 blocks from each CTA
-          if (!tc::mbar_wait_cl(&bars[V_FULL + st], ph, a.err, 260)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[V_FULL + st], ph, a.err, 260)) { ok = false; break; }
           arrive_leader(V_READY + st);
           tc::mbar_arrive(&bars[K_CP + st]);
-          tc::mbar_arrive_cluster(tc::mapa(smem_u32(&bars[K_CP + st]), rank ^ 1u));
+          tc::mbar_arrive_remote(tc::mapa(smem_u32(&bars[K_CP + st]), rank ^ 1u));
         }
         if (!ok) { abort_flag = 1; break; }
       }
       if (abort_flag) {
-        // copies already issued into this CTA land within microseconds; let them finish
-        // before the CTA (and its shared memory) goes away
+        // copies already issued by this CTA or the peer land within microseconds; let
+        // them finish before the CTA (and its shared memory) goes away
         const uint64_t t0 = tc::globaltimer_ns();
         while (tc::globaltimer_ns() - t0 < 50000ull) {
         }
