@@ -951,7 +951,8 @@ def _random_rows(torch, n_rows: int, device, gen, chunk: int = 1 << 20):
 
 def c4_inputs(torch, device, seqs, lens):
     """Device inputs for the sequences `seqs` (global ids): paged raw / compressed latent
-    caches with random page tables, dense per-sequence FP8 index keys, queries."""
+    caches with random page tables, the FP8 index keys in 64-key pages under the compressed
+    cache's page table, queries."""
     B = len(seqs)
     L = torch.tensor([int(lens[b]) for b in seqs], dtype=torch.int32)
     pages = (L + 63) // 64
@@ -974,10 +975,9 @@ def c4_inputs(torch, device, seqs, lens):
         o += int(cpages[i])
     raw = _random_rows(torch, n_raw * 64, device, g).view(n_raw, 64, 672)
     cmp = _random_rows(torch, n_cmp * 64, device, g).view(n_cmp, 64, 672)
-    T = int(cl.max())
-    kcodes = torch.randint(0, 255, (B, T, C4["Di"]), generator=g, device=device, dtype=torch.int32)
+    kcodes = torch.randint(0, 255, (n_cmp, 64, C4["Di"]), generator=g, device=device, dtype=torch.int32)
     k8 = torch.where((kcodes & 0x7F) == 0x7F, kcodes - 1, kcodes).to(torch.uint8).view(torch.float8_e4m3fn)
-    sk = (torch.rand(B, T, generator=g, device=device) * 3 + 1) / 448.0
+    sk = (torch.rand(n_cmp, 64, generator=g, device=device) * 3 + 1) / 448.0
     qcodes = torch.randint(0, 255, (B, 1, C4["Hi"], C4["Di"]), generator=g, device=device, dtype=torch.int32)
     q8 = torch.where((qcodes & 0x7F) == 0x7F, qcodes - 1, qcodes).to(torch.uint8).view(torch.float8_e4m3fn)
     sq = (torch.rand(B, 1, C4["Hi"], generator=g, device=device) * 3 + 1) / 448.0
@@ -991,7 +991,7 @@ def c4_inputs(torch, device, seqs, lens):
 def c4_step(x):
     from mzoo_b200 import indexer, sparse_mla
     idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"], scales=(x["sq"], x["sk"]),
-                       q_pos=x["pos"])
+                       q_pos=x["pos"], k_page_table=x["cpt"])
     return sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"], idx[:, 0],
                              window=C4["window"])
 
@@ -1051,10 +1051,10 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
         gather_ms = max_over_ranks(torch, dist, sum(t_g) / len(t_g), device)
     # dominant kernel legs
     from mzoo_b200 import indexer
-    qp, kp, wp, sqp, skp, scale, dt = indexer._prep(x["q8"], x["k8"], x["w"], (x["sq"], x["sk"]), None)
+    qp, kp, wp, sqp, skp, scale, dt = indexer._prep(x["q8"], x["k8"], x["w"], (x["sq"], x["sk"]), None, x["cpt"])
     qpos = x["pos"].to(torch.int32).contiguous()
-    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C4["ratio"], 0, scale, dt, False, False, qpos),
-                        args.steps)
+    t_score = timer.run(lambda: indexer._scores(qp, kp, wp, sqp, skp, C4["ratio"], 0, scale, dt, False, False, qpos,
+                                                x["cpt"]), args.steps)
     # e2e: queries / indexer queries / weights from pinned host memory, o back to the host
     hq, hq8, hw = x["q"].cpu().pin_memory(), x["q8"].view(torch.uint8).cpu().pin_memory(), x["w"].cpu().pin_memory()
     ho = torch.empty(n_mine, 128, 512, dtype=torch.bfloat16).pin_memory()
@@ -1095,7 +1095,7 @@ def bench_decode(args, torch, dist, rank, world, device) -> dict:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from mzoo_b200 import sparse_mla
         idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"],
-                           scales=(x["sq"], x["sk"]), q_pos=x["pos"], check=True)
+                           scales=(x["sq"], x["sk"]), q_pos=x["pos"], k_page_table=x["cpt"], check=True)
         o, lse = sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"],
                                    idx[:, 0], window=C4["window"], check=True)
         sample = _decode_sample(lens)
@@ -1134,8 +1134,10 @@ def _decode_item_from_device(torch, x, b: int, L: int) -> dict:
     wp = list(_window_pages(L))
     raw_pt = torch.zeros(-(-L // 64), dtype=torch.int64)
     raw_pt[wp] = torch.arange(len(wp))
+    cpages = x["cpt"][b, :ncp].long()
     return {"L": L, "q8": x["q8"][b, 0].cpu(), "sq": x["sq"][b, 0].cpu(), "w": x["w"][b, 0].cpu(),
-            "k8": x["k8"][b, :T].cpu(), "sk": x["sk"][b, :T].cpu(), "q": x["q"][b].cpu(),
+            "k8": x["k8"][cpages].reshape(-1, C4["Di"])[:T].cpu(), "sk": x["sk"][cpages].reshape(-1)[:T].cpu(),
+            "q": x["q"][b].cpu(),
             "cmp": x["cmp"][x["cpt"][b, :ncp].long()].cpu(), "cpt": torch.arange(ncp),
             "raw": x["raw"][x["pt"][b, wp].long()].cpu(), "pt": raw_pt}
 

@@ -89,11 +89,16 @@ MZB_API int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtyp
  *   ascending, -1 padded when fewer than topk keys are visible.  kbmax_ws is a float
  *   workspace of B*16 + B*S entries (key and query-row error-bound factors).  eps bounds the relative error of the fp32 scores (see
  *   indexer.cu); *err = MZB_ERR_BOUND if the bound leaves too many candidates.
+ * Paged keys (both entry points; a paged KV cache for decode, no counterpart in the
+ *   reference): with k_page_table != NULL, k holds k_pages pages of 64 key rows
+ *   [k_pages, 64, Di] and sk [k_pages, 64]; key t of batch b is row t % 64 of page
+ *   k_page_table[b * k_ptw + t / 64]; T <= 64 * k_ptw.  Entries past a sequence's visible
+ *   keys are never used (ids outside [0, k_pages) are clamped).  NULL: dense k [B,T,Di].
  */
 MZB_API int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,
                                const int32_t* q_pos, float* scores, int64_t B, int64_t S, int64_t T, int Hi, int Di,
-                               int dtype, int ratio, int64_t q_offset, float scale, int write_tail, int* err,
-                               void* stream);
+                               int dtype, int ratio, int64_t q_offset, float scale, int write_tail,
+                               const int32_t* k_page_table, int k_ptw, int64_t k_pages, int* err, void* stream);
 /* mzb_indexer_bwd -- replaces `indexer.bwd.bwd` / kernel `index_score_bwd`
  *   (src/mzoo/layers/attn/indexer/bwd.py:38-133): with r = q.k recomputed and d = dl on the
  *   group-causal visible keys (masked entries ignored whatever they hold), scale given:
@@ -108,7 +113,8 @@ MZB_API int mzb_indexer_bwd(const void* q, const void* k, const float* w, const 
 MZB_API int mzb_indexer_topk(const float* scores, const void* q, const void* k, const float* w, const float* sq,
                              const float* sk, const int32_t* q_pos, float* kbmax_ws, int32_t* out, int64_t B,
                              int64_t S, int64_t T, int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale,
-                             int topk, float eps, int* err, void* stream);
+                             int topk, float eps, const int32_t* k_page_table, int k_ptw, int64_t k_pages, int* err,
+                             void* stream);
 
 /* ------------------------------------------------------------------ shared-latent MQA (D <= 256)
  * mzb_attn_fwd -- replaces `swa_attn.fwd` / kernel `flashattn` (src/mzoo/layers/attn/
@@ -222,6 +228,12 @@ MZB_API int mzb_candidate_topk(const float* scores, const int32_t* blocks, const
 MZB_API int mzb_compress(const float* kv, const float* gate, const void* norm_w, const float* cos_v,
                          const float* sin_v, void* latent, void* cache, int64_t B, int64_t G, int ratio, int D,
                          int rope_dim, float eps, void* stream);
+
+/* Self-test of the bounded device waits (no counterpart in the reference: it checks this
+ * library's own failure path).  One thread waits on an mbarrier nothing arrives on; after
+ * limit_ns (<= 2e9) the wait gives up, writes 901 (scope 0: CTA-scope wait) or 902
+ * (scope 1: cluster-scope wait) into *err and the kernel returns normally. */
+MZB_API int mzb_selftest_bounded_wait(int64_t limit_ns, int scope, int* err, void* stream);
 
 #ifdef __cplusplus
 }

@@ -36,9 +36,9 @@ SIGNATURES = {
     "mzb_fq_fp4": [_P, _P, _I64, _I64, _I32, _I32, _I32, _P],
     "mzb_fq_fp8": [_P, _P, _I64, _I64, _I32, _I32, _I32, _P],
     "mzb_indexer_scores": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64, _F32,
-                           _I32, _P, _P],
+                           _I32, _P, _I32, _I64, _P, _P],
     "mzb_indexer_topk": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I32, _I64,
-                         _F32, _I32, _F32, _P, _P],
+                         _F32, _I32, _F32, _P, _I32, _I64, _P, _P],
     "mzb_indexer_bwd": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _I32, _I32, _I64, _F32, _P, _P],
     "mzb_attn_fwd": [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I64, _I32, _F32, _P, _P],
     "mzb_attn_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I64, _I64, _I32, _I32,
@@ -52,6 +52,7 @@ SIGNATURES = {
     "mzb_candidate_blocks": [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _P],
     "mzb_candidate_topk": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
     "mzb_compress": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _F32, _P],
+    "mzb_selftest_bounded_wait": [_I64, _I32, _P, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

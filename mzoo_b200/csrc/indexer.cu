@@ -21,6 +21,10 @@
 // block's causal frontier; with few (batch, query block) pairs (decode) every CTA takes an
 // equal share of all visible key tiles so every SM gets the same work.
 //
+// Keys are either dense rows [B, T] or, for a paged KV cache (decode), rows of 64-key
+// pages [P, 64] reached through a page table [B, max_pages] (`key_row`); the score kernel
+// then loads each 128-key tile as its two 64-row pages.
+//
 // Kernel 2 (`topk_kernel`): one CTA per query row.  The fp32 tensor-core scores carry a
 // rounding error bounded by delta = eps * A_s * max_t B_t, with
 // A_s = sum_h |w sq| * ||q_h||_2 and B_t = |scale| sk_t ||k_t||_2 (Cauchy-Schwarz on the
@@ -82,8 +86,20 @@ struct ScoreArgs {
   int write_tail;
   int kc, n_kc;  // key tiles per chunk, chunks per (batch, query block)
   int bal;       // 1: each CTA takes a contiguous 1/grid share of all key tiles (few units)
+  const int32_t* k_pt;  // [B, k_ptw] page table of 64-key pages, or null (dense keys)
+  int k_ptw, k_npages;
   int* err;
 };
+
+// Row of key t of batch b: dense [B, T] rows, or through the page table of 64-key pages.
+// Page ids are clamped into the pool: keys past a sequence's length are only ever masked,
+// whatever its table holds there, so their (clamped) reads just have to stay in bounds.
+__device__ __forceinline__ long long key_row(const int32_t* pt, int ptw, int npages, int T, int b, int t) {
+  if (!pt) return (long long)b * T + t;
+  int pg = __ldg(pt + (long long)b * ptw + (t >> 6));
+  pg = pg < 0 ? 0 : (pg >= npages ? npages - 1 : pg);
+  return (long long)pg * 64 + (t & 63);
+}
 
 __device__ __forceinline__ int visible_keys(long long q_offset, long long s, int ratio, int T) {
   long long v = (q_offset + s + 1) / ratio;
@@ -240,11 +256,25 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         q_issued |= 1u << qb;
         q_par[qb] = qpar;
         for (int kt = m.k0; kt < m.k1; ++kt) {
+          // paged keys: the tile's two page rows, read before the stage wait hides their latency
+          int r0 = 0, r1 = 0;
+          if (a.k_pt) {
+            r0 = int(key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, kt * BM));
+            r1 = int(key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, kt * BM + 64));
+          }
           if (!tc::mbar_wait(&k_empty[ks_i], ks_ph ^ 1, a.err, 102)) { *abort_flag = 1; break; }
           tc::mbar_expect_tx(&k_full[ks_i], C::K_BYTES);
-          for (int cb = 0; cb < C::NCB; ++cb)
-            tc::tma_load_3d(ks + ks_i * C::K_BYTES + cb * BM * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB,
-                            kt * BM, m.b);
+          if (a.k_pt) {  // two 64-key pages (2D map over the page pool's rows)
+            for (int cb = 0; cb < C::NCB; ++cb) {
+              uint8_t* dst = ks + ks_i * C::K_BYTES + cb * BM * C::SW;
+              tc::tma_load_2d(dst, &tk, &k_full[ks_i], cb * C::SW / C::EB, r0);
+              tc::tma_load_2d(dst + 64 * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB, r1);
+            }
+          } else {
+            for (int cb = 0; cb < C::NCB; ++cb)
+              tc::tma_load_3d(ks + ks_i * C::K_BYTES + cb * BM * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB,
+                              kt * BM, m.b);
+          }
           k_issued |= 1u << ks_i;
           k_par[ks_i] = ks_ph;
           if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
@@ -348,7 +378,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         if (acc != bwg) continue;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
-        const float skj = (j < a.T) ? (a.sk ? __ldg(a.sk + size_t(m.b) * a.T + j) : 1.0f) * a.scale : 0.0f;
+        const float skj =
+            (j < a.T) ? (a.sk ? __ldg(a.sk + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, j)) : 1.0f) * a.scale
+                      : 0.0f;
         if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
         acc_ph ^= 1;
         tc::fence_after_sync();
@@ -483,6 +515,8 @@ struct TopkArgs {
   long long q_offset;
   float scale, eps;
   int fp8;
+  const int32_t* k_pt;  // page table of 64-key pages, or null (dense keys)
+  int k_ptw, k_npages;
   int* err;
 };
 
@@ -552,31 +586,34 @@ __device__ void key_bound(const TopkArgs& a, int b, int part) {
   float m = 0.0f;
   if (a.fp8 && a.S <= 16) {
     float mk = 0.0f;
-    for (int t = t_lo + tid; t < t_hi; t += blockDim.x) mk = fmaxf(mk, fabsf(a.sk[size_t(b) * a.T + t]));
+    for (int t = t_lo + tid; t < t_hi; t += blockDim.x)
+      mk = fmaxf(mk, fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]));
     m = asc * mk * (448.0f * sqrtf(float(a.Di))) * 1.0001f;
   } else if (rb % 16 == 0 && lpr <= 32 && (lpr & (lpr - 1)) == 0) {
     const int rows = blockDim.x / lpr;
     for (int t0 = t_lo; t0 < t_hi; t0 += rows) {  // uniform trip count: shuffles see full warps
       const int t = t0 + tid / lpr;
       float ss = 0.0f;
-      if (t < t_hi) ss = sumsq16(*reinterpret_cast<const uint4*>(a.k + (size_t(b) * a.T + t) * rb + (tid % lpr) * 16),
-                                 a.fp8);
+      if (t < t_hi)
+        ss = sumsq16(*reinterpret_cast<const uint4*>(a.k + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t) * rb +
+                                                     (tid % lpr) * 16),
+                     a.fp8);
       for (int o = lpr >> 1; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       if (t < t_hi) {
-        const float sk = a.sk ? fabsf(a.sk[size_t(b) * a.T + t]) : 1.0f;
+        const float sk = a.sk ? fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]) : 1.0f;
         m = fmaxf(m, asc * sk * sqrtf(ss));
       }
     }
   } else {
     for (int t = t_lo + warp; t < t_hi; t += blockDim.x >> 5) {
-      const uint8_t* kr = a.k + (size_t(b) * a.T + t) * rb;
+      const uint8_t* kr = a.k + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t) * rb;
       float ss = 0.0f;
       for (int i = lane; i < a.Di; i += 32) {
         const float v = elem_f(kr, i, a.fp8);
         ss = fmaf(v, v, ss);
       }
       for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float sk = a.sk ? fabsf(a.sk[size_t(b) * a.T + t]) : 1.0f;
+      const float sk = a.sk ? fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]) : 1.0f;
       m = fmaxf(m, asc * sk * sqrtf(ss));
     }
   }
@@ -1047,7 +1084,7 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
     float* kd = kdall + warp * a.Di;
     for (int c = warp; c < nc && warp < RW; c += RW) {
       const int j = cand[c];
-      const uint8_t* kr = a.k + (size_t(b) * a.T + j) * rb;
+      const uint8_t* kr = a.k + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, j) * rb;
       __syncwarp();
       for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);  // exact in fp32
       __syncwarp();
@@ -1094,7 +1131,7 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
         }
       }
       if (lane == 0) {
-        const double skj = a.sk ? double(a.sk[size_t(b) * a.T + j]) : 1.0;
+        const double skj = a.sk ? double(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, j)]) : 1.0;
         exact[c] = __dmul_rn(__dmul_rn(acc, skj), double(a.scale));
       }
     }
@@ -1151,7 +1188,13 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
     int e = encode_tmap(&tq, dt, 3, q, dims, str, box, swz);
     if (e) return e;
   }
-  {
+  if (a.k_pt) {  // the page pool's rows, one 64-key page per load
+    const uint64_t dims[2] = {uint64_t(DI), uint64_t(a.k_npages) * 64};
+    const uint64_t str[1] = {uint64_t(C::R)};
+    const uint32_t box[2] = {uint32_t(C::SW / C::EB), 64};
+    int e = encode_tmap(&tk, dt, 2, k, dims, str, box, swz);
+    if (e) return e;
+  } else {
     const uint64_t dims[3] = {uint64_t(DI), uint64_t(a.T), uint64_t(a.B)};
     const uint64_t str[2] = {uint64_t(C::R), uint64_t(a.T) * C::R};
     const uint32_t box[3] = {uint32_t(C::SW / C::EB), uint32_t(BM), 1};
@@ -1206,12 +1249,24 @@ static int indexer_common_checks(const void* q, const void* k, int64_t B, int64_
   return MZB_OK;
 }
 
+static int indexer_page_checks(const int32_t* k_page_table, int k_ptw, int64_t k_pages, int64_t T) {
+  if (!k_page_table) return MZB_OK;
+  MZB_REQUIRE(k_ptw >= 1 && k_pages >= 1 && k_pages * 64 < (int64_t(1) << 31), MZB_ERR_SHAPE,
+              "indexer: paged keys need k_ptw >= 1 and 1 <= k_pages < 2^25 (got %d, %lld)", k_ptw,
+              (long long)k_pages);
+  MZB_REQUIRE(T <= int64_t(k_ptw) * 64, MZB_ERR_SHAPE, "indexer: T=%lld exceeds the page table's %d pages of 64",
+              (long long)T, k_ptw);
+  return MZB_OK;
+}
+
 extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, const float* sq, const float* sk,
                                   const int32_t* q_pos, float* scores, int64_t B, int64_t S, int64_t T, int Hi,
                                   int Di, int dtype, int ratio, int64_t q_offset, float scale, int write_tail,
-                                  int* err, void* stream) {
+                                  const int32_t* k_page_table, int k_ptw, int64_t k_pages, int* err,
+                                  void* stream) {
   int e = indexer_common_checks(q, k, B, S, T, Hi, Di, dtype, ratio);
   if (e) return e;
+  if ((e = indexer_page_checks(k_page_table, k_ptw, k_pages, T))) return e;
   MZB_REQUIRE(dtype == MZB_BF16 || (sq && sk), MZB_ERR_SHAPE, "indexer: fp8 inputs need sq and sk scales");
   if (T == 0) return MZB_OK;
   idx::ScoreArgs a{};
@@ -1223,6 +1278,7 @@ extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, 
   if (a.Tq > S) a.Tq = int(S);  // one-token decode: N = Hi columns, not a padded block
   a.N = a.Tq * Hi;
   a.ratio = ratio; a.q_offset = q_offset; a.scale = scale; a.write_tail = write_tail; a.err = err;
+  a.k_pt = k_page_table; a.k_ptw = k_ptw; a.k_npages = int(k_pages);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == MZB_E4M3) {
     switch (Di) {
@@ -1246,9 +1302,11 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
                                 const float* sk, const int32_t* q_pos, float* kbmax_ws, int32_t* out, int64_t B,
                                 int64_t S, int64_t T,
                                 int Hi, int Di, int dtype, int ratio, int64_t q_offset, float scale, int topk,
-                                float eps, int* err, void* stream) {
+                                float eps, const int32_t* k_page_table, int k_ptw, int64_t k_pages, int* err,
+                                void* stream) {
   int e = indexer_common_checks(q, k, B, S, T, Hi, Di, dtype, ratio);
   if (e) return e;
+  if ((e = indexer_page_checks(k_page_table, k_ptw, k_pages, T))) return e;
   MZB_REQUIRE(topk >= 1, MZB_ERR_SHAPE, "indexer topk: topk must be >= 1, got %d", topk);
   MZB_REQUIRE(err != nullptr, MZB_ERR_SHAPE, "indexer topk: needs an error word");
   MZB_REQUIRE(dtype == MZB_BF16 || (sq && sk), MZB_ERR_SHAPE, "indexer: fp8 inputs need sq and sk scales");
@@ -1265,6 +1323,7 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   a.out = out;
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi; a.Di = Di; a.topk = topk; a.ratio = ratio;
   a.q_offset = q_offset; a.scale = scale; a.eps = eps; a.fp8 = dtype == MZB_E4M3; a.err = err;
+  a.k_pt = k_page_table; a.k_ptw = k_ptw; a.k_npages = int(k_pages);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0 || S == 0) return MZB_OK;
   if (T > 0) {

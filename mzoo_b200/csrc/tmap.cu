@@ -39,6 +39,14 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
   }
   CUresult r = fn(map, dtype, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    // a host thread whose first CUDA call this is (e.g. the autograd engine's backward
+    // thread) has no current context yet: bind the current device's primary context and retry
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess)
+      r = fn(map, dtype, rank, const_cast<void*>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   MZB_REQUIRE(r == CUDA_SUCCESS, MZB_ERR_LAUNCH, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return MZB_OK;
 }

@@ -14,6 +14,10 @@ Additive keyword arguments (defaults reproduce the reference):
 - ``softmax_scale`` -- the overall factor (default ``Di**-0.5`` in bf16 mode, 1 in fp8).
 - ``q_pos`` -- int32 [B, S] absolute position per query (decode: ``seq_len - 1``);
   overrides ``q_offset``.
+- ``k_page_table`` -- int32 [B, pages]: paged keys (a decode KV cache) -- ``k`` is then
+  [P, 64, Di] (64 key rows per page, fp8 scales ``sk`` [P, 64]) and key t of batch b is
+  row t % 64 of page ``k_page_table[b, t // 64]``; T = 64 * pages (keys past a sequence's
+  visible count are never used, whatever its table holds there).
 
 ``attn`` returns, per query, the indices of the ``topk`` largest scores -- exact with
 respect to the fp64 canonical score (see ``csrc/indexer.cu``), ties to the lower index --
@@ -31,7 +35,7 @@ KB_PARTS = 16
 EPS = 2.0**-21
 
 
-def _prep(q, k, w, scales, softmax_scale):
+def _prep(q, k, w, scales, softmax_scale, k_page_table=None):
     require_cuda(q, k, w)
     fp8 = q.dtype == torch.float8_e4m3fn
     if fp8:
@@ -43,10 +47,16 @@ def _prep(q, k, w, scales, softmax_scale):
         assert scales is None, "scales are for fp8 inputs only"
         sq = sk = None
     B, S, Hi, Di = q.shape
-    assert k.dim() == 3 and k.shape[0] == B and k.shape[2] == Di, f"k must be [B, T, {Di}], got {tuple(k.shape)}"
+    if k_page_table is None:
+        assert k.dim() == 3 and k.shape[0] == B and k.shape[2] == Di, f"k must be [B, T, {Di}], got {tuple(k.shape)}"
+    else:
+        assert k.dim() == 3 and k.shape[1] == 64 and k.shape[2] == Di, \
+            f"paged k must be [pages, 64, {Di}], got {tuple(k.shape)}"
+        assert k_page_table.dim() == 2 and k_page_table.shape[0] == B, \
+            f"k_page_table must be [B, pages], got {tuple(k_page_table.shape)}"
     assert w.shape == (B, S, Hi), f"w must be [B, S, Hi]={(B, S, Hi)}, got {tuple(w.shape)}"
     if sq is not None:
-        assert sq.shape == (B, S, Hi) and sk.shape == (B, k.shape[1]), "scales must be [B,S,Hi] and [B,T]"
+        assert sq.shape == (B, S, Hi) and sk.shape == k.shape[:2], "scales must be [B,S,Hi] and k's leading dims"
     w = w.float().contiguous()
     q, k = q.contiguous(), k.contiguous()
     if Hi % 16:  # the kernel tiles heads by 16: zero-weight heads contribute exactly 0
@@ -60,8 +70,14 @@ def _prep(q, k, w, scales, softmax_scale):
     return q, k, w, sq, sk, float(scale), dt
 
 
-def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, check, q_pos=None):
-    return ops.indexer_scores(q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dt, write_tail, check)
+def _scores(q, k, w, sq, sk, ratio, q_offset, scale, dt, write_tail, check, q_pos=None, k_pt=None):
+    return ops.indexer_scores(q, k, w, sq, sk, q_pos, k_pt, ratio, q_offset, scale, dt, write_tail, check)
+
+
+def _page_table(k_page_table, device):
+    if k_page_table is None:
+        return None
+    return k_page_table.to(device=device, dtype=torch.int32).contiguous()
 
 
 def _positions(q_pos, B, S, device):
@@ -74,33 +90,36 @@ def _positions(q_pos, B, S, device):
 
 def fwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, q_offset: int = 0,
         scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
-        check: bool = False) -> torch.Tensor:
+        k_page_table: torch.Tensor | None = None, check: bool = False) -> torch.Tensor:
     """Lightning-indexer score matrix (``indexer/fwd.py:112``): q bf16 [B,S,Hi,Di], k bf16
     [B,T,Di], w fp32 [B,S,Hi] (already scaled by Hi**-0.5) -> fp32 [B,S,T], ``-inf`` where
     ``t >= (q_offset + s + 1) // compress_ratio``."""
     assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
-    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale)
+    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale, k_page_table)
     B, S = q.shape[:2]
-    if k.shape[1] == 0:
+    kpt = _page_table(k_page_table, q.device)
+    if (k.shape[1] if kpt is None else kpt.shape[1]) == 0:
         return q.new_empty((B, S, 0), dtype=torch.float32)
-    return _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, check, _positions(q_pos, B, S, q.device))
+    return _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, True, check, _positions(q_pos, B, S, q.device),
+                   kpt)
 
 
 def attn(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, *, compress_ratio: int, topk: int, q_offset: int = 0,
          scales=None, softmax_scale: float | None = None, q_pos: torch.Tensor | None = None,
-         check: bool = False) -> torch.Tensor:
+         k_page_table: torch.Tensor | None = None, check: bool = False) -> torch.Tensor:
     """``indexer/attn.py:67``: -> ``Indices`` int32 [B,S,topk] (``-1`` = empty slot)."""
     assert topk >= 0, f"topk must be >= 0, got {topk}"
     assert compress_ratio >= 1, f"compress_ratio must be >= 1, got {compress_ratio}"
-    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale)
+    q, k, w, sq, sk, scale, dt = _prep(q, k, w, scales, softmax_scale, k_page_table)
     B, S, Hi, Di = q.shape
-    T = k.shape[1]
-    out = torch.full((B, S, topk), -1, dtype=torch.int32, device=q.device)
+    kpt = _page_table(k_page_table, q.device)
+    T = k.shape[1] if kpt is None else 64 * kpt.shape[1]
     if topk == 0 or T == 0:
-        return out
+        return torch.full((B, S, topk), -1, dtype=torch.int32, device=q.device)
     qp = _positions(q_pos, B, S, q.device)
-    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, check, qp)
-    return ops.indexer_topk(sc, q, k, w, sq, sk, qp, compress_ratio, q_offset, scale, dt, topk, EPS, KB_PARTS, check)
+    sc = _scores(q, k, w, sq, sk, compress_ratio, q_offset, scale, dt, False, check, qp, kpt)
+    return ops.indexer_topk(sc, q, k, w, sq, sk, qp, kpt, compress_ratio, q_offset, scale, dt, topk, EPS, KB_PARTS,
+                            check)
 
 
 def bwd(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, dl: torch.Tensor, *, compress_ratio: int,

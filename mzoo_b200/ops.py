@@ -101,46 +101,57 @@ def check_errors(device=None) -> None:
 
 # ----------------------------------------------------------------------------- indexer
 
+def _keys_T(k: torch.Tensor, k_pt: torch.Tensor | None) -> int:
+    """Logical keys per batch: k [B,T,Di] dense, or 64 per page-table entry (k [P,64,Di])."""
+    return k.shape[1] if k_pt is None else 64 * k_pt.shape[1]
+
+
+def _pages(k: torch.Tensor, k_pt: torch.Tensor | None) -> tuple:
+    return (ptr(k_pt), 0, 0) if k_pt is None else (ptr(k_pt), k_pt.shape[1], k.shape[0])
+
+
 @torch.library.custom_op("mzb::indexer_scores", mutates_args=())
 def indexer_scores(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, sq: torch.Tensor | None,
-                   sk: torch.Tensor | None, q_pos: torch.Tensor | None, ratio: int, q_offset: int, scale: float,
-                   dtype: int, write_tail: bool, check: bool) -> torch.Tensor:
-    """fp32 [B,S,T] scores of ``mzb_indexer_scores`` (q [B,S,Hi,Di], k [B,T,Di] contiguous)."""
+                   sk: torch.Tensor | None, q_pos: torch.Tensor | None, k_pt: torch.Tensor | None, ratio: int,
+                   q_offset: int, scale: float, dtype: int, write_tail: bool, check: bool) -> torch.Tensor:
+    """fp32 [B,S,T] scores of ``mzb_indexer_scores`` (q [B,S,Hi,Di] and k [B,T,Di] contiguous, or
+    paged k [P,64,Di] with page table k_pt [B, pages] and T = 64 * pages)."""
     B, S, Hi, Di = q.shape
-    T = k.shape[1]
+    T = _keys_T(k, k_pt)
     out = torch.empty(B, S, T, device=q.device, dtype=torch.float32)
     err = _err(q.device, check)
     call("mzb_indexer_scores", ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(out), B, S, T, Hi, Di, dtype,
-         ratio, q_offset, scale, int(write_tail), ptr(err), stream_ptr(q.device))
+         ratio, q_offset, scale, int(write_tail), *_pages(k, k_pt), ptr(err), stream_ptr(q.device))
     if check:
         _raise_on(err, "indexer scores")
     return out
 
 
 @indexer_scores.register_fake
-def _(q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dtype, write_tail, check):
-    return q.new_empty((q.shape[0], q.shape[1], k.shape[1]), dtype=torch.float32)
+def _(q, k, w, sq, sk, q_pos, k_pt, ratio, q_offset, scale, dtype, write_tail, check):
+    return q.new_empty((q.shape[0], q.shape[1], _keys_T(k, k_pt)), dtype=torch.float32)
 
 
 @torch.library.custom_op("mzb::indexer_topk", mutates_args=())
 def indexer_topk(scores: torch.Tensor, q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, sq: torch.Tensor | None,
-                 sk: torch.Tensor | None, q_pos: torch.Tensor | None, ratio: int, q_offset: int, scale: float,
-                 dtype: int, topk: int, eps: float, kb_parts: int, check: bool) -> torch.Tensor:
+                 sk: torch.Tensor | None, q_pos: torch.Tensor | None, k_pt: torch.Tensor | None, ratio: int,
+                 q_offset: int, scale: float, dtype: int, topk: int, eps: float, kb_parts: int,
+                 check: bool) -> torch.Tensor:
     """int32 [B,S,topk] exact top-k of ``mzb_indexer_topk`` (ascending, -1 padded)."""
     B, S, Hi, Di = q.shape
-    T = k.shape[1]
+    T = _keys_T(k, k_pt)
     out = torch.empty(B, S, topk, dtype=torch.int32, device=q.device)
     kb = torch.empty(B * kb_parts + B * S, dtype=torch.float32, device=q.device)  # key and query bounds
     err = _err(q.device, check)
     call("mzb_indexer_topk", ptr(scores), ptr(q), ptr(k), ptr(w), ptr(sq), ptr(sk), ptr(q_pos), ptr(kb), ptr(out),
-         B, S, T, Hi, Di, dtype, ratio, q_offset, scale, topk, eps, ptr(err), stream_ptr(q.device))
+         B, S, T, Hi, Di, dtype, ratio, q_offset, scale, topk, eps, *_pages(k, k_pt), ptr(err), stream_ptr(q.device))
     if check:
         _raise_on(err, "indexer top-k")
     return out
 
 
 @indexer_topk.register_fake
-def _(scores, q, k, w, sq, sk, q_pos, ratio, q_offset, scale, dtype, topk, eps, kb_parts, check):
+def _(scores, q, k, w, sq, sk, q_pos, k_pt, ratio, q_offset, scale, dtype, topk, eps, kb_parts, check):
     return q.new_empty((q.shape[0], q.shape[1], topk), dtype=torch.int32)
 
 
@@ -330,3 +341,16 @@ def _(kv, gate, norm_w, cos, sin, ratio, rope_dim, eps):
     G = N // ratio
     return (kv.new_empty((B, G, D), dtype=torch.bfloat16),
             kv.new_empty((B, G, D) if cos is not None else (0,), dtype=torch.bfloat16))
+
+
+# ----------------------------------------------------------------------------- self-test
+
+def selftest_bounded_wait(device, limit_ns: int, scope: int, check: bool) -> int:
+    """Launch ``mzb_selftest_bounded_wait``: a wait that nothing satisfies runs out after
+    ``limit_ns`` and records its site code.  check=True returns the code of a fresh error
+    word (synchronising); check=False records it in the device's persistent word (read by
+    ``check_errors``) and returns 0."""
+    dev = torch.device(device)
+    err = _err(dev, check)
+    call("mzb_selftest_bounded_wait", int(limit_ns), int(scope), ptr(err), stream_ptr(dev))
+    return int(err.item()) if check else 0

@@ -7,8 +7,9 @@ outputs and lse.
 - C2: B=2, 4096 queries at positions 12288..16383 x 4096 compressed keys, Hi=64, Di=128,
   FP8, top-512: 256 sampled query rows (four 64-row chunks over both batches).
 - C3: 16384 tokens x 128 heads, top-2048 compressed + 128-token window: 32 sampled tokens.
-- C4: 128 sequences with lengths in [8192, 131072], paged FP8 latent caches, decode indexer
-  top-2048 + window 128: 8 sampled sequences (indexer sets and attention).
+- C4: 128 sequences with lengths in [8192, 131072], paged FP8 latent caches and index keys
+  (64-key pages), decode indexer top-2048 + window 128: 8 sampled sequences (indexer sets
+  and attention).
 """
 
 import numpy as np
@@ -89,7 +90,7 @@ def test_c4_decode_full_size(cuda):
     seqs = list(range(C4["B"]))
     x = bench.c4_inputs(torch, cuda, seqs, lens)
     idx = indexer.attn(x["q8"], x["k8"], x["w"], compress_ratio=C4["ratio"], topk=C4["topk"],
-                       scales=(x["sq"], x["sk"]), q_pos=x["pos"], check=True)
+                       scales=(x["sq"], x["sk"]), q_pos=x["pos"], k_page_table=x["cpt"], check=True)
     o, lse = sparse_mla.decode(x["q"], x["raw"], x["pt"], x["lens"], x["cmp"], x["cpt"], x["cmp_lens"], idx[:, 0],
                                window=C4["window"], check=True)
     idx_h = idx[:, 0].cpu().numpy()
@@ -100,10 +101,12 @@ def test_c4_decode_full_size(cuda):
     sample = sorted({int(order[0]), int(order[-1]), *[int(order[i]) for i in (16, 40, 64, 90, 110)], 0})
     for b in sample:
         T = int(L[b]) // C4["ratio"]
+        pages = x["cpt"][b, :-(-T // 64)].long()  # the index keys share the compressed cache's pages
         qv = x["q8"][b:b + 1].float().cpu().numpy()
-        kv = x["k8"][b:b + 1, :T].float().cpu().numpy()
-        canon = I.canonical_scores(qv, kv, x["w"][b:b + 1].cpu().numpy(), x["sq"][b:b + 1].cpu().numpy(),
-                                   x["sk"][b:b + 1, :T].cpu().numpy(), C4["ratio"], int(L[b]) - 1)
+        kv = x["k8"][pages].reshape(1, -1, C4["Di"])[:, :T].float().cpu().numpy()
+        skv = x["sk"][pages].reshape(1, -1)[:, :T].cpu().numpy()
+        canon = I.canonical_scores(qv, kv, x["w"][b:b + 1].cpu().numpy(), x["sq"][b:b + 1].cpu().numpy(), skv,
+                                   C4["ratio"], int(L[b]) - 1)
         ref_idx = I.canonical_topk(canon, C4["topk"], C4["ratio"], int(L[b]) - 1)[0, 0]
         assert np.array_equal(idx_h[b], ref_idx), b
         # attention over the window + selected rows, gathered through the page tables on the GPU

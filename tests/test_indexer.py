@@ -236,7 +236,7 @@ def test_topk_wide_band_exact(cuda):
     q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 11)
     qp, kp, wp, sqp, skp, scale, dt = indexer._prep(q8, k8, w, (sq, sk), None)
     sc = indexer._scores(qp, kp, wp, sqp, skp, ratio, T, scale, dt, False, True)
-    got = ops.indexer_topk(sc, qp, kp, wp, sqp, skp, None, ratio, T, scale, dt, topk, indexer.EPS * 1024,
+    got = ops.indexer_topk(sc, qp, kp, wp, sqp, skp, None, None, ratio, T, scale, dt, topk, indexer.EPS * 1024,
                            indexer.KB_PARTS, True).cpu().numpy()
     qv, kv = q8.float().cpu().numpy(), k8.float().cpu().numpy()
     canon = I.canonical_scores(qv, kv, w.cpu().numpy(), sq.cpu().numpy(), sk.cpu().numpy(), ratio, T)
@@ -285,6 +285,52 @@ def test_topk_fp8_matches_reference_fixture(cuda, topk):
                        softmax_scale=di**-0.5).cpu().numpy()
     r = np.sort(np.where(d[f"topk{topk}"] < 0, 1 << 30, d[f"topk{topk}"]), -1)
     assert np.array_equal(got, np.where(r == 1 << 30, -1, r).astype(np.int32))
+
+
+def _to_pages(torch, k8, sk, T, seed, extra=5):
+    """The keys [B, >=T, Di] (+ scales [B, >=T]) laid out as a pool of 64-key pages in random
+    order, pages past each batch's keys holding junk -> (pool [P,64,Di], scales [P,64],
+    page table [B, pages])."""
+    B, _, Di = k8.shape
+    pages = -(-T // 64)
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    P = B * pages + extra
+    perm = torch.randperm(P, generator=g)[:B * pages].view(B, pages)
+    junk = torch.randint(0, 120, (P, 64, Di), generator=g, dtype=torch.uint8)
+    pool = junk.to(k8.device).view(torch.float8_e4m3fn)
+    spool = (torch.rand(P, 64, generator=g) + 0.5).to(k8.device)
+    for b in range(B):
+        for pg in range(pages):
+            n = min(64, T - pg * 64)
+            pool[perm[b, pg], :n] = k8[b, pg * 64:pg * 64 + n]
+            spool[perm[b, pg], :n] = sk[b, pg * 64:pg * 64 + n]
+    return pool, spool, perm.to(torch.int32).to(k8.device)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", ["decode", "prefill"])
+def test_paged_keys_match_dense(cuda, shape):
+    """Keys reached through a page table of 64-key pages (a paged decode cache) give the
+    same scores bit for bit and the same index sets as the same keys stored dense."""
+    import torch
+    from mzoo_b200 import indexer
+    if shape == "decode":
+        B, S, Hi, Di, T, ratio, topk = 6, 1, 64, 128, 4000, 4, 256
+        q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 31)
+        lens = torch.tensor([16000, 1000, 9001, 4097, 15999, 777], dtype=torch.int32)
+        kw = dict(compress_ratio=ratio, scales=(sq, sk), q_pos=(lens - 1).view(B, 1).to(cuda))
+    else:
+        B, S, Hi, Di, T, ratio, topk = 2, 200, 64, 128, 300, 1, 64
+        q8, sq, k8, sk, w = _fp8_case(torch, cuda, B, S, Hi, Di, T, 32)
+        kw = dict(compress_ratio=ratio, scales=(sq, sk), q_offset=100)
+    pool, spool, pt = _to_pages(torch, k8, sk, T, 7)
+    kwp = dict(kw, scales=(sq, spool), k_page_table=pt)
+    dense = indexer.attn(q8, k8, w, topk=topk, check=True, **kw)
+    paged = indexer.attn(q8, pool, w, topk=topk, check=True, **kwp)
+    assert torch.equal(dense, paged)
+    sd = indexer.fwd(q8, k8, w, **kw)
+    sp = indexer.fwd(q8, pool, w, **kwp)
+    assert torch.equal(sd, sp[:, :, :T]) and torch.isneginf(sp[:, :, T:]).all()
 
 
 @pytest.mark.gpu

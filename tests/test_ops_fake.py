@@ -19,9 +19,12 @@ def test_fake_shapes():
     q = torch.empty(B, S, Hi, Di, dtype=torch.float8_e4m3fn, **M)
     k = torch.empty(B, T, Di, dtype=torch.float8_e4m3fn, **M)
     w = torch.empty(B, S, Hi, dtype=torch.float32, **M)
-    sc = torch.ops.mzb.indexer_scores(q, k, w, None, None, None, 4, 0, 1.0, 3, True, False)
+    sc = torch.ops.mzb.indexer_scores(q, k, w, None, None, None, None, 4, 0, 1.0, 3, True, False)
     assert sc.shape == (B, S, T) and sc.dtype == torch.float32
-    idx = torch.ops.mzb.indexer_topk(sc, q, k, w, None, None, None, 4, 0, 1.0, 3, 16, 2.0**-21, 16, False)
+    idx = torch.ops.mzb.indexer_topk(sc, q, k, w, None, None, None, None, 4, 0, 1.0, 3, 16, 2.0**-21, 16, False)
+    kp = torch.empty(9, 64, Di, dtype=torch.float8_e4m3fn, **M)
+    pt = torch.empty(B, 3, dtype=torch.int32, **M)
+    assert torch.ops.mzb.indexer_scores(q, kp, w, None, None, None, pt, 4, 0, 1.0, 3, True, False).shape == (B, S, 192)
     assert idx.shape == (B, S, 16) and idx.dtype == torch.int32
     qb = torch.empty(B, S, Hi, Di, dtype=torch.bfloat16, **M)
     kb = torch.empty(B, T, Di, dtype=torch.bfloat16, **M)
