@@ -21,6 +21,9 @@ distributions -- there is no dataset):
   queries x 65536 compressed positions.  Metric: Mq/s.
 - ``compressor`` (next row F3, not a BASELINE config): compressor pool + RMSNorm + RoPE +
   MXFP4 cache entry, 8 x 16384 tokens at ratio 4, 576 channels.  Metric: algorithmic HBM GB/s.
+- ``normrope`` (next row F3, not a BASELINE config): the fused RMSNorm + RoPE prologue of q,
+  forward + backward, at the reference's own benchmark shape (B1 S4096 H64 D128, rope 64).
+  Metric: algorithmic HBM GB/s.
 
 A "step" is one pass of the hot path over one batch.  ``value`` times the device path with
 inputs resident in HBM (L2 flushed with a 256 MB write before every timed step);
@@ -1460,14 +1463,177 @@ def reference_compressor(args, rank, world) -> dict:
                            cp_config(world), runs, "f32 (oracle port, numpy)", "synthetic")
 
 
+# ----------------------------------------------------------------------------- RMSNorm + RoPE prologue
+
+# The reference's own benchmark shape for its fused prologue (norm_rope_bench.py: q of
+# B1 S4096 H64 D128, rope_dim 64); a step is the forward and the backward.
+NR = dict(B=1, S=4096, H=64, D=128, rope=64)
+
+
+def nr_config(world: int) -> dict:
+    return {"workload": "F3 QK prologue: fused RMSNorm + RoPE forward + backward", "B": NR["B"], "S": NR["S"],
+            "heads": NR["H"], "head_dim": NR["D"], "rope_dim": NR["rope"],
+            "parallelism": f"x{world} independent" if world > 1 else "1 GPU",
+            "l2": "flushed (256 MB write) per step"}
+
+
+def nr_bytes() -> float:
+    """Algorithmic HBM bytes of a step: forward reads x, writes out and rstd; backward reads
+    x, dy and rstd, writes dx; cos / sin read by both."""
+    rows = NR["B"] * NR["S"] * NR["H"]
+    xb = rows * NR["D"] * 2
+    cs = 2 * NR["B"] * NR["S"] * (NR["rope"] // 2) * 4
+    return (2 * xb + rows * 4 + cs) + (3 * xb + rows * 4 + cs)
+
+
+def nr_inputs(torch, seed: int = 0):
+    g = torch.Generator().manual_seed(seed)
+    B, S, H, D, rd = (NR[k] for k in ("B", "S", "H", "D", "rope"))
+    x = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    w = torch.randn(D, generator=g).to(torch.bfloat16)
+    pos = torch.arange(S, dtype=torch.float32)
+    freqs = pos[:, None] / (10000.0 ** (torch.arange(0, rd, 2, dtype=torch.float32) / rd))
+    dy = torch.randn(B, S, H, D, generator=g).to(torch.bfloat16)
+    return x, w, freqs.cos()[None].expand(B, -1, -1).contiguous(), freqs.sin()[None].expand(B, -1, -1).contiguous(), dy
+
+
+def _graph(torch, device, fn):
+    """A CUDA graph of fn's launches (captured on a side stream after one eager call)."""
+    g = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(device)
+    cap.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(cap):
+        fn()
+        with torch.cuda.graph(g, stream=cap):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(cap)
+    g.replay()
+    torch.cuda.synchronize()
+    return g
+
+
+def bench_normrope(args, torch, dist, rank, world, device) -> dict:
+    from mzoo_b200 import norm_rope
+    xh, wh, ch, sh, dyh = nr_inputs(torch, seed=rank)
+    x, w, cos, sin, dy = (t.to(device) for t in (xh, wh, ch, sh, dyh))
+
+    def step():
+        out, rstd = norm_rope.fwd(x, w, cos, sin)
+        return out, norm_rope.bwd(x, w, cos, sin, rstd, dy)
+
+    timer = Timer(torch, device)
+    sampler = ClockSampler(device.index)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # A step is ~0.1 ms of device work: launched op by op its timing would include the host's
+    # launch overhead, so the timed step (and each leg) replays a CUDA graph of its launches.
+    out, rstd = norm_rope.fwd(x, w, cos, sin)
+    g_step, g_fwd, g_bwd = (_graph(torch, device, f) for f in (
+        step, lambda: norm_rope.fwd(x, w, cos, sin), lambda: norm_rope.bwd(x, w, cos, sin, rstd, dy)))
+    sampler.ready()
+    if dist:
+        dist.barrier()
+    t_steps = timer.run(g_step.replay, args.steps)
+    clocks = sampler.stop(busy=g_step.replay)
+    t_fwd = timer.run(g_fwd.replay, args.steps)
+    t_bwd = timer.run(g_bwd.replay, args.steps)
+    hx, hdy = xh.pin_memory(), dyh.pin_memory()
+    dx_, ddy = torch.empty_like(x), torch.empty_like(dy)
+    hout, hdx = torch.empty_like(hx).pin_memory(), torch.empty_like(hx).pin_memory()
+
+    def e2e():  # through the public, differentiable API
+        dx_.copy_(hx, non_blocking=True)
+        ddy.copy_(hdy, non_blocking=True)
+        xg = dx_.detach().requires_grad_()
+        o = norm_rope.qk_norm_rope(xg, w, cos, sin)
+        o.backward(ddy)
+        hout.copy_(o.detach(), non_blocking=True)
+        hdx.copy_(xg.grad, non_blocking=True)
+
+    for _ in range(2):
+        e2e()
+    t_e2e = timer.run(e2e, args.steps, flush=False)
+    ms = max_over_ranks(torch, dist, sum(t_steps) / len(t_steps), device)
+    ms_e2e = max_over_ranks(torch, dist, sum(t_e2e) / len(t_e2e), device)
+    ms_f, ms_b = sum(t_fwd) / len(t_fwd), sum(t_bwd) / len(t_bwd)
+    rows = NR["B"] * NR["S"] * NR["H"]
+    xb = rows * NR["D"] * 2
+    cs = 2 * NR["B"] * NR["S"] * (NR["rope"] // 2) * 4
+    bwd_bytes = 3 * xb + rows * 4 + cs
+    pk = peaks()
+    ach = bwd_bytes / (ms_b * 1e-3) / 1e9
+    total = nr_bytes()
+    res = {
+        "metric": "QK prologue (RMSNorm + RoPE fwd + bwd) HBM GB/s (algorithmic bytes)",
+        "value": total * world / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (fp32 statistics)",
+        "data": "synthetic (seeded N(0,1) bf16 q, dy and weight; RoPE angles of positions 0..S-1)",
+        "config": nr_config(world),
+        "timing": "value and legs: CUDA-graph replay of the step's launches; e2e: the public API op by op",
+        "legs": {"fwd_ms": ms_f, "fwd_gbs": (2 * xb + rows * 4 + cs) / (ms_f * 1e-3) / 1e9, "bwd_ms": ms_b},
+        "e2e": {"value": total * world / (ms_e2e * 1e-3) / 1e9, "unit": "GB/s",
+                "h2d_bytes_per_step": 2 * hx.numel() * 2, "d2h_bytes_per_step": 2 * hx.numel() * 2},
+        "roofline": {"bound": "hbm", "kernel": "mzb::nr::bwd_kernel<128>", "achieved": ach, "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": ach / pk["hbm_gbs"], "peak_note": f"{pk['_source']} copy bandwidth",
+                     "algorithmic_bytes_per_launch": bwd_bytes, "ms_per_launch": ms_b, "traffic": None},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r = cpu_normrope(torch, xh, wh, ch, sh, dyh)
+        ro, rdx = r.pop("result")
+        n = ro.shape[1]
+        eo = (out[:, :n].float().cpu() - ro.float()).abs().max().item()
+        r["parity"] = {"tokens": n, "max_abs_err_out": eo, "note": "GPU forward rows vs the CPU reference "
+                       "composition in bf16 on the sampled tokens (same rounding points: expected 0 or one bf16 step)"}
+        res["cpu_baseline"] = r
+    return res
+
+
+def cpu_normrope(torch, x, w, cos, sin, dy, n_tok: int = 1024) -> dict:
+    """The reference's CPU path (the model's RMSNorm + RoPE in torch, bf16, with autograd for
+    the backward) on the first ``n_tok`` tokens (all heads), all host threads."""
+    from oracle import torch_ref as R
+    cores = cpu_threads(torch)
+    xs = x[:, :n_tok].clone().requires_grad_()
+    ws = w.clone().requires_grad_()
+    t0 = time.perf_counter()
+    o = R.qk_norm_rope(xs, ws, cos[:, :n_tok], sin[:, :n_tok])
+    o.backward(dy[:, :n_tok])
+    dt = time.perf_counter() - t0
+    frac = n_tok / NR["S"]
+    return {"value": nr_bytes() * frac / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "port", "ms": dt * 1e3,
+            "sample": f"{n_tok} of {NR['S']} tokens x {NR['H']} heads: torch bf16 RMSNorm + RoPE forward + autograd "
+                      f"backward (the reference's eager composition), {dt:.2f} s",
+            "result": (o.detach(), xs.grad)}
+
+
+def reference_normrope(args, rank, world) -> dict:
+    import torch
+    if rank != 0:
+        return None
+    x, w, cos, sin, dy = nr_inputs(torch)
+    runs = []
+    for _ in range(args.warmup + args.steps):
+        r = cpu_normrope(torch, x, w, cos, sin, dy)
+        r.pop("result")
+        runs.append(r)
+    return _reference_line(args, world, "QK prologue (RMSNorm + RoPE fwd + bwd) HBM GB/s (algorithmic bytes)",
+                           "GB/s", nr_config(world), runs, "bf16 (reference CPU composition)", "synthetic",
+                           scaling="weak")
+
+
 CONFIGS = {"window": c1_config, "indexer": c2_config, "prefill": c3_config, "decode": c4_config,
-           "train": c5_config, "candidates": cf_config, "compressor": cp_config}
+           "train": c5_config, "candidates": cf_config, "compressor": cp_config, "normrope": nr_config}
 
 BENCHES = {"window": (bench_window, reference_window),
            "indexer": (bench_indexer, reference_indexer), "prefill": (bench_prefill, reference_prefill),
            "train": (bench_train, reference_train), "decode": (bench_decode, reference_decode),
            "candidates": (bench_candidates, reference_candidates),
-           "compressor": (bench_compressor, reference_compressor)}
+           "compressor": (bench_compressor, reference_compressor),
+           "normrope": (bench_normrope, reference_normrope)}
 
 
 def main():
@@ -1490,6 +1656,7 @@ def main():
         C4.update(B=8)
         CF.update(rows=256)
         CP.update(B=1, S=4096)
+        NR.update(S=1024)
         args.no_cpu_baseline = True
     assert args.warmup >= 3 or args.impl == "reference", "at least 3 warm-up steps"
 

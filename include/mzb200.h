@@ -229,6 +229,24 @@ MZB_API int mzb_compress(const float* kv, const float* gate, const void* norm_w,
                          const float* sin_v, void* latent, void* cache, int64_t B, int64_t G, int ratio, int D,
                          int rope_dim, float eps, void* stream);
 
+/* ------------------------------------------------------------------ RMSNorm + RoPE prologue
+ * mzb_norm_rope_fwd -- replaces `qk_norm_rope` / kernel `make_fwd`
+ *   (src/mzoo/layers/attn/norm_rope.py:52-110, 183-230; contract `qk_norm_rope_eager` :37-44 =
+ *   archs/dsv4/modeling_deepseek_v41.py:49-63 RMSNorm then :405-425 apply_rotary_pos_emb).
+ *   x, out bf16 [rows, dim] (rows = B*S*H, row r of token r / heads), w bf16 [dim], cos / sin
+ *   fp32 [rows / heads, rope_dim / 2] (NULL when rope_dim == 0); rstd fp32 [rows] (saved for
+ *   the backward).  dim in {64, 96, 128, 256}; rope_dim even; x, w, out 16-byte aligned.
+ * mzb_norm_rope_bwd -- replaces kernel `make_bwd` (norm_rope.py:113-180): dx bf16 [rows, dim],
+ *   dw fp32 [dim] = sum over rows, summed in a fixed order through dw_part, a float workspace
+ *   of parts * dim entries with parts >= mzb_norm_rope_bwd_parts(rows, dim).
+ */
+MZB_API int mzb_norm_rope_fwd(const void* x, const void* w, const float* cos, const float* sin, void* out,
+                              float* rstd, int64_t rows, int heads, int dim, int rope_dim, float eps, void* stream);
+MZB_API int mzb_norm_rope_bwd_parts(int64_t rows, int dim);
+MZB_API int mzb_norm_rope_bwd(const void* x, const void* dy, const void* w, const float* rstd, const float* cos,
+                              const float* sin, void* dx, float* dw_part, float* dw, int64_t rows, int heads,
+                              int dim, int rope_dim, int parts, void* stream);
+
 /* Self-test of the bounded device waits (no counterpart in the reference: it checks this
  * library's own failure path).  One thread waits on an mbarrier nothing arrives on; after
  * limit_ns (<= 2e9) the wait gives up, writes 901 (scope 0: CTA-scope wait) or 902

@@ -53,6 +53,9 @@ SIGNATURES = {
     "mzb_candidate_topk": [_P, _P, _P, _I64, _I64, _I32, _I32, _I32, _P, _P],
     "mzb_compress": [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _F32, _P],
     "mzb_selftest_bounded_wait": [_I64, _I32, _P, _P],
+    "mzb_norm_rope_fwd": [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _F32, _P],
+    "mzb_norm_rope_bwd_parts": [_I64, _I32],
+    "mzb_norm_rope_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

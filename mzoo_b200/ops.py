@@ -343,6 +343,48 @@ def _(kv, gate, norm_w, cos, sin, ratio, rope_dim, eps):
             kv.new_empty((B, G, D) if cos is not None else (0,), dtype=torch.bfloat16))
 
 
+# ----------------------------------------------------------------------------- RMSNorm + RoPE prologue
+
+@torch.library.custom_op("mzb::norm_rope_fwd", mutates_args=())
+def norm_rope_fwd(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor | None, sin: torch.Tensor | None,
+                  heads: int, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(out bf16 like x, rstd fp32 [rows]) of ``mzb_norm_rope_fwd``: x bf16 [rows, D] contiguous,
+    w bf16 [D], cos / sin fp32 [rows / heads, rope_dim / 2] contiguous (None: no rope)."""
+    rows, D = x.shape
+    out = torch.empty_like(x)
+    rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+    rd = 0 if cos is None else 2 * cos.shape[-1]
+    call("mzb_norm_rope_fwd", ptr(x), ptr(w), ptr(cos), ptr(sin), ptr(out), ptr(rstd), rows, heads, D, rd, eps,
+         stream_ptr(x.device))
+    return out, rstd
+
+
+@norm_rope_fwd.register_fake
+def _(x, w, cos, sin, heads, eps):
+    return torch.empty_like(x), x.new_empty((x.shape[0],), dtype=torch.float32)
+
+
+@torch.library.custom_op("mzb::norm_rope_bwd", mutates_args=())
+def norm_rope_bwd(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor | None, sin: torch.Tensor | None,
+                  rstd: torch.Tensor, dy: torch.Tensor, heads: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(dx bf16 like x, dw fp32 [D]) of ``mzb_norm_rope_bwd`` (dw summed over rows in a fixed
+    order through a [parts, D] fp32 workspace)."""
+    rows, D = x.shape
+    dx = torch.empty_like(x)
+    dw = torch.empty(D, dtype=torch.float32, device=x.device)
+    parts = _lib.lib().mzb_norm_rope_bwd_parts(rows, D)
+    part = torch.empty(parts * D, dtype=torch.float32, device=x.device)
+    rd = 0 if cos is None else 2 * cos.shape[-1]
+    call("mzb_norm_rope_bwd", ptr(x), ptr(dy), ptr(w), ptr(rstd), ptr(cos), ptr(sin), ptr(dx), ptr(part), ptr(dw), rows,
+         heads, D, rd, parts, stream_ptr(x.device))
+    return dx, dw
+
+
+@norm_rope_bwd.register_fake
+def _(x, w, cos, sin, rstd, dy, heads):
+    return torch.empty_like(x), x.new_empty((x.shape[1],), dtype=torch.float32)
+
+
 # ----------------------------------------------------------------------------- self-test
 
 def selftest_bounded_wait(device, limit_ns: int, scope: int, check: bool) -> int:

@@ -20,6 +20,8 @@ module restates the same float32 torch arithmetic, operation for operation, for 
 - ``topk_indices``      ``golden_ref.topk_indices`` (golden_ref.py:230-243)
 - ``pack_rows`` / ``unpack_rows``  576-channel latent <-> 672-byte FP8 rows (absmax/448
                         e4m3 per 64 channels, fp32 scales, bf16 rope)
+- ``qk_norm_rope``      the model's RMSNorm then interleaved-pair RoPE
+                        (modeling_deepseek_v41.py:49-63, :405-425; ``norm_rope.py:37-44``)
 - ``fake_quant_fp4_ocp`` / ``fake_quant_fp8_absmax``  the two rules BASELINE config 5
                         names, written like ``quant.py:49-86`` with the scale line swapped
 """
@@ -157,3 +159,19 @@ def fake_quant_fp8_absmax(x: torch.Tensor, block: int = 128) -> torch.Tensor:
     scale = torch.where(scale > 0, scale, torch.ones_like(scale))
     y = (xf / scale).clamp(-448, 448).to(torch.float8_e4m3fn).float() * scale
     return y.reshape(x.shape).to(x.dtype)
+
+
+def qk_norm_rope(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 eps: float = 1e-6) -> torch.Tensor:
+    """x [B,S,H,D], w [D], cos / sin [B,S,rd/2] -> RMSNorm (fp32 statistics, ``w * x.to(dtype)``)
+    then RoPE on the trailing rd channels' (even, odd) pairs, in x's dtype."""
+    dtype = x.dtype
+    h = x.float()
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    y = w * h.to(dtype)
+    rd = cos.shape[-1] * 2
+    nope, rope = y[..., :-rd], y[..., -rd:]
+    c, s = cos.unsqueeze(2), sin.unsqueeze(2)
+    even, odd = rope[..., 0::2].float(), rope[..., 1::2].float()
+    rot = torch.stack([even * c - odd * s, even * s + odd * c], dim=-1).flatten(-2)
+    return torch.cat([nope, rot.to(dtype)], dim=-1)

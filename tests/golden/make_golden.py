@@ -279,6 +279,39 @@ def make_indexer_fp8(golden_ref) -> None:
     np.savez_compressed(os.path.join(HERE, "indexer_fp8.npz"), **out)
 
 
+def make_norm_rope() -> None:
+    """The model's own RMSNorm + RoPE composition (``DeepseekV41RMSNorm`` and
+    ``apply_rotary_pos_emb``, modeling_deepseek_v41.py:49-63 / :405-425; the
+    ``qk_norm_rope_eager`` of layers/attn/norm_rope.py:37-44) on fp32 inputs with its
+    autograd gradients, and on bf16 inputs (forward only), for q-shaped and kv-shaped
+    tensors and non-power-of-two sizes."""
+    from mzoo.archs.dsv4.modeling_deepseek_v41 import DeepseekV41RMSNorm, apply_rotary_pos_emb  # noqa: E402
+    out = {}
+    g = torch.Generator().manual_seed(7)
+    cases = [(2, 33, 3, 64, 16), (1, 20, 1, 128, 64), (1, 7, 5, 96, 24), (1, 6, 2, 256, 64)]
+    for c, (b, s, h, d, rd) in enumerate(cases):
+        x = torch.randn(b, s, h, d, generator=g)
+        w = torch.randn(d, generator=g)
+        pos = torch.arange(s, dtype=torch.float32) + 3.0
+        freqs = pos[:, None] / (10000.0 ** (torch.arange(0, rd, 2, dtype=torch.float32) / rd))
+        cos = freqs.cos()[None].expand(b, -1, -1).contiguous()
+        sin = freqs.sin()[None].expand(b, -1, -1).contiguous()
+        dy = torch.randn(b, s, h, d, generator=g)
+        key = f"c{c}."
+        for dt, tag in ((torch.float32, "f32"), (torch.bfloat16, "bf16")):
+            xx, ww = x.to(dt).clone().requires_grad_(dt == torch.float32), w.to(dt).clone()
+            ww.requires_grad_(dt == torch.float32)
+            norm = DeepseekV41RMSNorm(d, eps=1e-6).to(dt)
+            y = apply_rotary_pos_emb(torch.func.functional_call(norm, {"weight": ww}, (xx,)), cos, sin)
+            out[key + tag + ".x"], out[key + tag + ".w"], out[key + tag + ".y"] = bits(xx.detach()), bits(ww.detach()), \
+                bits(y.detach())
+            if dt == torch.float32:
+                y.backward(dy)
+                out[key + "dy"], out[key + "dx"], out[key + "dw"] = dy.numpy(), xx.grad.numpy(), ww.grad.numpy()
+        out[key + "cos"], out[key + "sin"] = cos.numpy(), sin.numpy()
+    np.savez_compressed(os.path.join(HERE, "norm_rope.npz"), **out)
+
+
 def make_candidates() -> None:
     """Level one through the reference's ``select_candidate_blocks``
     (archs/owlet1/indexer.py:14-41 = archs/dsv4/modeling_deepseek_v41.py:427-454); level two
@@ -379,6 +412,8 @@ if __name__ == "__main__":
         make_mla(golden_ref)
     if not only or "indexer_fp8" in only:
         make_indexer_fp8(golden_ref)
+    if not only or "norm_rope" in only:
+        make_norm_rope()
     if not only or "candidates" in only:
         make_candidates()
     if not only or "compressor" in only:

@@ -19,7 +19,7 @@ import pytest
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
-@pytest.mark.parametrize("config", ["window", "indexer", "prefill", "decode", "train", "candidates", "compressor"])
+@pytest.mark.parametrize("config", ["window", "indexer", "prefill", "decode", "train", "candidates", "compressor", "normrope"])
 def test_reference_arm_json_line(config):
     cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--config", config,
            "--steps", "1", "--warmup", "1", "--cpu-sample", "64"]

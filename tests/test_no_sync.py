@@ -7,7 +7,7 @@ import pytest
 import torch
 from torch._subclasses.fake_tensor import FakeTensorMode
 
-from mzoo_b200 import csa2_attn, indexer, ops, quant, sparse_mla, swa_attn
+from mzoo_b200 import csa2_attn, indexer, norm_rope, ops, quant, sparse_mla, swa_attn
 
 # ops whose last argument asks for an error-word read (a host synchronisation) after the launch
 CHECKED_OPS = ("indexer_scores", "indexer_topk", "indexer_bwd", "attn_fwd", "attn_bwd", "sparse_mla_fwd")
@@ -83,3 +83,12 @@ def test_quant_wrappers_do_not_sync(fake):
     x = torch.empty(8, 128, device=fake, dtype=torch.bfloat16)
     quant._fake_quant_fp4_block(x, 32)
     quant._fake_quant_fp8_block(x, 32)
+
+
+def test_norm_rope_does_not_sync(fake):
+    x = torch.empty(1, 16, 4, 128, device=fake, dtype=torch.bfloat16)
+    w = torch.empty(128, device=fake, dtype=torch.bfloat16)
+    cs = torch.empty(1, 16, 32, device=fake)
+    out, rstd = norm_rope.fwd(x, w, cs, cs)
+    dx, dw = norm_rope.bwd(x, w, cs, cs, rstd, out)
+    assert dx.shape == x.shape and dw.shape == (128,)

@@ -10,7 +10,7 @@ M = dict(device="meta")
 
 def test_all_ops_registered():
     names = {"fq_fp4", "fq_fp8", "indexer_scores", "indexer_topk", "indexer_bwd", "attn_fwd", "attn_bwd",
-             "sparse_mla_fwd", "candidate_blocks", "candidate_topk", "compress"}
+             "sparse_mla_fwd", "candidate_blocks", "candidate_topk", "compress", "norm_rope_fwd", "norm_rope_bwd"}
     assert names <= set(dir(torch.ops.mzb))
 
 
@@ -61,3 +61,9 @@ def test_fake_shapes():
     lat, cache = torch.ops.mzb.compress(kv, kv, nw, cs, cs, 4, 64, 1e-6)
     assert lat.shape == (2, 10, 576) and cache.shape == (2, 10, 576) and lat.dtype == torch.bfloat16
     assert torch.ops.mzb.compress(kv, kv, nw, None, None, 4, 0, 1e-6)[1].shape == (0,)
+    xr = torch.empty(64, 128, dtype=torch.bfloat16, **M)
+    cs = torch.empty(16, 32, dtype=torch.float32, **M)
+    out, rstd = torch.ops.mzb.norm_rope_fwd(xr, torch.empty(128, dtype=torch.bfloat16, **M), cs, cs, 4, 1e-6)
+    assert out.shape == xr.shape and rstd.shape == (64,)
+    dx, dw = torch.ops.mzb.norm_rope_bwd(xr, torch.empty(128, dtype=torch.bfloat16, **M), cs, cs, rstd, xr, 4)
+    assert dx.shape == xr.shape and dw.shape == (128,) and dw.dtype == torch.float32
