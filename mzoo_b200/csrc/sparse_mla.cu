@@ -13,43 +13,48 @@
 //
 // Work item = one query token (all 128 heads).  A cluster of two CTAs owns an item:
 // tcgen05.mma.cta_group::2 with M = 128 heads (64 per CTA), so each SM keeps its heads'
-// fp32 O (64 x 512) in TMEM as 128 lanes x 256 columns and S (64 x 64 keys) as 128 lanes x
-// 32 columns.  Keys come in tiles of 64 (32 per CTA for the QK^T B operand).
+// fp32 O (64 x 512) in TMEM as 128 lanes x 256 columns.  Keys come in tiles of 128, 64 per
+// CTA (the QK^T B operand's N half): S (64 heads x 128 keys) is 128 lanes x 64 columns,
+// lanes 0-63 holding the leader's 64 keys and lanes 64-127 the peer's, double-buffered.
+// A 2-CTA MMA instruction costs about the same at N = 64 and N = 128 (~45 cycles), and
+// each QK^T tile re-reads this CTA's 73.7 KB Q block from shared memory, so 128-key tiles
+// halve both the QK^T instruction count and the Q reads per key against 64-key tiles.
 //
 // Warp roles per CTA (512 threads):
 //   0      TMA of this CTA's Q half (64 heads x 576, 9 swizzled 64-column blocks)
 //   1      TMEM allocation; in the leader CTA, the thread issuing the QK^T MMAs
-//   2      V copier: assembles the V tile from K tiles (below), waits for this CTA's V
-//          tile and tells the leader and the K-tile owners
+//   2      V copier: pushes V blocks out of this CTA's K tile (below), waits for this CTA's
+//          two V halves and tells the leader and the K-tile owners
 //   3      in the leader CTA, the thread issuing the PV MMAs
 //   4-7    softmax / O correction / epilogue (thread = TMEM lane = (head, key half))
-//   8-11   K producers for even tiles, 12-15 for odd tiles: gather + dequantise this CTA's
-//          32 keys x 576 channels to bf16 (two groups, so each has two tile-times to hide
-//          the gather latency)
-// V is not dequantised again: V tile block (64 keys x 64 channels) = the same channel
-// block of both CTAs' K tiles (32 keys each, identical 128-byte swizzle), so the copier
-// pushes 4 KB blocks of its K tile into its own and the peer's V tile with
-// cp.async.bulk shared::cta -> shared::cluster, completing on the destination's V_FULL.
-// QK^T and PV are issued by two threads: a tcgen05.mma issue blocks until the tensor pipe
-// takes the instruction, so one thread alternating QK_j, PV_{j-1} and their barrier waits
-// left the pipe idle between the bursts (measured: ~4500 cycles per 64-key tile against
-// ~2150 of MMA work); with two issuers one thread's waits overlap the other's MMAs.  The
-// softmax then waits P_EMPTY (PV of the tile two back done) before it rewrites a P buffer
-// or rescales O.  The running max is only raised when it grows by more than 2^8 (in exp2
-// units), which skips most O corrections.
+//   8-15   K producers: gather + dequantise this CTA's 64 keys x 576 channels to bf16
+//          (rows loaded into registers a tile ahead, written once QK^T of the previous
+//          tile and the V copies out of it are done)
+// Shared memory (227 KB): Q 72 KB, one K tile 72 KB, V 2 x 32 KB, P 2 x 8 KB.
+// V is not dequantised again: the PV B operand of CTA r for key half h is CTA h's 64 keys
+// x CTA r's 256 output channels, and each 64-channel block of it is one 8 KB block of CTA
+// h's K tile (identical 128-byte swizzle), so CTA h's copier pushes those blocks into its
+// own and the peer's V half h with cp.async.bulk shared::cta -> shared::cluster, completing
+// on the destination's V_FULL.  P (64 heads x 128 keys bf16) is written by the softmax
+// threads in two halves: lanes 0-63 the leader's keys, lanes 64-127 the peer's.
+// QK^T and PV are issued by two threads, so one thread's barrier waits overlap the other's
+// MMAs and the pipe takes QK^T of the next tile while the softmax of this one runs.  The
+// running max is only raised when it grows by more than 2^8 (in exp2 units), which skips
+// most O corrections.
 #include "tc.cuh"
 
 namespace mzb {
 namespace mla {
 
 constexpr int H = 128, HC = 64, DQK = 576, DV = 512, ROWB = 672, ROPE_OFF = 544, SCALE_OFF = 512;
-constexpr int NT = 64, NTH = 32;
+constexpr int NT = 128, NTH = 64;          // keys per tile, per CTA
 constexpr int QBLK = 9;
+constexpr int BLK = NTH * 128;             // one 64-channel block of a K tile / V half (8 KB)
 constexpr int Q_BYTES = QBLK * HC * 128;   // 73728
-constexpr int K_BYTES = QBLK * NTH * 128;  // 36864
-constexpr int V_BYTES = 4 * NT * 128;      // 32768
-constexpr int P_BYTES = HC * 128;          // 8192
-constexpr int TILE_BYTES = Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES;  // 229376
+constexpr int K_BYTES = QBLK * BLK;        // 73728
+constexpr int VH_BYTES = 4 * BLK;          // 32768: one key half x this CTA's 256 channels
+constexpr int PH_BYTES = HC * 128;         // 8192: 64 heads x 64 keys bf16
+constexpr int TILE_BYTES = Q_BYTES + K_BYTES + 2 * VH_BYTES + 2 * PH_BYTES;  // 229376
 // misc (barriers, exchange buffers) after the tiles; no static shared memory, so the
 // dynamic window starts 1024-aligned (checked at run time) and the total stays under the
 // 227 KB per-block limit.
@@ -57,20 +62,23 @@ constexpr int MISC_BYTES = 512 + 2 * 2 * 128 * 4;
 constexpr int SMEM_DYN = TILE_BYTES + MISC_BYTES;
 constexpr int NTHREADS = 512;
 constexpr int TMEM_COLS = 512;
-constexpr int S_COL0 = 256;
+constexpr int S_COL0 = 256, S_COLS = NTH;  // S buffers at columns 256 and 320
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 
 enum Bar {
   Q_FULL = 0, Q_READY, Q_EMPTY,
-  K_FULL, K_FULL1, K_EMPTY, K_EMPTY1,
-  K_WRIT, K_WRIT1,    // local: this CTA's K tile written (its 4 producer warps)
-  K_CP, K_CP1,        // local: the copies out of this CTA's K tile have landed (2 relays)
-  V_FULL, V_FULL1,    // local: this CTA's V tile complete (32 KB of copies)
-  V_READY, V_READY1,  // leader: both CTAs' V tiles complete (2 relays)
-  V_EMPTY, V_EMPTY1,  // local (multicast commit): PV done
+  K_FULL,             // leader: both CTAs' K tiles written (8 producer warps each)
+  K_EMPTY,            // local (multicast commit): QK^T of the tile done
+  K_WRIT,             // local: this CTA's K tile written (its 8 producer warps)
+  K_CP,               // local: the copies out of this CTA's K tile have landed (2 copiers)
+  V_FULL, V_FULL1,    // local: V half h complete (32 KB of copies from CTA h)
+  V_READY, V_READY1,  // leader: V half h complete in both CTAs (2 copiers)
+  V_EMPTY, V_EMPTY1,  // local (multicast commit): PV over key half h done
   S_FULL, S_FULL1, S_EMPTY, S_EMPTY1,
-  P_FULL, P_FULL1, P_EMPTY, P_EMPTY1, O_DONE, O_EMPTY,
+  P_FULL,             // leader: P written and O corrected (4 softmax warps x 2 CTAs)
+  O_DONE,             // local (multicast commit): both PV halves of the tile done
+  O_EMPTY,
   XCH, XCH1, XCH2, XCH3,  // row-max exchange per (S buffer, warp pair {4,6} / {5,7}), local
   XL, XL1,                // row-sum exchange per warp pair, local
   O_FINAL,            // multicast commit after an item's last PV (epilogue, item parity)
@@ -132,14 +140,6 @@ __device__ __forceinline__ const uint8_t* slot_row(const Args& a, const Slot& s,
   return a.cmp + row * ROWB;
 }
 
-__device__ __forceinline__ bool slot_valid(const Args& a, const Slot& s, int tk, int p) {
-  if (p < s.n_win) return true;
-  const int c = p - s.n_win;
-  if (c >= a.topk) return false;
-  const int g = a.idx[(long long)tk * a.topk + c];
-  return g >= 0 && g < s.g_lim;
-}
-
 // 16 e4m3 codes * scale -> 16 bf16 (two 16-byte chunks).
 __device__ __forceinline__ void dequant16(const uint4 raw, float scale, uint4& lo, uint4& hi) {
   const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -185,6 +185,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
     break;                                                            \
   }
 
+// Phases: every role walks the same (item, tile) sequence and counts tiles in g.  A barrier
+// completing once per tile is waited with parity g & 1 for tile g, and with (g & 1) ^ 1 for
+// the completion of tile g - 1 (immediate at g = 0).  Each waiter has already seen the
+// completion before the one it waits for, so a parity wait can never match an older phase.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     mla_fwd_kernel(const __grid_constant__ CUtensorMap tq, Args a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -200,8 +204,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   }
   uint8_t* qs = sm;
   uint8_t* ks = qs + Q_BYTES;
-  uint8_t* vs = ks + 2 * K_BYTES;
-  uint8_t* ps = vs + 2 * V_BYTES;
+  uint8_t* vs = ks + K_BYTES;
+  uint8_t* ps = vs + 2 * VH_BYTES;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = tc::cluster_ctarank();
@@ -209,11 +213,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     const uint32_t counts[NBAR] = {1, 2, 1,           // Q_FULL, Q_READY, Q_EMPTY
-                                   8, 8, 1, 1,        // K_FULL x2, K_EMPTY x2
-                                   4, 4, 2, 2,        // K_WRIT x2, K_CP x2
+                                   16, 1, 8, 2,       // K_FULL, K_EMPTY, K_WRIT, K_CP
                                    1, 1, 2, 2, 1, 1,  // V_FULL x2, V_READY x2, V_EMPTY x2
                                    1, 1, 8, 8,        // S_FULL x2, S_EMPTY x2
-                                   8, 8, 1, 1, 1, 8,  // P_FULL x2, P_EMPTY x2, O_DONE, O_EMPTY
+                                   8, 1, 8,           // P_FULL, O_DONE, O_EMPTY
                                    2, 2, 2, 2, 2, 2,  // XCH x4, XL x2 (the two warps holding one head's key halves)
                                    1};                // O_FINAL
     for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], counts[i]);
@@ -274,8 +277,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       // descriptors built once; the unrolled loop adds compile-time offsets (a single
       // thread issues every MMA, so per-MMA descriptor arithmetic would throttle issue)
       const uint64_t qd = tc::make_sdesc<128>(smem_u32(qs), 16, 1024);
-      const uint64_t kd[2] = {tc::make_sdesc<128>(smem_u32(ks), 16, 1024),
-                              tc::make_sdesc<128>(smem_u32(ks + K_BYTES), 16, 1024)};
+      const uint64_t kd = tc::make_sdesc<128>(smem_u32(ks), 16, 1024);
       int g = 0, ii = 0;
       for (int it = pair; it < items && !abort_flag; it += npairs) {
         int tk, sp, t0, t1;
@@ -285,18 +287,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         bool ok = true;
         for (int j = t0; j < t1; ++j, ++g) {
           const int st = g & 1, ph = (g >> 1) & 1;
-          if (!tc::mbar_wait(&bars[K_FULL + st], ph, a.err, 214) ||
+          if (!tc::mbar_wait(&bars[K_FULL], g & 1, a.err, 214) ||
               !tc::mbar_wait(&bars[S_EMPTY + st], ph ^ 1, a.err, 215)) { ok = false; break; }
           tc::fence_after_sync();
-          const uint32_t d = tmem + S_COL0 + st * 32;
-          const uint64_t kb = st ? kd[1] : kd[0];
+          const uint32_t d = tmem + S_COL0 + st * S_COLS;
 #pragma unroll
           for (int kk = 0; kk < 36; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma2_f16(d, tc::sdesc_add(qd, cb * 8192 + off), tc::sdesc_add(kb, cb * 4096 + off), idesc_qk,
+            tc::mma2_f16(d, tc::sdesc_add(qd, cb * 8192 + off), tc::sdesc_add(kd, cb * BLK + off), idesc_qk,
                          kk > 0 ? 1u : 0u);
           }
-          tc::mma2_commit_mc(&bars[K_EMPTY + st], 3);
+          tc::mma2_commit_mc(&bars[K_EMPTY], 3);
           tc::mma2_commit_mc(&bars[S_FULL + st], 3);
           if (j == t1 - 1) tc::mma2_commit_mc(&bars[Q_EMPTY], 3);
         }
@@ -309,9 +310,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     if (rank == 0 && lane == 0) {
       const uint32_t idesc_pv = tc::make_idesc(128, 256, 1, 1, false, true);
       const uint64_t pd[2] = {tc::make_sdesc<128>(smem_u32(ps), 16, 1024),
-                              tc::make_sdesc<128>(smem_u32(ps + P_BYTES), 16, 1024)};
-      const uint64_t vd[2] = {tc::make_sdesc<128>(smem_u32(vs), 8192, 1024),
-                              tc::make_sdesc<128>(smem_u32(vs + V_BYTES), 8192, 1024)};
+                              tc::make_sdesc<128>(smem_u32(ps + PH_BYTES), 16, 1024)};
+      const uint64_t vd[2] = {tc::make_sdesc<128>(smem_u32(vs), BLK, 1024),
+                              tc::make_sdesc<128>(smem_u32(vs + VH_BYTES), BLK, 1024)};
       int g = 0, ii = 0;
       for (int it = pair; it < items && !abort_flag; it += npairs) {
         int tk, sp, t0, t1;
@@ -320,22 +321,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         // the previous item's epilogue has read O
         MLA_WAIT(O_EMPTY, (ii & 1) ^ 1, 211);
         bool ok = true;
-        for (int j = t0; j < t1; ++j, ++g) {
-          const int st = g & 1, ph = (g >> 1) & 1;
-          if (!tc::mbar_wait(&bars[V_READY + st], ph, a.err, 212) ||
-              !tc::mbar_wait(&bars[P_FULL + st], ph, a.err, 213)) { ok = false; break; }
-          tc::fence_after_sync();
-          const uint64_t ad0 = st ? pd[1] : pd[0], bd0 = st ? vd[1] : vd[0];
+        for (int j = t0; j < t1 && ok; ++j, ++g) {
+          if (!tc::mbar_wait(&bars[P_FULL], g & 1, a.err, 213)) { ok = false; break; }
 #pragma unroll
-          for (int i = 0; i < 2; ++i) {
+          for (int h = 0; h < 2; ++h) {
+            if (!tc::mbar_wait(&bars[V_READY + h], g & 1, a.err, 212)) { ok = false; break; }
+            tc::fence_after_sync();
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj)
-              tc::mma2_f16(tmem + i * 128, tc::sdesc_add(ad0, jj * 32), tc::sdesc_add(bd0, 2 * i * 8192 + jj * 2048),
-                           idesc_pv, (j == t0 && jj == 0) ? 0u : 1u);
+            for (int i = 0; i < 2; ++i) {
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj)
+                tc::mma2_f16(tmem + i * 128, tc::sdesc_add(pd[h], jj * 32), tc::sdesc_add(vd[h], 2 * i * BLK + jj * 2048),
+                             idesc_pv, (j == t0 && h == 0 && jj == 0) ? 0u : 1u);
+            }
+            tc::mma2_commit_mc(&bars[V_EMPTY + h], 3);
           }
-          tc::mma2_commit_mc(&bars[V_EMPTY + st], 3);
-          tc::mma2_commit_mc(&bars[P_EMPTY + st], 3);
-          tc::mma2_commit_mc(&bars[O_DONE], 3);
+          if (ok) tc::mma2_commit_mc(&bars[O_DONE], 3);
         }
         if (!ok) { abort_flag = 1; break; }
         tc::mma2_commit_mc(&bars[O_FINAL], 3);
@@ -363,34 +364,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       const Slot s = item_info(a, tk);
       float m = -1e30f, lsum = 0.0f;
       bool ok = true;
-      // key validity: the index of this thread's key of tile j + 1 is loaded while tile j is
-      // processed (window slots need no load)
+      // key validity: this lane's two keys of tile j + 1 (slots kofs and kofs + 32 of the
+      // warp's key half) are looked up while tile j is processed (window slots need no load)
       auto slot_code = [&](int p) -> int {
         if (p < s.n_win) return 0;
         const int c = p - s.n_win;
         return c < a.topk ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
       };
+      auto slot_ok = [&](int p, int code) { return p < s.n_win || (code >= 0 && code < s.g_lim); };
       const int kofs = kh * NTH + lane;
-      int code_next = slot_code(t0 * NT + kofs);
+      int cn0 = slot_code(t0 * NT + kofs), cn1 = slot_code(t0 * NT + kofs + 32);
       for (int j = t0; j < t1; ++j, ++g) {
         const int st = g & 1, ph = (g >> 1) & 1;
-        const int code = code_next;
-        if (j + 1 < t1) code_next = slot_code((j + 1) * NT + kofs);
+        const int c0 = cn0, c1 = cn1;
+        if (j + 1 < t1) {
+          cn0 = slot_code((j + 1) * NT + kofs);
+          cn1 = slot_code((j + 1) * NT + kofs + 32);
+        }
         const int p = j * NT + kofs;
-        const uint32_t vmask = __ballot_sync(0xffffffffu, p < s.n_win || (code >= 0 && code < s.g_lim));
+        const uint32_t vm0 = __ballot_sync(0xffffffffu, slot_ok(p, c0));
+        const uint32_t vm1 = __ballot_sync(0xffffffffu, slot_ok(p + 32, c1));
         if (!tc::mbar_wait(&bars[S_FULL + st], ph, a.err, 220)) { ok = false; break; }
         tc::fence_after_sync();
-        uint32_t sr[32];
-        tc::tmem_ld32(tc::taddr(tmem, sw * 32, S_COL0 + st * 32), sr);
+        uint32_t sr[64];
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, S_COL0 + st * S_COLS), *reinterpret_cast<uint32_t(*)[32]>(sr));
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, S_COL0 + st * S_COLS + 32), *reinterpret_cast<uint32_t(*)[32]>(sr + 32));
         tc::tmem_wait_ld();
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) arrive_leader(S_EMPTY + st);
-        float sv[32];
+        float sv[64];
         float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          sv[i] = (vmask >> i & 1u) ? __uint_as_float(sr[i]) : -INFINITY;
+        for (int i = 0; i < 64; ++i) {
+          const uint32_t vm = i < 32 ? vm0 : vm1;
+          sv[i] = (vm >> (i & 31) & 1u) ? __uint_as_float(sr[i]) : -INFINITY;
           mx4[i & 3] = fmaxf(mx4[i & 3], sv[i]);
         }
         float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
@@ -401,30 +409,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         if (!tc::mbar_wait(&bars[XCH + 2 * st + (sw & 1)], ph, a.err, 223)) { ok = false; break; }
         mt = fmaxf(mt, red_m[st][l ^ 64]);
         const bool need = mt * sl > m * sl + 8.0f;
-        // PV of the tile two back (same P buffer) is done: P may be rewritten, and O_DONE's
-        // phase below cannot alias an older PV
-        if (!tc::mbar_wait(&bars[P_EMPTY + st], ph ^ 1, a.err, 225)) { ok = false; break; }
+        // both PV halves of the previous tile are done: P may be rewritten and O rescaled
+        if (!tc::mbar_wait(&bars[O_DONE], (g & 1) ^ 1, a.err, 225)) { ok = false; break; }
+        tc::fence_after_sync();
         const float m_new = need ? mt : m;
         const float alpha = fast_exp2((m - m_new) * sl);
         const float ms = m_new * sl;
-        uint32_t pk[16];
         float ps4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint8_t* prow = ps + kh * PH_BYTES + hrow * 128;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = fast_exp2(fmaf(sv[2 * i], sl, -ms));
-          const float p1 = fast_exp2(fmaf(sv[2 * i + 1], sl, -ms));
-          ps4[i & 3] += p0 + p1;
-          pk[i] = pack_bf16(p0, p1);
+        for (int c = 0; c < 8; ++c) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float p0 = fast_exp2(fmaf(sv[8 * c + 2 * i], sl, -ms));
+            const float p1 = fast_exp2(fmaf(sv[8 * c + 2 * i + 1], sl, -ms));
+            ps4[i] += p0 + p1;
+            pk[i] = pack_bf16(p0, p1);
+          }
+          st_shared16(prow + ((c ^ (hrow & 7)) * 16), make_uint4(pk[0], pk[1], pk[2], pk[3]));
         }
         const float psum = (ps4[0] + ps4[1]) + (ps4[2] + ps4[3]);
         lsum = lsum * alpha + psum;
-        uint8_t* prow = ps + st * P_BYTES + hrow * 128;
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-          st_shared16(prow + (((kh * 4 + c) ^ (hrow & 7)) * 16), make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]));
         if (j > t0 && __any_sync(0xffffffffu, need)) {
-          if (!tc::mbar_wait(&bars[O_DONE], (g - 1) & 1, a.err, 221)) { ok = false; break; }
-          tc::fence_after_sync();
           for (int c0 = 0; c0 < 256; c0 += 32) {
             uint32_t ov[32];
             tc::tmem_ld32(tc::taddr(tmem, sw * 32, c0), ov);
@@ -439,11 +446,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         tc::fence_async_smem();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) arrive_leader(P_FULL + st);
+        if (lane == 0) arrive_leader(P_FULL);
       }
       if (!ok) { abort_flag = 1; break; }
-      // epilogue: O / l, lse.  O_FINAL, not O_DONE: two PVs of this item can still be in
-      // flight here, and O_DONE's parity would alias the phase of an older PV.
+      // epilogue: O / l, lse.  O_FINAL, not O_DONE: the item's last PV can still be in flight
+      // here, and the epilogue's parity is per item.
       MLA_WAIT(O_FINAL, ii & 1, 222);
       tc::fence_after_sync();
       red_l[ii & 1][l] = lsum;
@@ -498,9 +505,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------------ K producers
-    // group 0 (warps 8-11) fills stage 0 (even tiles), group 1 (warps 12-15) stage 1
-    const int grp = (warp - 8) >> 2;
-    const int t = threadIdx.x - 256 - grp * 128;  // 0..127
+    // thread t: key kk = t / 4 of this CTA's 64, 16-byte chunks sub, sub + 4, ... of its row
+    const int t = threadIdx.x - 256;  // 0..255
     const int kk = t >> 2, sub = t & 3;
     int g = 0;
     for (int it = pair; it < items && !abort_flag; it += npairs) {
@@ -509,8 +515,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       const Slot s = item_info(a, tk);
       bool ok = true;
       for (int j = t0; j < t1; ++j, ++g) {
-        const int st = g & 1, ph = (g >> 1) & 1;
-        if (st != grp) continue;
         const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
         uint4 raw[10];
         float sc[8];
@@ -522,10 +526,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
 #pragma unroll
         for (int q = 0; q < 8; ++q) sc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
-        // the stage is free once its QK MMA is done and the copies out of it have landed
-        if (!tc::mbar_wait(&bars[K_EMPTY + st], ph ^ 1, a.err, 230) ||
-            !tc::mbar_wait(&bars[K_CP + st], ph ^ 1, a.err, 231)) { ok = false; break; }
-        uint8_t* kt = ks + st * K_BYTES + kk * 128;
+        // the tile is free once QK^T of the previous tile is done and the copies out of it
+        // have landed in both CTAs
+        if (!tc::mbar_wait(&bars[K_EMPTY], (g & 1) ^ 1, a.err, 230) ||
+            !tc::mbar_wait(&bars[K_CP], (g & 1) ^ 1, a.err, 231)) { ok = false; break; }
+        uint8_t* kt = ks + kk * 128;
 #pragma unroll
         for (int q = 0; q < 10; ++q) {
           const int c = sub + 4 * q;
@@ -533,27 +538,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
             uint4 lo, hi;
             dequant16(raw[q], sc[c >> 2], lo, hi);
             const int cb = c >> 2, ch = (c & 3) * 2;
-            st_shared16(kt + cb * 4096 + ((ch ^ (kk & 7)) * 16), lo);
-            st_shared16(kt + cb * 4096 + (((ch + 1) ^ (kk & 7)) * 16), hi);
+            st_shared16(kt + cb * BLK + ((ch ^ (kk & 7)) * 16), lo);
+            st_shared16(kt + cb * BLK + (((ch + 1) ^ (kk & 7)) * 16), hi);
           } else {
-            st_shared16(kt + 8 * 4096 + (((c - 32) ^ (kk & 7)) * 16), raw[q]);
+            st_shared16(kt + 8 * BLK + (((c - 32) ^ (kk & 7)) * 16), raw[q]);
           }
         }
         tc::fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tc::mbar_arrive(&bars[K_WRIT + st]);
-          arrive_leader(K_FULL + st);
+          tc::mbar_arrive(&bars[K_WRIT]);
+          arrive_leader(K_FULL);
         }
       }
       if (!ok) { abort_flag = 1; break; }
     }
   } else if (warp == 2) {
     // ------------------------------------------------------------------ V copier + relay
-    // V tile block lb (keys 0-31 | keys 32-63) of CTA r holds global channel block
-    // gb = (lb >> 1) * 4 + 2 r + (lb & 1); this CTA supplies its half of the keys.  Once
-    // both CTAs' copies into this CTA's V tile have landed, it tells the leader (V_READY)
-    // and both K-tile owners (K_CP: the stage may be overwritten).
+    // Block lb of V half h in CTA r holds channel block gb = (lb >> 1) * 4 + 2 r + (lb & 1)
+    // of CTA h's keys (PV chunk lb >> 1 of 256 channels, CTA r's 128 of them).  This CTA
+    // sends its K tile's blocks to V half `rank` of both CTAs, then waits for both of its own
+    // V halves and tells the leader (V_READY) and each half's source (K_CP: its K tile may
+    // be overwritten).
     if (lane == 0) {
       int g = 0;
       for (int it = pair; it < items && !abort_flag; it += npairs) {
@@ -561,25 +567,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         item_range(it, tk, sp, t0, t1);
         bool ok = true;
         for (int j = t0; j < t1; ++j, ++g) {
-          const int st = g & 1, ph = (g >> 1) & 1;
-          if (!tc::mbar_wait(&bars[K_WRIT + st], ph, a.err, 250) ||
-              !tc::mbar_wait(&bars[V_EMPTY + st], ph ^ 1, a.err, 251)) { ok = false; break; }
-          const uint32_t k_base = smem_u32(ks + st * K_BYTES), v_base = smem_u32(vs + st * V_BYTES);
+          if (!tc::mbar_wait(&bars[K_WRIT], g & 1, a.err, 250) ||
+              !tc::mbar_wait(&bars[V_EMPTY + rank], (g & 1) ^ 1, a.err, 251)) { ok = false; break; }
+          const uint32_t k_base = smem_u32(ks), v_base = smem_u32(vs + rank * VH_BYTES);
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            const uint32_t dst_bar = tc::mapa(smem_u32(&bars[V_FULL + st]), uint32_t(r));
+            const uint32_t dst_bar = tc::mapa(smem_u32(&bars[V_FULL + rank]), uint32_t(r));
 #pragma unroll
             for (int lb = 0; lb < 4; ++lb) {
               const int gb = (lb >> 1) * 4 + r * 2 + (lb & 1);
-              const uint32_t dst = tc::mapa(v_base + lb * 8192 + rank * 4096, uint32_t(r));
-              tc::bulk_copy_s2cluster(dst, k_base + gb * 4096, 4096, dst_bar);
+              tc::bulk_copy_s2cluster(tc::mapa(v_base + lb * BLK, uint32_t(r)), k_base + gb * BLK, BLK, dst_bar);
             }
           }
-          tc::mbar_expect_tx(&bars[V_FULL + st], 2 * 4 * 4096);  // 4 blocks from each CTA
-          if (!tc::mbar_wait(&bars[V_FULL + st], ph, a.err, 260)) { ok = false; break; }
-          arrive_leader(V_READY + st);
-          tc::mbar_arrive(&bars[K_CP + st]);
-          tc::mbar_arrive_remote(tc::mapa(smem_u32(&bars[K_CP + st]), rank ^ 1u));
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tc::mbar_expect_tx(&bars[V_FULL + h], VH_BYTES);  // 4 blocks from CTA h
+            if (!tc::mbar_wait(&bars[V_FULL + h], g & 1, a.err, 260)) { ok = false; break; }
+            arrive_leader(V_READY + h);
+            if (h == int(rank)) tc::mbar_arrive(&bars[K_CP]);
+            else tc::mbar_arrive_remote(tc::mapa(smem_u32(&bars[K_CP]), uint32_t(h)));
+          }
+          if (!ok) break;
         }
         if (!ok) { abort_flag = 1; break; }
       }
@@ -601,6 +609,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     tc::tmem_free2(tmem, TMEM_COLS);
   }
 }
+
 
 // n_slots[tk] = window length + (last valid compressed slot + 1): the key-list length the
 // fwd kernel walks (empty tail tiles are skipped).
