@@ -23,20 +23,21 @@
 // Warp roles per CTA (512 threads):
 //   0      TMA of this CTA's Q half (64 heads x 576, 9 swizzled 64-column blocks)
 //   1      TMEM allocation; in the leader CTA, the thread issuing the QK^T MMAs
-//   2      V copier: pushes V blocks out of this CTA's K tile (below), waits for this CTA's
-//          two V halves and tells the leader and the K-tile owners
 //   3      in the leader CTA, the thread issuing the PV MMAs
 //   4-7    softmax / O correction / epilogue (thread = TMEM lane = (head, key half))
-//   8-15   K producers: gather + dequantise this CTA's 64 keys x 576 channels to bf16
-//          (rows loaded into registers a tile ahead, written once QK^T of the previous
-//          tile and the V copies out of it are done)
+//   8-15   producers: gather + dequantise this CTA's 64 keys x 576 channels into the K
+//          tile, and fill this CTA's two V halves (below)
 // Shared memory (227 KB): Q 72 KB, one K tile 72 KB, V 2 x 32 KB, P 2 x 8 KB.
-// V is not dequantised again: the PV B operand of CTA r for key half h is CTA h's 64 keys
-// x CTA r's 256 output channels, and each 64-channel block of it is one 8 KB block of CTA
-// h's K tile (identical 128-byte swizzle), so CTA h's copier pushes those blocks into its
-// own and the peer's V half h with cp.async.bulk shared::cta -> shared::cluster, completing
-// on the destination's V_FULL.  P (64 heads x 128 keys bf16) is written by the softmax
-// threads in two halves: lanes 0-63 the leader's keys, lanes 64-127 the peer's.
+// The PV B operand of CTA r is all 128 keys of the tile x CTA r's 256 output channels (its
+// N half of each 256-channel PV chunk), in two key halves.  Half r (its own keys) is a copy
+// of four 8 KB blocks of its K tile (identical 128-byte swizzle); half 1 - r (the peer's
+// keys) is gathered from the FP8 rows in L2 and dequantised again.  Moving those blocks
+// between the pair's shared memories instead (cp.async.bulk shared::cta -> shared::cluster)
+// ran at ~29 bytes per cycle per SM through the cluster crossbar, local copies included,
+// and held each K tile until its copies had landed: that cost a quarter of the run time.
+// Now the K tile waits only for the previous QK^T and the V halves only for the previous
+// PV.  P (64 heads x 128 keys bf16) is written by the softmax threads in two halves: lanes
+// 0-63 the leader's keys, lanes 64-127 the peer's.
 // QK^T and PV are issued by two threads, so one thread's barrier waits overlap the other's
 // MMAs and the pipe takes QK^T of the next tile while the softmax of this one runs.  The
 // running max is only raised when it grows by more than 2^8 (in exp2 units), which skips
@@ -70,14 +71,10 @@ enum Bar {
   Q_FULL = 0, Q_READY, Q_EMPTY,
   K_FULL,             // leader: both CTAs' K tiles written (8 producer warps each)
   K_EMPTY,            // local (multicast commit): QK^T of the tile done
-  K_WRIT,             // local: this CTA's K tile written (its 8 producer warps)
-  K_CP,               // local: the copies out of this CTA's K tile have landed (2 copiers)
-  V_FULL, V_FULL1,    // local: V half h complete (32 KB of copies from CTA h)
-  V_READY, V_READY1,  // leader: V half h complete in both CTAs (2 copiers)
-  V_EMPTY, V_EMPTY1,  // local (multicast commit): PV over key half h done
+  V_FULL,             // leader: both CTAs' V halves written (8 producer warps each)
   S_FULL, S_FULL1, S_EMPTY, S_EMPTY1,
   P_FULL,             // leader: P written and O corrected (4 softmax warps x 2 CTAs)
-  O_DONE,             // local (multicast commit): both PV halves of the tile done
+  O_DONE,             // local (multicast commit): PV of the tile done (P, V and O free)
   O_EMPTY,
   XCH, XCH1, XCH2, XCH3,  // row-max exchange per (S buffer, warp pair {4,6} / {5,7}), local
   XL, XL1,                // row-sum exchange per warp pair, local
@@ -213,8 +210,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 
   if (threadIdx.x == 0) {
     const uint32_t counts[NBAR] = {1, 2, 1,           // Q_FULL, Q_READY, Q_EMPTY
-                                   16, 1, 8, 2,       // K_FULL, K_EMPTY, K_WRIT, K_CP
-                                   1, 1, 2, 2, 1, 1,  // V_FULL x2, V_READY x2, V_EMPTY x2
+                                   16, 1, 16,         // K_FULL, K_EMPTY, V_FULL
                                    1, 1, 8, 8,        // S_FULL x2, S_EMPTY x2
                                    8, 1, 8,           // P_FULL, O_DONE, O_EMPTY
                                    2, 2, 2, 2, 2, 2,  // XCH x4, XL x2 (the two warps holding one head's key halves)
@@ -322,11 +318,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         MLA_WAIT(O_EMPTY, (ii & 1) ^ 1, 211);
         bool ok = true;
         for (int j = t0; j < t1 && ok; ++j, ++g) {
-          if (!tc::mbar_wait(&bars[P_FULL], g & 1, a.err, 213)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[P_FULL], g & 1, a.err, 213) ||
+              !tc::mbar_wait(&bars[V_FULL], g & 1, a.err, 212)) { ok = false; break; }
+          tc::fence_after_sync();
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            if (!tc::mbar_wait(&bars[V_READY + h], g & 1, a.err, 212)) { ok = false; break; }
-            tc::fence_after_sync();
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
 #pragma unroll
@@ -334,9 +330,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                 tc::mma2_f16(tmem + i * 128, tc::sdesc_add(pd[h], jj * 32), tc::sdesc_add(vd[h], 2 * i * BLK + jj * 2048),
                              idesc_pv, (j == t0 && h == 0 && jj == 0) ? 0u : 1u);
             }
-            tc::mma2_commit_mc(&bars[V_EMPTY + h], 3);
           }
-          if (ok) tc::mma2_commit_mc(&bars[O_DONE], 3);
+          tc::mma2_commit_mc(&bars[O_DONE], 3);
         }
         if (!ok) { abort_flag = 1; break; }
         tc::mma2_commit_mc(&bars[O_FINAL], 3);
@@ -504,100 +499,124 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       ++ii;
     }
   } else if (warp >= 8) {
-    // ------------------------------------------------------------------ K producers
-    // thread t: key kk = t / 4 of this CTA's 64, 16-byte chunks sub, sub + 4, ... of its row
+    // ------------------------------------------------------------------ producers
+    // Thread t: key kk = t / 4 of this CTA's 64, 16-byte chunks sub, sub + 4, ... of its row
+    // (K tile), and chunks sub of each of this CTA's four V channel blocks of the peer's key
+    // kk (V half `peer`).  Per tile:
+    //   1. once QK^T of the previous tile is done: dequantise and write this CTA's K tile;
+    //      then load the next tile's own rows (held in registers until step 1 comes again);
+    //   2. once PV of the previous tile is done: copy this CTA's own V blocks out of its K
+    //      tile into V half `rank` (bf16 already, shared memory to shared memory), dequantise
+    //      the peer keys' chunks into V half `peer`; then load the next tile's peer chunks.
+    // The K tile waits only for QK^T and the V halves only for PV; nothing crosses the pair.
     const int t = threadIdx.x - 256;  // 0..255
     const int kk = t >> 2, sub = t & 3;
-    int g = 0;
-    for (int it = pair; it < items && !abort_flag; it += npairs) {
-      int tk, sp, t0, t1;
-      item_range(it, tk, sp, t0, t1);
-      const Slot s = item_info(a, tk);
-      bool ok = true;
-      for (int j = t0; j < t1; ++j, ++g) {
-        const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
-        uint4 raw[10];
-        float sc[8];
-#pragma unroll
-        for (int q = 0; q < 10; ++q) {
-          const int c = sub + 4 * q;
-          raw[q] = make_uint4(0, 0, 0, 0);
-          if (rp) raw[q] = ld_nc16(rp + (c < 32 ? 16 * c : ROPE_OFF + 16 * (c - 32)));
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) sc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
-        // the tile is free once QK^T of the previous tile is done and the copies out of it
-        // have landed in both CTAs
-        if (!tc::mbar_wait(&bars[K_EMPTY], (g & 1) ^ 1, a.err, 230) ||
-            !tc::mbar_wait(&bars[K_CP], (g & 1) ^ 1, a.err, 231)) { ok = false; break; }
-        uint8_t* kt = ks + kk * 128;
-#pragma unroll
-        for (int q = 0; q < 10; ++q) {
-          const int c = sub + 4 * q;
-          if (c < 32) {
-            uint4 lo, hi;
-            dequant16(raw[q], sc[c >> 2], lo, hi);
-            const int cb = c >> 2, ch = (c & 3) * 2;
-            st_shared16(kt + cb * BLK + ((ch ^ (kk & 7)) * 16), lo);
-            st_shared16(kt + cb * BLK + (((ch + 1) ^ (kk & 7)) * 16), hi);
-          } else {
-            st_shared16(kt + 8 * BLK + (((c - 32) ^ (kk & 7)) * 16), raw[q]);
-          }
-        }
-        tc::fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tc::mbar_arrive(&bars[K_WRIT]);
-          arrive_leader(K_FULL);
-        }
-      }
-      if (!ok) { abort_flag = 1; break; }
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------------ V copier + relay
-    // Block lb of V half h in CTA r holds channel block gb = (lb >> 1) * 4 + 2 r + (lb & 1)
-    // of CTA h's keys (PV chunk lb >> 1 of 256 channels, CTA r's 128 of them).  This CTA
-    // sends its K tile's blocks to V half `rank` of both CTAs, then waits for both of its own
-    // V halves and tells the leader (V_READY) and each half's source (K_CP: its K tile may
-    // be overwritten).
-    if (lane == 0) {
-      int g = 0;
-      for (int it = pair; it < items && !abort_flag; it += npairs) {
-        int tk, sp, t0, t1;
+    const int peer = int(rank) ^ 1;
+    // this CTA's V channel blocks: gb(lb) = (lb >> 1) * 4 + 2 rank + (lb & 1)
+    auto vblock = [&](int lb) { return (lb >> 1) * 4 + 2 * int(rank) + (lb & 1); };
+    int it = pair, j = 0, tk = 0, sp = 0, t0 = 0, t1 = 0;
+    Slot s{};
+    auto next_item = [&]() -> bool {  // first item at or after `it` that has tiles
+      for (; it < items; it += npairs) {
         item_range(it, tk, sp, t0, t1);
-        bool ok = true;
-        for (int j = t0; j < t1; ++j, ++g) {
-          if (!tc::mbar_wait(&bars[K_WRIT], g & 1, a.err, 250) ||
-              !tc::mbar_wait(&bars[V_EMPTY + rank], (g & 1) ^ 1, a.err, 251)) { ok = false; break; }
-          const uint32_t k_base = smem_u32(ks), v_base = smem_u32(vs + rank * VH_BYTES);
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const uint32_t dst_bar = tc::mapa(smem_u32(&bars[V_FULL + rank]), uint32_t(r));
-#pragma unroll
-            for (int lb = 0; lb < 4; ++lb) {
-              const int gb = (lb >> 1) * 4 + r * 2 + (lb & 1);
-              tc::bulk_copy_s2cluster(tc::mapa(v_base + lb * BLK, uint32_t(r)), k_base + gb * BLK, BLK, dst_bar);
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            tc::mbar_expect_tx(&bars[V_FULL + h], VH_BYTES);  // 4 blocks from CTA h
-            if (!tc::mbar_wait(&bars[V_FULL + h], g & 1, a.err, 260)) { ok = false; break; }
-            arrive_leader(V_READY + h);
-            if (h == int(rank)) tc::mbar_arrive(&bars[K_CP]);
-            else tc::mbar_arrive_remote(tc::mapa(smem_u32(&bars[K_CP]), uint32_t(h)));
-          }
-          if (!ok) break;
-        }
-        if (!ok) { abort_flag = 1; break; }
-      }
-      if (abort_flag) {
-        // copies already issued by this CTA or the peer land within microseconds; let
-        // them finish before the CTA (and its shared memory) goes away
-        const uint64_t t0 = tc::globaltimer_ns();
-        while (tc::globaltimer_ns() - t0 < 50000ull) {
+        if (t0 < t1) {
+          s = item_info(a, tk);
+          j = t0;
+          return true;
         }
       }
+      return false;
+    };
+    uint4 kraw[10], rraw[4];
+    float ksc[8], rsc[4];
+    auto load_k = [&]() {
+      const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
+#pragma unroll
+      for (int q = 0; q < 10; ++q) {
+        const int c = sub + 4 * q;
+        kraw[q] = make_uint4(0, 0, 0, 0);
+        if (rp) kraw[q] = ld_nc16(rp + (c < 32 ? 16 * c : ROPE_OFF + 16 * (c - 32)));
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) ksc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
+    };
+    auto load_r = [&]() {
+      const uint8_t* rp = slot_row(a, s, tk, j * NT + peer * NTH + kk);
+#pragma unroll
+      for (int lb = 0; lb < 4; ++lb) {
+        rraw[lb] = make_uint4(0, 0, 0, 0);
+        if (rp) rraw[lb] = ld_nc16(rp + vblock(lb) * 64 + sub * 16);
+        rsc[lb] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + vblock(lb)) : 0.0f;
+      }
+    };
+    bool have = next_item();
+    if (have) {
+      load_k();
+      load_r();
+    }
+    uint8_t* kt = ks + kk * 128;
+    int g = 0;
+    while (have && !abort_flag) {
+      // 1. K tile
+      if (!tc::mbar_wait(&bars[K_EMPTY], (g & 1) ^ 1, a.err, 230)) { abort_flag = 1; break; }
+#pragma unroll
+      for (int q = 0; q < 10; ++q) {
+        const int c = sub + 4 * q;
+        if (c < 32) {
+          uint4 lo, hi;
+          dequant16(kraw[q], ksc[c >> 2], lo, hi);
+          const int cb = c >> 2, ch = (c & 3) * 2;
+          st_shared16(kt + cb * BLK + ((ch ^ (kk & 7)) * 16), lo);
+          st_shared16(kt + cb * BLK + (((ch + 1) ^ (kk & 7)) * 16), hi);
+        } else {
+          st_shared16(kt + 8 * BLK + (((c - 32) ^ (kk & 7)) * 16), kraw[q]);
+        }
+      }
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) arrive_leader(K_FULL);
+      // the next tile's own rows (this item's next tile or the next item's first)
+      if (++j >= t1) {
+        it += npairs;
+        have = next_item();
+      }
+      if (have) load_k();
+      // 2. V halves
+      if (!tc::mbar_wait(&bars[O_DONE], (g & 1) ^ 1, a.err, 231)) { abort_flag = 1; break; }
+      {
+        // this thread's own K-tile chunks of the four V blocks (row kk, positions 2 sub and
+        // 2 sub + 1 of each block): the same places in V half `rank`, so each thread reads
+        // back only what it wrote itself and no producer waits for another
+        uint8_t* vd = vs + int(rank) * VH_BYTES + kk * 128;
+        uint4 cp[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int lb = m >> 1, pos = ((2 * sub + (m & 1)) ^ (kk & 7)) * 16;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(cp[m].x), "=r"(cp[m].y), "=r"(cp[m].z), "=r"(cp[m].w)
+                       : "r"(smem_u32(kt + vblock(lb) * BLK + pos)));
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const int lb = m >> 1, pos = ((2 * sub + (m & 1)) ^ (kk & 7)) * 16;
+          st_shared16(vd + lb * BLK + pos, cp[m]);
+        }
+      }
+      {
+        uint8_t* vt = vs + peer * VH_BYTES + kk * 128;
+#pragma unroll
+        for (int lb = 0; lb < 4; ++lb) {
+          uint4 lo, hi;
+          dequant16(rraw[lb], rsc[lb], lo, hi);
+          st_shared16(vt + lb * BLK + (((2 * sub) ^ (kk & 7)) * 16), lo);
+          st_shared16(vt + lb * BLK + (((2 * sub + 1) ^ (kk & 7)) * 16), hi);
+        }
+      }
+      tc::fence_async_smem();
+      __syncwarp();
+      if (lane == 0) arrive_leader(V_FULL);
+      if (have) load_r();
+      ++g;
     }
   }
 
