@@ -119,40 +119,51 @@ __device__ __forceinline__ Slot item_info(const Args& a, int tk) {
   return s;
 }
 
-// Row pointer of key slot p of token tk (window first, then the compressed list), or
-// nullptr for an empty / out-of-range slot.
-__device__ __forceinline__ const uint8_t* slot_row(const Args& a, const Slot& s, int tk, int p) {
+// Key slot p of token tk is window row ws + p for p < n_win, else compressed entry
+// idx[tk][p - n_win] (empty when that is out of range).  Its row address is found in two
+// steps, so the index load can be issued well before the row is needed: the compressed
+// index of slot p (-1 for a window slot or past the list) ...
+__device__ __forceinline__ int slot_index(const Args& a, const Slot& s, int tk, int p) {
+  const int c = p - s.n_win;
+  return (p >= s.n_win && c < a.topk) ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
+}
+
+// ... and the row pointer of slot p given that index (nullptr for an empty slot).
+__device__ __forceinline__ const uint8_t* slot_row_at(const Args& a, const Slot& s, int p, int g) {
   if (p < s.n_win) {
     const int r = s.ws + p;
     const long long row = a.raw_pt ? (long long)a.raw_pt[(long long)s.b * a.raw_ptw + (r >> 6)] * 64 + (r & 63)
                                    : (long long)s.b * a.raw_len + r;
     return a.raw + row * ROWB;
   }
-  const int c = p - s.n_win;
-  if (c >= a.topk) return nullptr;
-  const int g = a.idx[(long long)tk * a.topk + c];
   if (g < 0 || g >= s.g_lim) return nullptr;
   const long long row = a.cmp_pt ? (long long)a.cmp_pt[(long long)s.b * a.cmp_ptw + (g >> 6)] * 64 + (g & 63)
                                  : (long long)s.b * a.cmp_len + g;
   return a.cmp + row * ROWB;
 }
 
-// 16 e4m3 codes * scale -> 16 bf16 (two 16-byte chunks).
+// 16 e4m3 codes * scale -> 16 bf16 (two 16-byte chunks): e4m3 pairs -> f16x2 (exact) ->
+// two f32 (exact), one packed f32x2 multiply by the scale, round to bf16x2 (the same value
+// as fp32 code * scale rounded to bf16).
+__device__ __forceinline__ uint32_t dequant2(uint32_t pair16, float scale) {
+  uint32_t h2, out;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"((unsigned short)pair16));
+  asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 fl, fh;\n\t.reg .b64 v, sc;\n\t"
+      "mov.b32 {l, h}, %1;\n\t"
+      "cvt.f32.f16 fl, l;\n\tcvt.f32.f16 fh, h;\n\t"
+      "mov.b64 v, {fl, fh};\n\tmov.b64 sc, {%2, %2};\n\t"
+      "mul.rn.f32x2 v, v, sc;\n\t"
+      "mov.b64 {fl, fh}, v;\n\t"
+      "cvt.rn.bf16x2.f32 %0, fh, fl;\n\t}"
+      : "=r"(out) : "r"(h2), "f"(scale));
+  return out;
+}
+
 __device__ __forceinline__ void dequant16(const uint4 raw, float scale, uint4& lo, uint4& hi) {
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-  uint32_t out[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w[i] >> (16 * h)), __NV_E4M3);
-      const float2 f = __half22float2(__half2(hr));
-      const __nv_bfloat162 bb = __floats2bfloat162_rn(f.x * scale, f.y * scale);
-      out[i * 2 + h] = *reinterpret_cast<const uint32_t*>(&bb);
-    }
-  }
-  lo = make_uint4(out[0], out[1], out[2], out[3]);
-  hi = make_uint4(out[4], out[5], out[6], out[7]);
+  lo = make_uint4(dequant2(raw.x, scale), dequant2(raw.x >> 16, scale), dequant2(raw.y, scale),
+                  dequant2(raw.y >> 16, scale));
+  hi = make_uint4(dequant2(raw.z, scale), dequant2(raw.z >> 16, scale), dequant2(raw.w, scale),
+                  dequant2(raw.w >> 16, scale));
 }
 
 __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
@@ -509,11 +520,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
     //      tile into V half `rank` (bf16 already, shared memory to shared memory), dequantise
     //      the peer keys' chunks into V half `peer`; then load the next tile's peer chunks.
     // The K tile waits only for QK^T and the V halves only for PV; nothing crosses the pair.
+    // The compressed indices of tile g + 2 are requested at the end of tile g, so no row
+    // address waits on a dependent index load.
     const int t = threadIdx.x - 256;  // 0..255
     const int kk = t >> 2, sub = t & 3;
     const int peer = int(rank) ^ 1;
     // this CTA's V channel blocks: gb(lb) = (lb >> 1) * 4 + 2 rank + (lb & 1)
     auto vblock = [&](int lb) { return (lb >> 1) * 4 + 2 * int(rank) + (lb & 1); };
+    // cursor over this pair's (item, tile) sequence, items without tiles skipped
     int it = pair, j = 0, tk = 0, sp = 0, t0 = 0, t1 = 0;
     Slot s{};
     auto next_item = [&]() -> bool {  // first item at or after `it` that has tiles
@@ -527,10 +541,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       }
       return false;
     };
+    auto advance = [&]() -> bool {
+      if (++j < t1) return true;
+      it += npairs;
+      return next_item();
+    };
+    const int pk_ofs = int(rank) * NTH + kk, pr_ofs = peer * NTH + kk;  // own / peer key of the tile
     uint4 kraw[10], rraw[4];
     float ksc[8], rsc[4];
-    auto load_k = [&]() {
-      const uint8_t* rp = slot_row(a, s, tk, j * NT + int(rank) * NTH + kk);
+    auto load_k = [&](const uint8_t* rp) {
 #pragma unroll
       for (int q = 0; q < 10; ++q) {
         const int c = sub + 4 * q;
@@ -540,8 +559,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
 #pragma unroll
       for (int q = 0; q < 8; ++q) ksc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
     };
-    auto load_r = [&]() {
-      const uint8_t* rp = slot_row(a, s, tk, j * NT + peer * NTH + kk);
+    auto load_r = [&](const uint8_t* rp) {
 #pragma unroll
       for (int lb = 0; lb < 4; ++lb) {
         rraw[lb] = make_uint4(0, 0, 0, 0);
@@ -549,15 +567,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         rsc[lb] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + vblock(lb)) : 0.0f;
       }
     };
-    bool have = next_item();
+    // rows of tile 0 now; then the cursor moves to tile 1 and its two indices are requested
+    // (they arrive while tile 0 is written)
+    bool have = next_item(), have_next = false;
+    int nk = -1, nr = -1;
     if (have) {
-      load_k();
-      load_r();
+      const int p0 = j * NT;
+      load_k(slot_row_at(a, s, p0 + pk_ofs, slot_index(a, s, tk, p0 + pk_ofs)));
+      load_r(slot_row_at(a, s, p0 + pr_ofs, slot_index(a, s, tk, p0 + pr_ofs)));
+      have_next = advance();
+      if (have_next) {
+        nk = slot_index(a, s, tk, j * NT + pk_ofs);
+        nr = slot_index(a, s, tk, j * NT + pr_ofs);
+      }
     }
     uint8_t* kt = ks + kk * 128;
     int g = 0;
     while (have && !abort_flag) {
-      // 1. K tile
+      // 1. K tile g
       if (!tc::mbar_wait(&bars[K_EMPTY], (g & 1) ^ 1, a.err, 230)) { abort_flag = 1; break; }
 #pragma unroll
       for (int q = 0; q < 10; ++q) {
@@ -575,13 +602,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::fence_async_smem();
       __syncwarp();
       if (lane == 0) arrive_leader(K_FULL);
-      // the next tile's own rows (this item's next tile or the next item's first)
-      if (++j >= t1) {
-        it += npairs;
-        have = next_item();
-      }
-      if (have) load_k();
-      // 2. V halves
+      if (have_next) load_k(slot_row_at(a, s, j * NT + pk_ofs, nk));  // own rows of tile g + 1
+      // 2. V halves of tile g
       if (!tc::mbar_wait(&bars[O_DONE], (g & 1) ^ 1, a.err, 231)) { abort_flag = 1; break; }
       {
         // this thread's own K-tile chunks of the four V blocks (row kk, positions 2 sub and
@@ -615,7 +637,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::fence_async_smem();
       __syncwarp();
       if (lane == 0) arrive_leader(V_FULL);
-      if (have) load_r();
+      if (have_next) load_r(slot_row_at(a, s, j * NT + pr_ofs, nr));  // peer rows of tile g + 1
+      // the cursor moves to tile g + 2 and its indices are requested
+      have = have_next;
+      if (have_next) {
+        have_next = advance();
+        if (have_next) {
+          nk = slot_index(a, s, tk, j * NT + pk_ofs);
+          nr = slot_index(a, s, tk, j * NT + pr_ofs);
+        }
+      }
       ++g;
     }
   }
