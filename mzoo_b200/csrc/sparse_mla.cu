@@ -119,13 +119,31 @@ __device__ __forceinline__ Slot item_info(const Args& a, int tk) {
   return s;
 }
 
+// Loads issued where they are written: asm volatile keeps the compiler from sinking a
+// prefetch down to its first use.
+__device__ __forceinline__ int ld_nc_s32(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float ld_nc_f32(const void* p) {
+  float v;
+  asm volatile("ld.global.nc.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_nc_f32x4(const void* p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
 // Key slot p of token tk is window row ws + p for p < n_win, else compressed entry
 // idx[tk][p - n_win] (empty when that is out of range).  Its row address is found in two
 // steps, so the index load can be issued well before the row is needed: the compressed
 // index of slot p (-1 for a window slot or past the list) ...
 __device__ __forceinline__ int slot_index(const Args& a, const Slot& s, int tk, int p) {
   const int c = p - s.n_win;
-  return (p >= s.n_win && c < a.topk) ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
+  return (p >= s.n_win && c < a.topk) ? ld_nc_s32(a.idx + (long long)tk * a.topk + c) : -1;
 }
 
 // ... and the row pointer of slot p given that index (nullptr for an empty slot).
@@ -375,7 +393,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       auto slot_code = [&](int p) -> int {
         if (p < s.n_win) return 0;
         const int c = p - s.n_win;
-        return c < a.topk ? __ldg(a.idx + (long long)tk * a.topk + c) : -1;
+        return c < a.topk ? ld_nc_s32(a.idx + (long long)tk * a.topk + c) : -1;
       };
       auto slot_ok = [&](int p, int code) { return p < s.n_win || (code >= 0 && code < s.g_lim); };
       const int kofs = kh * NTH + lane;
@@ -557,14 +575,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         if (rp) kraw[q] = ld_nc16(rp + (c < 32 ? 16 * c : ROPE_OFF + 16 * (c - 32)));
       }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) ksc[q] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + q) : 0.0f;
+      if (rp) {  // the row's 8 scales: two 16-byte loads
+        const float4 s0 = ld_nc_f32x4(rp + SCALE_OFF), s1 = ld_nc_f32x4(rp + SCALE_OFF + 16);
+        ksc[0] = s0.x; ksc[1] = s0.y; ksc[2] = s0.z; ksc[3] = s0.w;
+        ksc[4] = s1.x; ksc[5] = s1.y; ksc[6] = s1.z; ksc[7] = s1.w;
+      } else {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) ksc[q] = 0.0f;
+      }
     };
     auto load_r = [&](const uint8_t* rp) {
 #pragma unroll
       for (int lb = 0; lb < 4; ++lb) {
         rraw[lb] = make_uint4(0, 0, 0, 0);
         if (rp) rraw[lb] = ld_nc16(rp + vblock(lb) * 64 + sub * 16);
-        rsc[lb] = rp ? __ldg(reinterpret_cast<const float*>(rp + SCALE_OFF) + vblock(lb)) : 0.0f;
+        rsc[lb] = rp ? ld_nc_f32(rp + SCALE_OFF + 4 * vblock(lb)) : 0.0f;
       }
     };
     // rows of tile 0 now; then the cursor moves to tile 1 and its two indices are requested
