@@ -291,6 +291,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         MLA_WAIT(Q_FULL, ii & 1, 202);
         issued = false;
         arrive_leader(Q_READY);
+        // the next item's Q block into L2 now, so its load at the item boundary (once this
+        // item's last QK^T has read Q) does not wait on HBM
+        for (int nx = it + npairs; nx < items; nx += npairs) {
+          int tk2, sp2, u0, u1;
+          item_range(nx, tk2, sp2, u0, u1);
+          if (u0 >= u1) continue;
+          for (int cb = 0; cb < QBLK; ++cb) tc::tma_prefetch_2d(&tq, cb * 64, tk2 * H + int(rank) * HC);
+          break;
+        }
         ++ii;
       }
       if (issued) tc::mbar_wait(&bars[Q_FULL], (ii & 1), nullptr, 0);  // drain before exit
