@@ -517,6 +517,7 @@ struct TopkArgs {
   int fp8;
   const int32_t* k_pt;  // page table of 64-key pages, or null (dense keys)
   int k_ptw, k_npages;
+  int fused_bound;  // decode: each row's block computes its own bound factors (no bound_kernel)
   int* err;
 };
 
@@ -679,6 +680,50 @@ __device__ void query_bound(const TopkArgs& a, int row) {
   if (lane == 0) const_cast<float*>(a.qnorm)[row] = part;
 }
 
+// The two bound factors of one decode row, computed by its own top-k block (one query per
+// sequence, so nothing is shared between rows): B = |scale| * max_t |sk_t| * 448 sqrt(Di)
+// over the row's visible keys (the e4m3 form of key_bound) and A_s of query_bound, one
+// 16-byte vector of q per thread.  Needs e4m3 rows of a power-of-two number (<= 32) of
+// 16-byte vectors.  Returns both through `red` (2 x 32 floats of shared memory).
+template <int NT>
+__device__ void row_bound(const TopkArgs& a, int row, int b, int V, float* red, float& kb, float& qn) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float mk = 0.0f;
+  for (int t = tid; t < V; t += NT) mk = fmaxf(mk, fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]));
+  const int lpr = a.Di >> 4, nv = a.Hi * lpr;
+  const uint8_t* qg = a.q + size_t(row) * a.Hi * a.Di;
+  float part = 0.0f;
+  for (int v0 = 0; v0 < nv; v0 += NT) {  // block-uniform trip count: full-warp shuffles
+    const int v = v0 + tid;
+    float ss = 0.0f, cabs = 0.0f;
+    if (v < nv) {
+      const int h = v / lpr;
+      ss = sumsq16(*reinterpret_cast<const uint4*>(qg + size_t(h) * a.Di + (v % lpr) * 16), 1);
+      if (v % lpr == 0) cabs = fabsf(a.w[size_t(row) * a.Hi + h] * a.sq[size_t(row) * a.Hi + h]);
+    }
+    for (int o = lpr >> 1; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    part += cabs * sqrtf(ss);  // cabs is 0 off the head leaders
+  }
+  for (int o = 16; o; o >>= 1) {
+    mk = fmaxf(mk, __shfl_xor_sync(0xffffffffu, mk, o));
+    part += __shfl_xor_sync(0xffffffffu, part, o);
+  }
+  if (lane == 0) {
+    red[warp] = mk;
+    red[32 + warp] = part;
+  }
+  __syncthreads();
+  mk = 0.0f;
+  part = 0.0f;
+  for (int i = 0; i < NT / 32; ++i) {
+    mk = fmaxf(mk, red[i]);
+    part += red[32 + i];
+  }
+  kb = fabsf(a.scale) * mk * (448.0f * sqrtf(float(a.Di))) * 1.0001f;
+  qn = part;
+  __syncthreads();
+}
+
 // The error-bound factors of the selection, one launch: blocks [0, B * KB_PARTS) bound
 // the keys (per batch and part), the rest the query rows (8 per block, one per warp).
 __global__ void __launch_bounds__(256) bound_kernel(TopkArgs a) {
@@ -752,6 +797,11 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
   }
   const int eb = a.fp8 ? 1 : 2;
   const int rb = a.Di * eb;  // bytes per q head row / k row
+  float fkb = 0.0f, fqn = 0.0f;
+  if (a.fused_bound) {
+    __shared__ float fred[64];
+    row_bound<TK_THREADS>(a, row, b, V, fred, fkb, fqn);
+  }
   // smem carve-up: one bin byte per key; the fp64 re-scoring buffers are used only once
   // the bins are dead and share their region
   const int region = topk_region_bytes(V, a.Hi, a.Di, RW);
@@ -983,9 +1033,12 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
     }
   }
   const float theta = key2f(prefix);
-  float kbm = 0.0f;
-  for (int i = 0; i < KB_PARTS; ++i) kbm = fmaxf(kbm, a.kbmax[b * KB_PARTS + i]);
-  const float delta = a.eps * a.qnorm[row] * kbm * 1.0001f;
+  float kbm = fkb, qn = fqn;
+  if (!a.fused_bound) {
+    for (int i = 0; i < KB_PARTS; ++i) kbm = fmaxf(kbm, a.kbmax[b * KB_PARTS + i]);
+    qn = a.qnorm[row];
+  }
+  const float delta = a.eps * qn * kbm * 1.0001f;
   const float hi_thr = __fadd_ru(theta, 2.0f * delta), lo_thr = __fsub_rd(theta, 2.0f * delta);
   // pass 3: certain keys into `sel`, the band between the thresholds into `cand`.  When the
   // band lies in bin bsel and the list holds all of that bin, the keys above it are exactly
@@ -1324,9 +1377,13 @@ extern "C" int mzb_indexer_topk(const float* scores, const void* q, const void* 
   a.B = int(B); a.S = int(S); a.T = int(T); a.Hi = Hi; a.Di = Di; a.topk = topk; a.ratio = ratio;
   a.q_offset = q_offset; a.scale = scale; a.eps = eps; a.fp8 = dtype == MZB_E4M3; a.err = err;
   a.k_pt = k_page_table; a.k_ptw = k_ptw; a.k_npages = int(k_pages);
+  // decode rows (few queries, e4m3 keys, the scale-only key bound): each top-k block computes
+  // its own row's bound factors, so no separate bound launch
+  const int lpr = Di / 16;
+  a.fused_bound = wide && dtype == MZB_E4M3 && S <= 16 && Di % 16 == 0 && lpr <= 32 && (lpr & (lpr - 1)) == 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B == 0 || S == 0) return MZB_OK;
-  if (T > 0) {
+  if (T > 0 && !a.fused_bound) {
     const long long blocks = B * idx::KB_PARTS + (B * S + 7) / 8;
     idx::bound_kernel<<<unsigned(blocks), 256, 0, st>>>(a);
     if (int r = launch_status("indexer_bound")) return r;
