@@ -65,23 +65,26 @@ class _Attn(torch.autograd.Function):
     """``csa2_attn/attn.py:20``: saves (q, kv, main_kv, indices, o, lse[, sinks])."""
 
     @staticmethod
-    def forward(ctx, q, kv, main_kv, indices, window, compress_ratio, causal, sinks):
+    def forward(ctx, q, kv, main_kv, indices, window, compress_ratio, causal, sinks, softmax_scale):
         o, lse = fwd(q, kv, main_kv, indices, window=window, compress_ratio=compress_ratio, causal=causal,
-                     sinks=sinks)
+                     sinks=sinks, softmax_scale=softmax_scale)
         saved = (q, kv, main_kv, indices, o, lse)
         ctx.save_for_backward(*(saved if sinks is None else saved + (sinks,)))
-        ctx.window, ctx.ratio, ctx.causal = window, compress_ratio, causal
+        ctx.window, ctx.ratio, ctx.causal, ctx.scale = window, compress_ratio, causal, softmax_scale
         return o
 
     @staticmethod
     def backward(ctx, do):
         q, kv, main_kv, indices, o, lse, *rest = ctx.saved_tensors
         dq, dkv, dmain, dsinks = bwd(q, kv, main_kv, indices, o, lse, do, window=ctx.window,
-                                     compress_ratio=ctx.ratio, causal=ctx.causal, sinks=rest[0] if rest else None)
-        return dq, dkv, dmain, None, None, None, None, dsinks
+                                     compress_ratio=ctx.ratio, causal=ctx.causal, sinks=rest[0] if rest else None,
+                                     softmax_scale=ctx.scale)
+        return dq, dkv, dmain, None, None, None, None, dsinks, None
 
 
 def attn(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch.Tensor, *, window: int,
-         compress_ratio: int, causal: bool = True, sinks: torch.Tensor | None = None) -> torch.Tensor:
-    """``csa2_attn/attn.py:40``: differentiable window + gathered attention -> o."""
-    return _Attn.apply(q, kv, main_kv, indices, window, compress_ratio, causal, sinks)
+         compress_ratio: int, causal: bool = True, sinks: torch.Tensor | None = None,
+         softmax_scale: float | None = None) -> torch.Tensor:
+    """``csa2_attn/attn.py:40``: differentiable window + gathered attention -> o
+    (``softmax_scale`` defaults to D**-0.5, as in ``fwd``)."""
+    return _Attn.apply(q, kv, main_kv, indices, window, compress_ratio, causal, sinks, softmax_scale)

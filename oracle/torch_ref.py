@@ -20,6 +20,9 @@ module restates the same float32 torch arithmetic, operation for operation, for 
 - ``topk_indices``      ``golden_ref.topk_indices`` (golden_ref.py:230-243)
 - ``pack_rows`` / ``unpack_rows``  576-channel latent <-> 672-byte FP8 rows (absmax/448
                         e4m3 per 64 channels, fp32 scales, bf16 rope)
+- ``eager_sink_attention``  the DeepSeek-V4.1 layer's ``eager_attention_forward``
+                        (modeling_deepseek_v41.py:581-611): shared K=V head, additive
+                        mask, the per-head sink as one denominator-only logit
 - ``qk_norm_rope``      the model's RMSNorm then interleaved-pair RoPE
                         (modeling_deepseek_v41.py:49-63, :405-425; ``norm_rope.py:37-44``)
 - ``fake_quant_fp4_ocp`` / ``fake_quant_fp8_absmax``  the two rules BASELINE config 5
@@ -175,3 +178,19 @@ def qk_norm_rope(x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch
     even, odd = rope[..., 0::2].float(), rope[..., 1::2].float()
     rot = torch.stack([even * c - odd * s, even * s + odd * c], dim=-1).flatten(-2)
     return torch.cat([nope, rot.to(dtype)], dim=-1)
+
+
+def eager_sink_attention(q: torch.Tensor, kv: torch.Tensor, mask: torch.Tensor | None, sinks: torch.Tensor,
+                         scaling: float) -> torch.Tensor:
+    """q [B,H,S,D], kv [B,1,T,D] (K == V), additive mask [B,1,S,T] or None, sinks [H] ->
+    o [B,S,H,D] float32: logits + mask, the sink column joined to the softmax and dropped
+    (it only grows the denominator), probabilities times the shared V."""
+    B, H, S, _ = q.shape
+    logits = torch.matmul(q.float(), kv.float().transpose(2, 3)) * scaling
+    if mask is not None:
+        logits = logits + mask.float()
+    sk = sinks.float().reshape(1, -1, 1, 1).expand(B, H, S, 1)
+    combined = torch.cat([logits, sk], dim=-1)
+    combined = combined - combined.max(dim=-1, keepdim=True).values
+    probs = torch.softmax(combined, dim=-1)[..., :-1]
+    return torch.matmul(probs, kv.float()).transpose(1, 2)
