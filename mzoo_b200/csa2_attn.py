@@ -10,7 +10,7 @@ the reference, ``compress_ratio`` is documentation only (group-causality lives i
 
 import torch
 
-from ._attn_common import check_mqa, run_bwd, run_fwd
+from ._attn_common import check_mqa, run_bwd_groups, run_fwd_groups
 
 
 def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch.Tensor, *, window: int,
@@ -22,7 +22,7 @@ def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch
     assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
     assert isinstance(compress_ratio, int) and compress_ratio >= 1, \
         f"compress_ratio must be a positive int, got {compress_ratio!r}"
-    B, S, H, D = check_mqa(q, kv, "csa2_attn")
+    B, S, H, D = check_mqa(q, kv, "csa2_attn", any_heads=True)
     G = main_kv.shape[1]
     assert main_kv.shape == (B, G, 1, D), f"main_kv must be [B, G, 1, D], got {tuple(main_kv.shape)}"
     assert indices.dtype in (torch.int32, torch.int64), f"indices must be int32/int64, got {indices.dtype}"
@@ -34,7 +34,7 @@ def fwd(q: torch.Tensor, kv: torch.Tensor, main_kv: torch.Tensor, indices: torch
     scale = softmax_scale if softmax_scale is not None else D**-0.5
     main = main_kv.contiguous() if G else None
     idx = indices.to(torch.int32).contiguous() if (G and indices.shape[2]) else None
-    return run_fwd(q.contiguous(), kv.contiguous(), None, main, idx, sinks, min(window, S), scale)
+    return run_fwd_groups(q.contiguous(), kv.contiguous(), None, main, idx, sinks, min(window, S), scale)
 
 
 def bwd(q, kv, main_kv, indices, o, lse, do, *, window: int, compress_ratio: int, causal: bool = True, sinks=None,
@@ -48,13 +48,13 @@ def bwd(q, kv, main_kv, indices, o, lse, do, *, window: int, compress_ratio: int
     assert scatter == "atomic", "only the atomic scatter is a real gradient"
     assert q.shape == o.shape == do.shape, "shape mismatch"
     assert isinstance(window, int) and window >= 1, f"window must be a positive int, got {window!r}"
-    B, S, H, D = check_mqa(q, kv, "csa2_attn")
+    B, S, H, D = check_mqa(q, kv, "csa2_attn", any_heads=True)
     assert D in (64, 96, 128, 256), f"csa2_attn backward supports head dim 64 / 96 / 128 / 256, got {D}"
     G = main_kv.shape[1]
     scale = softmax_scale if softmax_scale is not None else D**-0.5
     main = main_kv.contiguous() if G else None
     idx = indices.to(torch.int32).contiguous() if (G and indices.shape[2]) else None
-    dq, dkv, _, dmain, dsinks = run_bwd(q.contiguous(), kv.contiguous(), None, main, idx, o.contiguous(),
+    dq, dkv, _, dmain, dsinks = run_bwd_groups(q.contiguous(), kv.contiguous(), None, main, idx, o.contiguous(),
                                         lse.contiguous(), do.contiguous(), sinks, min(window, S), scale)
     if dmain is None:
         dmain = torch.zeros_like(main_kv)

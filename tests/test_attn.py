@@ -318,3 +318,35 @@ def test_csa2_attn_autograd(cuda, sinks):
     if sinks:
         assert torch.equal(sl.grad, dsinks)
         _check_grad(sl.grad, ref["dsinks"], "autograd csa2 dsinks")
+
+
+def test_head_groups():
+    """csa2 launches for any head count (csa2_attn/fwd.py:65-67 accepts any H): H | 128 runs
+    as is, H < 128 is padded to the next power of two, H > 128 runs in 128-head groups."""
+    from mzoo_b200._attn_common import head_groups
+    assert head_groups(64) == (64, 1) and head_groups(128) == (128, 1) and head_groups(1) == (1, 1)
+    assert head_groups(48) == (64, 1) and head_groups(96) == (128, 1) and head_groups(6) == (8, 1)
+    assert head_groups(256) == (128, 2) and head_groups(200) == (128, 2) and head_groups(384) == (128, 3)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("H", [6, 48, 96, 200, 256])
+def test_csa2_any_heads(cuda, H):
+    """Head counts that do not divide 128: forward and backward (with sinks) against the
+    oracle -- padded heads and head groups must leave no trace."""
+    import torch
+    from mzoo_b200 import csa2_attn
+    q, kv, _, main, idx, sk = _inputs(torch, cuda, 2, 160, H, 128, G=40, topk=32, seed=H, dup=True, holes=True,
+                                      sinks=True)
+    o, lse = csa2_attn.fwd(q, kv, main, idx, window=64, compress_ratio=4, sinks=sk)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=64, main_kv=_np(main)[:, :, 0],
+                              indices=idx.cpu().numpy(), sinks=_np(sk))
+    _check(o, lse, ref_o, ref_lse, f"csa2 H{H}")
+    do = _do(torch, cuda, q.shape, 3)
+    dq, dkv, dmain, dsinks = csa2_attn.bwd(q, kv, main, idx, o, lse, do, window=64, compress_ratio=4, sinks=sk)
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=64, main_kv=_np(main)[:, :, 0],
+                       indices=idx.cpu().numpy(), sinks=_np(sk))
+    _check_grad(dq, ref["dq"], f"csa2 dq H{H}")
+    _check_grad(dkv[:, :, 0], ref["dkv"], f"csa2 dkv H{H}")
+    _check_grad(dmain[:, :, 0], ref["dmain"], f"csa2 dmain H{H}")
+    _check_grad(dsinks, ref["dsinks"], f"csa2 dsinks H{H}")
