@@ -247,6 +247,25 @@ MZB_API int mzb_norm_rope_bwd(const void* x, const void* dy, const void* w, cons
                               const float* sin, void* dx, float* dw_part, float* dw, int64_t rows, int heads,
                               int dim, int rope_dim, int parts, void* stream);
 
+/* ------------------------------------------------------------------ quantised KV caches
+ * The cache formats of the DeepSeek-V4.1 attention (src/mzoo/layers/attn/csa_attn/README.md:
+ * 215-235, tickets/0010-csa2-fp-cache.md), bit-identical to the model's fake quantisers
+ * (archs/dsv4/modeling_deepseek_v41.py:359-402, :668-683): unpack(pack(x)) equals
+ * `_fake_quant_fp8_block(x, 32)` / `_fake_quant_fp4_block(x, 16, e4m3_scales=True)`.
+ * mzb_kv_pack_fp8   -- window cache: x bf16 [rows, D] -> e4m3 codes [rows, D] + ue8m0 scale
+ *                      bytes [rows, D/32] (scale = 2^(byte - 127)); D % 32 == 0.
+ * mzb_kv_unpack_fp8 -- codes + scales -> bf16 [rows, D].
+ * mzb_kv_pack_fp4   -- main cache: x bf16 [rows, D] -> e2m1 codes two per byte (low nibble =
+ *                      even channel) [rows, D/2] + e4m3 scale bytes [rows, D/16]; D % 16 == 0.
+ * mzb_kv_unpack_fp4 -- packed codes + scales -> bf16 [rows, D].
+ */
+MZB_API int mzb_kv_pack_fp8(const void* x, uint8_t* codes, uint8_t* scales, int64_t rows, int D, void* stream);
+MZB_API int mzb_kv_unpack_fp8(const uint8_t* codes, const uint8_t* scales, void* out, int64_t rows, int D,
+                              void* stream);
+MZB_API int mzb_kv_pack_fp4(const void* x, uint8_t* codes, uint8_t* scales, int64_t rows, int D, void* stream);
+MZB_API int mzb_kv_unpack_fp4(const uint8_t* codes, const uint8_t* scales, void* out, int64_t rows, int D,
+                              void* stream);
+
 /* Self-test of the bounded device waits (no counterpart in the reference: it checks this
  * library's own failure path).  One thread waits on an mbarrier nothing arrives on; after
  * limit_ns (<= 2e9) the wait gives up, writes 901 (scope 0: CTA-scope wait) or 902

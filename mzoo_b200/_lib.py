@@ -56,6 +56,10 @@ SIGNATURES = {
     "mzb_norm_rope_fwd": [_P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _F32, _P],
     "mzb_norm_rope_bwd_parts": [_I64, _I32],
     "mzb_norm_rope_bwd": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P],
+    "mzb_kv_pack_fp8": [_P, _P, _P, _I64, _I32, _P],
+    "mzb_kv_unpack_fp8": [_P, _P, _P, _I64, _I32, _P],
+    "mzb_kv_pack_fp4": [_P, _P, _P, _I64, _I32, _P],
+    "mzb_kv_unpack_fp4": [_P, _P, _P, _I64, _I32, _P],
 }
 _RESTYPE = {"mzb_last_error": ctypes.c_char_p}
 

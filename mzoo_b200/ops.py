@@ -396,3 +396,47 @@ def selftest_bounded_wait(device, limit_ns: int, scope: int, check: bool) -> int
     err = _err(dev, check)
     call("mzb_selftest_bounded_wait", int(limit_ns), int(scope), ptr(err), stream_ptr(dev))
     return int(err.item()) if check else 0
+
+
+# ----------------------------------------------------------------------------- KV cache formats
+
+@torch.library.custom_op("mzb::kv_pack", mutates_args=())
+def kv_pack(x: torch.Tensor, fmt: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """``mzb_kv_pack_fp8`` (fmt 8: e4m3 codes [rows, D] + ue8m0 bytes [rows, D/32]) or
+    ``mzb_kv_pack_fp4`` (fmt 4: packed e2m1 [rows, D/2] + e4m3 bytes [rows, D/16]) of a
+    contiguous bf16 [rows, D]."""
+    require_cuda(x)
+    rows, D = x.shape
+    if fmt == 8:
+        codes = torch.empty(rows, D, dtype=torch.uint8, device=x.device)
+        scales = torch.empty(rows, D // 32, dtype=torch.uint8, device=x.device)
+        call("mzb_kv_pack_fp8", ptr(x), ptr(codes), ptr(scales), rows, D, stream_ptr(x.device))
+    else:
+        codes = torch.empty(rows, D // 2, dtype=torch.uint8, device=x.device)
+        scales = torch.empty(rows, D // 16, dtype=torch.uint8, device=x.device)
+        call("mzb_kv_pack_fp4", ptr(x), ptr(codes), ptr(scales), rows, D, stream_ptr(x.device))
+    return codes, scales
+
+
+@kv_pack.register_fake
+def _(x, fmt):
+    rows, D = x.shape
+    if fmt == 8:
+        return x.new_empty((rows, D), dtype=torch.uint8), x.new_empty((rows, D // 32), dtype=torch.uint8)
+    return x.new_empty((rows, D // 2), dtype=torch.uint8), x.new_empty((rows, D // 16), dtype=torch.uint8)
+
+
+@torch.library.custom_op("mzb::kv_unpack", mutates_args=())
+def kv_unpack(codes: torch.Tensor, scales: torch.Tensor, D: int, fmt: int) -> torch.Tensor:
+    """bf16 [rows, D] of ``mzb_kv_unpack_fp8`` / ``mzb_kv_unpack_fp4``."""
+    require_cuda(codes, scales)
+    rows = codes.shape[0]
+    out = torch.empty(rows, D, dtype=torch.bfloat16, device=codes.device)
+    name = "mzb_kv_unpack_fp8" if fmt == 8 else "mzb_kv_unpack_fp4"
+    call(name, ptr(codes), ptr(scales), ptr(out), rows, D, stream_ptr(codes.device))
+    return out
+
+
+@kv_unpack.register_fake
+def _(codes, scales, D, fmt):
+    return codes.new_empty((codes.shape[0], D), dtype=torch.bfloat16)

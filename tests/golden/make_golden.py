@@ -398,6 +398,39 @@ def make_compressor() -> None:
     np.savez_compressed(os.path.join(HERE, "compressor.npz"), **out)
 
 
+def make_kvcache() -> None:
+    """The model's two cache quantizers (modeling_deepseek_v41.py:359-402, :668-683):
+    ``_fake_quant_fp8_block(x, 32)`` (window cache: e4m3, ue8m0 scale per 32 channels,
+    amax clamped to 1e-4) and ``_fake_quant_fp4_block(x, 16, e4m3_scales=True)`` (main
+    cache: e2m1, e4m3 scale per 16 channels, amax clamped to 6 * 2**-9), on bf16 rows with
+    the edge cases the rules have: all-zero blocks (the clamp floors), exact e2m1 ties at
+    0.25 / 0.75 / 1.25 / 1.75 / 2.5 / 3.5 / 5 times the scale, negative zeros and values
+    at the clip limits.  Stores the dequantized outputs, and for fp4 the codes and e4m3
+    scales the function forms on the way (its own ``_e2m1_codes`` / scale line)."""
+    from mzoo.archs.dsv4 import modeling_deepseek_v41 as m  # noqa: E402
+    g = torch.Generator().manual_seed(11)
+    out = {}
+    for c, (rows, d) in enumerate([(64, 128), (33, 64), (17, 256), (9, 96)]):
+        x = torch.randn(rows, d, generator=g) * torch.exp2(torch.randint(-6, 6, (rows, 1), generator=g).float())
+        x[0, :32] = 0.0                                   # zero blocks: the clamp floors
+        x[1, :16] = -0.0
+        ties = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0, -0.25, -0.75, -1.25, -1.75, -2.5, -3.5, -5.0, -6.0])
+        x[2, :16] = ties                                  # amax 6 -> e4m3 scale 1: exact ties
+        x[3, :32] = torch.linspace(-448.0, 448.0, 32)     # the e4m3 clip limits
+        xb = x.to(torch.bfloat16)
+        key = f"c{c}."
+        out[key + "x"] = bits(xb)
+        out[key + "fp8"] = bits(m._fake_quant_fp8_block(xb, 32))
+        out[key + "fp4"] = bits(m._fake_quant_fp4_block(xb, 16, e4m3_scales=True))
+        blocks = xb.float().view(rows, d // 16, 16)
+        amax = blocks.abs().amax(-1)
+        scale = (amax.clamp_min(6.0 * 2.0**-9) / m._FP4_MAX).to(torch.float8_e4m3fn)
+        q = (blocks / scale.float().unsqueeze(-1)).clamp(-m._FP4_MAX, m._FP4_MAX)
+        out[key + "fp4_codes"] = m._e2m1_codes(q).view(rows, d).numpy()
+        out[key + "fp4_scales"] = scale.view(torch.uint8).numpy()
+    np.savez_compressed(os.path.join(HERE, "kvcache.npz"), **out)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(1)
     quant, golden_ref = _ref()
@@ -418,4 +451,6 @@ if __name__ == "__main__":
         make_candidates()
     if not only or "compressor" in only:
         make_compressor()
+    if not only or "kvcache" in only:
+        make_kvcache()
     print("wrote", sorted(f for f in os.listdir(HERE) if f.endswith(".npz")))
