@@ -147,7 +147,7 @@ class ClockSampler:
 # A rank of a multi-GPU run reports it scaled by its share of the work (``traffic_for``).
 TRAFFIC_N1 = {
     "indexer": 72764928 + 69933824,
-    "prefill": 2535907584 + 2112252416,
+    "prefill": 2533523200 + 2108656128,
     "decode": 313127680 + 10324480,
     "train": (4376674816 + 94292736) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
     "candidates": 381950464 + 3411200,  # level two (gathered): 32-byte blocks cost ~2.8x in DRAM bursts
