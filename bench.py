@@ -149,7 +149,7 @@ TRAFFIC_N1 = {
     "indexer": 72764928 + 69933824,
     "prefill": 2533523200 + 2108656128,
     "decode": 313127680 + 10324480,
-    "train": (4376674816 + 94292736) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
+    "train": (1469937152 + 86258176) + (1107655936 + 505236480),  # dkv_kernel + dq_kernel
     "candidates": 381950464 + 3411200,  # level two (gathered): 32-byte blocks cost ~2.8x in DRAM bursts
     "compressor": 612400896 + 68001536,
 }

@@ -132,8 +132,23 @@ enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FU
              KV_NBAR };
 
 struct KvItem {
-  int b, kt, k0, sp, qt0, nq;  // query tiles [qt0, qt0 + nq) of this split (nq may be 0)
+  int b, kt, k0, sp, nq;  // nq query tiles in this split (may be 0)
+  int q_lo, total, s0;    // the key tile's query tiles [q_lo, q_lo + total); this split's first step
 };
+
+// Query tile of step i of an item.  A key tile's query tiles are visited rotated, step
+// s0 + i taking the tile q_lo + ((s0 + i - q_lo) mod total): every key tile with the full
+// window (total equal for all of them) then reads, at the same step, the tile whose index is
+// congruent to that step, so the ~window/128 + 1 key tiles that share a query tile -- issued
+// in the same wave of items -- read it at about the same time and L2 serves the repeats
+// (visited in plain order, adjacent key tiles reach a tile 128*H/128 steps apart, and every
+// query row came from DRAM once per key tile).  The split's sum does not depend on the order
+// beyond fp32 rounding; the order is fixed, so results stay deterministic.
+__device__ __forceinline__ int kv_qtile(const KvItem& m, int i) {
+  int r = (m.s0 + i - m.q_lo) % m.total;
+  if (r < 0) r += m.total;
+  return m.q_lo + r;
+}
 
 // Item = (key tile, batch, split of the query loop): the reference's split query loop
 // (swa_attn/bwd.py:66 pick_splits) so every SM has work; partials are summed by
@@ -151,7 +166,9 @@ __device__ __forceinline__ KvItem kv_item(const Args& a, int it) {
   const int total = q_hi - q_lo + 1;
   const int per = (total + a.splits - 1) / a.splits;
   const int s0 = min(total, m.sp * per), s1 = min(total, s0 + per);
-  m.qt0 = q_lo + s0;
+  m.q_lo = q_lo;
+  m.total = total;
+  m.s0 = s0;
   m.nq = s1 - s0;
   return m;
 }
@@ -205,7 +222,7 @@ __global__ void __launch_bounds__(384, 1)
           const int s = g % C::NST, ph = (g / C::NST) & 1;
           if (!tc::mbar_wait(&bars[QD_EMPTY + s], ph ^ 1, a.err, 402)) { ok = false; break; }
           uint8_t* sp = stage(s);
-          const int qt = m.qt0 + i;
+          const int qt = kv_qtile(m, i);
           tc::mbar_expect_tx(&bars[QD_FULL + s], 2 * C::T_BYTES + 1024);
           for (int cb = 0; cb < C::DB; ++cb) {
             tc::tma_load_3d(sp + cb * 128 * 128, &tq, &bars[QD_FULL + s], cb * 64, qt * 128, m.b);
@@ -298,7 +315,7 @@ __global__ void __launch_bounds__(384, 1)
         tc::fence_after_sync();
         const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
         const float* dl = l2 + 128;
-        const int tb = ((m.qt0 + i) * 128) >> a.hshift;  // token of column 0
+        const int tb = (kv_qtile(m, i) * 128) >> a.hshift;  // token of column 0
         // key j is seen by the tile's columns (packed rows of tokens t, j <= t < j + window,
         // t < S): one run [clo, chi] of columns, turned into one mask word per 32 columns
         int clo = 1, chi = 0;

@@ -10,16 +10,22 @@ outputs and lse.
 - C4: 128 sequences with lengths in [8192, 131072], paged FP8 latent caches and index keys
   (64-key pages), decode indexer top-2048 + window 128: 8 sampled sequences (indexer sets
   and attention).
+- C5: B=4, S=8192, 64 heads, D=128, window 512, after the MXFP4 / FP8 fake quant: dK / dV
+  of three 128-key tiles (first, middle, last) and dQ of the tokens beside them, against the
+  oracle's backward over the tokens those rows depend on; max-abs within 2e-2 + 1e-2 x the
+  tensor's largest magnitude (the gradient tolerance of the attention tests).
 """
 
 import numpy as np
 import pytest
 
 import bench
+from oracle import attention as A
 from oracle import indexer as I
 from oracle import mla as M
 
 ATOL = 2e-2
+GRAD_RTOL = 1e-2
 
 
 def _check_index_rows(idx: np.ndarray, vis: np.ndarray, topk: int) -> None:
@@ -118,3 +124,39 @@ def test_c4_decode_full_size(cuda):
         eo = np.abs(o[b].float().cpu().numpy() - ro).max()
         el = np.abs(lse[b].cpu().numpy() - rl).max()
         assert eo <= ATOL and el <= ATOL, (b, eo, el)
+
+
+@pytest.mark.gpu
+def test_c5_train_full_size(cuda):
+    import torch
+    C5 = bench.C5
+    B, S, H, D, W = (C5[x] for x in ("B", "S", "H", "D", "window"))
+    g = torch.Generator(device=cuda).manual_seed(10)  # bench_train's inputs at rank 0
+    q = torch.randn(B, S, H, D, generator=g, device=cuda, dtype=torch.bfloat16)
+    k = torch.randn(B, S, 1, D, generator=g, device=cuda, dtype=torch.bfloat16)
+    v = torch.randn(B, S, 1, D, generator=g, device=cuda, dtype=torch.bfloat16)
+    do = torch.randn(B, S, H, D, generator=g, device=cuda, dtype=torch.bfloat16)
+    dq, dk, dv = bench.c5_step(q, k, v, do)
+    torch.cuda.synchronize()
+    assert all(torch.isfinite(x).all() for x in (dq, dk, dv))
+    from mzoo_b200 import quant
+    qf = quant.fake_quant_fp4_block(q, 32, rule="ocp")
+    kf = quant.fake_quant_fp4_block(k, 32, rule="ocp")
+    vf = quant.fake_quant_fp8_block(v, 128, rule="absmax")
+
+    def host(x, b, lo, hi):
+        return x[b:b + 1, lo:hi].float().cpu().numpy()
+
+    for b, j0 in ((0, 0), (1, 4096), (3, S - 128)):
+        # keys [j0, j0 + 128) are seen by queries [j0, j0 + 128 + W - 1), whose windows start at
+        # j0 - W + 1 or later: the oracle's backward over that slice is exact for them
+        lo, hi = max(0, j0 - W + 1), min(S, j0 + 128 + W - 1)
+        ref = A.attend_bwd(host(qf, b, lo, hi), host(kf, b, lo, hi)[:, :, 0], host(do, b, lo, hi), window=W,
+                           v=host(vf, b, lo, hi)[:, :, 0])
+        sl = slice(j0 - lo, j0 - lo + 128)
+        for name, got, want in (("dk", dk[b, j0:j0 + 128, 0], ref["dk"][0, sl]),
+                                ("dv", dv[b, j0:j0 + 128, 0], ref["dv"][0, sl]),
+                                ("dq", dq[b, j0:j0 + 128], ref["dq"][0, sl])):
+            err = np.abs(got.float().cpu().numpy() - want).max()
+            tol = ATOL + GRAD_RTOL * np.abs(want).max()
+            assert err <= tol, (name, b, j0, err, tol)
