@@ -10,6 +10,14 @@ pmonad/mzoo's pure-PyTorch reference for the path the CUDA library replaces:
 - ``oracle.indexer``   lightning-indexer scores and top-k
                        (``golden_ref.py:213-243``, ``indexer/fwd.py``, ``indexer/bwd.py``);
 - ``oracle.mla``       576/512 latent sparse prefill and paged decode over FP8 rows;
+- ``oracle.candidates`` two-level block selection (``select_candidate_blocks``,
+                       ``archs/dsv4/modeling_deepseek_v41.py:427-454``);
+- ``oracle.compressor`` the compressor's pool / RMSNorm / RoPE / cache-entry step
+                       (``DeepseekV41Compressor``);
+- ``oracle.norm_rope`` fused RMSNorm + RoPE of q / kv, forward and backward
+                       (``src/mzoo/layers/attn/norm_rope.py``);
+- ``oracle.kvcache``   fp8 window / fp4 main cache codes and scales (the model's
+                       ``_fake_quant_fp8_block`` / ``_fake_quant_fp4_block`` as storage);
 - ``oracle.torch_ref`` the same reference arithmetic in torch float32 (the CPU path the
                        benchmark's reference arm times on the host cores).
 
@@ -20,6 +28,7 @@ anything from here and has no CPU fallback.
 Pinning: ``tests/golden/`` holds input/output vectors produced by importing the
 reference itself (``tests/golden/make_golden.py``); the CPU tests of ``tests/test_quant.py``,
 ``test_attn.py``, ``test_indexer.py``, ``test_sparse_mla.py``, ``test_candidates.py``,
-``test_compressor.py`` and ``test_torch_ref.py`` check this oracle against them
-bit-for-bit (quant, row packing, top-k sets) or to fp32 rounding (attention, scores).
+``test_compressor.py``, ``test_norm_rope.py``, ``test_kvcache.py`` and ``test_torch_ref.py``
+check this oracle against them bit-for-bit (quant, cache codes, row packing, top-k sets) or
+to fp32 rounding (attention, scores).
 """
