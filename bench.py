@@ -1661,7 +1661,7 @@ def main():
         C2.update(S=1024, q_offset=4096 - 1024)
         C3.update(S=2048)
         C5.update(B=1, S=2048)
-        C4.update(B=8)
+        C4.update(L_hi=16384)  # all 128 sequences (the latent kernel's full item count), short contexts
         CF.update(rows=256)
         CP.update(B=1, S=4096)
         NR.update(S=1024)

@@ -52,6 +52,9 @@ constexpr int EPI_WARP0 = 2;   // epilogue warp w reads TMEM lanes 32 * (w % 4):
                                // each cover all four lane quarters
 constexpr int KB_PARTS = 16;  // per-batch partial maxima of B_t
 constexpr int BAL_MAX = 512;  // (batch, query block) units of the tile-balanced split
+constexpr int SK_RING = 8;    // paged keys: per-tile key-scale slots in shared memory
+constexpr int PREF_BYTES = 2304;  // tile prefix [BAL_MAX + 1] ints, rounded up to 256
+static_assert((BAL_MAX + 1) * 4 <= PREF_BYTES, "prefix area");
 
 template <bool FP8, int DI>
 struct Cfg {
@@ -68,7 +71,8 @@ struct Cfg {
   static constexpr int KS_RAW = (BUDGET - Q_BUFS * Q_BYTES) / K_BYTES;
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
-  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + (BAL_MAX + 1) * 4 + 1024;
+  static constexpr int SMEM =
+      Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + PREF_BYTES + SK_RING * BM * 4 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
 };
@@ -88,6 +92,8 @@ struct ScoreArgs {
   int bal;       // 1: each CTA takes a contiguous 1/grid share of all key tiles (few units)
   const int32_t* k_pt;  // [B, k_ptw] page table of 64-key pages, or null (dense keys)
   int k_ptw, k_npages;
+  int sk_ring;  // paged keys with 16-byte aligned scales: the TMA warp copies each tile's
+                // 128 key scales into a shared-memory ring next to its key tile
   int* err;
 };
 
@@ -96,7 +102,8 @@ struct ScoreArgs {
 // whatever its table holds there, so their (clamped) reads just have to stay in bounds.
 __device__ __forceinline__ long long key_row(const int32_t* pt, int ptw, int npages, int T, int b, int t) {
   if (!pt) return (long long)b * T + t;
-  int pg = __ldg(pt + (long long)b * ptw + (t >> 6));
+  const int pi = min(t >> 6, ptw - 1);  // a tile's second page may lie past the table's last column
+  int pg = __ldg(pt + (long long)b * ptw + pi);
   pg = pg < 0 ? 0 : (pg >= npages ? npages - 1 : pg);
   return (long long)pg * 64 + (t & 63);
 }
@@ -135,9 +142,11 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
   uint64_t* k_empty = k_full + C::K_STAGES;
   uint64_t* acc_full = k_empty + C::K_STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* sk_full = acc_empty + 2;  // [SK_RING]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_full + SK_RING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [units + 1] tile prefix
+  float* sks = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256 + PREF_BYTES);  // [SK_RING][BM]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -147,6 +156,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       tc::mbar_init(&acc_full[i], 1);
       tc::mbar_init(&acc_empty[i], MODE == 2 ? 8 : 4);  // the warps of the warpgroup(s) of buffer i
     }
+    for (int i = 0; i < SK_RING; ++i) tc::mbar_init(&sk_full[i], 1);
     for (int i = 0; i < C::K_STAGES; ++i) {
       tc::mbar_init(&k_full[i], 1);
       tc::mbar_init(&k_empty[i], 1);
@@ -242,6 +252,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     if (lane == 0) {
       int ks_i = 0, ks_ph = 0, qi = 0;
       uint32_t k_issued = 0, k_par[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint32_t n_tiles = 0, sk_issued = 0, sk_par[SK_RING] = {0, 0, 0, 0, 0, 0, 0, 0};
       uint32_t q_issued = 0, q_par[2] = {0, 0};
       for (int k = 0; !*abort_flag; ++k) {
         Item m;
@@ -270,6 +281,19 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
               tc::tma_load_2d(dst, &tk, &k_full[ks_i], cb * C::SW / C::EB, r0);
               tc::tma_load_2d(dst + 64 * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB, r1);
             }
+            if (a.sk_ring) {
+              // The tile's key scales (two 256-byte page rows).  Slot reuse is safe without an
+              // empty barrier: this copy waited (k_empty above) for the MMA of the tile
+              // K_STAGES back, which waited for the epilogue to release the tile two before
+              // that, and the epilogue reads a tile's scales before releasing it -- so every
+              // tile up to K_STAGES + 2 back has been read, and SK_RING > K_STAGES + 2.
+              const int si = int(n_tiles % SK_RING);
+              tc::mbar_expect_tx(&sk_full[si], 2 * 64 * 4);
+              tc::bulk_load(sks + si * BM, a.sk + r0, 64 * 4, &sk_full[si]);
+              tc::bulk_load(sks + si * BM + 64, a.sk + r1, 64 * 4, &sk_full[si]);
+              sk_issued |= 1u << si;
+              sk_par[si] = (n_tiles / SK_RING) & 1u;
+            }
           } else {
             for (int cb = 0; cb < C::NCB; ++cb)
               tc::tma_load_3d(ks + ks_i * C::K_BYTES + cb * BM * C::SW, &tk, &k_full[ks_i], cb * C::SW / C::EB,
@@ -278,6 +302,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
           k_issued |= 1u << ks_i;
           k_par[ks_i] = ks_ph;
           if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
+          ++n_tiles;
         }
         ++qi;
       }
@@ -286,6 +311,8 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
           if (k_issued >> i & 1) tc::mbar_wait(&k_full[i], k_par[i], nullptr, 0);
         for (int i = 0; i < 2; ++i)
           if (q_issued >> i & 1) tc::mbar_wait(&q_full[i], q_par[i], nullptr, 0);
+        for (int i = 0; i < SK_RING; ++i)
+          if (sk_issued >> i & 1) tc::mbar_wait(&sk_full[i], sk_par[i], nullptr, 0);
       }
     }
   } else if (warp == 1) {
@@ -378,9 +405,15 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         if (acc != bwg) continue;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
-        const float skj =
-            (j < a.T) ? (a.sk ? __ldg(a.sk + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, j)) : 1.0f) * a.scale
-                      : 0.0f;
+        float skj;
+        if (a.sk_ring) {  // paged keys: from the ring the TMA warp filled (read before the release)
+          const int si = int(tcount % SK_RING);
+          if (!tc::mbar_wait(&sk_full[si], (tcount / SK_RING) & 1u, a.err, 107)) { ok = false; break; }
+          skj = (j < a.T) ? sks[si * BM + row] * a.scale : 0.0f;
+        } else {
+          skj = (j < a.T) ? (a.sk ? __ldg(a.sk + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, j)) : 1.0f) * a.scale
+                          : 0.0f;
+        }
         if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
         acc_ph ^= 1;
         tc::fence_after_sync();
@@ -689,7 +722,34 @@ template <int NT>
 __device__ void row_bound(const TopkArgs& a, int row, int b, int V, float* red, float& kb, float& qn) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float mk = 0.0f;
-  for (int t = tid; t < V; t += NT) mk = fmaxf(mk, fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]));
+  if (a.k_pt) {
+    // Paged keys, page by page: lane l first reads the id of the warp's l-th page (one
+    // load per lane, all in flight together), then the warp's pages are swept with the ids
+    // broadcast from the lanes, two coalesced 128-byte scale loads per page.  No load waits
+    // on another's result except once on the ids (key_row per key would chain a page-table
+    // read before every scale read).
+    constexpr int NW = NT / 32;
+    const int npg = (V + 63) >> 6;
+    for (int p0 = warp; p0 < npg; p0 += NW * 32) {
+      const int pl = p0 + NW * lane;
+      int pg = 0;
+      if (pl < npg) {
+        pg = __ldg(a.k_pt + (long long)b * a.k_ptw + min(pl, a.k_ptw - 1));
+        pg = pg < 0 ? 0 : (pg >= a.k_npages ? a.k_npages - 1 : pg);
+      }
+      const int cnt = min(32, (npg - p0 + NW - 1) / NW);  // this warp's pages in this sweep
+#pragma unroll 4
+      for (int i = 0; i < cnt; ++i) {
+        const int t = (p0 + NW * i) * 64 + lane;
+        const float* sp = a.sk + (long long)__shfl_sync(0xffffffffu, pg, i) * 64 + lane;
+        const float s0 = __ldg(sp), s1 = __ldg(sp + 32);
+        if (t < V) mk = fmaxf(mk, fabsf(s0));
+        if (t + 32 < V) mk = fmaxf(mk, fabsf(s1));
+      }
+    }
+  } else {
+    for (int t = tid; t < V; t += NT) mk = fmaxf(mk, fabsf(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, t)]));
+  }
   const int lpr = a.Di >> 4, nv = a.Hi * lpr;
   const uint8_t* qg = a.q + size_t(row) * a.Hi * a.Di;
   float part = 0.0f;
@@ -1332,6 +1392,7 @@ extern "C" int mzb_indexer_scores(const void* q, const void* k, const float* w, 
   a.N = a.Tq * Hi;
   a.ratio = ratio; a.q_offset = q_offset; a.scale = scale; a.write_tail = write_tail; a.err = err;
   a.k_pt = k_page_table; a.k_ptw = k_ptw; a.k_npages = int(k_pages);
+  a.sk_ring = (k_page_table && sk && reinterpret_cast<uintptr_t>(sk) % 16 == 0) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == MZB_E4M3) {
     switch (Di) {

@@ -23,6 +23,8 @@
 // Warp roles per CTA (512 threads):
 //   0      TMA of this CTA's Q half (64 heads x 576, 9 swizzled 64-column blocks)
 //   1      TMEM allocation; in the leader CTA, the thread issuing the QK^T MMAs
+//   2      paged rows (decode): L2 prefetch of this CTA's 64 rows of the tile two ahead of
+//          the producers (a hint only: nothing waits on it)
 //   3      in the leader CTA, the thread issuing the PV MMAs
 //   4-7    softmax / O correction / epilogue (thread = TMEM lane = (head, key half))
 //   8-15   producers: gather + dequantise this CTA's 64 keys x 576 channels into the K
@@ -81,7 +83,8 @@ enum Bar {
   O_FINAL,            // multicast commit after an item's last PV (epilogue, item parity)
   NBAR
 };
-static_assert(8 * NBAR + 8 <= 512, "barriers + TMEM slot + abort flag fit the first 512 misc bytes");
+static_assert(8 * NBAR + 12 <= 512, "barriers + TMEM slot + abort flag + progress fit the first 512 misc bytes");
+constexpr int PF_AHEAD = 2;  // the prefetch warp stays up to this many tiles ahead of the K writes
 static_assert(SMEM_DYN <= 232448, "shared memory budget");
 
 struct Args {
@@ -222,6 +225,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + TILE_BYTES);
   uint32_t& tmem_slot = *reinterpret_cast<uint32_t*>(sm + TILE_BYTES + 8 * NBAR);
   volatile int& abort_flag = *reinterpret_cast<volatile int*>(sm + TILE_BYTES + 8 * NBAR + 4);
+  // K tiles this CTA's producers have written (written by producer warp 8, read by warp 2)
+  volatile int& k_progress = *reinterpret_cast<volatile int*>(sm + TILE_BYTES + 8 * NBAR + 8);
   float (*red_m)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 512);
   float (*red_l)[128] = reinterpret_cast<float (*)[128]>(sm + TILE_BYTES + 512 + 1024);
   if (smem_u32(smem_raw) & 1023) {  // swizzled tiles need 1024-byte alignment
@@ -246,6 +251,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
                                    1};                // O_FINAL
     for (int i = 0; i < NBAR; ++i) tc::mbar_init(&bars[i], counts[i]);
     abort_flag = 0;
+    k_progress = 0;
     tc::fence_barrier_init();
   }
   if (warp == 1) tc::tmem_alloc2(&tmem_slot, TMEM_COLS);
@@ -337,6 +343,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         }
         if (!ok) { abort_flag = 1; break; }
         ++ii;
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ L2 prefetch (paged)
+    // Paged rows come from HBM in random 672-byte pieces, and a producer requests a tile's
+    // rows only one tile ahead, when the chain index -> page table -> row is still an HBM
+    // round trip.  This warp walks the same (item, tile) sequence and, while the producers
+    // write K tile g, issues an L2 prefetch of every row of this CTA's keys of tile
+    // g + PF_AHEAD, so the producers' own loads hit L2.  It only ever reads: if it falls
+    // behind it prefetches rows already loaded, and a stalled pipeline (a bounded wait that
+    // gave up) ends its wait after a bounded spin.
+    if (a.raw_pt || a.cmp_pt) {
+      int g = 0;
+      for (int it = pair; it < items && !abort_flag; it += npairs) {
+        int tk, sp, t0, t1;
+        item_range(it, tk, sp, t0, t1);
+        if (t0 >= t1) continue;
+        const Slot s = item_info(a, tk);
+        bool stop = false;
+        for (int j = t0; j < t1; ++j, ++g) {
+          for (int spin = 0; k_progress + PF_AHEAD < g; ++spin) {
+            if (abort_flag || spin > (1 << 16)) { stop = true; break; }
+            __nanosleep(128);
+          }
+          if (stop) break;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int p = j * NT + int(rank) * NTH + h * 32 + lane;
+            const uint8_t* rp = slot_row_at(a, s, p, slot_index(a, s, tk, p));
+            if (rp) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(rp), "n"(ROWB) : "memory");
+          }
+        }
+        if (stop) break;
       }
     }
   } else if (warp == 3) {
@@ -636,6 +675,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
       tc::fence_async_smem();
       __syncwarp();
       if (lane == 0) arrive_leader(K_FULL);
+      if (warp == 8 && lane == 0) k_progress = g + 1;
       if (have_next) load_k(slot_row_at(a, s, j * NT + pk_ofs, nk));  // own rows of tile g + 1
       // 2. V halves of tile g
       if (!tc::mbar_wait(&bars[O_DONE], (g & 1) ^ 1, a.err, 231)) { abort_flag = 1; break; }
