@@ -71,7 +71,9 @@ struct Cfg {
   static constexpr int KS_RAW = (BUDGET - Q_BUFS * Q_BYTES) / K_BYTES;
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
-  static constexpr int SMEM =
+  // dense keys: tiles, weights, barriers, tile prefix; paged keys add the key-scale ring
+  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + (BAL_MAX + 1) * 4 + 1024;
+  static constexpr int SMEM_PAGED =
       Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + PREF_BYTES + SK_RING * BM * 4 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
@@ -96,6 +98,14 @@ struct ScoreArgs {
                 // 128 key scales into a shared-memory ring next to its key tile
   int* err;
 };
+
+// 32-bit load issued where written (asm volatile keeps the compiler from sinking a
+// look-ahead load down to its first use).
+__device__ __forceinline__ int ld_nc_s32(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
 
 // Row of key t of batch b: dense [B, T] rows, or through the page table of 64-key pages.
 // Page ids are clamped into the pool: keys past a sequence's length are only ever masked,
@@ -126,7 +136,7 @@ __device__ __forceinline__ int visible_of(const int32_t* q_pos, long long q_offs
 // two of its tokens (twice the warps to hide the epilogue's latencies).
 __host__ __device__ constexpr int score_nthreads(int mode) { return mode == 2 ? NTHREADS + 256 : NTHREADS; }
 
-template <bool FP8, int DI, int MODE>
+template <bool FP8, int DI, int MODE, bool PAGED>
 __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     score_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, ScoreArgs a) {
   using C = Cfg<FP8, DI>;
@@ -266,16 +276,32 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
                           m.tb * a.Tq * a.Hi, m.b);
         q_issued |= 1u << qb;
         q_par[qb] = qpar;
-        for (int kt = m.k0; kt < m.k1; ++kt) {
-          // paged keys: the tile's two page rows, read before the stage wait hides their latency
-          int r0 = 0, r1 = 0;
-          if (a.k_pt) {
-            r0 = int(key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, kt * BM));
-            r1 = int(key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, kt * BM + 64));
+        // paged keys: each tile's two page ids are requested two tiles before its loads are
+        // issued (this one thread issues every load, so a page-table read per tile on its
+        // path would cap the key stream at one L2 round trip per tile)
+        const int32_t* ptrow = PAGED ? a.k_pt + (long long)m.b * a.k_ptw : nullptr;
+        auto page_id = [&](int t) { return ld_nc_s32(ptrow + min(t >> 6, a.k_ptw - 1)); };
+        int pc0 = 0, pc1 = 0, pn0 = 0, pn1 = 0;  // raw page ids of tiles kt and kt + 1
+        if (PAGED) {
+          pc0 = page_id(m.k0 * BM);
+          pc1 = page_id(m.k0 * BM + 64);
+          if (m.k0 + 1 < m.k1) {
+            pn0 = page_id((m.k0 + 1) * BM);
+            pn1 = page_id((m.k0 + 1) * BM + 64);
           }
+        }
+        for (int kt = m.k0; kt < m.k1; ++kt) {
+          int pf0 = 0, pf1 = 0;  // tile kt + 2
+          if (PAGED && kt + 2 < m.k1) {
+            pf0 = page_id((kt + 2) * BM);
+            pf1 = page_id((kt + 2) * BM + 64);
+          }
+          auto row_of = [&](int pg) { return (pg < 0 ? 0 : (pg >= a.k_npages ? a.k_npages - 1 : pg)) * 64; };
+          const int r0 = row_of(pc0), r1 = row_of(pc1);
+          pc0 = pn0; pc1 = pn1; pn0 = pf0; pn1 = pf1;
           if (!tc::mbar_wait(&k_empty[ks_i], ks_ph ^ 1, a.err, 102)) { *abort_flag = 1; break; }
           tc::mbar_expect_tx(&k_full[ks_i], C::K_BYTES);
-          if (a.k_pt) {  // two 64-key pages (2D map over the page pool's rows)
+          if constexpr (PAGED) {  // two 64-key pages (2D map over the page pool's rows)
             for (int cb = 0; cb < C::NCB; ++cb) {
               uint8_t* dst = ks + ks_i * C::K_BYTES + cb * BM * C::SW;
               tc::tma_load_2d(dst, &tk, &k_full[ks_i], cb * C::SW / C::EB, r0);
@@ -311,8 +337,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
           if (k_issued >> i & 1) tc::mbar_wait(&k_full[i], k_par[i], nullptr, 0);
         for (int i = 0; i < 2; ++i)
           if (q_issued >> i & 1) tc::mbar_wait(&q_full[i], q_par[i], nullptr, 0);
-        for (int i = 0; i < SK_RING; ++i)
-          if (sk_issued >> i & 1) tc::mbar_wait(&sk_full[i], sk_par[i], nullptr, 0);
+        if constexpr (PAGED)
+          for (int i = 0; i < SK_RING; ++i)
+            if (sk_issued >> i & 1) tc::mbar_wait(&sk_full[i], sk_par[i], nullptr, 0);
       }
     }
   } else if (warp == 1) {
@@ -406,12 +433,13 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
         float skj;
-        if (a.sk_ring) {  // paged keys: from the ring the TMA warp filled (read before the release)
+        if (PAGED && a.sk_ring) {  // paged keys: from the ring the TMA warp filled (read before the release)
           const int si = int(tcount % SK_RING);
           if (!tc::mbar_wait(&sk_full[si], (tcount / SK_RING) & 1u, a.err, 107)) { ok = false; break; }
           skj = (j < a.T) ? sks[si * BM + row] * a.scale : 0.0f;
         } else {
-          skj = (j < a.T) ? (a.sk ? __ldg(a.sk + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, m.b, j)) : 1.0f) * a.scale
+          skj = (j < a.T) ? (a.sk ? __ldg(a.sk + key_row(PAGED ? a.k_pt : nullptr, a.k_ptw, a.k_npages, a.T, m.b, j))
+                                  : 1.0f) * a.scale
                           : 0.0f;
         }
         if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
@@ -738,13 +766,22 @@ __device__ void row_bound(const TopkArgs& a, int row, int b, int V, float* red, 
         pg = pg < 0 ? 0 : (pg >= a.k_npages ? a.k_npages - 1 : pg);
       }
       const int cnt = min(32, (npg - p0 + NW - 1) / NW);  // this warp's pages in this sweep
-#pragma unroll 4
-      for (int i = 0; i < cnt; ++i) {
-        const int t = (p0 + NW * i) * 64 + lane;
-        const float* sp = a.sk + (long long)__shfl_sync(0xffffffffu, pg, i) * 64 + lane;
-        const float s0 = __ldg(sp), s1 = __ldg(sp + 32);
-        if (t < V) mk = fmaxf(mk, fabsf(s0));
-        if (t + 32 < V) mk = fmaxf(mk, fabsf(s1));
+      for (int i0 = 0; i0 < cnt; i0 += 8) {  // eight pages' loads in flight per batch
+        float sv[16];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int pgi = __shfl_sync(0xffffffffu, pg, (i0 + u) & 31);
+          const float* sp = a.sk + (long long)pgi * 64 + lane;
+          const bool ok = i0 + u < cnt;
+          sv[2 * u] = ok ? __ldg(sp) : 0.0f;
+          sv[2 * u + 1] = ok ? __ldg(sp + 32) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int t = (p0 + NW * (i0 + u)) * 64 + lane;
+          if (i0 + u < cnt && t < V) mk = fmaxf(mk, fabsf(sv[2 * u]));
+          if (i0 + u < cnt && t + 32 < V) mk = fmaxf(mk, fabsf(sv[2 * u + 1]));
+        }
       }
     }
   } else {
@@ -807,10 +844,13 @@ __device__ __forceinline__ void e4m3x2_to_f64(uint32_t w16, double& lo, double& 
 constexpr int BLIST = 256;  // keys of the selected linear bin ranked directly
 
 // bytes of the region shared by the bin bytes of V keys and the fp64 re-scoring buffers
-// (exact scores: CAND_MAX doubles, head weights: Hi doubles, per-warp key rows: rw x Di
-// floats), rounded up to 16
+// (exact scores: CAND_MAX doubles, head weights: Hi doubles, per-warp head products:
+// rw x Hi doubles, per-warp key rows: rw x Di floats), rounded up to 16
+__host__ __device__ constexpr int topk_rescore_bytes(int Hi, int Di, int rw) {
+  return CAND_MAX * 8 + Hi * 8 + rw * Hi * 8 + rw * Di * 4;
+}
 __host__ __device__ constexpr int topk_region_bytes(int V, int Hi, int Di, int rw) {
-  return ((V > CAND_MAX * 8 + Hi * 8 + rw * Di * 4 ? V : CAND_MAX * 8 + Hi * 8 + rw * Di * 4) + 15) & ~15;
+  return ((V > topk_rescore_bytes(Hi, Di, rw) ? V : topk_rescore_bytes(Hi, Di, rw)) + 15) & ~15;
 }
 
 // exclusive prefix (over the block, in thread order) of `cnt`; also returns the total.
@@ -868,7 +908,8 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
   uint8_t* bins = sm;                                                       // V (padded to 4)
   double* exact = reinterpret_cast<double*>(sm);                            // CAND_MAX
   double* cq = exact + CAND_MAX;                                            // Hi
-  float* kdall = reinterpret_cast<float*>(cq + a.Hi);                       // RW warps x Di
+  double* phall = cq + a.Hi;                                                // RW warps x Hi
+  float* kdall = reinterpret_cast<float*>(phall + RW * a.Hi);               // RW warps x Di
   uint32_t* sel = reinterpret_cast<uint32_t*>(sm + region);                 // ceil(V/32)
   const int nsel = (V + 31) >> 5;
   uint32_t* bl_key = sel + nsel;                                            // BLIST
@@ -1188,20 +1229,23 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
   } else {
     // exact fp64 re-scoring of the band, RW warps, one candidate per warp; lane l owns
     // heads l + 32 m; q is read from global memory (L1-resident after the first use).  The
-    // head products are summed in head order by lane 0, fetched by shuffles.
+    // head products go to the warp's shared-memory row and lane 0 sums them in head order
+    // (independent loads feeding one chain of adds).
     for (int h = tid; h < a.Hi; h += TK_THREADS) {
       const size_t o = size_t(row) * a.Hi + h;
       cq[h] = double(a.w[o]) * double(a.sq ? a.sq[o] : 1.0f);
     }
     __syncthreads();
     float* kd = kdall + warp * a.Di;
+    double* ph = phall + warp * a.Hi;
     for (int c = warp; c < nc && warp < RW; c += RW) {
       const int j = cand[c];
-      const uint8_t* kr = a.k + key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, j) * rb;
+      const long long krow = key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, j);
+      const uint8_t* kr = a.k + krow * rb;
+      const float skf = (lane == 0 && a.sk) ? a.sk[krow] : 1.0f;  // with the key row's loads
       __syncwarp();
       for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);  // exact in fp32
       __syncwarp();
-      double acc = 0.0;
       for (int m = 0; 32 * m < a.Hi; ++m) {
         const int h = 32 * m + lane;
         double pv = 0.0;
@@ -1210,16 +1254,16 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
           double dot = 0.0;
           if (a.fp8) {
             // e4m3 products are multiples of 2^-18 below 2^18 and the sums stay below 2^53
-            // units: exact in any order, so two chains
-            double d0 = 0.0, d1 = 0.0;
+            // units: exact in any order, so four chains
+            double d0 = 0.0, d1 = 0.0, d2 = 0.0, d3 = 0.0;
             auto word = [&](uint32_t w, int i) {
               double q0, q1, q2, q3;
               e4m3x2_to_f64(w, q0, q1);
               e4m3x2_to_f64(w >> 16, q2, q3);
               d0 = fma(q0, double(kd[i]), d0);
               d1 = fma(q1, double(kd[i + 1]), d1);
-              d0 = fma(q2, double(kd[i + 2]), d0);
-              d1 = fma(q3, double(kd[i + 3]), d1);
+              d2 = fma(q2, double(kd[i + 2]), d2);
+              d3 = fma(q3, double(kd[i + 3]), d3);
             };
             if ((rb & 15) == 0) {
               for (int i = 0; i < a.Di; i += 16) {
@@ -1232,20 +1276,19 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
             } else {
               for (int i = 0; i < a.Di; i += 4) word(__ldg(reinterpret_cast<const uint32_t*>(qh + i)), i);
             }
-            dot = d0 + d1;
+            dot = (d0 + d1) + (d2 + d3);
           } else {
             for (int i = 0; i < a.Di; ++i) dot = fma(double(elem_f(qh, i, 0)), double(kd[i]), dot);  // sequential
           }
           pv = __dmul_rn(cq[h], dot > 0.0 ? dot : 0.0);
-        }
-        for (int l = 0; l < 32; ++l) {  // heads 32 m + l in order
-          const double v = __shfl_sync(0xffffffffu, pv, l);
-          if (32 * m + l < a.Hi) acc = __dadd_rn(acc, v);
+          ph[h] = pv;
         }
       }
+      __syncwarp();
       if (lane == 0) {
-        const double skj = a.sk ? double(a.sk[key_row(a.k_pt, a.k_ptw, a.k_npages, a.T, b, j)]) : 1.0;
-        exact[c] = __dmul_rn(__dmul_rn(acc, skj), double(a.scale));
+        double acc = 0.0;
+        for (int h = 0; h < a.Hi; ++h) acc = __dadd_rn(acc, ph[h]);  // heads in order
+        exact[c] = __dmul_rn(__dmul_rn(acc, double(skf)), double(a.scale));
       }
     }
     __syncthreads();
@@ -1315,8 +1358,13 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
     if (e) return e;
   }
   const int mode = a.Hi != 64 ? 0 : (a.Tq == 4 ? 2 : 1);
-  auto kern = mode == 2 ? score_kernel<FP8, DI, 2> : (mode == 1 ? score_kernel<FP8, DI, 1> : score_kernel<FP8, DI, 0>);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+  const bool paged = a.k_pt != nullptr;
+  auto kern = paged ? (mode == 2 ? score_kernel<FP8, DI, 2, true>
+                                 : (mode == 1 ? score_kernel<FP8, DI, 1, true> : score_kernel<FP8, DI, 0, true>))
+                    : (mode == 2 ? score_kernel<FP8, DI, 2, false>
+                                 : (mode == 1 ? score_kernel<FP8, DI, 1, false> : score_kernel<FP8, DI, 0, false>));
+  const int smem = paged ? C::SMEM_PAGED : C::SMEM;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return launch_status("indexer_scores(smem attr)");
   // Few (batch, query block) pairs -- decode, short prefill -- would leave SMs idle while
   // each walks its whole key range: split the keys into chunks so there are about 8 items
@@ -1337,7 +1385,7 @@ static int launch_scores(const void* q, const void* k, const ScoreArgs& a, cudaS
   // few units: every CTA takes an equal share of all key tiles instead of whole chunks
   b.bal = (n_kc > 1 && base <= BAL_MAX) ? 1 : 0;
   const int grid = b.bal ? sms : (items < sms ? int(items) : sms);
-  kern<<<grid, score_nthreads(mode), C::SMEM, st>>>(tq, tk, b);
+  kern<<<grid, score_nthreads(mode), smem, st>>>(tq, tk, b);
   return launch_status("indexer_scores");
 }
 

@@ -553,20 +553,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NTHREADS, 1)
         ++ii;
         continue;
       }
+      // O / l to bf16: the eight 32-column TMEM loads double-buffered (the next one in flight
+      // while this one is scaled and stored); each lane's 64 contiguous bytes as two 32-byte
+      // stores (each warp store touches 32 head rows, so fewer, wider stores mean fewer
+      // L1 wavefronts -- this epilogue stalls the pipeline at every item boundary)
       __nv_bfloat16* orow = a.o + ((long long)tk * H + head) * DV;
+      const bool wide_st = (reinterpret_cast<uintptr_t>(a.o) & 31) == 0;
+      uint32_t ov[2][32];
+      auto ocol = [&](int it) { return tc::taddr(tmem, sw * 32, (it >> 2) * 128 + (it & 3) * 32); };
+      tc::tmem_ld32(ocol(0), ov[0]);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tc::tmem_ld32(tc::taddr(tmem, sw * 32, i * 128 + c * 32), ov);
-          tc::tmem_wait_ld();
-          uint4* dst = reinterpret_cast<uint4*>(orow + i * 256 + kh * 128 + c * 32);
+      for (int it = 0; it < 8; ++it) {
+        uint32_t (&cur)[32] = ov[it & 1];
+        tc::tmem_wait_ld();
+        tc::reg_after_wait(cur);
+        if (it + 1 < 8) tc::tmem_ld32(ocol(it + 1), ov[(it + 1) & 1]);
+        uint32_t w[16];
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(pack_bf16(__uint_as_float(ov[8 * q + 0]) * inv, __uint_as_float(ov[8 * q + 1]) * inv),
-                                pack_bf16(__uint_as_float(ov[8 * q + 2]) * inv, __uint_as_float(ov[8 * q + 3]) * inv),
-                                pack_bf16(__uint_as_float(ov[8 * q + 4]) * inv, __uint_as_float(ov[8 * q + 5]) * inv),
-                                pack_bf16(__uint_as_float(ov[8 * q + 6]) * inv, __uint_as_float(ov[8 * q + 7]) * inv));
+        for (int q = 0; q < 16; ++q)
+          w[q] = pack_bf16(__uint_as_float(cur[2 * q]) * inv, __uint_as_float(cur[2 * q + 1]) * inv);
+        __nv_bfloat16* dst = orow + (it >> 2) * 256 + kh * 128 + (it & 3) * 32;
+        if (wide_st) {
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2)
+            asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst + h2 * 16),
+                         "r"(w[8 * h2 + 0]), "r"(w[8 * h2 + 1]), "r"(w[8 * h2 + 2]), "r"(w[8 * h2 + 3]),
+                         "r"(w[8 * h2 + 4]), "r"(w[8 * h2 + 5]), "r"(w[8 * h2 + 6]), "r"(w[8 * h2 + 7])
+                         : "memory");
+        } else {
+          uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) d4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
         }
       }
       if (kh == 0) a.lse[(long long)tk * H + head] = (m * sl + log2f(ltot)) * LN2;
