@@ -52,9 +52,15 @@ constexpr int EPI_WARP0 = 2;   // epilogue warp w reads TMEM lanes 32 * (w % 4):
                                // each cover all four lane quarters
 constexpr int KB_PARTS = 16;  // per-batch partial maxima of B_t
 constexpr int BAL_MAX = 512;  // (batch, query block) units of the tile-balanced split
-constexpr int SK_RING = 8;    // paged keys: per-tile key-scale slots in shared memory
+constexpr int SK_RING = 16;   // paged keys: per-tile key-scale slots in shared memory
+constexpr int BARS_BYTES = 512;  // mbarriers, TMEM slot and abort flag
+// Accumulator buffers in TMEM: two of NMAX columns, or four of 128 when a tile's query
+// columns fit in 128 (decode: one token x 64 heads) -- small MMAs complete quickly but each
+// buffer waits for the epilogue's TMEM read, so more buffers keep the MMA issuing.
+__host__ __device__ constexpr int score_accs(int n) { return n <= 128 ? 4 : 2; }
 constexpr int PREF_BYTES = 2304;  // tile prefix [BAL_MAX + 1] ints, rounded up to 256
 static_assert((BAL_MAX + 1) * 4 <= PREF_BYTES, "prefix area");
+static_assert(SK_RING > 8 && (SK_RING & (SK_RING - 1)) == 0, "scale ring: more slots than K stages + accumulators");
 
 template <bool FP8, int DI>
 struct Cfg {
@@ -72,9 +78,10 @@ struct Cfg {
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
   // dense keys: tiles, weights, barriers, tile prefix; paged keys add the key-scale ring
-  static constexpr int SMEM = Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + (BAL_MAX + 1) * 4 + 1024;
+  static constexpr int SMEM =
+      Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + BARS_BYTES + (BAL_MAX + 1) * 4 + 1024;
   static constexpr int SMEM_PAGED =
-      Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + 256 + PREF_BYTES + SK_RING * BM * 4 + 1024;
+      Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + BARS_BYTES + PREF_BYTES + SK_RING * BM * 4 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
 };
@@ -151,18 +158,22 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
   uint64_t* k_full = bars + 4;
   uint64_t* k_empty = k_full + C::K_STAGES;
   uint64_t* acc_full = k_empty + C::K_STAGES;
-  uint64_t* acc_empty = acc_full + 2;
-  uint64_t* sk_full = acc_empty + 2;  // [SK_RING]
+  uint64_t* acc_empty = acc_full + 4;
+  uint64_t* sk_full = acc_empty + 4;  // [SK_RING]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_full + SK_RING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [units + 1] tile prefix
-  float* sks = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256 + PREF_BYTES);  // [SK_RING][BM]
+  int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES);  // [units + 1] tile prefix
+  float* sks = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES + PREF_BYTES);  // [SK_RING][BM]
+  const int n_acc = (MODE == 2 || C::NMAX != 256) ? 2 : score_accs(a.N);  // 4 x 128 columns need NMAX = 256
+  const int acc_cols = n_acc == 4 ? 128 : C::NMAX;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(&q_full[i], 1);
       tc::mbar_init(&q_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
       tc::mbar_init(&acc_full[i], 1);
       tc::mbar_init(&acc_empty[i], MODE == 2 ? 8 : 4);  // the warps of the warpgroup(s) of buffer i
     }
@@ -187,11 +198,18 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       vis = max(vis, visible_of(a.q_pos, a.q_offset, b, a.S, s, a.ratio, a.T));
     return (vis + BM - 1) / BM;
   };
-  if (a.bal && warp == 2) {  // tile prefix over units (u = b * n_tb + tb): pref[u] tiles before u
+  if (a.bal) {
+    // tile prefix over units (u = b * n_tb + tb): pref[u] tiles before u.  Every thread
+    // counts one unit's tiles (position loads all in flight at once), then warp 2 scans.
+    for (int u = threadIdx.x; u < units; u += blockDim.x) pref[u + 1] = unit_tiles(u / n_tb, u % n_tb);
+    __syncthreads();
+  }
+  if (a.bal && warp == 2) {
     int run = 0;
     for (int u0 = 0; u0 < units; u0 += 32) {
       const int u = u0 + lane;
-      const int nt = u < units ? unit_tiles(u / n_tb, u % n_tb) : 0;
+      const int nt = u < units ? pref[u + 1] : 0;
+      __syncwarp();
       int incl = nt;
       for (int o = 1; o < 32; o <<= 1) {
         const int v = __shfl_up_sync(0xffffffffu, incl, o);
@@ -262,7 +280,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     if (lane == 0) {
       int ks_i = 0, ks_ph = 0, qi = 0;
       uint32_t k_issued = 0, k_par[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      uint32_t n_tiles = 0, sk_issued = 0, sk_par[SK_RING] = {0, 0, 0, 0, 0, 0, 0, 0};
+      uint32_t n_tiles = 0, sk_issued = 0, sk_par[SK_RING] = {};
       uint32_t q_issued = 0, q_par[2] = {0, 0};
       for (int k = 0; !*abort_flag; ++k) {
         Item m;
@@ -310,9 +328,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
             if (a.sk_ring) {
               // The tile's key scales (two 256-byte page rows).  Slot reuse is safe without an
               // empty barrier: this copy waited (k_empty above) for the MMA of the tile
-              // K_STAGES back, which waited for the epilogue to release the tile two before
-              // that, and the epilogue reads a tile's scales before releasing it -- so every
-              // tile up to K_STAGES + 2 back has been read, and SK_RING > K_STAGES + 2.
+              // K_STAGES back, which waited for the epilogue to release the tile n_acc (<= 4)
+              // before that, and the epilogue reads a tile's scales before releasing it -- so
+              // every tile up to K_STAGES + 4 back has been read, and SK_RING > K_STAGES + 4.
               const int si = int(n_tiles % SK_RING);
               tc::mbar_expect_tx(&sk_full[si], 2 * 64 * 4);
               tc::bulk_load(sks + si * BM, a.sk + r0, 64 * 4, &sk_full[si]);
@@ -347,6 +365,11 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     if (lane == 0) {
       constexpr uint32_t kFmt = FP8 ? 0 : 1;
       const uint32_t idesc = tc::make_idesc(BM, a.N, kFmt, kFmt);
+      // Descriptors of stage / buffer 0 built once; per MMA only constant offsets are added
+      // (this one thread issues every MMA: building each descriptor from its address cost
+      // more issue time than the small decode MMAs themselves)
+      const uint64_t kd0 = tc::make_sdesc<C::SW>(smem_u32(ks), 16, 8 * C::SW);
+      const uint64_t qd0 = tc::make_sdesc<C::SW>(smem_u32(qs), 16, 8 * C::SW);
       int ks_i = 0, ks_ph = 0, acc = 0, acc_ph = 0, qi = 0;
       for (int k = 0; !*abort_flag; ++k) {
         Item m;
@@ -354,25 +377,23 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         if (m.k0 >= m.k1) continue;
         const int qb = qi % C::Q_BUFS, qpar = (qi / C::Q_BUFS) & 1;
         if (!tc::mbar_wait(&q_full[qb], qpar, a.err, 103)) { *abort_flag = 1; break; }
-        const uint32_t q_base = smem_u32(qs + qb * C::Q_BYTES);
+        const uint64_t qdesc = tc::sdesc_add(qd0, uint32_t(qb * C::Q_BYTES));
         for (int kt = m.k0; kt < m.k1; ++kt) {
           if (!tc::mbar_wait(&acc_empty[acc], acc_ph ^ 1, a.err, 104)) { *abort_flag = 1; break; }
           if (!tc::mbar_wait(&k_full[ks_i], ks_ph, a.err, 105)) { *abort_flag = 1; break; }
           tc::fence_after_sync();
-          const uint32_t k_base = smem_u32(ks + ks_i * C::K_BYTES);
-          const uint32_t d = tmem + uint32_t(acc * C::NMAX);
+          const uint64_t kdesc = tc::sdesc_add(kd0, uint32_t(ks_i * C::K_BYTES));
+          const uint32_t d = tmem + uint32_t(acc * acc_cols);
 #pragma unroll
           for (int kk = 0; kk < C::KSTEPS; ++kk) {
             const int byte = kk * 32, cb = byte / C::SW, off = byte % C::SW;
-            const uint64_t ad = tc::make_sdesc<C::SW>(k_base + cb * BM * C::SW + off, 16, 8 * C::SW);
-            const uint64_t bd = tc::make_sdesc<C::SW>(q_base + cb * C::NMAX * C::SW + off, 16, 8 * C::SW);
-            tc::mma_ss<FP8 ? 1 : 0>(d, ad, bd, idesc, kk > 0);
+            tc::mma_ss<FP8 ? 1 : 0>(d, tc::sdesc_add(kdesc, cb * BM * C::SW + off),
+                                    tc::sdesc_add(qdesc, cb * C::NMAX * C::SW + off), idesc, kk > 0);
           }
           tc::mma_commit(&k_empty[ks_i]);
           tc::mma_commit(&acc_full[acc]);
           if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
-          acc ^= 1;
-          if (acc == 0) acc_ph ^= 1;
+          if (++acc == n_acc) { acc = 0; acc_ph ^= 1; }
         }
         tc::mma_commit(&q_empty[qb]);
         ++qi;
@@ -386,13 +407,12 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) ...
     const int wg = ew >> 2;
-    const int bwg = MODE == 2 ? wg >> 1 : wg;  // the accumulator buffer this warpgroup drains
+    const int bwg = MODE == 2 ? wg >> 1 : wg;  // the parity of the accumulator buffers this warpgroup drains
     const int th = MODE == 2 ? wg & 1 : 0;     // MODE 2: tokens [2 th, 2 th + 2) of the block
     const int row = quarter * 32 + lane;  // key row inside the tile
     constexpr int CWN = MODE == 2 ? 128 : C::NMAX;  // weights per warp
     float* cwp = cw + ew * CWN;
     uint32_t tcount = 0;
-    int acc_ph = 0;
     auto write_tail = [&](int b, int tb) {  // keys no token of this block can see
       const int s0 = tb * a.Tq;
       const int n_kt = unit_tiles(b, tb);
@@ -428,8 +448,11 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       __syncwarp();
       bool ok = true;
       for (int kt = m.k0; kt < m.k1; ++kt, ++tcount) {
-        const int acc = int(tcount & 1u);
-        if (acc != bwg) continue;
+        // tile tcount: buffer tcount % n_acc, its (tcount / n_acc)-th use; buffers alternate
+        // between the warpgroups (two buffers each when there are four)
+        const int acc = int(tcount % uint32_t(n_acc));
+        if ((acc & 1) != bwg) continue;
+        const int acc_ph = int(tcount / uint32_t(n_acc)) & 1;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
         float skj;
@@ -443,9 +466,8 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
                           : 0.0f;
         }
         if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
-        acc_ph ^= 1;
         tc::fence_after_sync();
-        const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * C::NMAX);
+        const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * acc_cols);
         bool released = false;
         if constexpr (MODE >= 1) {  // the DeepSeek-V4 indexer: 64 columns per token, packed FMAs
           // Per token, both 32-column TMEM loads go out behind one wait; the buffer is released
