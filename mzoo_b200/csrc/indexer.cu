@@ -138,9 +138,10 @@ __device__ __forceinline__ int visible_of(const int32_t* q_pos, long long q_offs
 }
 
 // Epilogue modes: 0 the generic head loop; 1 the 64-head indexer's (packed FMAs, one TMEM
-// wait per token) with warpgroup g draining accumulator buffer g, i.e. alternate tiles, all
-// tokens; 2 the same for four-token blocks with four warpgroups, two per buffer, each taking
-// two of its tokens (twice the warps to hide the epilogue's latencies).
+// wait per token) with warpgroup g draining the accumulator buffers of parity g, i.e.
+// alternate tiles, all tokens; 2 the same for four-token blocks with four warpgroups that
+// each take one token of every tile (a buffer is released after four 16-column loads, so
+// the MMA of the tile two ahead is not held up by a longer chain of loads).
 __host__ __device__ constexpr int score_nthreads(int mode) { return mode == 2 ? NTHREADS + 256 : NTHREADS; }
 
 template <bool FP8, int DI, int MODE, bool PAGED>
@@ -175,7 +176,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     }
     for (int i = 0; i < 4; ++i) {
       tc::mbar_init(&acc_full[i], 1);
-      tc::mbar_init(&acc_empty[i], MODE == 2 ? 8 : 4);  // the warps of the warpgroup(s) of buffer i
+      tc::mbar_init(&acc_empty[i], MODE == 2 ? 16 : 4);  // the warps of the warpgroup(s) of buffer i
     }
     for (int i = 0; i < SK_RING; ++i) tc::mbar_init(&sk_full[i], 1);
     for (int i = 0; i < C::K_STAGES; ++i) {
@@ -407,10 +408,10 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     const int ew = warp - EPI_WARP0;
     const int quarter = warp & 3;  // TMEM lanes 32 * (warp % 4) ...
     const int wg = ew >> 2;
-    const int bwg = MODE == 2 ? wg >> 1 : wg;  // the parity of the accumulator buffers this warpgroup drains
-    const int th = MODE == 2 ? wg & 1 : 0;     // MODE 2: tokens [2 th, 2 th + 2) of the block
+    const int bwg = wg;                    // modes 0 / 1: the parity of the buffers this warpgroup drains
+    const int th = MODE == 2 ? wg : 0;     // MODE 2: token th of the block, every tile
     const int row = quarter * 32 + lane;  // key row inside the tile
-    constexpr int CWN = MODE == 2 ? 128 : C::NMAX;  // weights per warp
+    constexpr int CWN = MODE == 2 ? 64 : C::NMAX;  // weights per warp
     float* cwp = cw + ew * CWN;
     uint32_t tcount = 0;
     auto write_tail = [&](int b, int tb) {  // keys no token of this block can see
@@ -432,9 +433,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       if (a.write_tail && m.kc == 0) write_tail(m.b, m.tb);
       if (m.k0 >= m.k1) continue;
       const int tq_n = min(a.Tq, a.S - s0);  // real tokens in this block
-      const int t0 = MODE == 2 ? min(2 * th, tq_n) : 0, t1 = MODE == 2 ? min(2 * th + 2, tq_n) : tq_n;
-      for (int i = lane; i < (MODE == 2 ? 128 : a.N); i += 32) {
-        const int ci = (MODE == 2 ? th * 128 : 0) + i;  // column (token, head) of the block
+      const int t0 = MODE == 2 ? min(th, tq_n) : 0, t1 = MODE == 2 ? min(th + 1, tq_n) : tq_n;
+      for (int i = lane; i < (MODE == 2 ? 64 : a.N); i += 32) {
+        const int ci = (MODE == 2 ? th * 64 : 0) + i;  // column (token, head) of the block
         const int s = s0 + ci / a.Hi, h = ci % a.Hi;
         float c = 0.0f;
         if (s < a.S) {
@@ -451,7 +452,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         // tile tcount: buffer tcount % n_acc, its (tcount / n_acc)-th use; buffers alternate
         // between the warpgroups (two buffers each when there are four)
         const int acc = int(tcount % uint32_t(n_acc));
-        if ((acc & 1) != bwg) continue;
+        if (MODE != 2 && (acc & 1) != bwg) continue;
         const int acc_ph = int(tcount / uint32_t(n_acc)) & 1;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
@@ -509,14 +510,52 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
             }
           };
           const int nu = 2 * t1;  // halves of this warp's tokens: [2 t0, 2 t1)
-          if constexpr (MODE == 2) {  // 96 registers a thread: one 32-column load at a time
-            for (int u = 2 * t0; u < nu; ++u) {
-              uint32_t r[32];
-              tc::tmem_ld32(tbase + u * 32, r);
+          if constexpr (MODE == 2) {
+            // 16 columns at a time, double-buffered (96 registers a thread): the next load is
+            // in flight while these are summed, so the buffer is released one load latency
+            // after its last load instead of after every earlier column's math -- the MMA
+            // of the tile two ahead waits on that release.  Same summation order as `half`.
+            auto quarter = [&](const uint32_t (&r)[16], int qq) {  // qq = 4 t + (quarter of token t)
+              const int t = qq >> 2;
+              if ((qq & 3) == 0) sum4[0] = sum4[1] = sum4[2] = sum4[3] = 0ull;
+              const float4* cq4 = reinterpret_cast<const float4*>(cwp + (qq - 4 * t0) * 16);
+#pragma unroll
+              for (int i = 0; i < 2; ++i) {
+                const float4 c0 = cq4[2 * i], c1 = cq4[2 * i + 1];
+                sum4[0] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 0]), 0.0f),
+                                                fmaxf(__uint_as_float(r[8 * i + 1]), 0.0f)),
+                                     pack_f32x2(c0.x, c0.y), sum4[0]);
+                sum4[1] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 2]), 0.0f),
+                                                fmaxf(__uint_as_float(r[8 * i + 3]), 0.0f)),
+                                     pack_f32x2(c0.z, c0.w), sum4[1]);
+                sum4[2] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 4]), 0.0f),
+                                                fmaxf(__uint_as_float(r[8 * i + 5]), 0.0f)),
+                                     pack_f32x2(c1.x, c1.y), sum4[2]);
+                sum4[3] = ffma_f32x2(pack_f32x2(fmaxf(__uint_as_float(r[8 * i + 6]), 0.0f),
+                                                fmaxf(__uint_as_float(r[8 * i + 7]), 0.0f)),
+                                     pack_f32x2(c1.z, c1.w), sum4[3]);
+              }
+              if ((qq & 3) == 3) {
+                const float2 p0 = unpack_f32x2(sum4[0]), p1 = unpack_f32x2(sum4[1]);
+                const float2 p2 = unpack_f32x2(sum4[2]), p3 = unpack_f32x2(sum4[3]);
+                const float sum = ((p0.x + p0.y) + (p1.x + p1.y)) + ((p2.x + p2.y) + (p3.x + p3.y));
+                const int vis = __shfl_sync(0xffffffffu, vis_l, t);
+                if (j < a.T) a.scores[(size_t(m.b) * a.S + s0 + t) * a.T + j] = (j < vis) ? sum * skj : -INFINITY;
+              }
+            };
+            uint32_t ra[16], rb[16];
+            const int q0 = 4 * t0, cnt = 4 * (t1 - t0);  // this warp's token quarters: 0 or 4
+            if (cnt > 0) tc::tmem_ld16(tbase + q0 * 16, ra);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (k >= cnt) break;
+              uint32_t (&cur)[16] = (k & 1) ? rb : ra;
+              uint32_t (&nxt)[16] = (k & 1) ? ra : rb;
               tc::tmem_wait_ld();
-              tc::reg_after_wait(r);
-              if (u + 1 == nu) release();
-              half(r, u);
+              tc::reg_after_wait(cur);
+              if (k + 1 < cnt) tc::tmem_ld16(tbase + (q0 + k + 1) * 16, nxt);
+              else release();
+              quarter(cur, q0 + k);
             }
           } else {
             for (int u = 2 * t0; u < nu; u += 2) {
