@@ -894,6 +894,18 @@ __global__ void __launch_bounds__(256) bound_kernel(TopkArgs a) {
   }
 }
 
+// An e4m3 code as an integer in units of 2^-9: value = M * 2^(e' - 10) with M = 8 + m
+// (normal) or m (subnormal) and e' = max(e, 1), i.e. (M << (e' - 1)) * 2^-9, |.| < 2^18.  A
+// product of two is an integer in units of 2^-18 below 2^36 and a 128-term sum stays below
+// 2^43, so an int64 dot product is exact and equals the fp64 sum of the products.  NaN codes
+// (0x7F / 0xFF) are reported through `nan` (the caller keeps the fp64 path for them).
+__device__ __forceinline__ int e4m3_int(uint32_t c, bool& nan) {
+  const int e = int(c >> 3) & 15, m = int(c) & 7;
+  nan |= (c & 0x7Fu) == 0x7Fu;
+  const int v = (e ? (8 | m) : m) << (e ? e - 1 : 0);
+  return (c & 0x80u) ? -v : v;
+}
+
 // exact fp64 value of an e4m3 code pair (the low and high byte of a 16-bit word)
 __device__ __forceinline__ void e4m3x2_to_f64(uint32_t w16, double& lo, double& hi) {
   const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(w16 & 0xFFFFu), __NV_E4M3);
@@ -907,11 +919,12 @@ constexpr int BLIST = 256;  // keys of the selected linear bin ranked directly
 // bytes of the region shared by the bin bytes of V keys and the fp64 re-scoring buffers
 // (exact scores: CAND_MAX doubles, head weights: Hi doubles, per-warp head products:
 // rw x Hi doubles, per-warp key rows: rw x Di floats), rounded up to 16
-__host__ __device__ constexpr int topk_rescore_bytes(int Hi, int Di, int rw) {
-  return CAND_MAX * 8 + Hi * 8 + rw * Hi * 8 + rw * Di * 4;
+// qint: bytes of the integer copy of an e4m3 query row (wide blocks, see e4m3_int)
+__host__ __device__ constexpr int topk_rescore_bytes(int Hi, int Di, int rw, int qint) {
+  return CAND_MAX * 8 + Hi * 8 + rw * Hi * 8 + rw * Di * 4 + qint;
 }
-__host__ __device__ constexpr int topk_region_bytes(int V, int Hi, int Di, int rw) {
-  return ((V > topk_rescore_bytes(Hi, Di, rw) ? V : topk_rescore_bytes(Hi, Di, rw)) + 15) & ~15;
+__host__ __device__ constexpr int topk_region_bytes(int V, int Hi, int Di, int rw, int qint) {
+  return ((V > topk_rescore_bytes(Hi, Di, rw, qint) ? V : topk_rescore_bytes(Hi, Di, rw, qint)) + 15) & ~15;
 }
 
 // exclusive prefix (over the block, in thread order) of `cnt`; also returns the total.
@@ -965,12 +978,16 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
   }
   // smem carve-up: one bin byte per key; the fp64 re-scoring buffers are used only once
   // the bins are dead and share their region
-  const int region = topk_region_bytes(V, a.Hi, a.Di, RW);
+  // wide blocks with e4m3 rows re-score the band in integers (e4m3_int): the query row's
+  // integer copy [Di][Hi] follows the per-warp key rows
+  const bool int_dot = TK_THREADS == 1024 && a.fp8;
+  const int region = topk_region_bytes(V, a.Hi, a.Di, RW, int_dot ? a.Hi * a.Di * 4 : 0);
   uint8_t* bins = sm;                                                       // V (padded to 4)
   double* exact = reinterpret_cast<double*>(sm);                            // CAND_MAX
   double* cq = exact + CAND_MAX;                                            // Hi
   double* phall = cq + a.Hi;                                                // RW warps x Hi
   float* kdall = reinterpret_cast<float*>(phall + RW * a.Hi);               // RW warps x Di
+  int* qint = reinterpret_cast<int*>(kdall + RW * a.Di);                    // [Di][Hi] (int_dot)
   uint32_t* sel = reinterpret_cast<uint32_t*>(sm + region);                 // ceil(V/32)
   const int nsel = (V + 31) >> 5;
   uint32_t* bl_key = sel + nsel;                                            // BLIST
@@ -1296,7 +1313,18 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
       const size_t o = size_t(row) * a.Hi + h;
       cq[h] = double(a.w[o]) * double(a.sq ? a.sq[o] : 1.0f);
     }
-    __syncthreads();
+    // wide e4m3 rows: the query row as integers, transposed so a warp's lanes (heads) read
+    // consecutive words; fp64 conversions per product were the re-scoring's throughput limit
+    bool q_nan = false;
+    if (int_dot)  // one 16-code vector per thread; consecutive threads = consecutive heads
+      for (int v = tid; v < a.Hi * (a.Di >> 4); v += TK_THREADS) {
+        const int h = v % a.Hi, i0 = (v / a.Hi) << 4;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(qg + size_t(h) * a.Di + i0);
+        const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int k = 0; k < 16; ++k) qint[(i0 + k) * a.Hi + h] = e4m3_int((w[k >> 2] >> (8 * (k & 3))) & 0xFFu, q_nan);
+      }
+    const bool row_int = int_dot && !__syncthreads_or(q_nan);
     float* kd = kdall + warp * a.Di;
     double* ph = phall + warp * a.Hi;
     for (int c = warp; c < nc && warp < RW; c += RW) {
@@ -1305,9 +1333,34 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
       const uint8_t* kr = a.k + krow * rb;
       const float skf = (lane == 0 && a.sk) ? a.sk[krow] : 1.0f;  // with the key row's loads
       __syncwarp();
-      for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);  // exact in fp32
+      bool k_nan = false;
+      if (row_int) {
+        int* ki = reinterpret_cast<int*>(kd);
+        for (int i = lane; i < a.Di; i += 32) ki[i] = e4m3_int(kr[i], k_nan);
+      } else {
+        for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);  // exact in fp32
+      }
+      const bool use_int = row_int && !__any_sync(0xffffffffu, k_nan);
+      if (row_int && !use_int)  // a NaN code in the key row: its fp64 path
+        for (int i = lane; i < a.Di; i += 32) kd[i] = elem_f(kr, i, a.fp8);
       __syncwarp();
-      for (int m = 0; 32 * m < a.Hi; ++m) {
+      if (use_int) {  // two heads per lane per pass: each key word read once for both
+        const int* ki = reinterpret_cast<const int*>(kd);
+        for (int m = 0; 32 * m < a.Hi; m += 2) {
+          const int h0 = 32 * m + lane, h1 = h0 + 32;
+          const int c0 = min(h0, a.Hi - 1), c1 = min(h1, a.Hi - 1);  // clamped reads, results dropped
+          long long s0 = 0, s1 = 0;
+#pragma unroll 4
+          for (int i = 0; i < a.Di; ++i) {
+            const long long kv = ki[i];
+            s0 += qint[i * a.Hi + c0] * kv;
+            s1 += qint[i * a.Hi + c1] * kv;
+          }
+          if (h0 < a.Hi) ph[h0] = __dmul_rn(cq[h0], s0 > 0 ? double(s0) * 3.814697265625e-06 : 0.0);  // 2^-18
+          if (h1 < a.Hi) ph[h1] = __dmul_rn(cq[h1], s1 > 0 ? double(s1) * 3.814697265625e-06 : 0.0);
+        }
+      }
+      for (int m = 0; 32 * m < a.Hi && !use_int; ++m) {
         const int h = 32 * m + lane;
         double pv = 0.0;
         if (h < a.Hi) {
@@ -1386,9 +1439,9 @@ __global__ void __launch_bounds__(TK_THREADS, TK_THREADS == 128 ? 12 : 1) topk_k
 }
 
 static size_t topk_smem(int T, int Hi, int Di, int eb, int threads) {
-  (void)eb;
   const int rw = std::min(threads / 32, 8);
-  return size_t(topk_region_bytes(T, Hi, Di, rw)) + size_t((T + 31) / 32) * 4 + BLIST * 8 + CAND_MAX * 4;
+  const int qint = (threads == 1024 && eb == 1) ? Hi * Di * 4 : 0;
+  return size_t(topk_region_bytes(T, Hi, Di, rw, qint)) + size_t((T + 31) / 32) * 4 + BLIST * 8 + CAND_MAX * 4;
 }
 
 template <bool FP8, int DI>
