@@ -101,6 +101,39 @@ def test_canonical_fp8_dot_is_order_independent():
     assert np.array_equal(a, b)
 
 
+def _e4m3_int(c: int) -> int:
+    """The top-k kernel's integer form of an e4m3 code (``e4m3_int`` in csrc/indexer.cu):
+    value = (M << (e' - 1)) * 2^-9, M = 8 + m (normal) or m (subnormal), e' = max(e, 1)."""
+    e, m = (c >> 3) & 15, c & 7
+    v = ((8 | m) if e else m) << ((e - 1) if e else 0)
+    return -v if c & 0x80 else v
+
+
+def test_e4m3_integer_dot_is_exact():
+    """The wide top-k blocks re-score e4m3 band keys as int64 dot products in units of
+    2^-18: every non-NaN code's integer form is its value x 2^9, and a 128-term integer dot
+    (below 2^43) times 2^-18 equals the exact fp64 sum the canonical score defines."""
+    import torch
+    codes = np.arange(256, dtype=np.uint8)
+    nan = (codes & 0x7F) == 0x7F
+    vals = torch.from_numpy(codes).view(torch.float8_e4m3fn).double().numpy()
+    ints = np.array([_e4m3_int(int(c)) for c in codes], dtype=np.int64)
+    assert np.array_equal(ints[~nan].astype(np.float64) * 2.0**-9, vals[~nan])
+    assert np.abs(ints[~nan]).max() < 2**18
+    rng = np.random.default_rng(1)
+    ok = codes[~nan]
+    q = rng.choice(ok, size=(64, 128))
+    k = rng.choice(ok, size=(16, 128))
+    k[0] = 0x7E  # the largest codes: the bound's edge
+    q[0] = 0x7E
+    qi, ki = ints[q], ints[k]
+    qv = torch.from_numpy(q).view(torch.float8_e4m3fn).double().numpy()
+    kv = torch.from_numpy(k).view(torch.float8_e4m3fn).double().numpy()
+    dot_int = qi @ ki.T  # int64, exact
+    assert np.abs(dot_int).max() < 2**43
+    assert np.array_equal(dot_int.astype(np.float64) * 2.0**-18, qv @ kv.T)
+
+
 # ----------------------------------------------------------------------------- GPU
 
 def _bf16_inputs(torch, dev, B, S, Hi, Di, T, seed=0):
