@@ -158,14 +158,14 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
   uint64_t* q_empty = bars + 2;
   uint64_t* k_full = bars + 4;
   uint64_t* k_empty = k_full + C::K_STAGES;
-  uint64_t* acc_full = k_empty + C::K_STAGES;
-  uint64_t* acc_empty = acc_full + 4;
+  uint64_t* acc_empty = k_empty + C::K_STAGES;  // [4]
   uint64_t* sk_full = acc_empty + 4;  // [SK_RING]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_full + SK_RING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES);  // [units + 1] tile prefix
   float* sks = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES + PREF_BYTES);  // [SK_RING][BM]
-  const int n_acc = (MODE == 2 || C::NMAX != 256) ? 2 : score_accs(a.N);  // 4 x 128 columns need NMAX = 256
+  // 4 x 128 columns need NMAX = 256; n_acc <= K_STAGES for the epilogue's k_empty wait
+  const int n_acc = (MODE == 2 || C::NMAX != 256 || C::K_STAGES < 4) ? 2 : score_accs(a.N);
   const int acc_cols = n_acc == 4 ? 128 : C::NMAX;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -175,7 +175,6 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       tc::mbar_init(&q_empty[i], 1);
     }
     for (int i = 0; i < 4; ++i) {
-      tc::mbar_init(&acc_full[i], 1);
       tc::mbar_init(&acc_empty[i], MODE == 2 ? 16 : 4);  // the warps of the warpgroup(s) of buffer i
     }
     for (int i = 0; i < SK_RING; ++i) tc::mbar_init(&sk_full[i], 1);
@@ -391,8 +390,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
             tc::mma_ss<FP8 ? 1 : 0>(d, tc::sdesc_add(kdesc, cb * BM * C::SW + off),
                                     tc::sdesc_add(qdesc, cb * C::NMAX * C::SW + off), idesc, kk > 0);
           }
+          // one commit per tile: k_empty both frees the key stage and tells the epilogue the
+          // accumulator is complete (it waits on that stage's barrier, below)
           tc::mma_commit(&k_empty[ks_i]);
-          tc::mma_commit(&acc_full[acc]);
           if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
           if (++acc == n_acc) { acc = 0; acc_ph ^= 1; }
         }
@@ -453,7 +453,6 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         // between the warpgroups (two buffers each when there are four)
         const int acc = int(tcount % uint32_t(n_acc));
         if (MODE != 2 && (acc & 1) != bwg) continue;
-        const int acc_ph = int(tcount / uint32_t(n_acc)) & 1;
         // the key scale does not depend on the MMA: load it before waiting
         const int j = kt * BM + row;
         float skj;
@@ -466,7 +465,13 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
                                   : 1.0f) * a.scale
                           : 0.0f;
         }
-        if (!tc::mbar_wait(&acc_full[acc], acc_ph, a.err, 106)) { ok = false; break; }
+        // the tile's MMAs are complete when its key stage's k_empty phase completes (the one
+        // commit per tile).  That phase cannot be overtaken before this wait: the stage's next
+        // completion needs the MMA of tile tcount + K_STAGES, which waits for this
+        // accumulator's release (n_acc <= K_STAGES, K_STAGES >= 2), and each buffer's tiles are
+        // drained in order.
+        if (!tc::mbar_wait(&k_empty[tcount % uint32_t(C::K_STAGES)], (tcount / uint32_t(C::K_STAGES)) & 1u, a.err,
+                           106)) { ok = false; break; }
         tc::fence_after_sync();
         const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * acc_cols);
         bool released = false;
