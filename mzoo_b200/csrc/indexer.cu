@@ -60,7 +60,7 @@ constexpr int BARS_BYTES = 512;  // mbarriers, TMEM slot and abort flag
 __host__ __device__ constexpr int score_accs(int n) { return n <= 128 ? 4 : 2; }
 constexpr int PREF_BYTES = 2304;  // tile prefix [BAL_MAX + 1] ints, rounded up to 256
 static_assert((BAL_MAX + 1) * 4 <= PREF_BYTES, "prefix area");
-static_assert(SK_RING > 8 && (SK_RING & (SK_RING - 1)) == 0, "scale ring: more slots than K stages + accumulators");
+static_assert(SK_RING > 12 && (SK_RING & (SK_RING - 1)) == 0, "scale ring: more slots than K stages + accumulators");
 
 template <bool FP8, int DI>
 struct Cfg {
@@ -76,12 +76,14 @@ struct Cfg {
   static constexpr int Q_BUFS = (2 * Q_BYTES + 2 * K_BYTES <= BUDGET) ? 2 : 1;
   static constexpr int KS_RAW = (BUDGET - Q_BUFS * Q_BYTES) / K_BYTES;
   static constexpr int K_STAGES = KS_RAW > 4 ? 4 : KS_RAW;
+  // paged keys (decode: one query, a long key stream per unit) keep up to 8 tiles in flight
+  static constexpr int K_STAGES_PAGED = KS_RAW > 8 ? 8 : KS_RAW;
   static constexpr int TMEM_COLS = 2 * NMAX;
   // dense keys: tiles, weights, barriers, tile prefix; paged keys add the key-scale ring
   static constexpr int SMEM =
       Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + BARS_BYTES + (BAL_MAX + 1) * 4 + 1024;
   static constexpr int SMEM_PAGED =
-      Q_BUFS * Q_BYTES + K_STAGES * K_BYTES + 8 * NMAX * 4 + BARS_BYTES + PREF_BYTES + SK_RING * BM * 4 + 1024;
+      Q_BUFS * Q_BYTES + K_STAGES_PAGED * K_BYTES + 8 * NMAX * 4 + BARS_BYTES + PREF_BYTES + SK_RING * BM * 4 + 1024;
   static_assert(R % 32 == 0, "row bytes must be a multiple of 32");
   static_assert(K_STAGES >= 2, "smem budget");
 };
@@ -148,24 +150,25 @@ template <bool FP8, int DI, int MODE, bool PAGED>
 __global__ void __launch_bounds__(score_nthreads(MODE), 1)
     score_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, ScoreArgs a) {
   using C = Cfg<FP8, DI>;
+  constexpr int KST = PAGED ? C::K_STAGES_PAGED : C::K_STAGES;  // key stages in the ring
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
   uint8_t* ks = qs + C::Q_BUFS * C::Q_BYTES;
-  float* cw = reinterpret_cast<float*>(ks + C::K_STAGES * C::K_BYTES);
+  float* cw = reinterpret_cast<float*>(ks + KST * C::K_BYTES);
   uint64_t* bars = reinterpret_cast<uint64_t*>(cw + 8 * C::NMAX);
   uint64_t* q_full = bars;
   uint64_t* q_empty = bars + 2;
   uint64_t* k_full = bars + 4;
-  uint64_t* k_empty = k_full + C::K_STAGES;
-  uint64_t* acc_empty = k_empty + C::K_STAGES;  // [4]
+  uint64_t* k_empty = k_full + KST;
+  uint64_t* acc_empty = k_empty + KST;  // [4]
   uint64_t* sk_full = acc_empty + 4;  // [SK_RING]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sk_full + SK_RING);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* pref = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES);  // [units + 1] tile prefix
   float* sks = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + BARS_BYTES + PREF_BYTES);  // [SK_RING][BM]
   // 4 x 128 columns need NMAX = 256; n_acc <= K_STAGES for the epilogue's k_empty wait
-  const int n_acc = (MODE == 2 || C::NMAX != 256 || C::K_STAGES < 4) ? 2 : score_accs(a.N);
+  const int n_acc = (MODE == 2 || C::NMAX != 256 || KST < 4) ? 2 : score_accs(a.N);
   const int acc_cols = n_acc == 4 ? 128 : C::NMAX;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -178,7 +181,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
       tc::mbar_init(&acc_empty[i], MODE == 2 ? 16 : 4);  // the warps of the warpgroup(s) of buffer i
     }
     for (int i = 0; i < SK_RING; ++i) tc::mbar_init(&sk_full[i], 1);
-    for (int i = 0; i < C::K_STAGES; ++i) {
+    for (int i = 0; i < KST; ++i) {
       tc::mbar_init(&k_full[i], 1);
       tc::mbar_init(&k_empty[i], 1);
     }
@@ -328,9 +331,9 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
             if (a.sk_ring) {
               // The tile's key scales (two 256-byte page rows).  Slot reuse is safe without an
               // empty barrier: this copy waited (k_empty above) for the MMA of the tile
-              // K_STAGES back, which waited for the epilogue to release the tile n_acc (<= 4)
+              // KST back, which waited for the epilogue to release the tile n_acc (<= 4)
               // before that, and the epilogue reads a tile's scales before releasing it -- so
-              // every tile up to K_STAGES + 4 back has been read, and SK_RING > K_STAGES + 4.
+              // every tile up to KST + 4 back has been read, and SK_RING > KST + 4.
               const int si = int(n_tiles % SK_RING);
               tc::mbar_expect_tx(&sk_full[si], 2 * 64 * 4);
               tc::bulk_load(sks + si * BM, a.sk + r0, 64 * 4, &sk_full[si]);
@@ -345,13 +348,13 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
           }
           k_issued |= 1u << ks_i;
           k_par[ks_i] = ks_ph;
-          if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
+          if (++ks_i == KST) { ks_i = 0; ks_ph ^= 1; }
           ++n_tiles;
         }
         ++qi;
       }
       if (*abort_flag) {  // drain this CTA's own copies before the CTA (and its smem) goes away
-        for (int i = 0; i < C::K_STAGES; ++i)
+        for (int i = 0; i < KST; ++i)
           if (k_issued >> i & 1) tc::mbar_wait(&k_full[i], k_par[i], nullptr, 0);
         for (int i = 0; i < 2; ++i)
           if (q_issued >> i & 1) tc::mbar_wait(&q_full[i], q_par[i], nullptr, 0);
@@ -393,7 +396,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
           // one commit per tile: k_empty both frees the key stage and tells the epilogue the
           // accumulator is complete (it waits on that stage's barrier, below)
           tc::mma_commit(&k_empty[ks_i]);
-          if (++ks_i == C::K_STAGES) { ks_i = 0; ks_ph ^= 1; }
+          if (++ks_i == KST) { ks_i = 0; ks_ph ^= 1; }
           if (++acc == n_acc) { acc = 0; acc_ph ^= 1; }
         }
         tc::mma_commit(&q_empty[qb]);
@@ -470,7 +473,7 @@ __global__ void __launch_bounds__(score_nthreads(MODE), 1)
         // completion needs the MMA of tile tcount + K_STAGES, which waits for this
         // accumulator's release (n_acc <= K_STAGES, K_STAGES >= 2), and each buffer's tiles are
         // drained in order.
-        if (!tc::mbar_wait(&k_empty[tcount % uint32_t(C::K_STAGES)], (tcount / uint32_t(C::K_STAGES)) & 1u, a.err,
+        if (!tc::mbar_wait(&k_empty[tcount % uint32_t(KST)], (tcount / uint32_t(KST)) & 1u, a.err,
                            106)) { ok = false; break; }
         tc::fence_after_sync();
         const uint32_t tbase = tc::taddr(tmem, quarter * 32, acc * acc_cols);
