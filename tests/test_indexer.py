@@ -180,6 +180,17 @@ def test_scores_partial_token_blocks(cuda, S):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("S", [1, 2, 3])
+@pytest.mark.parametrize("heads,dim", [(64, 64), (64, 128), (32, 64)])
+def test_scores_few_tokens(cuda, S, heads, dim):
+    """Query blocks of one to three tokens (decode-like): tiles of at most 128 query columns
+    run on four 128-column TMEM accumulators when the key ring has four stages, wider ones on
+    two; the epilogue waits on each key stage's barrier either way."""
+    import torch
+    _check_scores(torch, cuda, 3, S, heads, dim, 700, 2, q_offset=600)
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("ratio", [1, 2, 4])
 def test_compress_ratios(cuda, ratio):
     import torch
