@@ -442,7 +442,8 @@ def c2_config(world: int) -> dict:
             "Hi": C2["Hi"], "Di": C2["Di"], "compress_ratio": C2["ratio"], "topk": C2["topk"],
             "q_offset": C2["q_offset"],
             "parallelism": (f"(batch x 128-query chunk) units cyclic over {world} GPUs, keys replicated, no "
-                            "collective in the step" if world > 1 else "1 GPU"),
+                            "collective in the step; the optional index gather timed on its own (legs)"
+                            if world > 1 else "1 GPU"),
             "l2": "flushed (256 MB write) per step"}
 
 
@@ -530,6 +531,15 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
     torch.cuda.synchronize()
     out_idx = indexer.attn(q8, k8, w, **dict(kw, check=True))  # one checked call: raises on a device error word
     assert torch.equal(hout, out_idx.cpu()), "e2e index sets differ from the device step"
+    gather_ms = None
+    if dist:  # the optional index gather (every rank's rows to every rank, padded shards), timed alone
+        width = max(len(p) for p in shard_tokens(S, world, 128))
+        pad = out_idx.new_full((B, width, C2["topk"]), -1)
+        pad[:, :len(toks)] = out_idx
+        gbuf = out_idx.new_empty((world, B, width, C2["topk"]))
+        dist.all_gather_into_tensor(gbuf, pad)  # untimed: the collective's lazy setup
+        t_g = timer.run(lambda: dist.all_gather_into_tensor(gbuf, pad), 3, flush=False)
+        gather_ms = max_over_ranks(torch, dist, sum(t_g) / len(t_g), device)
     h2d = sum(x.numel() * x.element_size() for x in (hq8, hk8, hsq, hsk, hw))
     d2h = hout.numel() * hout.element_size()
 
@@ -548,6 +558,7 @@ def bench_indexer(args, torch, dist, rank, world, device) -> dict:
         "dtype": "e4m3 (fp32 accumulate)", "data": "synthetic (seeded N(0,1), absmax fp8)",
         "config": c2_config(world),
         "timing": "value: CUDA-graph replay of the step's launches; e2e: the public API op by op",
+        "legs": {"idx_gather_ms": gather_ms},
         "e2e": {"value": queries / (ms_e2e * 1e-3) / 1e6, "unit": "Mq/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "note": f"indexer.attn on {len(chunks)} chunks (batch x query halves), each chunk's H2D / kernels / "
