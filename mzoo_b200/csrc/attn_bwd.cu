@@ -128,8 +128,9 @@ struct KvCfg {
 // warpgroups never store over columns the other one has still to read.
 __device__ __forceinline__ int pt_col(int c) { return c / 2 + (c >= 64 ? 32 : 0); }
 
-enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FULL, PT_FULL, O_DONE, ACC_EMPTY,
-             KV_NBAR };
+// S_FULL / PT_FULL per query half h (columns [64 h, 64 h + 64)): S_FULL + h, PT_FULL + h
+enum KvBar { KV_FULL = 0, KV_EMPTY, QD_FULL, QD_FULL1, QD_EMPTY, QD_EMPTY1, S_FULL, S_FULL1, PT_FULL, PT_FULL1,
+             O_DONE, ACC_EMPTY, KV_NBAR };
 
 struct KvItem {
   int b, kt, k0, sp, nq;  // nq query tiles in this split (may be 0)
@@ -191,7 +192,7 @@ __global__ void __launch_bounds__(384, 1)
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < KV_NBAR; ++i) tc::mbar_init(&bars[i], i == PT_FULL ? 8 : (i == ACC_EMPTY ? 4 : 1));
+    for (int i = 0; i < KV_NBAR; ++i) tc::mbar_init(&bars[i], (i == PT_FULL || i == PT_FULL1 || i == ACC_EMPTY) ? 4 : 1);
     *abort_flag = 0;
     tc::fence_barrier_init();
   }
@@ -237,9 +238,50 @@ __global__ void __launch_bounds__(384, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t idesc_s = tc::make_idesc(128, 128, 1, 1);
+      // S^T / dP^T and the dV / dK MMAs go in query halves h (columns / rows [64 h, 64 h + 64)),
+      // software-pipelined: for tile i the order is TS_lo(i), S_lo(i+1) + dP_lo(i+1),
+      // TS_hi(i), S_hi(i+1) + dP_hi(i+1), so while one compute warpgroup turns its half of
+      // tile i+1 into P^T / dS^T the tensor core runs the other half's MMAs.  Each S / dP
+      // half MMA is issued after the TS MMAs that read that half's packed columns (one
+      // thread, in order).
+      const uint32_t idesc_s = tc::make_idesc(128, 64, 1, 1);
       const uint32_t idesc_acc = tc::make_idesc(128, D, 1, 1, false, true);
       const uint32_t k_base = smem_u32(ks), v_base = smem_u32(vs);
+      const uint64_t kd = tc::make_sdesc<128>(k_base, 16, 1024), vd = tc::make_sdesc<128>(v_base, 16, 1024);
+      // S^T(h) = K Q_h^T and dP^T(h) = V dO_h^T of stage s (query rows 64 h.. of the tile)
+      auto issue_sdp = [&](int s, int h) {
+        const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
+        const uint64_t qd = tc::make_sdesc<128>(q_base + h * 8192, 16, 1024);
+        const uint64_t dod = tc::make_sdesc<128>(do_base + h * 8192, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int cb = kk >> 2, off = (kk & 3) * 32;
+          tc::mma_ss<0>(tmem + C::C_S + 64 * h, tc::sdesc_add(kd, cb * 16384 + off),
+                        tc::sdesc_add(qd, cb * 16384 + off), idesc_s, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int cb = kk >> 2, off = (kk & 3) * 32;
+          tc::mma_ss<0>(tmem + C::C_DP + 64 * h, tc::sdesc_add(vd, cb * 16384 + off),
+                        tc::sdesc_add(dod, cb * 16384 + off), idesc_s, kk > 0);
+        }
+        tc::mma_commit(&bars[S_FULL + h]);
+      };
+      // dV += P^T(h) dO_h, dK += dS^T(h) Q_h over the half's 64 query rows (16 per step)
+      auto issue_ts = [&](int s, int h, bool first) {
+        const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
+        const uint64_t q_mn = tc::make_sdesc<128>(q_base, 16384, 1024);
+        const uint64_t do_mn = tc::make_sdesc<128>(do_base, 16384, 1024);
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = 4 * h + k4;
+          const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+          const int pc = pt_col(16 * kk);
+          tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + pc, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
+          tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + pc, tc::sdesc_add(q_mn, kk * 2048), idesc_acc,
+                     C::MERGE ? 1u : acc);
+        }
+      };
       int g = 0, ii = -1;
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x) {
         const KvItem m = kv_item(a, it);
@@ -247,41 +289,42 @@ __global__ void __launch_bounds__(384, 1)
         ++ii;
         if (!tc::mbar_wait(&bars[KV_FULL], ii & 1, a.err, 410)) { *abort_flag = 1; break; }
         bool ok = true;
-        for (int i = 0; i < m.nq; ++i, ++g) {
+        {  // both halves of the item's first tile
           const int s = g % C::NST, ph = (g / C::NST) & 1;
-          if (!tc::mbar_wait(&bars[QD_FULL + s], ph, a.err, 411)) { ok = false; break; }
-          tc::fence_after_sync();
-          const uint32_t q_base = smem_u32(stage(s)), do_base = q_base + C::T_BYTES;
-          // descriptors once per tile; the unrolled loops add constant offsets
-          const uint64_t kd = tc::make_sdesc<128>(k_base, 16, 1024), vd = tc::make_sdesc<128>(v_base, 16, 1024);
-          const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
-          const uint64_t q_mn = tc::make_sdesc<128>(q_base, 16384, 1024);
-          const uint64_t do_mn = tc::make_sdesc<128>(do_base, 16384, 1024);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_S, tc::sdesc_add(kd, cb * 16384 + off), tc::sdesc_add(qd, cb * 16384 + off),
-                          idesc_s, kk > 0);
+          if (!tc::mbar_wait(&bars[QD_FULL + s], ph, a.err, 411)) ok = false;
+          if (ok) {
+            tc::fence_after_sync();
+            issue_sdp(s, 0);
+            issue_sdp(s, 1);
           }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::C_DP, tc::sdesc_add(vd, cb * 16384 + off), tc::sdesc_add(dod, cb * 16384 + off),
-                          idesc_s, kk > 0);
-          }
-          tc::mma_commit(&bars[S_FULL]);
+        }
+        for (int i = 0; i < m.nq && ok; ++i, ++g) {
+          const int s = g % C::NST;
+          const int s1 = (g + 1) % C::NST, ph1 = ((g + 1) / C::NST) & 1;
+          const bool more = i + 1 < m.nq;
           if (i == 0 && !tc::mbar_wait(&bars[ACC_EMPTY], (ii & 1) ^ 1, a.err, 412)) { ok = false; break; }
-          if (!tc::mbar_wait(&bars[PT_FULL], g & 1, a.err, 413)) { ok = false; break; }
+          if (!tc::mbar_wait(&bars[PT_FULL], g & 1, a.err, 413)) { ok = false; break; }  // half 0 of tile i
           tc::fence_after_sync();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // 128 query rows, 16 per step
-            const uint32_t acc = (i == 0 && kk == 0) ? 0u : 1u;
-            const int pc = pt_col(16 * kk);
-            tc::mma_ts(tmem + C::C_DV, tmem + C::C_S + pc, tc::sdesc_add(do_mn, kk * 2048), idesc_acc, acc);
-            tc::mma_ts(tmem + C::C_DK, tmem + C::C_DP + pc, tc::sdesc_add(q_mn, kk * 2048), idesc_acc,
-                       C::MERGE ? 1u : acc);
+          issue_ts(s, 0, i == 0);
+          // with one Q / dO stage (D = 256) tile i + 1 loads only after this tile's TS MMAs
+          // release the stage, so its S^T / dP^T wait for them
+          if (more && C::NST > 1) {
+            if (!tc::mbar_wait(&bars[QD_FULL + s1], ph1, a.err, 411)) { ok = false; break; }
+            tc::fence_after_sync();
+            issue_sdp(s1, 0);
           }
+          if (!tc::mbar_wait(&bars[PT_FULL1], g & 1, a.err, 414)) { ok = false; break; }
+          tc::fence_after_sync();
+          issue_ts(s, 1, false);
           tc::mma_commit(&bars[QD_EMPTY + s]);
+          if (more) {
+            if (C::NST == 1) {
+              if (!tc::mbar_wait(&bars[QD_FULL + s1], ph1, a.err, 411)) { ok = false; break; }
+              tc::fence_after_sync();
+              issue_sdp(s1, 0);
+            }
+            issue_sdp(s1, 1);
+          }
           if (i == m.nq - 1) {
             tc::mma_commit(&bars[O_DONE]);
             tc::mma_commit(&bars[KV_EMPTY]);
@@ -311,7 +354,7 @@ __global__ void __launch_bounds__(384, 1)
       bool ok = true;
       for (int i = 0; i < m.nq; ++i, ++g) {
         const int s = g % C::NST;
-        if (!tc::mbar_wait(&bars[S_FULL], g & 1, a.err, 420)) { ok = false; break; }
+        if (!tc::mbar_wait(&bars[S_FULL + (second ? 1 : 0)], g & 1, a.err, 420)) { ok = false; break; }
         tc::fence_after_sync();
         const float* l2 = reinterpret_cast<const float*>(stage(s) + 2 * C::T_BYTES);
         const float* dl = l2 + 128;
@@ -361,7 +404,7 @@ __global__ void __launch_bounds__(384, 1)
         tc::tmem_wait_st();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bars[PT_FULL]);
+        if (lane == 0) tc::mbar_arrive(&bars[PT_FULL + (second ? 1 : 0)]);
       }
       if (!ok) { *abort_flag = 1; break; }
       if (second) continue;  // the first warpgroup writes the partial dK / dV
