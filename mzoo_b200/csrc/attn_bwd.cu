@@ -499,8 +499,10 @@ struct QCfg {
   static_assert(!(WIDE && SEP_V), "a separate V needs D <= 128");
 };
 
+// S_FULL_Q / DS_FULL cover the whole key tile, or with SPLIT its first half of keys;
+// S_FULL_Q1 / DS_FULL1 the second half (SPLIT only)
 enum QBar { Q_FULL = 0, Q_EMPTY, S_FULL_Q, DS_FULL, DM_FULL, DM_EMPTY, QO_DONE, QACC_EMPTY, KVW_FULL,
-            KVG_FULL = KVW_FULL + 2, KVQ_EMPTY = KVG_FULL + 2, Q_NBAR = KVQ_EMPTY + 2 };
+            KVG_FULL = KVW_FULL + 2, KVQ_EMPTY = KVG_FULL + 2, S_FULL_Q1 = KVQ_EMPTY + 2, DS_FULL1, Q_NBAR };
 
 struct QItem {
   int b, qt, t0, t1, kt0, n_win, n_gat, gtiles, tq_valid;
@@ -546,8 +548,8 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Q_NBAR; ++i) {
       uint32_t c = 1;
-      if (i == DS_FULL) c = C::SPLIT ? 8 : 4;
-      if (i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1) c = 4;
+      if (i == DS_FULL || i == DS_FULL1 || i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1)
+        c = 4;
       tc::mbar_init(&bars[i], c);
     }
     *abort_flag = 0;
@@ -603,6 +605,76 @@ __global__ void __launch_bounds__(384, 1)
         const int n = m.n_win + m.n_gat;
         if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 510)) { *abort_flag = 1; break; }
         bool ok = true;
+        if constexpr (C::SPLIT) {
+          // window tiles only (a separate V excludes gathered rows).  S / dP and dQ += dS K run
+          // in halves of KT / 2 keys, one per compute warpgroup; the next tile's S / dP half is
+          // issued as soon as its warpgroup has packed dS of this tile, so it computes while
+          // the other warpgroup works
+          const uint32_t idesc_h = tc::make_idesc(128, KT / 2, 1, 1);
+          const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
+          auto kv_wait = [&](int gg) {
+            if (!tc::mbar_wait(&bars[KVW_FULL + (gg & 1)], (gg >> 1) & 1, a.err, 511)) return false;
+            tc::fence_after_sync();
+            return true;
+          };
+          auto issue_s = [&](int gg, int h) {
+            const uint32_t kb = kv_base + (gg & 1) * C::KV_STAGE + h * (KT / 2) * 128;
+            const uint64_t kd = tc::make_sdesc<128>(kb, 16, 1024), vd = tc::make_sdesc<128>(kb + C::KV_BYTES, 16, 1024);
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int cb = kk >> 2, off = (kk & 3) * 32;
+              tc::mma_ss<0>(tmem + C::C_S + h * (KT / 2), tc::sdesc_add(qd, cb * 16384 + off),
+                            tc::sdesc_add(kd, cb * KB + off), idesc_h, kk > 0);
+            }
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const int cb = kk >> 2, off = (kk & 3) * 32;
+              tc::mma_ss<0>(tmem + C::C_DP + h * (KT / 2), tc::sdesc_add(dod, cb * 16384 + off),
+                            tc::sdesc_add(vd, cb * KB + off), idesc_h, kk > 0);
+            }
+            tc::mma_commit(&bars[h ? S_FULL_Q1 : S_FULL_Q]);
+          };
+          auto issue_dq = [&](int gg, int h, bool first) {
+            const uint64_t k_mn = tc::make_sdesc<128>(kv_base + (gg & 1) * C::KV_STAGE, KB, 1024);
+#pragma unroll
+            for (int k4 = 0; k4 < KT / 32; ++k4) {  // 16 keys per step; half h's packed dS columns
+              const uint32_t ds_col = h ? C::C_DS2 + k4 * 8 : C::C_S + k4 * 8;
+              tc::mma_ts(tmem + C::C_DQ, tmem + ds_col, tc::sdesc_add(k_mn, (h * (KT / 32) + k4) * 2048), idesc_dq,
+                         (first && k4 == 0) ? 0u : 1u);
+            }
+          };
+          if (n > 0) {
+            if (kv_wait(g)) {
+              issue_s(g, 0);
+              issue_s(g, 1);
+            } else {
+              ok = false;
+            }
+          }
+          for (int j = 0; ok && j < n; ++j, ++g) {
+            const bool more = j + 1 < n;
+            if (j == 0 && !tc::mbar_wait(&bars[QACC_EMPTY], (ii & 1) ^ 1, a.err, 512)) { ok = false; break; }
+            if (!tc::mbar_wait(&bars[DS_FULL], g & 1, a.err, 513)) { ok = false; break; }
+            tc::fence_after_sync();
+            issue_dq(g, 0, j == 0);
+            if (more) {
+              if (!kv_wait(g + 1)) { ok = false; break; }
+              issue_s(g + 1, 0);
+            }
+            if (!tc::mbar_wait(&bars[DS_FULL1], g & 1, a.err, 515)) { ok = false; break; }
+            tc::fence_after_sync();
+            issue_dq(g, 1, false);
+            tc::mma_commit(&bars[KVQ_EMPTY + (g & 1)]);
+            if (more) {
+              issue_s(g + 1, 1);
+            } else {
+              tc::mma_commit(&bars[Q_EMPTY]);
+              tc::mma_commit(&bars[QO_DONE]);
+            }
+          }
+          if (!ok) { *abort_flag = 1; break; }
+          continue;
+        }
         for (int j = 0; j < n; ++j, ++g) {
           const int st = g & 1;
           const bool win = j < m.n_win;
@@ -721,7 +793,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         const bool full = row_ok && win && wlo <= 0 && whi >= KT - 1;
         const bool warp_full = __all_sync(0xffffffffu, full);
-        if (!tc::mbar_wait(&bars[S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
+        if (!tc::mbar_wait(&bars[second ? S_FULL_Q1 : S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
 #pragma unroll 1
         for (int c0 = cbeg; c0 < cend; c0 += 32) {
@@ -768,7 +840,7 @@ __global__ void __launch_bounds__(384, 1)
         if (!win) tc::fence_async_smem();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&bars[DS_FULL]);
+        if (lane == 0) tc::mbar_arrive(&bars[second ? DS_FULL1 : DS_FULL]);
         if (!win && !second) {
           if (!tc::mbar_wait(&bars[DM_FULL], gm & 1, a.err, 521)) { ok = false; break; }
           tc::fence_after_sync();
