@@ -35,6 +35,14 @@ __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
 }
+__device__ __forceinline__ uint4 ld_shared16(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(smem_u32(p))
+               : "memory");
+  return v;
+}
 // bits [lo, hi] of a 32-bit word (empty when hi < lo; lo, hi clipped to [0, 31])
 __device__ __forceinline__ uint32_t run_bits(int lo, int hi) {
   lo = max(lo, 0);
@@ -490,19 +498,23 @@ struct QCfg {
   static constexpr int SMEM = TILE_BYTES + 512;
   static constexpr int C_DQ = 0, C_S = D, C_DP = D + KT, C_DM = D + 2 * KT;
   // window-only (separate V): warps 8-11 are free, so the columns of each key tile are split
-  // over two compute warpgroups; the second half's packed dS goes to the unused dM columns
+  // over two compute warpgroups, each packing its dS into the front of its own S half; the
+  // unused dM columns hold the item's Q and dO rows (bf16 pairs), the TMEM A operands of the
+  // S and dP MMAs, so shared memory carries only K / V operands for them and the Q / dO
+  // buffer is free for the next item as soon as it has been copied
   static constexpr bool SPLIT = SEP_V;
-  static constexpr int C_DS2 = C_DM;
+  static constexpr int C_QT = C_DM, C_DOT = C_DM + D / 2;
   static_assert(C_DP + KT <= 512 && (SEP_V || C_DM + (WIDE ? 2 * KT : D) <= 512), "TMEM");
-  static_assert(!SPLIT || C_DS2 + KT / 4 <= 512, "TMEM");
+  static_assert(!SPLIT || C_DOT + D / 2 <= 512, "TMEM");
   static_assert(SMEM <= 232448, "smem");
   static_assert(!(WIDE && SEP_V), "a separate V needs D <= 128");
 };
 
 // S_FULL_Q / DS_FULL cover the whole key tile, or with SPLIT its first half of keys;
-// S_FULL_Q1 / DS_FULL1 the second half (SPLIT only)
+// S_FULL_Q1 / DS_FULL1 the second half, QT_FULL the item's Q / dO rows in TMEM (SPLIT only)
 enum QBar { Q_FULL = 0, Q_EMPTY, S_FULL_Q, DS_FULL, DM_FULL, DM_EMPTY, QO_DONE, QACC_EMPTY, KVW_FULL,
-            KVG_FULL = KVW_FULL + 2, KVQ_EMPTY = KVG_FULL + 2, S_FULL_Q1 = KVQ_EMPTY + 2, DS_FULL1, Q_NBAR };
+            KVG_FULL = KVW_FULL + 2, KVQ_EMPTY = KVG_FULL + 2, S_FULL_Q1 = KVQ_EMPTY + 2, DS_FULL1, QT_FULL,
+            Q_NBAR };
 
 struct QItem {
   int b, qt, t0, t1, kt0, n_win, n_gat, gtiles, tq_valid;
@@ -548,8 +560,10 @@ __global__ void __launch_bounds__(384, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < Q_NBAR; ++i) {
       uint32_t c = 1;
-      if (i == DS_FULL || i == DS_FULL1 || i == DM_EMPTY || i == QACC_EMPTY || i == KVG_FULL || i == KVG_FULL + 1)
+      if (i == DS_FULL || i == DS_FULL1 || i == QT_FULL || i == DM_EMPTY || i == KVG_FULL || i == KVG_FULL + 1)
         c = 4;
+      if (i == QACC_EMPTY) c = C::SPLIT ? 8 : 4;  // with SPLIT both warpgroups store half of dQ
+      if (i == Q_EMPTY && C::SPLIT) c = 4;        // released by the warps that copy Q / dO to TMEM
       tc::mbar_init(&bars[i], c);
     }
     *abort_flag = 0;
@@ -603,7 +617,7 @@ __global__ void __launch_bounds__(384, 1)
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
         const QItem m = q_item<KT>(a, it, n_qt);
         const int n = m.n_win + m.n_gat;
-        if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 510)) { *abort_flag = 1; break; }
+        if (!tc::mbar_wait(&bars[C::SPLIT ? QT_FULL : Q_FULL], ii & 1, a.err, 510)) { *abort_flag = 1; break; }
         bool ok = true;
         if constexpr (C::SPLIT) {
           // window tiles only (a separate V excludes gathered rows).  S / dP and dQ += dS K run
@@ -611,7 +625,7 @@ __global__ void __launch_bounds__(384, 1)
           // issued as soon as its warpgroup has packed dS of this tile, so it computes while
           // the other warpgroup works
           const uint32_t idesc_h = tc::make_idesc(128, KT / 2, 1, 1);
-          const uint64_t qd = tc::make_sdesc<128>(q_base, 16, 1024), dod = tc::make_sdesc<128>(do_base, 16, 1024);
+          tc::fence_after_sync();
           auto kv_wait = [&](int gg) {
             if (!tc::mbar_wait(&bars[KVW_FULL + (gg & 1)], (gg >> 1) & 1, a.err, 511)) return false;
             tc::fence_after_sync();
@@ -623,14 +637,14 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const int cb = kk >> 2, off = (kk & 3) * 32;
-              tc::mma_ss<0>(tmem + C::C_S + h * (KT / 2), tc::sdesc_add(qd, cb * 16384 + off),
-                            tc::sdesc_add(kd, cb * KB + off), idesc_h, kk > 0);
+              tc::mma_ts(tmem + C::C_S + h * (KT / 2), tmem + C::C_QT + kk * 8, tc::sdesc_add(kd, cb * KB + off),
+                         idesc_h, kk > 0 ? 1u : 0u);
             }
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               const int cb = kk >> 2, off = (kk & 3) * 32;
-              tc::mma_ss<0>(tmem + C::C_DP + h * (KT / 2), tc::sdesc_add(dod, cb * 16384 + off),
-                            tc::sdesc_add(vd, cb * KB + off), idesc_h, kk > 0);
+              tc::mma_ts(tmem + C::C_DP + h * (KT / 2), tmem + C::C_DOT + kk * 8, tc::sdesc_add(vd, cb * KB + off),
+                         idesc_h, kk > 0 ? 1u : 0u);
             }
             tc::mma_commit(&bars[h ? S_FULL_Q1 : S_FULL_Q]);
           };
@@ -638,7 +652,7 @@ __global__ void __launch_bounds__(384, 1)
             const uint64_t k_mn = tc::make_sdesc<128>(kv_base + (gg & 1) * C::KV_STAGE, KB, 1024);
 #pragma unroll
             for (int k4 = 0; k4 < KT / 32; ++k4) {  // 16 keys per step; half h's packed dS columns
-              const uint32_t ds_col = h ? C::C_DS2 + k4 * 8 : C::C_S + k4 * 8;
+              const uint32_t ds_col = C::C_S + h * (KT / 2) + k4 * 8;
               tc::mma_ts(tmem + C::C_DQ, tmem + ds_col, tc::sdesc_add(k_mn, (h * (KT / 32) + k4) * 2048), idesc_dq,
                          (first && k4 == 0) ? 0u : 1u);
             }
@@ -665,12 +679,10 @@ __global__ void __launch_bounds__(384, 1)
             tc::fence_after_sync();
             issue_dq(g, 1, false);
             tc::mma_commit(&bars[KVQ_EMPTY + (g & 1)]);
-            if (more) {
+            if (more)
               issue_s(g + 1, 1);
-            } else {
-              tc::mma_commit(&bars[Q_EMPTY]);
+            else
               tc::mma_commit(&bars[QO_DONE]);
-            }
           }
           if (!ok) { *abort_flag = 1; break; }
           continue;
@@ -704,7 +716,7 @@ __global__ void __launch_bounds__(384, 1)
           tc::fence_after_sync();
 #pragma unroll
           for (int kk = 0; kk < KT / 16; ++kk) {  // KT keys, 16 per step: dQ += dS K
-            const uint32_t ds_col = (C::SPLIT && kk >= KT / 32) ? C::C_DS2 + (kk - KT / 32) * 8 : C::C_S + kk * 8;
+            const uint32_t ds_col = C::C_S + kk * 8;  // (SPLIT kernels take the pipelined path above)
             tc::mma_ts(tmem + C::C_DQ, tmem + ds_col, tc::sdesc_add(k_mn, kk * 2048), idesc_dq,
                        (j == 0 && kk == 0) ? 0u : 1u);
           }
@@ -755,6 +767,54 @@ __global__ void __launch_bounds__(384, 1)
     const bool second = C::SPLIT && warp >= 8;
     const int cbeg = second ? KT / 2 : 0, cend = (C::SPLIT && !second) ? KT / 2 : KT;
     const float sl = a.scale_log2;
+    // dQ columns [c_lo, c_hi) of item mm (index iim) -> bf16 rows; frees the accumulator
+    auto store_dq = [&](const QItem& mm, int iim, int c_lo, int c_hi) {
+      if (!tc::mbar_wait(&bars[QO_DONE], iim & 1, a.err, 522)) return false;
+      tc::fence_after_sync();
+      const bool ok_row = mm.t0 + r / a.H < a.S;
+      const long long grow = (long long)mm.qt * 128 + r;
+#pragma unroll 1
+      for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
+        uint32_t qv[32];
+        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DQ + c0), qv);
+        tc::tmem_wait_ld();
+        if (ok_row) {
+          uint4* dst = reinterpret_cast<uint4*>(a.dq + ((long long)mm.b * a.S * a.H + grow) * D + c0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            dst[q] = make_uint4(pack_bf16(__uint_as_float(qv[8 * q]) * a.scale, __uint_as_float(qv[8 * q + 1]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 2]) * a.scale, __uint_as_float(qv[8 * q + 3]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 4]) * a.scale, __uint_as_float(qv[8 * q + 5]) * a.scale),
+                                pack_bf16(__uint_as_float(qv[8 * q + 6]) * a.scale, __uint_as_float(qv[8 * q + 7]) * a.scale));
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bars[QACC_EMPTY]);
+      return true;
+    };
+    // SPLIT: row r of a 128-row bf16 tile in shared memory (64-channel blocks of 128-byte rows,
+    // 16-byte chunks swizzled by r % 8) -> TMEM lane r, columns col.. as bf16 pairs
+    auto rows_to_tmem = [&](const uint8_t* src, int col) {
+#pragma unroll
+      for (int cb = 0; cb < C::DB; ++cb) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t v[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int ch = h2 * 4 + c;
+            const uint4 x = ld_shared16(src + cb * 16384 + r * 128 + ((ch ^ (r & 7)) * 16));
+            v[4 * c] = x.x;
+            v[4 * c + 1] = x.y;
+            v[4 * c + 2] = x.z;
+            v[4 * c + 3] = x.w;
+          }
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, col + cb * 32 + h2 * 16), v);
+        }
+      }
+    };
+    QItem prev{};
     int g = 0, ii = 0, gm = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
       const QItem m = q_item<KT>(a, it, n_qt);
@@ -764,6 +824,23 @@ __global__ void __launch_bounds__(384, 1)
       const long long grow = (long long)m.qt * 128 + r;
       const float l2 = a.lse2[(long long)m.b * a.Rpad + grow];
       const float dl = a.delta[(long long)m.b * a.Rpad + grow];
+      if (C::SPLIT && second) {
+        // this item's Q and dO rows into TMEM: every S / dP MMA of the previous item has
+        // completed (this warpgroup saw its last S_FULL_Q1), and the shared-memory buffer is
+        // released for the next item's rows at once; then the previous item's upper dQ half
+        if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 523)) { *abort_flag = 1; break; }
+        tc::fence_after_sync();
+        rows_to_tmem(qs, C::C_QT);
+        rows_to_tmem(dos, C::C_DOT);
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          tc::mbar_arrive(&bars[QT_FULL]);
+          tc::mbar_arrive(&bars[Q_EMPTY]);
+        }
+        if (ii > 0 && !store_dq(prev, ii - 1, D / 2, D)) { *abort_flag = 1; break; }
+      }
       bool ok = true;
       for (int j = 0; j < n; ++j, ++g) {
         const bool win = j < m.n_win;
@@ -819,7 +896,7 @@ __global__ void __launch_bounds__(384, 1)
           uint32_t dd[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) dd[q] = pack_bf16(__uint_as_float(dv[2 * q]), __uint_as_float(dv[2 * q + 1]));
-          tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_DS2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_S + KT / 2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
           if (!win) {  // keep scale*dS (dK carries the softmax scale) and P in smem for the gathered-row gradient
             uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
             uint8_t* pr = dsr + C::P_BYTES;
@@ -894,28 +971,14 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       if (!ok) { *abort_flag = 1; break; }
-      if (second) continue;  // the first warpgroup writes dQ
-      if (!tc::mbar_wait(&bars[QO_DONE], ii & 1, a.err, 522)) { *abort_flag = 1; break; }
-      tc::fence_after_sync();
-#pragma unroll 1
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        uint32_t qv[32];
-        tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DQ + c0), qv);
-        tc::tmem_wait_ld();
-        if (row_ok) {
-          uint4* dst = reinterpret_cast<uint4*>(a.dq + ((long long)m.b * a.S * a.H + grow) * D + c0);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_uint4(pack_bf16(__uint_as_float(qv[8 * q]) * a.scale, __uint_as_float(qv[8 * q + 1]) * a.scale),
-                                pack_bf16(__uint_as_float(qv[8 * q + 2]) * a.scale, __uint_as_float(qv[8 * q + 3]) * a.scale),
-                                pack_bf16(__uint_as_float(qv[8 * q + 4]) * a.scale, __uint_as_float(qv[8 * q + 5]) * a.scale),
-                                pack_bf16(__uint_as_float(qv[8 * q + 6]) * a.scale, __uint_as_float(qv[8 * q + 7]) * a.scale));
-        }
+      if (second) {  // the upper dQ half of this item is stored at the start of the next one
+        prev = m;
+        continue;
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&bars[QACC_EMPTY]);
+      if (!store_dq(m, ii, 0, C::SPLIT ? D / 2 : D)) { *abort_flag = 1; break; }
     }
+    // the last item's upper dQ half
+    if (C::SPLIT && second && ii > 0 && !*abort_flag && !store_dq(prev, ii - 1, D / 2, D)) *abort_flag = 1;
   } else if (warp >= 8) {
     // gathered-row producers (csa2): main_kv rows -> the K stage (K == V)
     const int t = threadIdx.x - 256, row = t;  // 128 rows, one per thread

@@ -241,18 +241,21 @@ def test_swa_bwd(cuda, H, D, window):
 
 
 @pytest.mark.gpu
-def test_swa_bwd_separate_v(cuda):
+@pytest.mark.parametrize("B,S,H,D,window", [(2, 256, 64, 128, 200), (1, 1200, 64, 128, 512), (2, 700, 16, 64, 300)])
+def test_swa_bwd_separate_v(cuda, B, S, H, D, window):
+    # the window-only (separate V) kernels: several query-tile items per CTA (S = 1200 at 64
+    # heads is 600 items), ragged last tiles, and head dim 64
     import torch
     from mzoo_b200 import swa_attn
-    q, kv, v, _, _, _ = _inputs(torch, cuda, 2, 256, 64, 128, seed=11, sep_v=True)
-    o, lse = swa_attn.fwd(q, kv, window=200, v=v)
+    q, kv, v, _, _, _ = _inputs(torch, cuda, B, S, H, D, seed=11, sep_v=True)
+    o, lse = swa_attn.fwd(q, kv, window=window, v=v)
     do = _do(torch, cuda, q.shape, 8)
-    dq, dk, _, dv = swa_attn.bwd(q, kv, o, lse, do, window=200, v=v)
-    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=200, v=_np(v)[:, :, 0])
-    tq, tk, tv = _torch_bf16_grads(torch, q, kv, do, 200, v=v)
-    _check_grad(dq, ref["dq"], "swa K!=V dq", tq)
-    _check_grad(dk[:, :, 0], ref["dk"], "swa K!=V dk", tk[:, :, 0])
-    _check_grad(dv[:, :, 0], ref["dv"], "swa K!=V dv", tv[:, :, 0])
+    dq, dk, _, dv = swa_attn.bwd(q, kv, o, lse, do, window=window, v=v)
+    ref = A.attend_bwd(_np(q), _np(kv)[:, :, 0], _np(do), window=window, v=_np(v)[:, :, 0])
+    tq, tk, tv = _torch_bf16_grads(torch, q, kv, do, window, v=v)
+    _check_grad(dq, ref["dq"], f"swa K!=V dq S{S} H{H} D{D}", tq)
+    _check_grad(dk[:, :, 0], ref["dk"], f"swa K!=V dk S{S} H{H} D{D}", tk[:, :, 0])
+    _check_grad(dv[:, :, 0], ref["dv"], f"swa K!=V dv S{S} H{H} D{D}", tv[:, :, 0])
 
 
 @pytest.mark.gpu
