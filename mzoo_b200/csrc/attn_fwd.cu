@@ -61,6 +61,11 @@ struct Cfg {
   static constexpr int NQ = SPLIT ? NK / 64 : NK / 32;  // 32-column chunks per softmax warp
   static constexpr int X_COL = D + 2 * NK;
   static_assert(!SPLIT || X_COL + 6 <= 512, "TMEM budget");
+  // SPLIT: the item's Q rows (bf16 pairs, the TS operand layout) in the last D / 2 columns;
+  // S = Q K^T then reads only K from shared memory, and the Q buffer is free for the next
+  // item once warps 8-11 have copied it
+  static constexpr int C_QT = 512 - D / 2;
+  static_assert(!SPLIT || X_COL + 6 <= C_QT, "TMEM budget");
   // P (bf16) goes back into its own S buffer: the 32-bit column of keys (c, c + 1) is
   // pt_col(c); each column half [0, NK/2), [NK/2, NK) packs into the front of its own
   // columns, so the two softmax warpgroups never store over S columns the other still reads
@@ -82,8 +87,10 @@ struct Args {
 
 // O_FINAL: commit after an item's last PV, waited on by the epilogue with the item parity
 // (two PVs can still be in flight there, so O_DONE's parity would alias an older phase).
+// QK_DONE: commit after an item's last QK^T; QT_FULL: the item's Q rows are in TMEM (SPLIT).
 enum Bar { Q_FULL = 0, Q_EMPTY, O_DONE, O_EMPTY, S_FULL, S_FULL1, S_EMPTY, S_EMPTY1, P_FULL, P_FULL1, KV_FULL_W,
-           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, EPI_FULL, MX, NBAR = MX + 4 };
+           KV_FULL_G = KV_FULL_W + 4, KV_EMPTY = KV_FULL_G + 4, O_FINAL = KV_EMPTY + 4, EPI_FULL, MX,
+           QK_DONE = MX + 4, QT_FULL, NBAR };
 
 __device__ __forceinline__ void st_shared16(uint8_t* p, const uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
@@ -141,7 +148,8 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
       uint32_t c = 1;
       if (i == O_EMPTY) c = 4;
       if (i == S_EMPTY || i == S_EMPTY1 || i == P_FULL || i == P_FULL1 || i == EPI_FULL) c = C::SPLIT ? 8 : 4;
-      if (i >= MX) c = 2;  // the two softmax warps of one TMEM lane quarter
+      if (i >= MX && i < MX + 4) c = 2;  // the two softmax warps of one TMEM lane quarter
+      if (i == QT_FULL || (i == Q_EMPTY && C::SPLIT)) c = 4;  // warps 8-11 copy Q to TMEM
       if (i >= KV_FULL_G && i < KV_EMPTY) c = 4;
       tc::mbar_init(&bars[i], c);
     }
@@ -219,7 +227,7 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
       for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
         const Item m = make_item<NK>(a, it, n_qt);
         const int n = m.n_win + m.n_gat;
-        if (!tc::mbar_wait(&bars[Q_FULL], ii & 1, a.err, 310)) { *abort_flag = 1; break; }
+        if (!tc::mbar_wait(&bars[C::SPLIT ? QT_FULL : Q_FULL], ii & 1, a.err, 310)) { *abort_flag = 1; break; }
         bool ok = true;
         for (int j = 0; j < n; ++j, ++g) {
           const int st = g % C::STAGES, sb = g & 1;
@@ -233,11 +241,15 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int cb = kk >> 2, off = (kk & 3) * 32;
-            tc::mma_ss<0>(tmem + C::S_COL0 + sb * NK, tc::sdesc_add(qd, cb * 128 * 128 + off),
-                          tc::sdesc_add(kd, cb * NK * 128 + off), idesc_qk, kk > 0 ? 1u : 0u);
+            if constexpr (C::SPLIT)
+              tc::mma_ts(tmem + C::S_COL0 + sb * NK, tmem + C::C_QT + kk * 8, tc::sdesc_add(kd, cb * NK * 128 + off),
+                         idesc_qk, kk > 0 ? 1u : 0u);
+            else
+              tc::mma_ss<0>(tmem + C::S_COL0 + sb * NK, tc::sdesc_add(qd, cb * 128 * 128 + off),
+                            tc::sdesc_add(kd, cb * NK * 128 + off), idesc_qk, kk > 0 ? 1u : 0u);
           }
           tc::mma_commit(&bars[S_FULL + sb]);
-          if (j == n - 1) tc::mma_commit(&bars[Q_EMPTY]);
+          if (j == n - 1) tc::mma_commit(&bars[C::SPLIT ? QK_DONE : Q_EMPTY]);
           if (j >= 1 && !pv(g - 1, j == 1, ii)) { ok = false; break; }
         }
         if (!ok || !pv(g - 1, n == 1, ii)) { *abort_flag = 1; break; }
@@ -449,11 +461,51 @@ __global__ void __launch_bounds__(Cfg<D, SEP_V>::NT, 1)
   } else if (warp >= 8 && epi_warps) {
     // ---------------------------------------------------------------- epilogue (window-only)
     const int sw = warp - 8, r = sw * 32 + lane;  // TMEM lane quarter warp % 4, as the softmax
+    // SPLIT: Q of item number k (shared tile, 64-channel blocks of 128-byte rows with 16-byte
+    // chunks swizzled by row % 8) -> TMEM lane r, columns C_QT.. as bf16 pairs; the previous
+    // item's QK^T MMAs have completed (QK_DONE), and the shared buffer is released at once
+    auto q_to_tmem = [&](int k) {
+      if (!tc::mbar_wait(&bars[Q_FULL], k & 1, a.err, 324)) return false;
+      if (k > 0 && !tc::mbar_wait(&bars[QK_DONE], (k - 1) & 1, a.err, 325)) return false;
+      tc::fence_after_sync();
+#pragma unroll
+      for (int cb = 0; cb < C::DB; ++cb) {
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          uint32_t v[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int ch = h2 * 4 + c;
+            uint4 x;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w)
+                         : "r"(smem_u32(qs + cb * 128 * 128 + r * 128 + ((ch ^ (r & 7)) * 16)))
+                         : "memory");
+            v[4 * c] = x.x;
+            v[4 * c + 1] = x.y;
+            v[4 * c + 2] = x.z;
+            v[4 * c + 3] = x.w;
+          }
+          tc::tmem_st16(tc::taddr(tmem, sw * 32, C::C_QT + cb * 32 + h2 * 16), v);
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(&bars[QT_FULL]);
+        tc::mbar_arrive(&bars[Q_EMPTY]);
+      }
+      return true;
+    };
+    if (C::SPLIT && (int)blockIdx.x < items && !q_to_tmem(0)) *abort_flag = 1;
     int ii = 0;
     for (int it = blockIdx.x; it < items && !*abort_flag; it += gridDim.x, ++ii) {
       const Item m = make_item<NK>(a, it, n_qt);
       const int t = m.t0 + r / a.H, h = r % a.H;
       const bool row_ok = t < a.S;
+      // the next item's Q first: its QK^T can start while this item's O is written
+      if (C::SPLIT && it + (int)gridDim.x < items && !q_to_tmem(ii + 1)) { *abort_flag = 1; break; }
       if (!tc::mbar_wait(&bars[EPI_FULL], ii & 1, a.err, 323) ||
           !tc::mbar_wait(&bars[O_FINAL], ii & 1, a.err, 322)) { *abort_flag = 1; break; }
       tc::fence_after_sync();

@@ -125,13 +125,17 @@ def test_swa_windows_and_sinks(cuda, window):
 
 
 @pytest.mark.gpu
-def test_swa_separate_v(cuda):
+@pytest.mark.parametrize("B,S,H,D,window", [(2, 300, 64, 128, 160), (1, 1200, 64, 128, 512), (2, 700, 16, 64, 300),
+                                            (1, 500, 8, 256, 200)])
+def test_swa_separate_v(cuda, B, S, H, D, window):
+    # several query-tile items per CTA (S = 1200 at 64 heads is 600 items), ragged last
+    # tiles, head dims 64 / 128 (two softmax warpgroups) and 256
     import torch
     from mzoo_b200 import swa_attn
-    q, kv, v, _, _, _ = _inputs(torch, cuda, 2, 300, 64, 128, seed=4, sep_v=True)
-    o, lse = swa_attn.fwd(q, kv, window=160, v=v)
-    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=160, v=_np(v)[:, :, 0])
-    _check(o, lse, ref_o, ref_lse, "swa K!=V")
+    q, kv, v, _, _, _ = _inputs(torch, cuda, B, S, H, D, seed=4, sep_v=True)
+    o, lse = swa_attn.fwd(q, kv, window=window, v=v)
+    ref_o, ref_lse = A.attend(_np(q), _np(kv)[:, :, 0], window=window, v=_np(v)[:, :, 0])
+    _check(o, lse, ref_o, ref_lse, f"swa K!=V S{S} H{H} D{D}")
 
 
 @pytest.mark.gpu
