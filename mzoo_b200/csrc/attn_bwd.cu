@@ -16,10 +16,12 @@
 //               front of its own columns, which the TS MMAs dV += P^T dO, dK += dS^T Q
 //               read as their A operand.
 //   dq          query owner: 128 rows; loops over window tiles then gathered tiles;
-//               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K; window-only: warps
-//               8-11 take the upper column half, its dS in the unused dM columns); gathered tiles also
+//               S = Q K^T, dP = dO V^T; dS -> TMEM (A of dQ += dS K); gathered tiles also
 //               keep dS and P in shared memory for dM = dS^T Q + P^T dO, scattered into
-//               dmain by the compute warps with fp32 atomics.
+//               dmain by the compute warps with fp32 atomics.  Window-only (separate V):
+//               warps 8-11 take the upper key half of every tile and copy each item's Q /
+//               dO rows into the unused dM columns, so S and dP are TS MMAs issued per key
+//               half and software-pipelined across the two warpgroups.
 // Column visibility (window run, or a token's valid gathered slots) is one mask word per
 // 32 columns, built per tile.  D = 256 (K == V): the key owner keeps one Q/dO stage and a
 // merged dK + dV accumulator; the query owner uses 64-key tiles and forms the gathered-row

@@ -21,7 +21,9 @@
 //   warps 12-15 (separate V, D <= 128 only) a second softmax warpgroup on the upper half of
 //               each tile's key columns; the pair of warps on one TMEM lane quarter swaps
 //               partial row maxima through TMEM columns [X_COL, X_COL + 4) under a count-2
-//               mbarrier, and the upper half's row sum reaches the epilogue the same way
+//               mbarrier, and the upper half's row sum reaches the epilogue the same way;
+//               there warps 8-11 also copy each item's Q rows into TMEM one item ahead, so
+//               QK^T is a TS MMA and the Q buffer is free for the next item at once
 // S = Q K^T (M=128 rows, N=NK keys) and O += P V (N=D) accumulate in TMEM; P (bf16) is
 // written back into its S buffer and read from there as the A operand of the PV MMA, so
 // shared memory carries only Q, K and V.  MMA order QK_0, QK_1, PV_0, QK_2, PV_1, ...
