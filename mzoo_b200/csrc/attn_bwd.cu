@@ -874,44 +874,78 @@ __global__ void __launch_bounds__(384, 1)
         const bool warp_full = __all_sync(0xffffffffu, full);
         if (!tc::mbar_wait(&bars[second ? S_FULL_Q1 : S_FULL_Q], g & 1, a.err, 520)) { ok = false; break; }
         tc::fence_after_sync();
-#pragma unroll 1
-        for (int c0 = cbeg; c0 < cend; c0 += 32) {
-          uint32_t sv[32], dv[32];
-          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
-          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
-          // this row's valid columns of the chunk as bits (window run, or its gathered slots)
-          uint32_t mw = 0xFFFFFFFFu;
+if constexpr (C::SPLIT) {
+          // window tiles only: both 32-column chunks of this warpgroup's key half in flight at
+          // once, so the half costs one TMEM load round trip (this step is on the critical
+          // path between the two halves' MMAs)
+          uint32_t sv0[32], dv0[32], sv1[32], dv1[32];
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + cbeg), sv0);
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + cbeg), dv0);
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + cbeg + 32), sv1);
+          tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + cbeg + 32), dv1);
+          uint32_t mw0 = 0xFFFFFFFFu, mw1 = 0xFFFFFFFFu;
           if (!warp_full) {
-            mw = 0u;
-            if (row_ok) mw = win ? run_bits(wlo - c0, whi - c0) : (tr == gtok ? gmask[c0 >> 5] : 0u);
+            mw0 = row_ok ? run_bits(wlo - cbeg, whi - cbeg) : 0u;
+            mw1 = row_ok ? run_bits(wlo - cbeg - 32, whi - cbeg - 32) : 0u;
           }
           tc::tmem_wait_ld();
-          tc::reg_after_wait(sv);
-          tc::reg_after_wait(dv);
-          // P and dS overwrite S and dP in place; only gathered tiles pack the extra copies
+          tc::reg_after_wait(sv0);
+          tc::reg_after_wait(dv0);
+          tc::reg_after_wait(sv1);
+          tc::reg_after_wait(dv1);
+          auto chunk = [&](const int c0, const uint32_t mw, uint32_t(&sv)[32], uint32_t(&dv)[32]) {
+            uint32_t dd[16];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float p = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
-            sv[c] = __float_as_uint(p);
-            dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - dl));
-          }
-          uint32_t dd[16];
-#pragma unroll
-          for (int q = 0; q < 16; ++q) dd[q] = pack_bf16(__uint_as_float(dv[2 * q]), __uint_as_float(dv[2 * q + 1]));
-          tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_S + KT / 2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
-          if (!win) {  // keep scale*dS (dK carries the softmax scale) and P in smem for the gathered-row gradient
-            uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
-            uint8_t* pr = dsr + C::P_BYTES;
-            auto ds2 = [&](int c) {
-              return pack_bf16(__uint_as_float(dv[c]) * a.scale, __uint_as_float(dv[c + 1]) * a.scale);
-            };
-            auto pp2 = [&](int c) { return pack_bf16(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])); };
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const int ch = ((c0 & 63) >> 3) + q;
-              const int c = 8 * q;
-              st_shared16(dsr + ((ch ^ (r & 7)) * 16), make_uint4(ds2(c), ds2(c + 2), ds2(c + 4), ds2(c + 6)));
-              st_shared16(pr + ((ch ^ (r & 7)) * 16), make_uint4(pp2(c), pp2(c + 2), pp2(c + 4), pp2(c + 6)));
+            for (int q = 0; q < 16; ++q) {
+              const int c = 2 * q;
+              const float p0 = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
+              const float p1 = (mw >> (c + 1)) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c + 1]), sl, -l2)) : 0.0f;
+              dd[q] = pack_bf16(p0 * (__uint_as_float(dv[c]) - dl), p1 * (__uint_as_float(dv[c + 1]) - dl));
+            }
+            tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_S + KT / 2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
+          };
+          chunk(cbeg, mw0, sv0, dv0);
+          chunk(cbeg + 32, mw1, sv1, dv1);
+        } else {
+  #pragma unroll 1
+          for (int c0 = cbeg; c0 < cend; c0 += 32) {
+            uint32_t sv[32], dv[32];
+            tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_S + c0), sv);
+            tc::tmem_ld32(tc::taddr(tmem, sw * 32, C::C_DP + c0), dv);
+            // this row's valid columns of the chunk as bits (window run, or its gathered slots)
+            uint32_t mw = 0xFFFFFFFFu;
+            if (!warp_full) {
+              mw = 0u;
+              if (row_ok) mw = win ? run_bits(wlo - c0, whi - c0) : (tr == gtok ? gmask[c0 >> 5] : 0u);
+            }
+            tc::tmem_wait_ld();
+            tc::reg_after_wait(sv);
+            tc::reg_after_wait(dv);
+            // P and dS overwrite S and dP in place; only gathered tiles pack the extra copies
+  #pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const float p = (mw >> c) & 1u ? fast_exp2(fmaf(__uint_as_float(sv[c]), sl, -l2)) : 0.0f;
+              sv[c] = __float_as_uint(p);
+              dv[c] = __float_as_uint(p * (__uint_as_float(dv[c]) - dl));
+            }
+            uint32_t dd[16];
+  #pragma unroll
+            for (int q = 0; q < 16; ++q) dd[q] = pack_bf16(__uint_as_float(dv[2 * q]), __uint_as_float(dv[2 * q + 1]));
+            tc::tmem_st16(tc::taddr(tmem, sw * 32, second ? C::C_S + KT / 2 + (c0 - KT / 2) / 2 : C::C_S + c0 / 2), dd);
+            if (!win) {  // keep scale*dS (dK carries the softmax scale) and P in smem for the gathered-row gradient
+              uint8_t* dsr = dss + (c0 >> 6) * 16384 + r * 128;
+              uint8_t* pr = dsr + C::P_BYTES;
+              auto ds2 = [&](int c) {
+                return pack_bf16(__uint_as_float(dv[c]) * a.scale, __uint_as_float(dv[c + 1]) * a.scale);
+              };
+              auto pp2 = [&](int c) { return pack_bf16(__uint_as_float(sv[c]), __uint_as_float(sv[c + 1])); };
+  #pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int ch = ((c0 & 63) >> 3) + q;
+                const int c = 8 * q;
+                st_shared16(dsr + ((ch ^ (r & 7)) * 16), make_uint4(ds2(c), ds2(c + 2), ds2(c + 4), ds2(c + 6)));
+                st_shared16(pr + ((ch ^ (r & 7)) * 16), make_uint4(pp2(c), pp2(c + 2), pp2(c + 4), pp2(c + 6)));
+              }
             }
           }
         }
