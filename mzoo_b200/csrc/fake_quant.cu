@@ -73,6 +73,25 @@ __device__ __forceinline__ float amax_step(float a, float v) {
   return (isnan(a) || isnan(v)) ? __uint_as_float(0x7fffffffu) : fmaxf(a, fabsf(v));
 }
 
+// The same over eight bf16 values in their packed form: |x| by clearing the sign bits, then
+// NaN-propagating bf16x2 maxima (bf16 -> f32 is exact, so the maximum is the same value);
+// three packed instructions in place of eight conversions and eight scalar steps.
+__device__ __forceinline__ float bf16x8_amax(const uint4 w) {
+  uint32_t m;
+  asm("{\n\t.reg .b32 a, b, c, d;\n\t"
+      "and.b32 a, %1, 0x7FFF7FFF;\n\t"
+      "and.b32 b, %2, 0x7FFF7FFF;\n\t"
+      "and.b32 c, %3, 0x7FFF7FFF;\n\t"
+      "and.b32 d, %4, 0x7FFF7FFF;\n\t"
+      "max.NaN.bf16x2 a, a, b;\n\t"
+      "max.NaN.bf16x2 c, c, d;\n\t"
+      "max.NaN.bf16x2 %0, a, c;\n\t}"
+      : "=r"(m)
+      : "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w));
+  const float lo = __uint_as_float(m << 16), hi = __uint_as_float(m & 0xFFFF0000u);
+  return (isnan(lo) || isnan(hi)) ? __uint_as_float(0x7fffffffu) : fmaxf(lo, hi);
+}
+
 template <int DT, int G, class Op>
 __global__ void __launch_bounds__(256) fq_vec_kernel(const void* __restrict__ x_, void* __restrict__ y_,
                                                       int64_t total_threads, Op op) {
@@ -103,9 +122,12 @@ __global__ void __launch_bounds__(256) fq_vec_kernel(const void* __restrict__ x_
       float amax = 0.0f;
       const T* e = reinterpret_cast<const T*>(&raw[u]);
 #pragma unroll
-      for (int i = 0; i < V; ++i) {
-        v[i] = E::load(e[i]);
-        amax = amax_step(amax, v[i]);
+      for (int i = 0; i < V; ++i) v[i] = E::load(e[i]);
+      if constexpr (DT == MZB_BF16) {
+        amax = bf16x8_amax(raw[u]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) amax = amax_step(amax, v[i]);
       }
 #pragma unroll
       for (int off = 1; off < G; off <<= 1) {
