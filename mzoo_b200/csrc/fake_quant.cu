@@ -17,8 +17,10 @@ namespace mzb {
 enum Fp4Rule { FP4_UE8M0 = 0, FP4_E4M3 = 1, FP4_OCP = 2 };
 enum Fp8Rule { FP8_UE8M0 = 0, FP8_ABSMAX = 1 };
 
+// The rule is a template parameter: every per-element choice below is made at compile time.
+template <int RULE>
 struct Fp4Op {
-  int rule;
+  static constexpr int rule = RULE;
   __device__ __forceinline__ float scale(float amax) const {
     if (rule == FP4_E4M3) {
       return e4m3_round(__fdiv_rn(fmaxf(amax, 6.0f * 0x1p-9f), 6.0f));
@@ -50,8 +52,9 @@ struct Fp4Op {
   }
 };
 
+template <int RULE>
 struct Fp8Op {
-  int rule;
+  static constexpr int rule = RULE;
   __device__ __forceinline__ float scale(float amax) const {
     if (rule == FP8_UE8M0) return pow2_ceil(__fmul_rn(fmaxf(amax, 1e-4f), 1.0f / 448.0f));
     float s = __fdiv_rn(amax, 448.0f);
@@ -224,11 +227,16 @@ static int dispatch_fq(const void* x, void* y, int64_t rows, int64_t n, int dtyp
 extern "C" int mzb_fq_fp4(const void* x, void* y, int64_t rows, int64_t n, int dtype, int block_size,
                           int rule, void* stream) {
   MZB_REQUIRE(rule >= 0 && rule <= 2, MZB_ERR_UNSUPPORTED, "mzb_fq_fp4: unknown rule %d", rule);
-  return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp4Op{rule}, static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rule == mzb::FP4_UE8M0) return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp4Op<mzb::FP4_UE8M0>{}, st);
+  if (rule == mzb::FP4_E4M3) return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp4Op<mzb::FP4_E4M3>{}, st);
+  return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp4Op<mzb::FP4_OCP>{}, st);
 }
 
 extern "C" int mzb_fq_fp8(const void* x, void* y, int64_t rows, int64_t n, int dtype, int block_size,
                           int rule, void* stream) {
   MZB_REQUIRE(rule >= 0 && rule <= 1, MZB_ERR_UNSUPPORTED, "mzb_fq_fp8: unknown rule %d", rule);
-  return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp8Op{rule}, static_cast<cudaStream_t>(stream));
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rule == mzb::FP8_UE8M0) return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp8Op<mzb::FP8_UE8M0>{}, st);
+  return mzb::dispatch_fq(x, y, rows, n, dtype, block_size, mzb::Fp8Op<mzb::FP8_ABSMAX>{}, st);
 }
