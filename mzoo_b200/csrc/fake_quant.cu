@@ -42,9 +42,12 @@ struct Fp4Op {
     float q = clamp_nan(pow2() ? __fmul_rn(x, inv) : __fdiv_rn(x, s), -6.0f, 6.0f);
     return __fmul_rn(e2m1_value(q), s);
   }
+  // The clamp to [-6, 6] of `apply` is left to the conversion: `satfinite` saturates
+  // |q| > 6 (infinities included) to the largest code, 6, which is what rounding the
+  // clamped value gives, and a NaN q is mapped to 0 from q itself.
   __device__ __forceinline__ void apply2(float x0, float x1, float s, float inv, float& r0, float& r1) const {
-    const float q0 = clamp_nan(pow2() ? __fmul_rn(x0, inv) : __fdiv_rn(x0, s), -6.0f, 6.0f);
-    const float q1 = clamp_nan(pow2() ? __fmul_rn(x1, inv) : __fdiv_rn(x1, s), -6.0f, 6.0f);
+    const float q0 = pow2() ? __fmul_rn(x0, inv) : __fdiv_rn(x0, s);
+    const float q1 = pow2() ? __fmul_rn(x1, inv) : __fdiv_rn(x1, s);
     float v0, v1;
     e2m1_value2(q0, q1, v0, v1);
     r0 = __fmul_rn(v0, s);
